@@ -1,0 +1,344 @@
+/* ork_oracle.c -- CPU restatement of ork-driver's resident-weight matmul path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the checker that the B200 library is compared against; it is
+ * never linked into, loaded by, or called from the product library (ork-driver_b200/). Only tests/,
+ * __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference legs load it.
+ *
+ * Every function restates one piece of the reference (paths are relative to the ork-driver project) in
+ * plain scalar C. Build flags: -O2 -ffp-contract=off, so the float quantizers round exactly like the
+ * reference's x86 scalar build (no FMA contraction; lrintf = round-half-even in the default FP mode).
+ *
+ * Parity pin: the integer GEMM reproduces the reference's own fnv64 goldens (examples/quant.c:72-81,
+ * examples/test_matmul.c:84-86, :611-612, :639-641) and the quantizers/O4N1 writer are compared byte for
+ * byte against the reference's compiled CPU code (oracle/_ref, built by oracle/Makefile) by
+ * tests/golden/make_fixtures.py and tests/test_oracle.py.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ---------------------------------------------------------------------------------------------------
+ * Integer GEMM. src/npu/core/buf.c:428-477 (orki_cpu_gemm_i32): C[M][N] int32 = A[M][K] int8 x B[K][N]
+ * int8 (B row-major), k-outer AXPY into a zeroed C row, exact int32 accumulation. Parallel over M. */
+ORC_API void orc_gemm_i32(int M, int K, int N, const int8_t *A, const int8_t *B, int32_t *C)
+{
+#pragma omp parallel for schedule(static) if (M > 1)
+    for (int m = 0; m < M; m++) {
+        const int8_t *arow = A + (size_t)m * K;
+        int32_t *crow = C + (size_t)m * N;
+        for (int n = 0; n < N; n++) crow[n] = 0;
+        for (int k = 0; k < K; k++) {
+            const int32_t a = arow[k];
+            if (!a) continue;
+            const int8_t *brow = B + (size_t)k * N;
+            for (int n = 0; n < N; n++) crow[n] += a * (int32_t)brow[n];
+        }
+    }
+}
+
+/* Same arithmetic with B given n-major (Bt[N][K]), which is how the quantizers emit codes. */
+ORC_API void orc_gemm_i32_nk(int M, int K, int N, const int8_t *A, const int8_t *Bt, int32_t *C)
+{
+#pragma omp parallel for schedule(static) collapse(2) if (M * N > 64)
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++) {
+            const int8_t *a = A + (size_t)m * K, *b = Bt + (size_t)n * K;
+            int32_t s = 0;
+            for (int k = 0; k < K; k++) s += (int32_t)a[k] * (int32_t)b[k];
+            C[(size_t)m * N + n] = s;
+        }
+}
+
+/* ---------------------------------------------------------------------------------------------------
+ * fp16 reference. examples/test_matmul.c:37 and examples/layer.c:43: C[m][n] = sequential f32 sum over k
+ * of (float)A[m][k] * (float)B[k][n]; A [M][K], B [K][N] row-major IEEE half bit patterns. */
+static float orc_h2f(uint16_t h)
+{
+    uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 0x1f, f = h & 0x3ff, u;
+    if (e == 0) {
+        if (f == 0) u = s;
+        else { /* subnormal: renormalise */
+            int sh = 0;
+            while (!(f & 0x400)) { f <<= 1; sh++; }
+            f &= 0x3ff;
+            u = s | ((uint32_t)(113 - sh) << 23) | (f << 13);
+        }
+    } else if (e == 31) u = s | 0x7f800000u | (f << 13);
+    else u = s | ((e + 112) << 23) | (f << 13);
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
+ORC_API void orc_gemm_f16(int M, int K, int N, const uint16_t *A, const uint16_t *B, float *C)
+{
+    float *bt = (float *)malloc((size_t)K * N * sizeof(float));
+    if (!bt) return;
+    for (size_t i = 0; i < (size_t)K * N; i++) bt[i] = orc_h2f(B[i]);
+#pragma omp parallel for schedule(static) if (M > 1)
+    for (int m = 0; m < M; m++) {
+        float *acc = C + (size_t)m * N;
+        for (int n = 0; n < N; n++) acc[n] = 0.0f;
+        for (int k = 0; k < K; k++) { /* k-outer keeps the per-(m,n) sum sequential in k */
+            const float a = orc_h2f(A[(size_t)m * K + k]);
+            const float *brow = bt + (size_t)k * N;
+            for (int n = 0; n < N; n++) acc[n] += a * brow[n];
+        }
+    }
+    free(bt);
+}
+
+/* ---------------------------------------------------------------------------------------------------
+ * Per-output-channel int8 quantization of f32[N][K] (n-major).
+ * src/npu.c:854-865 (orki_chan_scales_f32): mx = max(1e-9, max|w|), inv = 127/mx, bscale = mx/127;
+ * src/npu/i8/pack.c:450-452 (quant32_f32_i8, scalar branch): q = lrintf(w*inv) clamped to [-127,127].
+ * codes_nk is [N][K]; bscale may be NULL. */
+ORC_API void orc_i8_quant_f32(int K, int N, const float *f32, int8_t *codes_nk, float *bscale)
+{
+    for (int n = 0; n < N; n++) {
+        const float *fr = f32 + (size_t)n * K;
+        float mx = 1e-9f;
+        for (int k = 0; k < K; k++) { float v = fabsf(fr[k]); if (v > mx) mx = v; }
+        const float inv = 127.0f / mx;
+        if (bscale) bscale[n] = mx / 127.0f;
+        int8_t *dst = codes_nk + (size_t)n * K;
+        for (int k = 0; k < K; k++) {
+            int q = (int)lrintf(fr[k] * inv);
+            dst[k] = (int8_t)(q > 127 ? 127 : q < -127 ? -127 : q);
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------------------------------
+ * int4 / NF4 quantizers. */
+
+/* src/npu.c:888-892 (ORKI_NF4_LEVELS): the 16 normalised NF4 levels. */
+static const float ORC_NF4[16] = {
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+
+/* src/npu/i4/quant.c:26 (ORK_IM_CLIP_GRID): clip ratios tried by the imatrix scale search. */
+static const float ORC_CLIP[7] = {1.0f, 0.92f, 0.85f, 0.78f, 0.70f, 0.62f, 0.55f};
+
+/* src/npu/internal.h:589 (ork_xs32): the xorshift32 used for stochastic rounding. */
+static uint32_t orc_xs32(uint32_t *s) { uint32_t x = *s; x ^= x << 13; x ^= x >> 17; x ^= x << 5; *s = x; return x; }
+
+/* src/npu/i4/pack.c:128-131 et al.: the NF4 int8 LUT, lut[i] = (int8)lrintf(level[i]*127). */
+ORC_API void orc_nf4_lut(int8_t lut[16])
+{
+    for (int i = 0; i < 16; i++) lut[i] = (int8_t)lrintf(ORC_NF4[i] * 127.0f);
+}
+
+/* NF4 nearest/stochastic index of one normalised weight. src/npu/i4/quant.c:73-86: clamp to [-1,1],
+ * hi = first level >= wn, lo = hi-1 (or 0); ties (t >= 0.5) go to hi; SR picks hi when t > u. */
+static int orc_nf4_index(float wn, int sr, uint32_t *seed)
+{
+    if (wn > 1.0f) wn = 1.0f; else if (wn < -1.0f) wn = -1.0f;
+    int hi = 0;
+    while (hi < 15 && ORC_NF4[hi] < wn) hi++;
+    int lo = hi > 0 ? hi - 1 : 0;
+    if (lo == hi) return hi;
+    float t = (wn - ORC_NF4[lo]) / (ORC_NF4[hi] - ORC_NF4[lo]);
+    if (sr) {
+        float u = (float)(orc_xs32(seed) >> 8) * (1.0f / 16777216.0f);
+        return (t > u) ? hi : lo;
+    }
+    return (t >= 0.5f) ? hi : lo;
+}
+
+/* Weighted reconstruction error of one channel at a candidate absmax. src/npu/i4/quant.c:130-151
+ * (wq_err_chan): f32 sequential sum of im[k]*d*d (strict left-to-right, no contraction). */
+static float orc_wq_err(const float *fr, int K, float absmax, int nf4, const float *im)
+{
+    float e = 0.0f;
+    if (nf4) {
+        float sc = absmax / 127.0f, inv = absmax > 0 ? 1.0f / absmax : 0.0f;
+        for (int k = 0; k < K; k++) {
+            int idx = orc_nf4_index(fr[k] * inv, 0, NULL);
+            float dq = (float)((int8_t)lrintf(ORC_NF4[idx] * 127.0f)) * sc;
+            float d = fr[k] - dq;
+            e += (im ? im[k] : 1.0f) * d * d;
+        }
+    } else {
+        float scale = absmax / 7.0f, inv = scale > 0 ? 1.0f / scale : 0.0f;
+        for (int k = 0; k < K; k++) {
+            int q = (int)lrintf(fr[k] * inv);
+            if (q > 7) q = 7; else if (q < -7) q = -7;
+            float dq = (float)q * scale;
+            float d = fr[k] - dq;
+            e += (im ? im[k] : 1.0f) * d * d;
+        }
+    }
+    return e;
+}
+
+/* src/npu/i4/quant.c:153-161 (orki_wq_best_absmax): try each clip ratio, keep the strictly smaller error. */
+static float orc_best_absmax(const float *fr, int K, float raw, int nf4, const float *im)
+{
+    float best_abs = raw, best_e = orc_wq_err(fr, K, raw, nf4, im);
+    for (int g = 1; g < 7; g++) {
+        float cand = raw * ORC_CLIP[g];
+        float e = orc_wq_err(fr, K, cand, nf4, im);
+        if (e < best_e) { best_e = e; best_abs = cand; }
+    }
+    return best_abs;
+}
+
+/* The compact O4N1 blob of ork_i4a8_mm_pack_im + ork_i4a8_w_dump, equivalently ork_i4a8_pack_cpu_blob.
+ * src/npu/i4/pack.c:806-863 (ork_i4a8_pack_cpu_blob_qerr) with quant.c:28-40 (uniform) and :70-90 (NF4):
+ *   header {u32 0x4F344E31, u32 version=1, i32 K, i32 N, u32 quant_kind} (src/npu/internal.h:584,597),
+ *   bscale[N] f32, then Bi4[N][K/2] with the low nibble holding the even k.
+ *   per channel: mx = max(1e-9, max|w|) -> optional imatrix clip search -> uniform: scale = mx/7,
+ *   q = clamp(lrintf(w*(1/scale)), +-7) stored as q&0xf; NF4: bscale = mx/127, index of the nearest level.
+ *   sr != 0 reproduces ORK_SR (one xorshift stream seeded 0x2545F491 for the whole call).
+ * Returns the blob size (out == NULL queries the size), or 0 on bad dims / short cap. */
+ORC_API size_t orc_i4a8_blob(int K, int N, const float *f32, const float *imatrix, int nf4, int sr,
+                             void *out, size_t cap)
+{
+    if (K % 32 || N % 32 || !f32 || K <= 0 || N <= 0) return 0;
+    const size_t hdr = 20, sc = (size_t)N * 4, nib = (size_t)K * N / 2, need = hdr + sc + nib;
+    if (!out) return need;
+    if (cap < need) return 0;
+    nf4 = nf4 ? 1 : 0;
+    uint32_t seed = 0x2545F491u;
+    uint8_t *p = (uint8_t *)out;
+    float *bscale = (float *)(p + hdr);
+    uint8_t *bi4 = p + hdr + sc;
+    for (int n = 0; n < N; n++) {
+        const float *fr = f32 + (size_t)n * K;
+        float mx = 1e-9f;
+        for (int k = 0; k < K; k++) { float v = fabsf(fr[k]); if (v > mx) mx = v; }
+        if (imatrix) mx = orc_best_absmax(fr, K, mx, nf4, imatrix);
+        uint8_t *nb = bi4 + (size_t)n * (K / 2);
+        if (nf4) {
+            bscale[n] = mx / 127.0f;
+            float inv = mx > 0 ? 1.0f / mx : 0.0f;
+            for (int k = 0; k < K; k++) {
+                uint8_t v = (uint8_t)(orc_nf4_index(fr[k] * inv, sr, &seed) & 0xf);
+                if (k & 1) nb[k >> 1] |= (uint8_t)(v << 4); else nb[k >> 1] = v;
+            }
+        } else {
+            float scale = mx / 7.0f;
+            bscale[n] = scale;
+            float inv = scale > 0 ? 1.0f / scale : 0.0f;
+            for (int k = 0; k < K; k++) {
+                int q;
+                if (sr) {
+                    float u = (float)(orc_xs32(&seed) >> 8) * (1.0f / 16777216.0f);
+                    q = (int)floorf(fr[k] * inv + u);
+                } else q = (int)lrintf(fr[k] * inv);
+                if (q > 7) q = 7; else if (q < -7) q = -7;
+                uint8_t v = (uint8_t)(q & 0xf);
+                if (k & 1) nb[k >> 1] |= (uint8_t)(v << 4); else nb[k >> 1] = v;
+            }
+        }
+    }
+    uint32_t h[5] = {0x4F344E31u, 1u, (uint32_t)K, (uint32_t)N, (uint32_t)(nf4 ? 1 : 0)};
+    memcpy(p, h, hdr);
+    return need;
+}
+
+/* Decode an O4N1 blob to int8 codes exactly as the offline loader does. src/npu/i4/pack.c:115-150
+ * (ork_i4a8_mm_load): exact size, magic, version 1, K, N and kind checks; uniform nibbles sign-extend,
+ * NF4 nibbles map through lut[]. codes_kn is [K][N] (the reference's cpu_codes orientation). Returns 0 on
+ * success, -1 on a refused blob. */
+ORC_API int orc_i4a8_blob_codes(int K, int N, const void *blob, size_t n, int8_t *codes_kn, float *bscale, int *qk)
+{
+    if (K % 32 || N % 32 || K <= 0 || N <= 0 || !blob) return -1;
+    const size_t hdr = 20, sc = (size_t)N * 4, nib = (size_t)K * N / 2;
+    if (n != hdr + sc + nib) return -1;
+    uint32_t h[5];
+    memcpy(h, blob, hdr);
+    if (h[0] != 0x4F344E31u || h[1] != 1u || (int32_t)h[2] != K || (int32_t)h[3] != N) return -1;
+    if (h[4] != 0 && h[4] != 1) return -1;
+    const uint8_t *p = (const uint8_t *)blob;
+    if (bscale) memcpy(bscale, p + hdr, sc);
+    if (qk) *qk = (int)h[4];
+    int8_t lut[16];
+    orc_nf4_lut(lut);
+    const uint8_t *nibs = p + hdr + sc;
+    for (int nn = 0; nn < N; nn++) {
+        const uint8_t *nb = nibs + (size_t)nn * (K / 2);
+        for (int k = 0; k < K; k++) {
+            uint8_t ix = (k & 1) ? (nb[k >> 1] >> 4) : (nb[k >> 1] & 0xf);
+            codes_kn[(size_t)k * N + nn] = h[4] ? lut[ix] : (int8_t)(ix >= 8 ? (int)ix - 16 : (int)ix);
+        }
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------------
+ * Fixed-seed input generators of the reference's example tests (restated so golden checksums can be
+ * reproduced on identical inputs), and the FNV-1a checksum they hash the int32 output with. */
+
+/* examples/quant.c:18 (frand): sd = sd*1103515245 + 12345; ((int)((sd>>9)&0x3fff) - 8192)/16384.0f. */
+ORC_API void orc_gen_frand(uint32_t *sd, float *out, size_t n)
+{
+    uint32_t s = *sd;
+    for (size_t i = 0; i < n; i++) {
+        s = s * 1103515245u + 12345u;
+        out[i] = ((int)((s >> 9) & 0x3fff) - 8192) / 16384.0f;
+    }
+    *sd = s;
+}
+
+/* examples/test_matmul.c:11 (rnd): sd = sd*1103515245 + 12345; (sd>>16)%4; the int8 tests use rnd()-1. */
+ORC_API void orc_gen_rnd_i8(uint32_t *sd, int8_t *out, size_t n, int offset)
+{
+    uint32_t s = *sd;
+    for (size_t i = 0; i < n; i++) {
+        s = s * 1103515245u + 12345u;
+        out[i] = (int8_t)((int)((s >> 16) % 4) - offset);
+    }
+    *sd = s;
+}
+
+/* The same stream as IEEE half bit patterns of the small integers 0..3 (examples/test_matmul.c:23-24). */
+ORC_API void orc_gen_rnd_f16(uint32_t *sd, uint16_t *out, size_t n)
+{
+    static const uint16_t h[4] = {0x0000, 0x3c00, 0x4000, 0x4200}; /* 0.0, 1.0, 2.0, 3.0 */
+    uint32_t s = *sd;
+    for (size_t i = 0; i < n; i++) {
+        s = s * 1103515245u + 12345u;
+        out[i] = h[(s >> 16) % 4];
+    }
+    *sd = s;
+}
+
+/* Advance the LCG by n steps in O(log n) (affine-map squaring). */
+ORC_API uint32_t orc_lcg_skip(uint32_t sd, uint64_t n)
+{
+    uint32_t a = 1103515245u, c = 12345u, ra = 1u, rc = 0u;
+    while (n) {
+        if (n & 1) { ra = ra * a; rc = rc * a + c; }
+        c = c * a + c;
+        a = a * a;
+        n >>= 1;
+    }
+    return ra * sd + rc;
+}
+
+/* FNV-1a 64 chained over a buffer (examples/quant.c:22-23, examples/test_matmul.c:15-17). */
+ORC_API uint64_t orc_fnv64(uint64_t h, const void *p, size_t n)
+{
+    const uint8_t *b = (const uint8_t *)p;
+    for (size_t i = 0; i < n; i++) { h ^= b[i]; h *= 1099511628211ULL; }
+    return h;
+}
+
+ORC_API int orc_threads(void)
+{
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
