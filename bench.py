@@ -1,0 +1,350 @@
+#!/usr/bin/env python3
+"""bench.py -- throughput of the B200 resident-weight matmul engine on BASELINE configs[1].
+
+Workload (one "step"): the w8a8 per-channel GEMM sweep of configs[1] -- (K,N) in {(2048,2048),
+(2048,6144),(6144,2048)} x M in {1,8,128,512}, twelve ork_i8_mm_run calls -- with B ~ N(0,0.02) given as
+f32 [N][K] to ork_i8_mm_pack_f32 and A int8 ~ U[-127,127]. Metric: algorithmic HBM GB/s,
+bytes = K*N (weight) + M*K (A) + 4*M*N (int32 C) per call, summed over the step and divided by the step
+time; every config is HBM-bound by that formula on B200 (int32 C is heavy), so GB/s is the common unit.
+
+- value: device-resident inputs, the twelve calls queued back to back on the library's stream
+  (ork_i8_mm_run_async), timed with CUDA events on that stream, max over ranks.
+- e2e: the same sweep through the synchronous public call ork_i8_mm_run with pinned host buffers: each
+  call copies A in, runs, copies C out and synchronises.
+- L2: inputs larger than L2 -- 9 distinct packed copies of every weight (265 MB) plus per-copy A/C
+  buffers, cycled so no call finds its weight in the 126 MB L2.
+- roofline: the dominant kernel (largest share of the step) timed alone with CUDA events.
+- cpu_baseline / --impl reference: the reference's own CPU int8 GEMM (orki_cpu_gemm_i32 via
+  ork_i8_mm_run_cpu in oracle/_ref, OpenMP over M on all host cores) on the same sweep.
+
+Multi-GPU (torchrun, --gpus N): configs[1] does not shard, so every rank runs an independent replica of
+the sweep; value = total bytes of all ranks / max rank time (weak scaling).
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ork-driver_b200"))
+
+SHAPES = [(2048, 2048), (2048, 6144), (6144, 2048)]
+MS = [1, 8, 128, 512]
+CONFIGS = [(K, N, M) for (K, N) in SHAPES for M in MS]
+NCOPIES = 9
+WORKLOAD = ("w8a8 per-channel GEMM (BASELINE configs[1]): (K,N) in {(2048,2048),(2048,6144),(6144,2048)} x "
+            "M in {1,8,128,512}; B~N(0,0.02) f32 -> ork_i8_mm_pack_f32, A int8~U[-127,127], C int32")
+METRIC = "w8a8 GEMM algorithmic HBM GB/s (configs[1] sweep)"
+
+
+def alg_bytes(K, N, M):
+    return K * N + M * K + 4 * M * N
+
+
+STEP_BYTES = sum(alg_bytes(K, N, M) for K, N, M in CONFIGS)
+STEP_OPS = sum(2 * M * K * N for K, N, M in CONFIGS)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev, self.rows, self.p = dev, [], None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.p = None
+        return self
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) >= 9:
+                for name, v in zip(names, r[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_sweep(min_seconds, max_reps=3):
+    """The reference's CPU int8 GEMM over the sweep: oracle/_ref (its own code) if built, else the
+    restatement. Returns (GB/s, cores, kind, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_ffi as of
+
+    ref = of.reference()
+    kind = "reference" if ref is not None else "port"
+    rng = np.random.default_rng(0)
+    data = []
+    for K, N in SHAPES:
+        f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        codes, _ = of.i8_quant_f32(f32)
+        B = np.ascontiguousarray(codes.T)
+        for M in MS:
+            A = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+            data.append((K, N, M, A, B, np.zeros((M, N), np.int32)))
+    fn = ref.ork_i8_mm_run_cpu if ref is not None else of.restated().orc_gemm_i32
+    reps, t_total = 0, 0.0
+    while reps < max_reps and (reps == 0 or t_total < min_seconds):
+        t0 = time.perf_counter()
+        for K, N, M, A, B, Cm in data:
+            fn(M, K, N, of._p(A), of._p(B), of._p(Cm))
+        t_total += time.perf_counter() - t0
+        reps += 1
+    cores = of.restated().orc_threads()
+    gbs = STEP_BYTES * reps / t_total / 1e9
+    sample = f"{reps} full sweep(s) of the 12 configs[1] calls ({t_total:.2f} s)"
+    return gbs, cores, kind, sample, t_total / reps
+
+
+def run_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    per_step = []
+    cores = kind = sample = None
+    for _ in range(args.warmup):
+        cpu_reference_sweep(0.0, 1)
+    for _ in range(args.steps):
+        gbs, cores, kind, sample, t = cpu_reference_sweep(0.0, 1)
+        per_step.append(t)
+    t = statistics.mean(per_step)
+    value = STEP_BYTES / t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "parallelism": "host CPU, OpenMP over M"},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": f"each step = one full sweep of the 12 calls on the host ({sample})"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+
+    import ork_b200
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    L = ork_b200.lib()
+    ctx = ork_b200.Context()
+    stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+
+    # ---- weights: NCOPIES distinct packs of each shape (inputs larger than L2) ----------------
+    rng = np.random.default_rng(1234 + rank)
+    weights = {}
+    for K, N in SHAPES:
+        f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        weights[(K, N)] = []
+        for _ in range(NCOPIES):
+            w, _ = ctx.i8_pack_f32(f32)
+            assert w, "pack failed"
+            weights[(K, N)].append(w)
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    bufs = {}
+    for K, N, M in CONFIGS:
+        bufs[(K, N, M)] = [(torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g),
+                            torch.empty((M, N), dtype=torch.int32, device="cuda")) for _ in range(NCOPIES)]
+    torch.cuda.synchronize()
+
+    def call(K, N, M, i):
+        w = weights[(K, N)][i % NCOPIES]
+        a, c = bufs[(K, N, M)][i % NCOPIES]
+        rc = L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr())
+        assert rc == 0
+
+    def step(s):
+        for r, (K, N, M) in enumerate(CONFIGS):
+            call(K, N, M, s * len(CONFIGS) + r)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for s in range(args.warmup):
+        step(s)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ctx.launches()
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for s in range(args.steps):
+            step(args.warmup + s)
+        ev1.record(stream)
+        barrier()
+    launches = ctx.launches() - launches0
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * STEP_BYTES * args.steps / (ms / 1e3) / 1e9
+
+    # ---- per-config breakdown and the dominant kernel (each config alone, back to back) --------
+    breakdown = {}
+    reps = 30
+    for K, N, M in CONFIGS:
+        for i in range(3):
+            call(K, N, M, i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = ctx.launches()
+        e0.record(stream)
+        for i in range(reps):
+            call(K, N, M, i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / reps
+        nl = (ctx.launches() - l0) / reps
+        breakdown[f"{K}x{N}xM{M}"] = {"ms": per, "GB/s": alg_bytes(K, N, M) / (per / 1e3) / 1e9,
+                                      "TOPS": 2 * M * K * N / (per / 1e3) / 1e12, "launches": nl,
+                                      "route": L.ork_b200_route(weights[(K, N)][0].h, M)}
+    tot = sum(b["ms"] for b in breakdown.values())
+    dom = max(breakdown, key=lambda k: breakdown[k]["ms"])
+    K, N, M = (int(x) for x in dom.replace("M", "").split("x"))
+    hbm, bf16, src = peaks()
+    db = breakdown[dom]
+    per_launch_ms = db["ms"] / max(db["launches"], 1)
+    achieved = alg_bytes(K, N, M) / max(db["launches"], 1) / (per_launch_ms / 1e3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get(dom)
+    except Exception:
+        pass
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": traffic, "kernel": dom, "share": db["ms"] / tot, "peak_source": src,
+                "algorithmic_bytes_per_launch": alg_bytes(K, N, M) / max(db["launches"], 1)}
+
+    # ---- e2e through the synchronous public call with pinned host buffers ---------------------
+    host = {}
+    for K, N, M in CONFIGS:
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8).pin_memory()
+        c = torch.empty((M, N), dtype=torch.int32).pin_memory()
+        host[(K, N, M)] = (a, c)
+    h2d = sum(M * K for K, N, M in CONFIGS)
+    d2h = sum(4 * M * N for K, N, M in CONFIGS)
+
+    def e2e_step(s):
+        for r, (K, N, M) in enumerate(CONFIGS):
+            a, c = host[(K, N, M)]
+            w = weights[(K, N)][(s * len(CONFIGS) + r) % NCOPIES]
+            assert L.ork_i8_mm_run(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
+
+    for s in range(args.warmup):
+        e2e_step(s)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        e2e_step(s)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * STEP_BYTES * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, cores, kind, sample, _ = cpu_reference_sweep(10.0)
+        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+
+    dec = [k for k in breakdown if k.endswith("M1") or k.endswith("M8")]
+    pre = [k for k in breakdown if k not in dec]
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD,
+                       "l2": f"inputs larger than L2: {NCOPIES} distinct packed copies per weight "
+                             f"({NCOPIES * sum(K * N for K, N in SHAPES) / 1e6:.0f} MB) plus per-copy A/C, cycled",
+                       "parallelism": "replicas" if world > 1 else "single GPU",
+                       "step_bytes": STEP_BYTES, "step_ops": STEP_OPS},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+            "gpu_launches": int(launches),
+            "decode_gbs": sum(alg_bytes(*map(int, k.replace("M", "").split("x"))) for k in dec)
+            / (sum(breakdown[k]["ms"] for k in dec) / 1e3) / 1e9,
+            "prefill_tops": sum(2 * np.prod([int(x) for x in k.replace("M", "").split("x")]) for k in pre)
+            / (sum(breakdown[k]["ms"] for k in pre) / 1e3) / 1e12,
+            "breakdown": breakdown}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for ws in weights.values():
+        for w in ws:
+            w.free()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

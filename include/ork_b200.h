@@ -1,0 +1,51 @@
+/* ork_b200.h -- B200-specific additions to the ork_npu.h API (no counterpart in ork-driver).
+ *
+ * The reference's run calls are synchronous over host buffers; on a GPU the same matmuls are most
+ * useful stream-ordered over device buffers, so they can be queued back to back (or captured in a CUDA
+ * graph) without a host round trip per call. These entry points expose that, plus the little a caller
+ * needs to integrate the context with its own CUDA stream. Include after ork_npu.h.
+ */
+#ifndef ORK_B200_H
+#define ORK_B200_H
+#include "ork_npu.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Asynchronous device-pointer runs: A and C must be device memory of the context's GPU; the matmul is
+ * enqueued on the context's stream and the call returns without waiting. Same argument rules and return
+ * codes as the synchronous runs; launch errors are reported here, execution errors by ork_b200_sync. */
+int ork_i8_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
+int ork_i4_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
+int ork_f16_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *dA, float *dC);
+
+/* Wait for everything queued on the context's stream; 0 ok, -1 if the GPU reported an error. */
+int ork_b200_sync(ork_npu *ctx);
+/* The cudaStream_t the context queues on, and a way to substitute the caller's own stream (NULL restores
+ * the context's private stream). The caller keeps ownership of a stream it passes in. */
+void *ork_b200_stream(ork_npu *ctx);
+int ork_b200_set_stream(ork_npu *ctx, void *cuda_stream);
+/* CUDA device ordinal of the context. */
+int ork_b200_device(const ork_npu *ctx);
+/* Programmatic dependent launch for the async runs (default on): a queued matmul starts streaming its
+ * weights while the previous kernel on the stream drains, and waits for that kernel before reading A. */
+int ork_b200_set_pdl(ork_npu *ctx, int on);
+/* Number of kernels this context has launched (all kernels are this library's own). */
+uint64_t ork_b200_launches(const ork_npu *ctx);
+/* Device address and byte size of a weight's resident storage (read-only for callers). */
+const void *ork_b200_weight_ptr(const ork_w *w);
+/* Copy a weight's resident bytes (the K-major resident format: int8 [N][K], fp16 [N][K], or nibbles
+ * [N][K/2] with the low nibble holding the even k) to host memory. Returns the bytes copied, or the
+ * size needed when out is NULL, 0 on error or a short cap. For tests and tooling. */
+size_t ork_b200_weight_read(const ork_w *w, void *out, size_t cap);
+/* Which kernel path a run of M rows would take: 0 = CUDA-core decode GEMV, 1 = tcgen05 tensor-core
+ * GEMM. Exposed for tests and benchmarks. */
+int ork_b200_route(const ork_w *w, int M);
+/* Force a route for subsequent runs on this context: -1 automatic (default), 0 GEMV, 1 tensor core. */
+int ork_b200_force_route(ork_npu *ctx, int route);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ORK_B200_H */

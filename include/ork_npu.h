@@ -1,0 +1,131 @@
+/* ork_npu.h -- resident-weight matmul engine, B200 (sm_100a) implementation.
+ *
+ * Drop-in for the hot path of ork-driver's C API (ork-driver include/ork_npu.h and its parts
+ * include/ork/{context,weights,run}.h): pack a weight B[K,N] once into HBM-resident storage, then run
+ * C = A.B many times, and persist / reload int4 weights in the compact 'O4N1' blob. Same symbol names,
+ * argument meanings, return conventions and blob bytes as the reference; the device behind them is a
+ * CUDA GPU instead of an RK35xx NPU, so the NPU-specific surface (IOMMU domains, orkd, SDP LUTs, core
+ * budgets, regcmd probes) is not part of this library.
+ *
+ *   int8   C[M,N] int32 = A[M,K] int8  x B[K,N] int8   (raw sums; caller applies scales)
+ *   w4a8   C[M,N] int32 = A[M,K] int8  x int4-quantized B (uniform grid or NF4 codebook, nibbles in HBM)
+ *   W4A4   C[M,N] int32 = A[M,K] int4-in-int8 x B[K,N] int4-in-int8
+ *   fp16   C[M,N] fp32  = A[M,K] fp16  x B[K,N] fp16
+ *
+ * A and C are row-major; run calls are synchronous: when a run returns 0, C is complete. A and C may be
+ * host pointers (copied through the context's CUDA stream) or device pointers (used in place).
+ * Threading: one context per process and per GPU; calls on one context are not thread-safe, exactly as
+ * in the reference (ork-driver include/ork_npu.h:20, include/ork/context.h:60-68).
+ */
+#ifndef ORK_NPU_H
+#define ORK_NPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ork-driver include/ork_npu.h:19-21. The fp16 element type is the compiler's IEEE binary16; compilers
+ * without _Float16 may define ORK_F16_AS_U16 to see the same bits as uint16_t (identical ABI). */
+#ifdef ORK_F16_AS_U16
+typedef uint16_t ork_f16;
+#else
+typedef _Float16 ork_f16;
+#endif
+typedef struct ork_npu ork_npu; /* device context (one per process per GPU) */
+typedef struct ork_w ork_w;     /* resident packed weights for one B[K,N] */
+
+/* ork-driver include/ork_npu.h:30 and :37. */
+#define ORK_NPU_VERSION "1.0.190"
+#define ORK_PACK_FORMAT_VERSION 1u
+
+/* ork-driver include/ork/weights.h:115: int4 weight-store codebook kind. */
+enum { ORK_QK_UNIFORM = 0, ORK_QK_CODEBOOK_NF4 = 1 };
+
+/* ork-driver include/ork/run.h:27. Never returned here: every shape inside the API's dimension rules
+ * has a verified path on the GPU. Defined so callers that test for it still compile. */
+#define ORK_RC_WEDGE_PRONE (-501)
+
+/* ---- context (ork-driver include/ork/context.h) ------------------------------------------------ */
+
+/* include/ork/context.h:14. "1.0.190+b200". */
+const char *ork_npu_version(void);
+/* include/ork/context.h:37. The O4N1 blob version this build reads and writes (1). */
+uint32_t ork_pack_format_version(void);
+/* include/ork/context.h:73. Opens the calling thread's current CUDA device (cudaSetDevice first to pick
+ * another), creates the context's stream. NULL when no CUDA device is present or usable. */
+ork_npu *ork_npu_init(void);
+/* include/ork/context.h:83. Frees the context. Weights packed on it must be freed first (ork_mm_free). */
+void ork_npu_free(ork_npu *ctx);
+
+/* ---- pack / load / dump (ork-driver include/ork/weights.h) -------------------------------------- */
+
+/* include/ork/weights.h:39. B row-major fp16 [K][N]; K%32==0, N%16==0, else NULL. */
+ork_w *ork_f16_mm_pack(ork_npu *ctx, int K, int N, const ork_f16 *B);
+/* include/ork/weights.h:47. B row-major int8 [K][N]; K%32==0, N%32==0, else NULL. */
+ork_w *ork_i8_mm_pack(ork_npu *ctx, int K, int N, const int8_t *B);
+/* include/ork/weights.h:92. f32 given n-major [N][K]; per-output-channel symmetric int8:
+ * bscale[n] = max(1e-9,max|w|)/127, code = clamp(rint(w*(127/max)), +-127). Writes bscale_out[N] when
+ * non-NULL; the weight itself keeps no scale (ork_w_bscale returns NULL), as in the reference. */
+ork_w *ork_i8_mm_pack_f32(ork_npu *ctx, int K, int N, const float *f32, float *bscale_out);
+/* include/ork/weights.h:116. w4a8: f32 n-major [N][K] quantized per output channel to int4, kept as
+ * nibbles in HBM. Uniform grid (scale = max/7, codes in [-7,7]) unless env ORK_NF4 is set (NF4 codebook,
+ * bscale = max/127, quant_kind = ORK_QK_CODEBOOK_NF4). Env ORK_SR selects stochastic rounding. The weight
+ * runs through ork_i8_mm_run. K%32, N%32. */
+ork_w *ork_i4a8_mm_pack(ork_npu *ctx, int K, int N, const float *f32, float *bscale_out);
+/* include/ork/weights.h:124. As above with an optional importance matrix imatrix[K] selecting each
+ * channel's clip scale from the grid {1,.92,.85,.78,.70,.62,.55}; NULL is byte-identical to the above. */
+ork_w *ork_i4a8_mm_pack_im(ork_npu *ctx, int K, int N, const float *f32, const float *imatrix, float *bscale_out);
+/* include/ork/weights.h:125. W4A4: B row-major int8 [K][N] holding int4 values [-8,7] (the low nibble
+ * is kept). K%32, N%64. Runs through ork_i4_mm_run. */
+ork_w *ork_i4_mm_pack(ork_npu *ctx, int K, int N, const int8_t *B);
+
+/* include/ork/weights.h:230. Compact int4 persist of an ork_i4a8_mm_pack(_im)/ork_i4a8_mm_load weight:
+ * {u32 0x4F344E31 'O4N1', u32 version 1, i32 K, i32 N, u32 quant_kind} + bscale[N] f32 + nibbles[N][K/2]
+ * (low nibble = even k). out == NULL returns the size; returns 0 if cap is short or w has no int4 store. */
+size_t ork_i4a8_w_dump(const ork_w *w, void *out, size_t cap);
+/* include/ork/weights.h:255. Reload an O4N1 blob; NULL unless the size is exact and magic, version, K,
+ * N and quant_kind all check. The loaded weight runs via ork_i8_mm_run and re-dumps byte-identically. */
+ork_w *ork_i4a8_mm_load(ork_npu *ctx, int K, int N, const void *blob, size_t n);
+/* include/ork/weights.h:288 and :294. CPU-only O4N1 writer: the exact bytes ork_i4a8_mm_pack_im +
+ * ork_i4a8_w_dump would produce (nf4 chosen by the argument, not ORK_NF4), with no device involved; the
+ * _qerr form also reports sqrt(sum imp*(w-q)^2 / sum imp*w^2). ctx may be NULL. out == NULL -> size. */
+size_t ork_i4a8_pack_cpu_blob(ork_npu *ctx, int K, int N, const float *f32, const float *imatrix, int nf4,
+                              void *out, size_t cap);
+size_t ork_i4a8_pack_cpu_blob_qerr(ork_npu *ctx, int K, int N, const float *f32, const float *imatrix,
+                                   int nf4, void *out, size_t cap, float *qerr_out);
+
+/* include/ork/weights.h:141. Frees a weight's host bookkeeping. Unlike the reference (which leaves the
+ * NPU window to teardown), device memory is released here as well: HBM has no IOVA window to protect. */
+void ork_w_free(ork_w *w);
+/* include/ork/weights.h:149. Frees a weight and its device memory. */
+void ork_mm_free(ork_npu *ctx, ork_w *w);
+/* include/ork/weights.h:150. Resident device bytes of the packed weight. */
+size_t ork_w_bytes(const ork_w *w);
+/* include/ork/weights.h:154. (K,N) of the weight; NULL w yields 0,0. */
+void ork_w_dims(const ork_w *w, int *K, int *N);
+/* include/ork/weights.h:155. ORK_QK_* of an int4 weight store; 0 for other weights, -1 for NULL. */
+int ork_w_quant_kind(const ork_w *w);
+/* include/ork/weights.h:158. Per-output-channel scale[N] of an int4-packed/loaded weight, else NULL. */
+const float *ork_w_bscale(const ork_w *w);
+
+/* ---- run (ork-driver include/ork/run.h, include/ork/weights.h:345) ------------------------------- */
+
+/* include/ork/weights.h:345. C fp32 [M][N] = A fp16 [M][K] x B. 0 ok; -1 on bad args, a weight of
+ * another dtype, overlapping A/C, or a device error. */
+int ork_f16_mm_run(ork_npu *ctx, ork_w *w, int M, const ork_f16 *A, float *C);
+/* include/ork/run.h:21. C int32 [M][N] = A int8 [M][K] x B, exact. Accepts int8 packs (ork_i8_mm_pack,
+ * ork_i8_mm_pack_f32) and int4 stores (ork_i4a8_mm_pack(_im), ork_i4a8_mm_load). Errors as above. */
+int ork_i8_mm_run(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
+/* include/ork/run.h:111. W4A4: C int32 = A (int4 values in int8) x B; exact int32 accumulation. */
+int ork_i4_mm_run(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
+
+/* include/ork/run.h:132. The API's explicit CPU int8 matmul (B row-major raw codes). It exists for
+ * callers who want to time the CPU side of a routing decision; no run function above ever calls it. */
+void ork_i8_mm_run_cpu(int M, int K, int N, const int8_t *A, const int8_t *B, int32_t *C);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ORK_NPU_H */

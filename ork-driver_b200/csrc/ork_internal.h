@@ -1,0 +1,45 @@
+// ork_internal.h -- shared definitions of the B200 resident-weight matmul engine (not installed).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace orkb {
+
+// Resident weight formats. Every format keeps the weight K-major, i.e. as B^T with one output channel
+// per row, so a channel's K values are contiguous in HBM:
+//   FMT_F16 : [N][K] IEEE binary16
+//   FMT_I8  : [N][K] int8 codes
+//   FMT_U4  : [N][K/2] bytes, two's-complement int4 codes, low nibble = even k (the O4N1 nibble layout)
+//   FMT_NF4 : [N][K/2] bytes, NF4 codebook indices 0..15, low nibble = even k (the O4N1 nibble layout)
+enum Fmt { FMT_F16 = 0, FMT_I8 = 1, FMT_U4 = 2, FMT_NF4 = 3 };
+
+// Which public run function a weight belongs to (ork-driver src/npu/internal.h DT_* values).
+enum ApiDtype { DT_F16 = 0, DT_I8 = 1, DT_I4 = 2 };
+
+inline size_t fmt_row_bytes(int fmt, int K) {
+  return fmt == FMT_F16 ? (size_t)K * 2 : fmt == FMT_I8 ? (size_t)K : (size_t)K / 2;
+}
+
+// The NF4 int8 lookup table lut[i] = rint(level[i]*127) (ork-driver src/npu/i4/pack.c:128-131 with the
+// levels of src/npu.c:888-892), as the kernels use it: two 8-byte tables whose entries are all >= 0,
+// negneg = -lut[0..7] and pos = lut[8..15].
+extern const int8_t kNf4Lut[16];
+
+// ---- kernel launchers (gemv.cu, gemm_sm100.cu) --------------------------------------------------
+struct RunArgs {
+  const void *W;   // resident weight
+  const void *A;   // device activations [M][K] (int8 or fp16), 16-byte aligned rows
+  void *C;         // device output [M][N] (int32 or fp32)
+  int M, K, N;
+  int fmt;
+};
+
+// Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M).
+cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
+
+// Tensor-core path (tcgen05). Returns cudaErrorNotSupported when the shape/format has no TC kernel.
+cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
+bool gemm_tc_supports(int fmt, int M, int K, int N);
+
+}  // namespace orkb

@@ -1,0 +1,268 @@
+"""CUDA path vs the oracle, through the C ABI (needs a B200).
+
+Integer paths (w8a8, w4a8 uniform / NF4, W4A4) must be bit-exact int32; fp16 must stay within
+max|err| <= 1e-3 * sqrt(K) * max|A| * max|B| of the sequential-f32 reference (the tolerance of the
+north star), and exact on integer-valued inputs. Also the reference's own goldens (examples/quant.c,
+examples/test_matmul.c), the O4N1 round trip of examples/test_matmul.c:507-557, the overlap guard of
+:559-589, the dtype / dimension refusals, and device-pointer (sync and async) runs.
+"""
+import numpy as np
+import pytest
+
+import oracle_ffi as of
+import ork_b200
+import reference_goldens as rg
+from make_fixtures import seeded_imatrix, seeded_weights
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(32, 64), (64, 128), (288, 192), (2048, 2048), (6144, 2048), (2048, 6144)]
+MS = [1, 2, 3, 5, 8, 9, 17, 64]
+
+
+def f16_tol(A, B):
+    K = A.shape[1]
+    return 1e-3 * np.sqrt(K) * float(np.abs(A.astype(np.float32)).max()) * float(np.abs(B.astype(np.float32)).max())
+
+
+def rand_i8(rng, shape, lo=-128, hi=128):
+    return rng.integers(lo, hi, size=shape, dtype=np.int8)
+
+
+@pytest.mark.parametrize("K,N", SHAPES)
+def test_i8_pack_run_exact(ctx, K, N):
+    rng = np.random.default_rng(K * 7 + N)
+    B = rand_i8(rng, (K, N))
+    w = ctx.i8_pack(B)
+    assert w
+    res = w.resident().view(np.int8).reshape(N, K)
+    assert np.array_equal(res, B.T)
+    for M in MS:
+        A = rand_i8(rng, (M, K))
+        rc, Cm = ctx.run(w, A)
+        assert rc == 0
+        assert np.array_equal(Cm, of.gemm_i32(A, B)), M
+    w.free()
+
+
+@pytest.mark.parametrize("K,N", [(64, 32), (2048, 2048), (6144, 2048), (2048, 6144)])
+def test_i8_pack_f32_codes_and_run_exact(ctx, K, N):
+    f32 = seeded_weights(K + N, N, K)
+    w, bs = ctx.i8_pack_f32(f32)
+    codes, obs = of.i8_quant_f32(f32)
+    assert np.array_equal(bs, obs)
+    assert w.bscale() is None  # the scale goes only to bscale_out (src/npu/i8/pack.c:475-494)
+    assert np.array_equal(w.resident().view(np.int8).reshape(N, K), codes)
+    rng = np.random.default_rng(1)
+    for M in (1, 8, 13):
+        A = rand_i8(rng, (M, K), -127, 128)
+        rc, Cm = ctx.run(w, A)
+        assert rc == 0 and np.array_equal(Cm, of.gemm_i32_nk(A, codes))
+    w.free()
+
+
+@pytest.mark.parametrize("nf4", [False, True])
+@pytest.mark.parametrize("use_im", [False, True])
+@pytest.mark.parametrize("K,N", [(64, 32), (2048, 512), (6144, 2048), (2048, 12288)])
+def test_i4a8_pack_run_exact(ctx, env_clean, nf4, use_im, K, N):
+    if nf4:
+        env_clean.setenv("ORK_NF4", "1")
+    f32 = seeded_weights(3 * K + N, N, K)
+    im = seeded_imatrix(K, K) if use_im else None
+    w, bs = ctx.i4a8_pack(f32, im)
+    assert w and w.quant_kind() == (1 if nf4 else 0)
+    blob = of.i4a8_blob(f32, im, nf4=nf4)
+    codes, obs, _ = of.i4a8_blob_codes(blob, K, N)
+    assert np.array_equal(bs, obs) and np.array_equal(w.bscale(), obs)
+    assert np.array_equal(w.resident(), blob[20 + 4 * N:])  # resident nibbles == O4N1 payload
+    rng = np.random.default_rng(2)
+    for M in (1, 3, 8, 32):
+        A = rand_i8(rng, (M, K))
+        rc, Cm = ctx.run(w, A)
+        assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), M
+    w.free()
+
+
+@pytest.mark.parametrize("K,N", [(32, 64), (288, 128), (6144, 2048), (2048, 12288)])
+def test_w4a4_exact(ctx, K, N):
+    rng = np.random.default_rng(K + 3 * N)
+    B = rand_i8(rng, (K, N), -8, 8)
+    w = ctx.i4_pack(B)
+    assert w
+    for M in (1, 2, 7, 8, 32):
+        A = rand_i8(rng, (M, K), -8, 8)
+        rc, Cm = ctx.run(w, A)
+        assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B)), M
+    # full int8 range activations still accumulate exactly in int32 (no int16 saturation)
+    A = rand_i8(rng, (3, K))
+    rc, Cm = ctx.run(w, A)
+    assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B))
+    w.free()
+
+
+def test_w4a4_saturation_case(ctx):
+    """examples/i4.c:37-58: the all -8 x -8 product that overflows int16 on the NPU stays exact here."""
+    K, N = 1024, 64
+    B = np.full((K, N), -8, np.int8)
+    A = np.full((2, K), -8, np.int8)
+    w = ctx.i4_pack(B)
+    rc, Cm = ctx.run(w, A)
+    assert rc == 0 and np.all(Cm == 64 * K)
+    w.free()
+
+
+@pytest.mark.parametrize("K,N", [(32, 16), (64, 48), (2048, 6144)])
+def test_f16_within_tolerance(ctx, K, N):
+    rng = np.random.default_rng(K + N)
+    B = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+    w = ctx.f16_pack(B)
+    assert w
+    for M in (1, 4, 8, 64):
+        A = rng.uniform(-1, 1, size=(M, K)).astype(np.float16)
+        rc, Cm = ctx.run(w, A)
+        ref = of.gemm_f16(A, B)
+        assert rc == 0
+        assert np.abs(Cm - ref).max() <= f16_tol(A, B), M
+    w.free()
+
+
+def _run_golden(ctx, kind, Ms, K, N, A, B):
+    w = ctx.f16_pack(B) if kind == "f16" else ctx.i8_pack(B)
+    h = of.FNV_OFFSET
+    for m in Ms:
+        rc, Cm = ctx.run(w, A[:m], m)
+        assert rc == 0
+        h = of.fnv64(Cm, h)
+    w.free()
+    return h
+
+
+@pytest.mark.parametrize("which", ["quant", "f16", "chain", "check_i8"])
+def test_reference_goldens_on_gpu(ctx, which):
+    for name, kind, Ms, K, N, A, B, gold in rg.cases(of.Lcg, which=(which,)):
+        assert _run_golden(ctx, kind, Ms, K, N, A, B) == gold, name
+
+
+@pytest.mark.parametrize("nf4", [True, False])
+def test_o4n1_dump_load_roundtrip(ctx, env_clean, nf4):
+    """examples/test_matmul.c:507-557 on the GPU path."""
+    if nf4:
+        env_clean.setenv("ORK_NF4", "1")
+    K, N, M = 2048, 512, 8
+    rng = np.random.default_rng(4)
+    f32 = rng.standard_normal((N, K), dtype=np.float32)
+    w, bs = ctx.i4a8_pack(f32)
+    A = rand_i8(rng, (M, K), -127, 128)
+    rc1, C_res = ctx.run(w, A)
+    blob = w.dump()
+    assert blob is not None and blob.size == 5 * 4 + N * 4 + K * N // 2
+    assert np.array_equal(blob, of.i4a8_blob(f32, None, nf4=nf4))
+    wl = ctx.i4a8_load(blob, K, N)
+    assert wl
+    rc2, C_str = ctx.run(wl, A)
+    assert rc1 == 0 and rc2 == 0 and np.array_equal(C_res, C_str)
+    assert np.array_equal(wl.dump(), blob)
+    assert np.array_equal(wl.bscale(), bs)
+    assert wl.quant_kind() == (1 if nf4 else 0)
+    # a short cap returns 0, the size query the full size
+    L = ork_b200.lib()
+    assert L.ork_i4a8_w_dump(wl.h, blob.ctypes.data, blob.size - 1) == 0
+    w.free()
+    wl.free()
+
+
+def test_null_imatrix_identity(ctx, env_clean):
+    """examples/test_matmul.c:467-471: pack_im(NULL) scale is exactly absmax/7."""
+    K, N = 2048, 64
+    f32 = seeded_weights(6, N, K)
+    w, bs = ctx.i4a8_pack(f32, None)
+    mx = np.maximum(np.abs(f32).max(axis=1), np.float32(1e-9)).astype(np.float32)
+    assert np.array_equal(bs, (mx / np.float32(7)).astype(np.float32))
+    w.free()
+
+
+def test_load_refuses_malformed_blobs(ctx):
+    K, N = 64, 32
+    blob = ork_b200.cpu_blob(seeded_weights(2, N, K))
+    assert ctx.i4a8_load(blob, K, N)
+    assert not ctx.i4a8_load(blob[:-1], K, N)
+    assert not ctx.i4a8_load(np.concatenate([blob, blob[:1]]), K, N)
+    assert not ctx.i4a8_load(blob, K, N + 32)
+    for off, val in ((0, 0x4F344E32), (4, 2), (8, 96), (12, 64), (16, 7)):
+        bad = blob.copy()
+        bad[off:off + 4] = np.frombuffer(np.uint32(val).tobytes(), np.uint8)
+        assert not ctx.i4a8_load(bad, K, N), off
+
+
+def test_bad_dims_refused(ctx):
+    L = ork_b200.lib()
+    B = np.zeros(64 * 128, np.int8)
+    f = np.zeros(64 * 128, np.float32)
+    for K, N in ((33, 32), (32, 33), (16, 32)):
+        assert not L.ork_i8_mm_pack(ctx.ctx, K, N, B.ctypes.data)
+        assert not L.ork_i8_mm_pack_f32(ctx.ctx, K, N, f.ctypes.data, None)
+        assert not L.ork_i4a8_mm_pack(ctx.ctx, K, N, f.ctypes.data, None)
+    assert not L.ork_i4_mm_pack(ctx.ctx, 32, 32, B.ctypes.data)  # W4A4 needs N%64
+    assert not L.ork_f16_mm_pack(ctx.ctx, 32, 24, B.ctypes.data)  # fp16 needs N%16
+
+
+def test_dtype_mismatch_refused(ctx):
+    rng = np.random.default_rng(0)
+    wi8 = ctx.i8_pack(rand_i8(rng, (64, 64)))
+    wi4 = ctx.i4_pack(rand_i8(rng, (64, 64), -8, 8))
+    wf = ctx.f16_pack(np.zeros((64, 64), np.float16))
+    L = ork_b200.lib()
+    A = np.zeros((1, 64), np.int8)
+    Ah = np.zeros((1, 64), np.float16)
+    Cm = np.zeros((1, 64), np.int32)
+    Cf = np.zeros((1, 64), np.float32)
+    assert L.ork_i4_mm_run(ctx.ctx, wi8.h, 1, A.ctypes.data, Cm.ctypes.data) == -1
+    assert L.ork_i8_mm_run(ctx.ctx, wi4.h, 1, A.ctypes.data, Cm.ctypes.data) == -1
+    assert L.ork_f16_mm_run(ctx.ctx, wi8.h, 1, Ah.ctypes.data, Cf.ctypes.data) == -1
+    assert L.ork_i8_mm_run(ctx.ctx, wf.h, 1, A.ctypes.data, Cm.ctypes.data) == -1
+    assert L.ork_i8_mm_run(ctx.ctx, wi8.h, 0, A.ctypes.data, Cm.ctypes.data) == -1
+    for w in (wi8, wi4, wf):
+        w.free()
+
+
+def test_overlap_guard(ctx):
+    """examples/test_matmul.c:559-589: A and C sharing memory is refused with -1."""
+    w = ctx.i8_pack(np.ones((32, 32), np.int8))
+    shared = np.zeros(256, np.int8)
+    L = ork_b200.lib()
+    assert L.ork_i8_mm_run(ctx.ctx, w.h, 1, shared.ctypes.data, shared.ctypes.data + 16) == -1
+    w.free()
+
+
+def test_device_pointer_runs(ctx):
+    import torch
+
+    rng = np.random.default_rng(9)
+    K, N, M = 2048, 2048, 8
+    B = rand_i8(rng, (K, N))
+    w = ctx.i8_pack(B)
+    A = rand_i8(rng, (M, K))
+    ref = of.gemm_i32(A, B)
+    dA = torch.from_numpy(A).cuda()
+    dC = torch.zeros((M, N), dtype=torch.int32, device="cuda")
+    L = ork_b200.lib()
+    torch.cuda.synchronize()
+    assert L.ork_i8_mm_run(ctx.ctx, w.h, M, dA.data_ptr(), dC.data_ptr()) == 0
+    assert np.array_equal(dC.cpu().numpy(), ref)
+    dC.zero_()
+    torch.cuda.synchronize()
+    assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, dA.data_ptr(), dC.data_ptr()) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    assert np.array_equal(dC.cpu().numpy(), ref)
+    # async refuses host pointers' misalignment and overlap like the sync path
+    assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, dA.data_ptr() + 1, dC.data_ptr()) == -1
+    w.free()
+
+
+def test_kernels_are_launched(ctx):
+    before = ctx.launches()
+    w = ctx.i8_pack(np.ones((64, 64), np.int8))
+    rc, Cm = ctx.run(w, np.ones((3, 64), np.int8))
+    assert rc == 0 and np.all(Cm == 64)
+    assert ctx.launches() > before
+    w.free()
