@@ -8,7 +8,8 @@ bytes = K*N (weight) + M*K (A) + 4*M*N (int32 C) per call, summed over the step 
 time; every config is HBM-bound by that formula on B200 (int32 C is heavy), so GB/s is the common unit.
 
 - value: device-resident inputs, the twelve calls queued back to back on the library's stream
-  (ork_i8_mm_run_async), timed with CUDA events on that stream, max over ranks.
+  (ork_i8_mm_run_async, with programmatic dependent launch) and replayed as one CUDA graph per step,
+  timed with CUDA events on that stream, max over ranks.
 - e2e: the same sweep through the synchronous public call ork_i8_mm_run with pinned host buffers: each
   call copies A in, runs, copies C out and synchronises.
 - L2: inputs larger than L2 -- 9 distinct packed copies of every weight (265 MB) plus per-copy A/C
@@ -62,50 +63,47 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons sampled every ~2 ms (NVML) while the timed region runs."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, dev):
-        self.dev, self.rows, self.p = dev, [], None
+        self.dev, self.samples, self.stop, self.t = dev, [], threading.Event(), None
 
     def __enter__(self):
         try:
-            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
-                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def loop():
+                while not self.stop.is_set():
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((sm, rs))
+                    except Exception:
+                        pass
+                    time.sleep(0.002)
+
+            self.t = threading.Thread(target=loop, daemon=True)
             self.t.start()
         except Exception:
-            self.p = None
+            self.max = None
         return self
 
-    def _read(self):
-        for line in self.p.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
-
     def __exit__(self, *a):
-        if self.p:
-            self.p.terminate()
-            try:
-                self.p.wait(timeout=5)
-            except Exception:
-                self.p.kill()
+        self.stop.set()
+        if self.t:
+            self.t.join(timeout=2)
 
     def summary(self):
-        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            if len(r) >= 9:
-                for name, v in zip(names, r[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [s for s, _ in self.samples]
+        reasons = sorted({n for _, rs in self.samples for n, bit in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max, "reasons": reasons,
+                "samples": len(sm), "source": "nvml"}
 
 
 def cpu_reference_sweep(min_seconds, max_reps=3):
@@ -164,8 +162,8 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
@@ -216,9 +214,14 @@ def main():
         rc = L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr())
         assert rc == 0
 
-    def step(s):
-        for r, (K, N, M) in enumerate(CONFIGS):
-            call(K, N, M, s * len(CONFIGS) + r)
+    # Step s issues the 12 calls; call i of a shape (i = 0..3 over the M values) uses packed copy
+    # (4*s + i) % NCOPIES of that shape, so a copy is reused only after NCOPIES calls of its shape
+    # (~270 MB of other weights in between). The copy pattern repeats every NCOPIES steps, so one CUDA
+    # graph per residue class replays a step without per-call host overhead.
+    def step_calls(s):
+        for K, N in SHAPES:
+            for i, M in enumerate(MS):
+                call(K, N, M, 4 * s + i)
 
     def barrier():
         torch.cuda.synchronize()
@@ -226,18 +229,32 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    for s in range(NCOPIES):  # eager warm-up of every call (kernel attributes, tensor maps)
+        step_calls(s)
+    torch.cuda.synchronize()
+    graphs = []
+    launches_per_step = []
+    for s in range(NCOPIES):
+        g = torch.cuda.CUDAGraph()
+        l0 = ctx.launches()
+        with torch.cuda.graph(g, stream=stream):
+            step_calls(s)
+        launches_per_step.append(ctx.launches() - l0)
+        graphs.append(g)
+    torch.cuda.synchronize()
+
     for s in range(args.warmup):
-        step(s)
+        graphs[s % NCOPIES].replay()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = ctx.launches()
     with Clocks(local) as clk:
-        ev0.record(stream)
-        for s in range(args.steps):
-            step(args.warmup + s)
-        ev1.record(stream)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for s in range(args.steps):
+                graphs[(args.warmup + s) % NCOPIES].replay()
+            ev1.record(stream)
         barrier()
-    launches = ctx.launches() - launches0
+    launches = sum(launches_per_step[(args.warmup + s) % NCOPIES] for s in range(args.steps))
     ms = ev0.elapsed_time(ev1)
     if dist is not None:
         t = torch.tensor([ms], device="cuda")
@@ -246,25 +263,31 @@ def main():
     ms_per_step = ms / args.steps
     value = world * STEP_BYTES * args.steps / (ms / 1e3) / 1e9
 
-    # ---- per-config breakdown and the dominant kernel (each config alone, back to back) --------
+    # ---- per-config breakdown and the dominant kernel: each config alone, NCOPIES calls per graph ----
     breakdown = {}
-    reps = 30
+    reps = 20
     for K, N, M in CONFIGS:
-        for i in range(3):
-            call(K, N, M, i)
+        g = torch.cuda.CUDAGraph()
+        l0 = ctx.launches()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(NCOPIES):
+                call(K, N, M, i)
+        nl = (ctx.launches() - l0) / NCOPIES
+        for _ in range(2):
+            g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        l0 = ctx.launches()
-        e0.record(stream)
-        for i in range(reps):
-            call(K, N, M, i)
-        e1.record(stream)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
         torch.cuda.synchronize()
-        per = e0.elapsed_time(e1) / reps
-        nl = (ctx.launches() - l0) / reps
+        per = e0.elapsed_time(e1) / (reps * NCOPIES)
         breakdown[f"{K}x{N}xM{M}"] = {"ms": per, "GB/s": alg_bytes(K, N, M) / (per / 1e3) / 1e9,
                                       "TOPS": 2 * M * K * N / (per / 1e3) / 1e12, "launches": nl,
                                       "route": L.ork_b200_route(weights[(K, N)][0].h, M)}
+        del g
     tot = sum(b["ms"] for b in breakdown.values())
     dom = max(breakdown, key=lambda k: breakdown[k]["ms"])
     K, N, M = (int(x) for x in dom.replace("M", "").split("x"))
@@ -281,6 +304,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": traffic, "kernel": dom, "share": db["ms"] / tot, "peak_source": src,
                 "algorithmic_bytes_per_launch": alg_bytes(K, N, M) / max(db["launches"], 1)}
+    del graphs
 
     # ---- e2e through the synchronous public call with pinned host buffers ---------------------
     host = {}

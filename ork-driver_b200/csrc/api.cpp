@@ -176,6 +176,10 @@ int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype
     log_err(name, e);
     return -1;
   }
+  if (tc_error_flag(true)) {
+    fprintf(stderr, "[ork] ERROR [%s]: a tensor-core pipeline wait timed out; result discarded\n", name);
+    return -1;
+  }
   return 0;
 }
 
@@ -417,6 +421,10 @@ int ork_b200_sync(ork_npu *c) {
   const cudaError_t e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) {
     log_err("ork_b200_sync", e);
+    return -1;
+  }
+  if (tc_error_flag(true)) {
+    fprintf(stderr, "[ork] ERROR ork_b200_sync: a tensor-core pipeline wait timed out\n");
     return -1;
   }
   return 0;

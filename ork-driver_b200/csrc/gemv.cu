@@ -51,8 +51,12 @@ __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
   return __dp4a((int)a, (int)b, c);
 }
 
+// prmt.b32 in its default mode. Emitted directly because the selector's bit 3 (replicate the sign of
+// the selected byte) is part of the NF4 lookup, and __byte_perm only honours the low 3 bits.
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  return __byte_perm(a, b, sel);
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
 }
 
 template <int FMT> struct Acc { using T = int; };

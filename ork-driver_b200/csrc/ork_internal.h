@@ -41,5 +41,8 @@ cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launche
 // Tensor-core path (tcgen05). Returns cudaErrorNotSupported when the shape/format has no TC kernel.
 cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
 bool gemm_tc_supports(int fmt, int M, int K, int N);
+// Sticky device flag a tensor-core kernel sets when one of its bounded mbarrier waits expired (the kernel
+// then exits without a result). Read after a synchronisation; reset clears it.
+unsigned int tc_error_flag(bool reset);
 
 }  // namespace orkb

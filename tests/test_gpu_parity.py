@@ -266,3 +266,43 @@ def test_kernels_are_launched(ctx):
     assert rc == 0 and np.all(Cm == 64)
     assert ctx.launches() > before
     w.free()
+
+
+@pytest.mark.parametrize("K,N", [(288, 192), (2048, 1024), (6144, 2048)])
+def test_tensor_core_and_gemv_routes_agree_i8(ctx, K, N):
+    """Both kernel paths forced over M values that straddle the router's threshold and the 128-row tile
+    (K and N tails included), each compared with the oracle."""
+    L = ork_b200.lib()
+    rng = np.random.default_rng(K + N)
+    B = rand_i8(rng, (K, N))
+    w = ctx.i8_pack(B)
+    try:
+        for M in (1, 7, 8, 9, 16, 100, 128, 130, 256, 512):
+            A = rand_i8(rng, (M, K))
+            ref = of.gemm_i32(A, B)
+            for route in (1, 0):
+                assert L.ork_b200_force_route(ctx.ctx, route) == 0
+                rc, Cm = ctx.run(w, A)
+                assert rc == 0 and np.array_equal(Cm, ref), (M, route)
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w.free()
+
+
+@pytest.mark.parametrize("K,N", [(288, 48), (2048, 6144)])
+def test_tensor_core_route_f16(ctx, K, N):
+    L = ork_b200.lib()
+    rng = np.random.default_rng(K * N)
+    B = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+    w = ctx.f16_pack(B)
+    try:
+        for M in (1, 16, 64, 200):
+            A = rng.uniform(-1, 1, size=(M, K)).astype(np.float16)
+            ref = of.gemm_f16(A, B)
+            for route in (1, 0):
+                assert L.ork_b200_force_route(ctx.ctx, route) == 0
+                rc, Cm = ctx.run(w, A)
+                assert rc == 0 and np.abs(Cm - ref).max() <= f16_tol(A, B), (M, route)
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w.free()
