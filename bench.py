@@ -159,6 +159,33 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(spec):
+    """One config, packed once, run 5 times with a synchronisation after each: a small, self-contained
+    workload for `ncu -k <kernel> -s <skip> -c <count>` captures."""
+    import torch
+
+    import ork_b200
+
+    parts = [int(x) for x in spec.split(",")]
+    K, N, M = parts[:3]
+    route = parts[3] if len(parts) > 3 else -1
+    L = ork_b200.lib()
+    ctx = ork_b200.Context()
+    L.ork_b200_force_route(ctx.ctx, route)
+    rng = np.random.default_rng(0)
+    f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    w, _ = ctx.i8_pack_f32(f32)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+    c = torch.empty((M, N), dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(5):
+        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
+        assert L.ork_b200_sync(ctx.ctx) == 0
+    print(json.dumps({"profile": spec, "route": L.ork_b200_route(w.h, M), "launches": ctx.launches()}))
+    w.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -166,10 +193,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--profile", default=None,
+                    help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        return run_profile(args.profile)
 
     import torch
 
@@ -266,7 +297,7 @@ def main():
     # ---- per-config breakdown and the dominant kernel: each config alone, NCOPIES calls per graph ----
     breakdown = {}
     reps = 20
-    for K, N, M in CONFIGS:
+    def time_config(K, N, M):
         g = torch.cuda.CUDAGraph()
         l0 = ctx.launches()
         with torch.cuda.graph(g, stream=stream):
@@ -283,11 +314,19 @@ def main():
                 g.replay()
             e1.record(stream)
         torch.cuda.synchronize()
-        per = e0.elapsed_time(e1) / (reps * NCOPIES)
-        breakdown[f"{K}x{N}xM{M}"] = {"ms": per, "GB/s": alg_bytes(K, N, M) / (per / 1e3) / 1e9,
-                                      "TOPS": 2 * M * K * N / (per / 1e3) / 1e12, "launches": nl,
-                                      "route": L.ork_b200_route(weights[(K, N)][0].h, M)}
         del g
+        return e0.elapsed_time(e1) / (reps * NCOPIES), nl
+
+    for K, N, M in CONFIGS:
+        per, nl = time_config(K, N, M)
+        entry = {"ms": per, "GB/s": alg_bytes(K, N, M) / (per / 1e3) / 1e9,
+                 "TOPS": 2 * M * K * N / (per / 1e3) / 1e12, "launches": nl,
+                 "route": L.ork_b200_route(weights[(K, N)][0].h, M)}
+        for route, name in ((0, "ms_gemv"), (1, "ms_tc")):  # both kernel paths, for the router threshold
+            L.ork_b200_force_route(ctx.ctx, route)
+            entry[name] = time_config(K, N, M)[0]
+        L.ork_b200_force_route(ctx.ctx, -1)
+        breakdown[f"{K}x{N}xM{M}"] = entry
     tot = sum(b["ms"] for b in breakdown.values())
     dom = max(breakdown, key=lambda k: breakdown[k]["ms"])
     K, N, M = (int(x) for x in dom.replace("M", "").split("x"))

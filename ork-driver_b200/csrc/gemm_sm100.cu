@@ -1,18 +1,23 @@
-// gemm_sm100.cu -- batched-M matmul on the 5th-generation tensor cores (tcgen05), sm_100a.
+// gemm_sm100.cu -- matmul on the 5th-generation tensor cores (tcgen05), sm_100a.
 //
 // C[M][N] = A[M][K] . W[N][K]^T with both operands K-major (the activations as given, the weight in its
-// resident [N][K] layout). One CTA computes a 128 x TN output tile:
-//   warp 0      TMA producer: 2-D tiled bulk-tensor loads of a 128 x 128-byte A tile and a TN x 128-byte
-//               W tile per K block into a STAGES-deep shared-memory ring (128-byte swizzle, the UMMA
-//               canonical K-major layout), completion tracked by mbarrier transaction counts;
-//   warp 1      allocates TN TMEM columns; one thread issues tcgen05.mma (kind::i8 -> s32, or
-//               kind::f16 -> f32) per 32-byte K step, and tcgen05.commit frees each stage and finally
+// resident [N][K] layout). A CTA owns a 128 x TN tile of the MMA's D = R . S^T, where the 128-row
+// operand R and the TN-row operand S are either (A, W) or, for small M ("swap", M <= 64), (W, A): the
+// weight then fills the 128-row side and the activations the narrow side, so decode-sized M wastes no
+// MMA rows. Roles inside a CTA (192 threads):
+//   warp 0      TMA producer: 2-D tiled bulk-tensor loads of a 128 x 128-byte R tile and a TN x 128-byte
+//               S tile per K block into a STAGES-deep ring (128-byte swizzle, the UMMA canonical K-major
+//               layout); completion tracked by mbarrier transaction counts;
+//   warp 1      allocates the TMEM accumulator; one thread issues tcgen05.mma (kind::i8 -> s32, or
+//               kind::f16 -> f32) per 32-byte K step; tcgen05.commit frees each stage and finally
 //               signals the epilogue;
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from their TMEM sub-partition and
-//               store the int32 / fp32 row segment to C.
-// Integer accumulation in TMEM is exact int32, so results equal ork-driver's CPU oracle bit for bit.
-// Out-of-range rows / K columns are zero-filled by the tensor map, so M, N and K need no padding
-// beyond the API's own alignment rules.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from their TMEM sub-partition.
+// Split-K across a thread-block cluster: the SK CTAs of a cluster (gridDim.z = cluster z = SK) take
+// consecutive K ranges of the same tile; each dumps its partial tile to its own shared memory, the
+// cluster synchronises, and every CTA reduces a slice of the tile by reading all SK partials through
+// distributed shared memory, then stores it. No atomics, no workspace, no zeroing of C; the integer
+// sum is exact in any order, so results equal ork-driver's CPU oracle bit for bit.
+// Out-of-range rows / K columns are zero-filled by the tensor maps, so M, N and K need no padding.
 //
 // Every mbarrier wait is bounded by a clock deadline; on expiry the kernel records an error in a
 // device flag that the host checks, and all roles fall through to the common exit (no hang).
@@ -29,8 +34,8 @@ __device__ unsigned int g_tc_error = 0;
 
 namespace {
 
-constexpr int BM = 128;          // MMA M (rows of A per tile)
-constexpr int BK_BYTES = 128;    // K bytes per stage (one 128-byte swizzle row)
+constexpr int BM = 128;                          // MMA M: rows of the R operand per tile
+constexpr int BK_BYTES = 128;                    // K bytes per stage (one 128-byte swizzle row)
 constexpr uint64_t kWaitCycles = 4000000000ull;  // ~2 s at 1.9 GHz
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -90,11 +95,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 // operands K-major, M = 128, N = TN.
 template <bool F16>
 __host__ __device__ constexpr uint32_t idesc(int tn) {
-  return (F16 ? (1u << 4) : (2u << 4))        // D format: f32 / s32
-         | (F16 ? 0u : (1u << 7))             // A format: f16 / signed int8
-         | (F16 ? 0u : (1u << 10))            // B format: f16 / signed int8
-         | ((uint32_t)(tn >> 3) << 17)        // N >> 3
-         | ((uint32_t)(BM >> 4) << 24);       // M >> 4
+  return (F16 ? (1u << 4) : (2u << 4))   // D format: f32 / s32
+         | (F16 ? 0u : (1u << 7))        // A format: f16 / signed int8
+         | (F16 ? 0u : (1u << 10))       // B format: f16 / signed int8
+         | ((uint32_t)(tn >> 3) << 17)   // N >> 3
+         | ((uint32_t)(BM >> 4) << 24);  // M >> 4
 }
 
 template <bool F16>
@@ -116,39 +121,74 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 32 lanes x 16 consecutive 32-bit TMEM columns into registers (one row per thread).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <bool F16, int TN, int STAGES>
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+template <bool F16>
+__device__ __forceinline__ uint4 add4(uint4 a, uint4 b) {
+  if constexpr (F16) {
+    return make_uint4(__float_as_uint(__uint_as_float(a.x) + __uint_as_float(b.x)),
+                      __float_as_uint(__uint_as_float(a.y) + __uint_as_float(b.y)),
+                      __float_as_uint(__uint_as_float(a.z) + __uint_as_float(b.z)),
+                      __float_as_uint(__uint_as_float(a.w) + __uint_as_float(b.w)));
+  } else {
+    return make_uint4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+  }
+}
+
+constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 128 ? 128 : 256; }
+
+template <bool F16, bool SWAP, int TN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW, void *__restrict__ Cout,
-               int M, int N, int K) {
-  constexpr uint32_t A_BYTES = BM * BK_BYTES;
-  constexpr uint32_t W_BYTES = TN * BK_BYTES;
+gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
+               void *__restrict__ Cout, int M, int N, int K) {
+  constexpr uint32_t R_BYTES = BM * BK_BYTES;
+  constexpr uint32_t S_BYTES = TN * BK_BYTES;
   constexpr int ESZ = F16 ? 2 : 1;
   constexpr int KSTEPS = BK_BYTES / 32;  // 32-byte MMA K steps per stage (K=32 int8 / K=16 f16)
+  constexpr int TCOLS = tmem_cols(TN);
+  // split-K partial tile in shared memory (reuses the drained stage ring): [128][TN+4] or, swapped,
+  // [TN][128+4] so that the reduced output is read in C's row-major order
+  constexpr int PSTR = SWAP ? (BM + 4) : (TN + 4);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t *sA = smem;
-  uint8_t *sW = smem + STAGES * A_BYTES;
-  uint64_t *bars = (uint64_t *)(sW + STAGES * W_BYTES);  // full[STAGES], empty[STAGES], done
+  uint8_t *sR = smem;
+  uint8_t *sS = smem + STAGES * R_BYTES;
+  uint64_t *bars = (uint64_t *)(sS + STAGES * S_BYTES);  // full[STAGES], empty[STAGES], done
   uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 1);
+  uint32_t *P = (uint32_t *)smem;
 
   asm volatile("griddepcontrol.launch_dependents;");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * TN, m0 = blockIdx.y * BM;
+  const int r0 = blockIdx.x * BM, c0 = blockIdx.y * TN;
+  const int SK = gridDim.z, ks = blockIdx.z;
   const int KB = (K * ESZ + BK_BYTES - 1) / BK_BYTES;
+  const int kb0 = (int)((long long)KB * ks / SK), kb1 = (int)((long long)KB * (ks + 1) / SK);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), done = smem_u32(bars + 2 * STAGES);
+  const int rows_R = SWAP ? N : M, rows_S = SWAP ? M : N;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -157,12 +197,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapA) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapW) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapR) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapS) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TN));
+                 "r"(TCOLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   __syncthreads();
@@ -171,61 +211,114 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
 
   if (warp == 0) {
     if (lane == 0) {
+      // the weight tiles do not depend on the previous kernel: the first ring's worth is requested
+      // before waiting on it (programmatic dependent launch); activations only after the wait
+      const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+      for (int i = 0; i < pre; i++) {
+        mbar_expect_tx(full0 + 8 * i, R_BYTES + S_BYTES);
+        const int x = (kb0 + i) * (BK_BYTES / ESZ);
+        if (SWAP) tma_load_2d(smem_u32(sR + i * R_BYTES), &mapR, x, r0, full0 + 8 * i);
+        else tma_load_2d(smem_u32(sS + i * S_BYTES), &mapS, x, c0, full0 + 8 * i);
+      }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int kb = 0; kb < KB; kb++) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+      for (int i = 0; i < pre; i++) {
+        const int x = (kb0 + i) * (BK_BYTES / ESZ);
+        if (SWAP) tma_load_2d(smem_u32(sS + i * S_BYTES), &mapS, x, c0, full0 + 8 * i);
+        else tma_load_2d(smem_u32(sR + i * R_BYTES), &mapR, x, r0, full0 + 8 * i);
+      }
+      for (int kb = kb0 + pre; kb < kb1; kb++) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) break;
-        mbar_expect_tx(full0 + 8 * s, A_BYTES + W_BYTES);
+        mbar_expect_tx(full0 + 8 * s, R_BYTES + S_BYTES);
         const int x = kb * (BK_BYTES / ESZ);
-        tma_load_2d(smem_u32(sA + s * A_BYTES), &mapA, x, m0, full0 + 8 * s);
-        tma_load_2d(smem_u32(sW + s * W_BYTES), &mapW, x, n0, full0 + 8 * s);
+        tma_load_2d(smem_u32(sR + s * R_BYTES), &mapR, x, r0, full0 + 8 * s);
+        tma_load_2d(smem_u32(sS + s * S_BYTES), &mapS, x, c0, full0 + 8 * s);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id = idesc<F16>(TN);
-      bool ok = true;
-      for (int kb = 0; kb < KB && ok; kb++) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        ok = mbar_wait(full0 + 8 * s, ph);
-        if (!ok) break;
+      for (int kb = kb0; kb < kb1; kb++) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        if (!mbar_wait(full0 + 8 * s, ph)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
-        const uint64_t wd = sw128_desc(smem_u32(sW + s * W_BYTES));
+        const uint64_t rd = sw128_desc(smem_u32(sR + s * R_BYTES));
+        const uint64_t sd = sw128_desc(smem_u32(sS + s * S_BYTES));
 #pragma unroll
         for (int k = 0; k < KSTEPS; k++)  // advance 32 bytes (2 x 16-byte units) along K within the row
-          umma<F16>(tmem, ad + 2 * k, wd + 2 * k, id, (kb | k) != 0);
+          umma<F16>(tmem, rd + 2 * k, sd + 2 * k, id, (kb > kb0 || k > 0) ? 1u : 0u);
         umma_commit(empty0 + 8 * s);
       }
       umma_commit(done);
     }
   } else {
-    // epilogue: warps 2..5 -> TMEM sub-partitions (warp % 4)
+    // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = tile row of R
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
-    const int m = m0 + row;
     const bool ok = mbar_wait(done, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < TN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)c0, r);
-        if (m < M) {
-          uint32_t *dst = (uint32_t *)Cout + (size_t)m * N + n0 + c0;
+      for (int cc = 0; cc < TN; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)cc, r);
+        if (SK > 1) {  // stage the partial tile for the cluster reduction
+          if (SWAP) {
 #pragma unroll
-          for (int q = 0; q < 8; q++)
-            if (n0 + c0 + 4 * q < N)
-              *reinterpret_cast<uint4 *>(dst + 4 * q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            for (int q = 0; q < 16; q++) P[(cc + q) * PSTR + row] = r[q];
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; q += 4)
+              *reinterpret_cast<uint4 *>(P + row * PSTR + cc + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
+          }
+        } else if (SWAP) {  // D[n][m] -> C[m][n]: lanes are consecutive n, so each store is coalesced
+          const int n = r0 + row;
+          if (n < N) {
+            uint32_t *Cp = (uint32_t *)Cout;
+#pragma unroll
+            for (int q = 0; q < 16; q++)
+              if (c0 + cc + q < M) Cp[(size_t)(c0 + cc + q) * N + n] = r[q];
+          }
+        } else {
+          const int m = r0 + row;
+          if (m < M) {
+            uint32_t *dst = (uint32_t *)Cout + (size_t)m * N + c0 + cc;
+#pragma unroll
+            for (int q = 0; q < 16; q += 4)
+              if (c0 + cc + q < N) *reinterpret_cast<uint4 *>(dst + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
+          }
         }
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  if (SK > 1) {
+    cluster_sync();  // every CTA's partial tile is in its shared memory
+    // reduce: output items are (output row, 4-column vector) of the tile in C's row-major order
+    const int out_rows = SWAP ? min(TN, M - c0) : min(BM, M - r0);
+    const int out_cols = SWAP ? min(BM, N - r0) : min(TN, N - c0);
+    const int vpr = out_cols / 4;  // N is a multiple of 16, tiles start at multiples of 16
+    const int items = out_rows * vpr;
+    const uint32_t pbase = smem_u32(P);
+    uint32_t *Cp = (uint32_t *)Cout;
+    for (int t = ks * 192 + (int)threadIdx.x; t < items; t += SK * 192) {
+      const int orow = t / vpr, ov = t % vpr;
+      const uint32_t off = (uint32_t)(orow * PSTR + 4 * ov) * 4u;
+      uint4 acc = ld_dsmem_v4(pbase + off, 0);
+      for (int q = 1; q < SK; q++) acc = add4<F16>(acc, ld_dsmem_v4(pbase + off, (uint32_t)q));
+      const int m = SWAP ? c0 + orow : r0 + orow;
+      const int n = (SWAP ? r0 : c0) + 4 * ov;
+      *reinterpret_cast<uint4 *>(Cp + (size_t)m * N + n) = acc;
+    }
+    cluster_sync();  // no CTA leaves while its partial tile may still be read
+  }
   __syncthreads();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TN));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
+  (void)rows_R;
+  (void)rows_S;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -256,13 +349,19 @@ bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int esz, i
   return r == CUDA_SUCCESS;
 }
 
-template <bool F16, int TN, int STAGES>
-cudaError_t launch_tc(const RunArgs &a, cudaStream_t s, bool pdl) {
+template <bool F16, bool SWAP, int TN, int STAGES>
+cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   constexpr int ESZ = F16 ? 2 : 1;
-  CUtensorMap mA, mW;
-  if (!make_map(&mA, a.A, a.M, a.K, ESZ, BM) || !make_map(&mW, a.W, a.N, a.K, ESZ, TN)) return cudaErrorInvalidValue;
-  constexpr size_t smem = 1024 + (size_t)STAGES * (BM + TN) * BK_BYTES + (2 * STAGES + 1) * 8 + 16;
-  auto kern = gemm_tc_kernel<F16, TN, STAGES>;
+  CUtensorMap mR, mS;
+  const void *R = SWAP ? a.W : a.A, *S = SWAP ? a.A : a.W;
+  const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
+  if (!make_map(&mR, R, rowsR, a.K, ESZ, BM) || !make_map(&mS, S, rowsS, a.K, ESZ, TN)) return cudaErrorInvalidValue;
+  constexpr size_t ring = (size_t)STAGES * (BM + TN) * BK_BYTES;
+  constexpr size_t part = (size_t)(SWAP ? TN * (BM + 4) : BM * (TN + 4)) * 4;
+  static_assert(part <= ring, "partial tile must fit in the stage ring");
+  constexpr size_t smem = 1024 + ring + (2 * STAGES + 1) * 8 + 16;
+  static_assert(smem <= 232448, "shared memory budget");
+  auto kern = gemm_tc_kernel<F16, SWAP, TN, STAGES>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -270,16 +369,49 @@ cudaError_t launch_tc(const RunArgs &a, cudaStream_t s, bool pdl) {
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + TN - 1) / TN, (a.M + BM - 1) / BM);
+  cfg.gridDim = dim3((rowsR + BM - 1) / BM, (rowsS + TN - 1) / TN, sk);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 1;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = sk;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, mA, mW, a.C, a.M, a.N, a.K);
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K);
+}
+
+struct TcCfg {
+  bool swap;
+  int tn, sk;
+};
+
+// Tile and split choice: swapped operands with the narrowest N-tile covering M for M <= 64, else
+// 128 x 128 activation x weight tiles; then split K over a cluster (up to 8 CTAs) until the grid
+// covers the 148 SMs, keeping at least one K block per CTA.
+TcCfg choose_tc(int fmt, int M, int K, int N) {
+  TcCfg c;
+  c.swap = M <= 64;
+  c.tn = c.swap ? (M <= 16 ? 16 : M <= 32 ? 32 : 64) : 128;
+  const int tiles = c.swap ? (N + BM - 1) / BM : ((M + BM - 1) / BM) * ((N + c.tn - 1) / c.tn);
+  const int KB = (K * (fmt == FMT_F16 ? 2 : 1) + BK_BYTES - 1) / BK_BYTES;
+  c.sk = 1;
+  while (tiles * c.sk < 128 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
+  return c;
+}
+
+template <bool F16>
+cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl) {
+  if (c.swap) {
+    if (c.tn == 16) return launch_tc<F16, true, 16, 8>(a, c.sk, s, pdl);
+    if (c.tn == 32) return launch_tc<F16, true, 32, 8>(a, c.sk, s, pdl);
+    return launch_tc<F16, true, 64, 6>(a, c.sk, s, pdl);
+  }
+  return launch_tc<F16, false, 128, 6>(a, c.sk, s, pdl);
 }
 
 }  // namespace
@@ -293,9 +425,10 @@ bool gemm_tc_supports(int fmt, int M, int K, int N) {
 
 cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *launches) {
   if ((uintptr_t)a.A % 16 || (uintptr_t)a.W % 16 || (uintptr_t)a.C % 16) return cudaErrorMisalignedAddress;
+  const TcCfg c = choose_tc(a.fmt, a.M, a.K, a.N);
   cudaError_t e;
-  if (a.fmt == FMT_I8) e = launch_tc<false, 128, 6>(a, s, pdl);
-  else if (a.fmt == FMT_F16) e = launch_tc<true, 128, 6>(a, s, pdl);
+  if (a.fmt == FMT_I8) e = dispatch<false>(a, c, s, pdl);
+  else if (a.fmt == FMT_F16) e = dispatch<true>(a, c, s, pdl);
   else return cudaErrorNotSupported;
   if (e == cudaSuccess && launches) ++*launches;
   return e;

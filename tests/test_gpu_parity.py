@@ -277,7 +277,7 @@ def test_tensor_core_and_gemv_routes_agree_i8(ctx, K, N):
     B = rand_i8(rng, (K, N))
     w = ctx.i8_pack(B)
     try:
-        for M in (1, 7, 8, 9, 16, 100, 128, 130, 256, 512):
+        for M in (1, 7, 8, 9, 16, 24, 40, 64, 65, 100, 128, 130, 256, 512):
             A = rand_i8(rng, (M, K))
             ref = of.gemm_i32(A, B)
             for route in (1, 0):
@@ -296,7 +296,7 @@ def test_tensor_core_route_f16(ctx, K, N):
     B = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
     w = ctx.f16_pack(B)
     try:
-        for M in (1, 16, 64, 200):
+        for M in (1, 16, 33, 64, 200):
             A = rng.uniform(-1, 1, size=(M, K)).astype(np.float16)
             ref = of.gemm_f16(A, B)
             for route in (1, 0):
