@@ -118,19 +118,32 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
   return w;
 }
 
+// 0 = CUDA-core GEMV, 1 = tcgen05 GEMM, -1 = no kernel for this weight / shape.
 int route_for(const ork_npu *c, const ork_w *w, int M) {
-  if (c && c->force_route == 0) return 0;
-  if (c && c->force_route == 1) return gemm_tc_supports(w->fmt, M, w->K, w->N) ? 1 : 0;
-  if (M <= 8) return 0;
-  return gemm_tc_supports(w->fmt, M, w->K, w->N) ? 1 : 0;
+  const bool tc = gemm_tc_supports(w->fmt, M, w->K, w->N), gv = gemv_supports(w->fmt, w->K);
+  if (!tc && !gv) return -1;
+  if (c && c->force_route == 0) return gv ? 0 : 1;
+  if (c && c->force_route == 1) return tc ? 1 : 0;
+  if (M <= 4) return gv ? 0 : 1;
+  return tc ? 1 : 0;
+}
+
+// Sticky device-side error flags (a bounded wait that expired); cleared when read.
+bool device_error() {
+  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true);
+  return (t | g) != 0;
 }
 
 // Launch one matmul on device buffers (A, C already on the context's GPU).
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
   RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt};
   int n = 0;
-  cudaError_t e = route_for(c, w, M) == 1 ? launch_gemm_tc(a, c->stream, c->pdl, &n)
-                                          : launch_gemv(a, c->stream, c->pdl, &n);
+  const int route = route_for(c, w, M);
+  if (route < 0) {
+    fprintf(stderr, "[ork] ERROR: no kernel for this weight format at K=%d\n", w->K);
+    return -1;
+  }
+  cudaError_t e = route == 1 ? launch_gemm_tc(a, c->stream, c->pdl, &n) : launch_gemv(a, c->stream, c->pdl, &n);
   c->launches += (uint64_t)n;
   if (e != cudaSuccess) {
     log_err("kernel launch", e);
@@ -176,8 +189,8 @@ int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype
     log_err(name, e);
     return -1;
   }
-  if (tc_error_flag(true)) {
-    fprintf(stderr, "[ork] ERROR [%s]: a tensor-core pipeline wait timed out; result discarded\n", name);
+  if (device_error()) {
+    fprintf(stderr, "[ork] ERROR [%s]: a kernel's bounded pipeline wait timed out; result discarded\n", name);
     return -1;
   }
   return 0;
@@ -423,8 +436,8 @@ int ork_b200_sync(ork_npu *c) {
     log_err("ork_b200_sync", e);
     return -1;
   }
-  if (tc_error_flag(true)) {
-    fprintf(stderr, "[ork] ERROR ork_b200_sync: a tensor-core pipeline wait timed out\n");
+  if (device_error()) {
+    fprintf(stderr, "[ork] ERROR ork_b200_sync: a kernel's bounded pipeline wait timed out\n");
     return -1;
   }
   return 0;

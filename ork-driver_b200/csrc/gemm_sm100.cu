@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "ork_internal.h"
@@ -397,10 +398,19 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
   TcCfg c;
   c.swap = M <= 64;
   c.tn = c.swap ? (M <= 16 ? 16 : M <= 32 ? 32 : 64) : 128;
+  // ORKB_TC_TN / ORKB_TC_SK: tuning overrides of the non-swapped tile width (128 or 256) and of the
+  // split factor (1..8), read on every launch
+  static const char *env_tn = getenv("ORKB_TC_TN");
+  if (!c.swap && env_tn && atoi(env_tn) == 256) c.tn = 256;
   const int tiles = c.swap ? (N + BM - 1) / BM : ((M + BM - 1) / BM) * ((N + c.tn - 1) / c.tn);
   const int KB = (K * (fmt == FMT_F16 ? 2 : 1) + BK_BYTES - 1) / BK_BYTES;
   c.sk = 1;
   while (tiles * c.sk < 128 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
+  static const char *env_sk = getenv("ORKB_TC_SK");
+  if (env_sk) {
+    const int v = atoi(env_sk);
+    if (v >= 1 && v <= 8 && v <= KB) c.sk = v;
+  }
   return c;
 }
 
@@ -411,6 +421,7 @@ cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl)
     if (c.tn == 32) return launch_tc<F16, true, 32, 8>(a, c.sk, s, pdl);
     return launch_tc<F16, true, 64, 6>(a, c.sk, s, pdl);
   }
+  if (c.tn == 256) return launch_tc<F16, false, 256, 4>(a, c.sk, s, pdl);
   return launch_tc<F16, false, 128, 6>(a, c.sk, s, pdl);
 }
 

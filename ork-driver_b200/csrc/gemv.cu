@@ -1,8 +1,17 @@
 // gemv.cu -- decode-path matmul (M <= 8 rows of activations per launch) on CUDA cores, sm_100a.
 //
 // C[m][n] = sum_k A[m][k] * B[k][n] with the weight resident K-major (one output channel per row, see
-// ork_internal.h). The path is HBM-bound: every weight byte is read exactly once per launch, with
-// 128-bit loads that bypass L1, and the arithmetic is done in registers:
+// ork_internal.h). The path is HBM-bound: every weight byte is read exactly once per launch.
+//
+// Staging: a CTA owns TR consecutive output channels, i.e. one contiguous TR x rowB block of the
+// resident weight. At kernel start a single thread requests the whole block with bulk asynchronous
+// copies (cp.async.bulk, the TMA engine's 1-D form), one per group of 8 channels, each completing on its
+// own mbarrier -- so every byte a CTA will ever read is in flight immediately, with no register cost,
+// and a warp starts computing as soon as its 8 channels have landed. The copies are issued before
+// griddepcontrol.wait, so under programmatic dependent launch the weight stream of the next matmul
+// overlaps the tail of the previous one; activations are read only after the wait.
+//
+// Arithmetic, in registers:
 //   int8  : 4 x dp4a per 16 weight bytes and activation row;
 //   int4  : the nibble is moved to the top of a byte ((w<<4)&0xF0F0F0F0 / w&0xF0F0F0F0), so each byte
 //           holds 16*code; dp4a then accumulates 16*dot exactly and the lane's sum is shifted right by 4
@@ -13,14 +22,11 @@
 //   fp16  : converted to fp32 and accumulated with FFMA.
 // Every integer result is exact int32, identical to ork-driver's CPU oracle (src/npu/core/buf.c:428).
 //
-// Work mapping: a warp owns 4*R output channels. Eight lanes cover one channel, each loading 16 B, so
-// one warp-wide load moves 4 channels x 128 contiguous bytes and the activation chunk it multiplies is
-// shared (broadcast) by the 4 channel groups. The warps of a CTA may split K (KS > 1); partial sums are
-// reduced with a butterfly shuffle across the 8 lanes, then across the K-split warps in shared memory.
-//
-// Programmatic dependent launch: the kernel triggers its dependents immediately and issues its first
-// weight loads before griddepcontrol.wait, so when launched with the PDL attribute the weight stream
-// overlaps the previous kernel's tail; activations are only read after the wait.
+// Work mapping: eight lanes cover one channel, 16 bytes each, so one warp-wide shared-memory read moves
+// 4 channels x 128 contiguous bytes and the activation chunk it multiplies is shared by the 4 channel
+// groups; each lane holds R = 2 channels (8 per warp) to reuse every activation load twice. The WK warps
+// that share a channel group split K; partials are reduced with a butterfly shuffle across the 8 lanes,
+// then across the K-split warps in shared memory.
 #include <cuda_fp16.h>
 
 #include "ork_internal.h"
@@ -29,14 +35,14 @@ namespace orkb {
 
 namespace {
 
-constexpr int kU = 4;  // 128-byte steps in flight per lane and row
+constexpr int kR = 2;        // channels per lane
+constexpr int kWarps = 4;    // warps per CTA
+constexpr uint64_t kWaitCycles = 4000000000ull;
 
-__device__ __forceinline__ uint4 ldg_stream(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
+__device__ unsigned int g_gemv_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
 __device__ __forceinline__ uint4 ldg_keep(const void *p) {
@@ -47,9 +53,13 @@ __device__ __forceinline__ uint4 ldg_keep(const void *p) {
   return v;
 }
 
-__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
-  return __dp4a((int)a, (int)b, c);
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
 }
+
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
 // prmt.b32 in its default mode. Emitted directly because the selector's bit 3 (replicate the sign of
 // the selected byte) is part of the NF4 lookup, and __byte_perm only honours the low 3 bits.
@@ -57,6 +67,24 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
+}
+
+// Bounded mbarrier wait (parity 0: each barrier completes exactly once per launch).
+__device__ __forceinline__ bool mbar_wait0(uint32_t bar) {
+  const uint64_t t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_gemv_error, 1u);
+      return false;
+    }
+  }
 }
 
 template <int FMT> struct Acc { using T = int; };
@@ -80,26 +108,129 @@ __device__ __forceinline__ void bfly_step(T *v, int lane) {
   }
 }
 
-template <int FMT, int MT, int R, int KS, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32)
-gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout,
-            int M, int K, int N, uint32_t t_neg0, uint32_t t_neg1, uint32_t t_pos0, uint32_t t_pos1) {
+struct Tables {
+  uint32_t neg0, neg1, pos0, pos1;
+};
+
+// acc[r*MT+m] += <activation chunk of row m, weight chunk of channel r> for one 16-byte weight chunk per
+// channel; `o` is the chunk's byte offset within a weight row.
+template <int FMT, int MT, typename T>
+__device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], const uint8_t *__restrict__ A, size_t a_row, size_t o,
+                                          int M, T *acc, T *neg, const Tables &tb) {
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    if (m >= M) break;
+    const uint8_t *arow = A + (size_t)m * a_row;
+    if constexpr (FMT == FMT_I8) {
+      const uint4 a = ldg_keep(arow + o);
+#pragma unroll
+      for (int r = 0; r < kR; r++) {
+        T &c = acc[r * MT + m];
+        c = dp4a(a.x, wv[r].x, c);
+        c = dp4a(a.y, wv[r].y, c);
+        c = dp4a(a.z, wv[r].z, c);
+        c = dp4a(a.w, wv[r].w, c);
+      }
+    } else if constexpr (FMT == FMT_U4) {
+      const uint4 a0 = ldg_keep(arow + 2 * o), a1 = ldg_keep(arow + 2 * o + 16);
+      const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      uint32_t ev[4], od[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        ev[q] = prmt(aw[2 * q], aw[2 * q + 1], 0x6420);  // k = 8q + {0,2,4,6}
+        od[q] = prmt(aw[2 * q], aw[2 * q + 1], 0x7531);  // k = 8q + {1,3,5,7}
+      }
+#pragma unroll
+      for (int r = 0; r < kR; r++) {
+        const uint32_t ww[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+        T &c = acc[r * MT + m];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          c = dp4a(ev[q], (ww[q] << 4) & 0xF0F0F0F0u, c);
+          c = dp4a(od[q], ww[q] & 0xF0F0F0F0u, c);
+        }
+      }
+    } else if constexpr (FMT == FMT_NF4) {
+      const uint4 a0 = ldg_keep(arow + 2 * o), a1 = ldg_keep(arow + 2 * o + 16);
+      const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int r = 0; r < kR; r++) {
+        const uint32_t ww[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+        T &c = acc[r * MT + m];
+        T &d = neg[r * MT + m];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {  // nibble i of word q is k = 8q + i
+          const uint32_t w = ww[q], x = ww[q] ^ 0x88888888u;
+          c = dp4a(aw[2 * q], prmt(tb.pos0, tb.pos1, x), c);
+          c = dp4a(aw[2 * q + 1], prmt(tb.pos0, tb.pos1, x >> 16), c);
+          d = dp4a(aw[2 * q], prmt(tb.neg0, tb.neg1, w), d);
+          d = dp4a(aw[2 * q + 1], prmt(tb.neg0, tb.neg1, w >> 16), d);
+        }
+      }
+    } else {  // FMT_F16
+      const uint4 a = ldg_keep(arow + o);
+      const __half2 *ah = reinterpret_cast<const __half2 *>(&a);
+      float2 af[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) af[q] = __half22float2(ah[q]);
+#pragma unroll
+      for (int r = 0; r < kR; r++) {
+        const __half2 *wh = reinterpret_cast<const __half2 *>(&wv[r]);
+        T &c = acc[r * MT + m];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float2 wf = __half22float2(wh[q]);
+          c = fmaf(af[q].x, wf.x, c);
+          c = fmaf(af[q].y, wf.y, c);
+        }
+      }
+    }
+  }
+}
+
+// TR channels per CTA (8 per warp-row group), WK = 4 / (TR / 8) warps split K.
+template <int FMT, int MT, int TR>
+__global__ void __launch_bounds__(kWarps * 32)
+gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M, int K,
+            int N, Tables tb) {
   using T = typename Acc<FMT>::T;
-  constexpr int WR = WARPS / KS;
-  constexpr int ROWS_W = 4 * R;
-  constexpr int ROWS_CTA = WR * ROWS_W;
-  constexpr int V = R * MT;
+  constexpr int WR = TR / (4 * kR);  // warp-row groups
+  constexpr int WK = kWarps / WR;    // warps splitting K
+  constexpr int V = kR * MT;
+  constexpr int NGRP = TR / 8;       // 8-channel copy groups (one mbarrier each)
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[NGRP];
+  __shared__ T red[WK > 1 ? WK : 1][TR][MT];
 
   asm volatile("griddepcontrol.launch_dependents;");
-
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 3, j = lane & 7;
-  const int wr = warp / KS, wk = warp % KS;
-  const int cta_row0 = blockIdx.x * ROWS_CTA;
-  const int row0 = cta_row0 + wr * ROWS_W + g;
+  const int wr = warp / WK, wk = warp % WK;
+  const int n0 = blockIdx.x * TR;
+  const int rows = min(TR, N - n0);
   const size_t rowB = (FMT == FMT_F16) ? (size_t)K * 2 : (FMT == FMT_I8) ? (size_t)K : (size_t)K / 2;
-  const int S = (int)((rowB + 127) / 128);
-  const size_t a_row_bytes = (FMT == FMT_F16) ? (size_t)K * 2 : (size_t)K;
+  const size_t a_row = (FMT == FMT_F16) ? (size_t)K * 2 : (size_t)K;
+  const uint32_t sW = smem_u32(smem);
+
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < NGRP; q++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[q])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const uint8_t *src = W + (size_t)n0 * rowB;
+    for (int q = 0; q < NGRP; q++) {
+      const int r0 = q * 8, nr = min(8, rows - r0);
+      const uint32_t bar = smem_u32(&bars[q]);
+      const uint32_t bytes = nr > 0 ? (uint32_t)(nr * rowB) : 0u;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+      if (nr > 0)
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         sW + (uint32_t)(r0 * rowB)),
+                     "l"(src + (size_t)r0 * rowB), "r"(bytes), "r"(bar)
+                     : "memory");
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __syncthreads();  // barrier init visible to every thread
 
   T acc[V];
   T neg[(FMT == FMT_NF4) ? V : 1];
@@ -108,110 +239,23 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
 #pragma unroll
   for (int i = 0; i < ((FMT == FMT_NF4) ? V : 1); i++) neg[i] = T(0);
 
-  const uint8_t *wrow[R];
-  bool rowok[R];
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    const int n = row0 + 4 * r;
-    rowok[r] = n < N;
-    wrow[r] = W + (size_t)(rowok[r] ? n : 0) * rowB;
-  }
-
-  bool waited = false;
-  for (int s0 = wk; s0 < S; s0 += KS * kU) {
-    uint4 wv[kU][R];
-    bool ok[kU];
-#pragma unroll
-    for (int u = 0; u < kU; u++) {
-      const int s = s0 + u * KS;
+  // this lane's channels: local rows wr*8 + g + 4r, r < kR (the warp-row group is one copy group)
+  const int lrow0 = wr * 8 + g;
+  const bool ok = mbar_wait0(smem_u32(&bars[wr]));
+  const int S = (int)((rowB + 127) / 128);
+  if (ok && wr * 8 < rows) {
+    const uint32_t base0 = sW + (uint32_t)(lrow0 * rowB) + (uint32_t)(j * 16);
+#pragma unroll 4
+    for (int s = wk; s < S; s += WK) {
       const size_t o = (size_t)s * 128 + (size_t)j * 16;
-      ok[u] = (s < S) && (o < rowB);
+      if (o >= rowB) break;
+      uint4 wv[kR];
 #pragma unroll
-      for (int r = 0; r < R; r++)
-        wv[u][r] = (ok[u] && rowok[r]) ? ldg_stream(wrow[r] + o) : make_uint4(0, 0, 0, 0);
-    }
-    if (!waited) {
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      waited = true;
-    }
-#pragma unroll
-    for (int u = 0; u < kU; u++) {
-      if (!ok[u]) continue;
-      const size_t o = (size_t)(s0 + u * KS) * 128 + (size_t)j * 16;
-#pragma unroll
-      for (int m = 0; m < MT; m++) {
-        if (m >= M) break;
-        const uint8_t *arow = A + (size_t)m * a_row_bytes;
-        if constexpr (FMT == FMT_I8) {
-          const uint4 a = ldg_keep(arow + o);
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            T &c = acc[r * MT + m];
-            c = dp4a(a.x, wv[u][r].x, c);
-            c = dp4a(a.y, wv[u][r].y, c);
-            c = dp4a(a.z, wv[u][r].z, c);
-            c = dp4a(a.w, wv[u][r].w, c);
-          }
-        } else if constexpr (FMT == FMT_U4) {
-          const uint4 a0 = ldg_keep(arow + 2 * o), a1 = ldg_keep(arow + 2 * o + 16);
-          const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-          uint32_t ev[4], od[4];
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            ev[q] = prmt(aw[2 * q], aw[2 * q + 1], 0x6420);
-            od[q] = prmt(aw[2 * q], aw[2 * q + 1], 0x7531);
-          }
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            const uint32_t ww[4] = {wv[u][r].x, wv[u][r].y, wv[u][r].z, wv[u][r].w};
-            T &c = acc[r * MT + m];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              c = dp4a(ev[q], (ww[q] << 4) & 0xF0F0F0F0u, c);
-              c = dp4a(od[q], ww[q] & 0xF0F0F0F0u, c);
-            }
-          }
-        } else if constexpr (FMT == FMT_NF4) {
-          const uint4 a0 = ldg_keep(arow + 2 * o), a1 = ldg_keep(arow + 2 * o + 16);
-          const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            const uint32_t ww[4] = {wv[u][r].x, wv[u][r].y, wv[u][r].z, wv[u][r].w};
-            T &c = acc[r * MT + m];
-            T &d = neg[r * MT + m];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              const uint32_t w = ww[q], x = ww[q] ^ 0x88888888u;
-              c = dp4a(aw[2 * q], prmt(t_pos0, t_pos1, x), c);
-              c = dp4a(aw[2 * q + 1], prmt(t_pos0, t_pos1, x >> 16), c);
-              d = dp4a(aw[2 * q], prmt(t_neg0, t_neg1, w), d);
-              d = dp4a(aw[2 * q + 1], prmt(t_neg0, t_neg1, w >> 16), d);
-            }
-          }
-        } else {  // FMT_F16
-          const uint4 a = ldg_keep(arow + o);
-          const __half2 *ah = reinterpret_cast<const __half2 *>(&a);
-          float2 af[4];
-#pragma unroll
-          for (int q = 0; q < 4; q++) af[q] = __half22float2(ah[q]);
-#pragma unroll
-          for (int r = 0; r < R; r++) {
-            const __half2 *wh = reinterpret_cast<const __half2 *>(&wv[u][r]);
-            T &c = acc[r * MT + m];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              const float2 wf = __half22float2(wh[q]);
-              c = fmaf(af[q].x, wf.x, c);
-              c = fmaf(af[q].y, wf.y, c);
-            }
-          }
-        }
-      }
+      for (int r = 0; r < kR; r++) wv[r] = lds128(base0 + (uint32_t)(4 * r * rowB) + (uint32_t)(s * 128));
+      mac_chunk<FMT, MT, T>(wv, A, a_row, o, M, acc, neg, tb);
     }
   }
-  if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // per-lane finalisation (linear, so it commutes with the reduction)
   if constexpr (FMT == FMT_U4) {
 #pragma unroll
     for (int i = 0; i < V; i++) acc[i] >>= 4;
@@ -219,7 +263,6 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
 #pragma unroll
     for (int i = 0; i < V; i++) acc[i] -= neg[i];
   }
-
   bfly_step<V, 4>(acc, lane);
   bfly_step<(V / 2 > 1 ? V / 2 : 1), 2>(acc, lane);
   bfly_step<(V / 4 > 1 ? V / 4 : 1), 1>(acc, lane);
@@ -231,86 +274,92 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
   const bool writer = (V >= 8) || (V == 4 && !(j & 1)) || (V == 2 && !(j & 3)) || (V == 1 && j == 0);
 
   T *C = reinterpret_cast<T *>(Cout);
-  if constexpr (KS == 1) {
+  if constexpr (WK == 1) {
     if (writer) {
 #pragma unroll
       for (int i = 0; i < HELD; i++) {
         const int idx = base + i, r = idx / MT, m = idx % MT;
-        const int n = row0 + 4 * r;
-        if (m < M && n < N) C[(size_t)m * N + n] = acc[i];
+        const int lr = lrow0 + 4 * r;
+        if (m < M && lr < rows) C[(size_t)m * N + n0 + lr] = acc[i];
       }
     }
   } else {
-    __shared__ T red[KS][ROWS_CTA][MT];
     if (writer) {
 #pragma unroll
       for (int i = 0; i < HELD; i++) {
         const int idx = base + i, r = idx / MT, m = idx % MT;
-        red[wk][wr * ROWS_W + g + 4 * r][m] = acc[i];
+        red[wk][lrow0 + 4 * r][m] = acc[i];
       }
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < ROWS_CTA * MT; t += WARPS * 32) {
-      const int m = t / ROWS_CTA, rl = t % ROWS_CTA, n = cta_row0 + rl;
-      if (m < M && n < N) {
-        T s = red[0][rl][m];
+    for (int t = threadIdx.x; t < TR * MT; t += kWarps * 32) {
+      const int m = t / TR, lr = t % TR;
+      if (m < M && lr < rows) {
+        T s = red[0][lr][m];
 #pragma unroll
-        for (int q = 1; q < KS; q++) s += red[q][rl][m];
-        C[(size_t)m * N + n] = s;
+        for (int q = 1; q < WK; q++) s += red[q][lr][m];
+        C[(size_t)m * N + n0 + lr] = s;
       }
     }
   }
 }
 
 struct Cfg {
-  int mt, ks;
+  int mt, tr;
 };
 
-// Pick the row tile (M rows per launch, padded to 1/2/4/8) and how many warps of a CTA split K: enough
-// CTAs to cover the 148 SMs a couple of times, while each warp still walks a few 128-byte steps.
+// Row tile: as many channels per CTA as keep the staged block <= 48 KB (several CTAs per SM, so the
+// next launch's copies overlap this one under PDL) while the grid still covers the 148 SMs twice.
 Cfg choose(int fmt, int M, int K, int N) {
   Cfg c;
   c.mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
-  const int S = (int)((fmt_row_bytes(fmt, K) + 127) / 128);
-  c.ks = 1;
-  auto ctas = [N](int ks) { const int rows = (4 / ks) * 8; return (N + rows - 1) / rows; };  // WARPS=4, R=2
-  while (c.ks < 4 && ctas(c.ks) < 2 * 148 && S / (2 * c.ks) >= 2) c.ks *= 2;
+  const size_t rowB = fmt_row_bytes(fmt, K);
+  c.tr = 8;
+  for (int tr : {16, 32})
+    if ((size_t)tr * rowB <= 48 * 1024 && (N + tr - 1) / tr >= 2 * 148) c.tr = tr;
   return c;
 }
 
-template <int FMT, int MT, int KS>
+template <int FMT, int MT, int TR>
 cudaError_t launch_one(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cudaStream_t s, bool pdl,
-                       uint32_t tn0, uint32_t tn1, uint32_t tp0, uint32_t tp1) {
-  constexpr int WARPS = 4, R = 2;
-  constexpr int ROWS_CTA = (WARPS / KS) * 4 * R;
+                       const Tables &tb) {
+  const size_t smem = (size_t)TR * fmt_row_bytes(FMT, a.K);
+  auto kern = gemv_kernel<FMT, MT, TR>;
+  if (smem > 48 * 1024) {
+    static int set_for = 0;  // opt in once to the largest size seen
+    if ((int)smem > set_for) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      set_for = (int)smem;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + ROWS_CTA - 1) / ROWS_CTA);
-  cfg.blockDim = dim3(WARPS * 32);
+  cfg.gridDim = dim3((a.N + TR - 1) / TR);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, MT, R, KS, WARPS>, (const uint8_t *)a.W, Ab, Cb, m, a.K,
-                            a.N, tn0, tn1, tp0, tp1);
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t *)a.W, Ab, Cb, m, a.K, a.N, tb);
 }
 
 template <int FMT>
 cudaError_t dispatch_fmt(const RunArgs &a, const Cfg &c, const uint8_t *Ab, void *Cb, int m, cudaStream_t s,
-                         bool pdl, uint32_t tn0, uint32_t tn1, uint32_t tp0, uint32_t tp1) {
-#define ORKB_GEMV_CASE(MT_, KS_)                                                          \
-  if (c.mt == MT_ && c.ks == KS_)                                                         \
-    return launch_one<FMT, MT_, KS_>(a, Ab, Cb, m, s, pdl, tn0, tn1, tp0, tp1);
-  ORKB_GEMV_CASE(1, 1) ORKB_GEMV_CASE(1, 2) ORKB_GEMV_CASE(1, 4)
-  ORKB_GEMV_CASE(2, 1) ORKB_GEMV_CASE(2, 2) ORKB_GEMV_CASE(2, 4)
-  ORKB_GEMV_CASE(4, 1) ORKB_GEMV_CASE(4, 2) ORKB_GEMV_CASE(4, 4)
-  ORKB_GEMV_CASE(8, 1) ORKB_GEMV_CASE(8, 2) ORKB_GEMV_CASE(8, 4)
+                         bool pdl, const Tables &tb) {
+#define ORKB_GEMV_CASE(MT_, TR_) \
+  if (c.mt == MT_ && c.tr == TR_) return launch_one<FMT, MT_, TR_>(a, Ab, Cb, m, s, pdl, tb);
+  ORKB_GEMV_CASE(1, 8) ORKB_GEMV_CASE(1, 16) ORKB_GEMV_CASE(1, 32)
+  ORKB_GEMV_CASE(2, 8) ORKB_GEMV_CASE(2, 16) ORKB_GEMV_CASE(2, 32)
+  ORKB_GEMV_CASE(4, 8) ORKB_GEMV_CASE(4, 16) ORKB_GEMV_CASE(4, 32)
+  ORKB_GEMV_CASE(8, 8) ORKB_GEMV_CASE(8, 16) ORKB_GEMV_CASE(8, 32)
 #undef ORKB_GEMV_CASE
   return cudaErrorInvalidConfiguration;
 }
 
-uint32_t pack4(int8_t a, int8_t b, int8_t c, int8_t d) {
+uint32_t pack4(int a, int b, int c, int d) {
   return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
          ((uint32_t)(uint8_t)d << 24);
 }
@@ -318,9 +367,10 @@ uint32_t pack4(int8_t a, int8_t b, int8_t c, int8_t d) {
 }  // namespace
 
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches) {
+  if ((uintptr_t)a.W % 16 || (uintptr_t)a.A % 16) return cudaErrorMisalignedAddress;
   const int8_t *L = kNf4Lut;
-  const uint32_t tn0 = pack4(-L[0], -L[1], -L[2], -L[3]), tn1 = pack4(-L[4], -L[5], -L[6], -L[7]);
-  const uint32_t tp0 = pack4(L[8], L[9], L[10], L[11]), tp1 = pack4(L[12], L[13], L[14], L[15]);
+  const Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
+                  pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
   const size_t a_row = (a.fmt == FMT_F16) ? (size_t)a.K * 2 : (size_t)a.K;
   const size_t c_row = (size_t)a.N * 4;
   for (int m0 = 0; m0 < a.M; m0 += 8) {
@@ -330,16 +380,26 @@ cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launche
     void *Cb = (uint8_t *)a.C + (size_t)m0 * c_row;
     cudaError_t e;
     switch (a.fmt) {
-      case FMT_I8: e = dispatch_fmt<FMT_I8>(a, c, Ab, Cb, m, s, pdl, tn0, tn1, tp0, tp1); break;
-      case FMT_U4: e = dispatch_fmt<FMT_U4>(a, c, Ab, Cb, m, s, pdl, tn0, tn1, tp0, tp1); break;
-      case FMT_NF4: e = dispatch_fmt<FMT_NF4>(a, c, Ab, Cb, m, s, pdl, tn0, tn1, tp0, tp1); break;
-      case FMT_F16: e = dispatch_fmt<FMT_F16>(a, c, Ab, Cb, m, s, pdl, tn0, tn1, tp0, tp1); break;
+      case FMT_I8: e = dispatch_fmt<FMT_I8>(a, c, Ab, Cb, m, s, pdl, tb); break;
+      case FMT_U4: e = dispatch_fmt<FMT_U4>(a, c, Ab, Cb, m, s, pdl, tb); break;
+      case FMT_NF4: e = dispatch_fmt<FMT_NF4>(a, c, Ab, Cb, m, s, pdl, tb); break;
+      case FMT_F16: e = dispatch_fmt<FMT_F16>(a, c, Ab, Cb, m, s, pdl, tb); break;
       default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
     if (launches) ++*launches;
   }
   return cudaSuccess;
+}
+
+unsigned int gemv_error_flag(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof v);
+  if (reset && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_gemv_error, &z, sizeof z);
+  }
+  return v;
 }
 
 }  // namespace orkb

@@ -35,8 +35,11 @@ struct RunArgs {
   int fmt;
 };
 
-// Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M).
+// Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M). A CTA stages
+// 8 whole weight rows in shared memory, which bounds the row size (gemv_supports).
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
+inline bool gemv_supports(int fmt, int K) { return fmt_row_bytes(fmt, K) * 8 <= 192 * 1024; }
+unsigned int gemv_error_flag(bool reset);
 
 // Tensor-core path (tcgen05). Returns cudaErrorNotSupported when the shape/format has no TC kernel.
 cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
