@@ -124,7 +124,9 @@ int route_for(const ork_npu *c, const ork_w *w, int M) {
   if (!tc && !gv) return -1;
   if (c && c->force_route == 0) return gv ? 0 : 1;
   if (c && c->force_route == 1) return tc ? 1 : 0;
-  if (M <= 4) return gv ? 0 : 1;
+  // measured crossover: the CUDA-core GEMV wins up to M = 4 everywhere and up to M = 8 on small
+  // weights; the tensor-core kernel wins beyond
+  if (M <= 4 || (M <= 8 && (size_t)w->K * w->N <= ((size_t)4 << 20))) return gv ? 0 : 1;
   return tc ? 1 : 0;
 }
 

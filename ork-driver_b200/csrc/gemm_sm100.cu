@@ -163,7 +163,7 @@ __device__ __forceinline__ uint4 add4(uint4 a, uint4 b) {
 constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 128 ? 128 : 256; }
 
 template <bool F16, bool SWAP, int TN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
                void *__restrict__ Cout, int M, int N, int K) {
   constexpr uint32_t R_BYTES = BM * BK_BYTES;
@@ -391,22 +391,27 @@ struct TcCfg {
   int tn, sk;
 };
 
-// Tile and split choice: swapped operands with the narrowest N-tile covering M for M <= 64, else
-// 128 x 128 activation x weight tiles; then split K over a cluster (up to 8 CTAs) until the grid
-// covers the 148 SMs, keeping at least one K block per CTA.
+// Tile and split choice (measured on B200 over the BASELINE shapes): swapped operands with the
+// narrowest N-tile covering M for M <= 64, else 128 x 128 activation x weight tiles, widened to 256
+// once there are enough tiles to fill the GPU. Then K is split over a cluster: up to 8 ways for the
+// swapped (weight-streaming) tiles until ~192 CTAs, up to 4 ways for the MMA-heavy tiles until ~128
+// CTAs (beyond that the extra partial-tile traffic costs more than the parallelism gains); each CTA
+// keeps at least one K block.
 TcCfg choose_tc(int fmt, int M, int K, int N) {
   TcCfg c;
   c.swap = M <= 64;
   c.tn = c.swap ? (M <= 16 ? 16 : M <= 32 ? 32 : 64) : 128;
+  if (!c.swap && ((M + BM - 1) / BM) * ((N + 127) / 128) >= 192) c.tn = 256;
   // ORKB_TC_TN / ORKB_TC_SK: tuning overrides of the non-swapped tile width (128 or 256) and of the
   // split factor (1..8), read on every launch
-  static const char *env_tn = getenv("ORKB_TC_TN");
-  if (!c.swap && env_tn && atoi(env_tn) == 256) c.tn = 256;
+  const char *env_tn = getenv("ORKB_TC_TN");
+  if (!c.swap && env_tn) c.tn = atoi(env_tn) == 256 ? 256 : 128;
   const int tiles = c.swap ? (N + BM - 1) / BM : ((M + BM - 1) / BM) * ((N + c.tn - 1) / c.tn);
   const int KB = (K * (fmt == FMT_F16 ? 2 : 1) + BK_BYTES - 1) / BK_BYTES;
+  const int max_sk = c.swap ? 8 : 4, target = c.swap ? 192 : 128;
   c.sk = 1;
-  while (tiles * c.sk < 128 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
-  static const char *env_sk = getenv("ORKB_TC_SK");
+  while (tiles * c.sk * 2 <= target && c.sk * 2 <= max_sk && c.sk * 2 <= KB) c.sk *= 2;
+  const char *env_sk = getenv("ORKB_TC_SK");
   if (env_sk) {
     const int v = atoi(env_sk);
     if (v >= 1 && v <= 8 && v <= KB) c.sk = v;
@@ -416,10 +421,12 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
 
 template <bool F16>
 cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl) {
+  // swapped (decode-sized M) tiles keep the ring at 72-80 KB so three CTAs fit on an SM: the next
+  // launch's CTAs then start streaming their weights while this one drains (programmatic launch)
   if (c.swap) {
-    if (c.tn == 16) return launch_tc<F16, true, 16, 8>(a, c.sk, s, pdl);
-    if (c.tn == 32) return launch_tc<F16, true, 32, 8>(a, c.sk, s, pdl);
-    return launch_tc<F16, true, 64, 6>(a, c.sk, s, pdl);
+    if (c.tn == 16) return launch_tc<F16, true, 16, 4>(a, c.sk, s, pdl);
+    if (c.tn == 32) return launch_tc<F16, true, 32, 4>(a, c.sk, s, pdl);
+    return launch_tc<F16, true, 64, 3>(a, c.sk, s, pdl);
   }
   if (c.tn == 256) return launch_tc<F16, false, 256, 4>(a, c.sk, s, pdl);
   return launch_tc<F16, false, 128, 6>(a, c.sk, s, pdl);

@@ -45,14 +45,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ uint4 ldg_keep(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -113,16 +105,17 @@ struct Tables {
 };
 
 // acc[r*MT+m] += <activation chunk of row m, weight chunk of channel r> for one 16-byte weight chunk per
-// channel; `o` is the chunk's byte offset within a weight row.
+// channel. `sa` is the shared-memory address of activation row 0 at the chunk's first k, `a_row` the
+// activation row pitch in bytes.
 template <int FMT, int MT, typename T>
-__device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], const uint8_t *__restrict__ A, size_t a_row, size_t o,
-                                          int M, T *acc, T *neg, const Tables &tb) {
+__device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], uint32_t sa, uint32_t a_row, int M, T *acc, T *neg,
+                                          const Tables &tb) {
 #pragma unroll
   for (int m = 0; m < MT; m++) {
     if (m >= M) break;
-    const uint8_t *arow = A + (size_t)m * a_row;
+    const uint32_t arow = sa + (uint32_t)m * a_row;
     if constexpr (FMT == FMT_I8) {
-      const uint4 a = ldg_keep(arow + o);
+      const uint4 a = lds128(arow);
 #pragma unroll
       for (int r = 0; r < kR; r++) {
         T &c = acc[r * MT + m];
@@ -132,7 +125,7 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], const uint8_t *
         c = dp4a(a.w, wv[r].w, c);
       }
     } else if constexpr (FMT == FMT_U4) {
-      const uint4 a0 = ldg_keep(arow + 2 * o), a1 = ldg_keep(arow + 2 * o + 16);
+      const uint4 a0 = lds128(arow), a1 = lds128(arow + 16);
       const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       uint32_t ev[4], od[4];
 #pragma unroll
@@ -151,7 +144,7 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], const uint8_t *
         }
       }
     } else if constexpr (FMT == FMT_NF4) {
-      const uint4 a0 = ldg_keep(arow + 2 * o), a1 = ldg_keep(arow + 2 * o + 16);
+      const uint4 a0 = lds128(arow), a1 = lds128(arow + 16);
       const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
       for (int r = 0; r < kR; r++) {
@@ -168,7 +161,7 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], const uint8_t *
         }
       }
     } else {  // FMT_F16
-      const uint4 a = ldg_keep(arow + o);
+      const uint4 a = lds128(arow);
       const __half2 *ah = reinterpret_cast<const __half2 *>(&a);
       float2 af[4];
 #pragma unroll
@@ -199,7 +192,7 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
   constexpr int V = kR * MT;
   constexpr int NGRP = TR / 8;       // 8-channel copy groups (one mbarrier each)
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bars[NGRP];
+  __shared__ __align__(8) uint64_t bars[NGRP + 1];  // one per 8-channel weight group, then activations
   __shared__ T red[WK > 1 ? WK : 1][TR][MT];
 
   asm volatile("griddepcontrol.launch_dependents;");
@@ -213,7 +206,7 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
   const uint32_t sW = smem_u32(smem);
 
   if (threadIdx.x == 0) {
-    for (int q = 0; q < NGRP; q++)
+    for (int q = 0; q <= NGRP; q++)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[q])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     const uint8_t *src = W + (size_t)n0 * rowB;
@@ -230,6 +223,15 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
     }
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the activations (written by the previous kernel) come after the wait: one copy of the M x K block
+  const uint32_t sA = sW + (uint32_t)(TR * rowB);
+  if (threadIdx.x == 0) {
+    const uint32_t bar = smem_u32(&bars[NGRP]), bytes = (uint32_t)(M * a_row);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sA),
+                 "l"(A), "r"(bytes), "r"(bar)
+                 : "memory");
+  }
   __syncthreads();  // barrier init visible to every thread
 
   T acc[V];
@@ -241,18 +243,19 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
 
   // this lane's channels: local rows wr*8 + g + 4r, r < kR (the warp-row group is one copy group)
   const int lrow0 = wr * 8 + g;
-  const bool ok = mbar_wait0(smem_u32(&bars[wr]));
+  const bool ok = mbar_wait0(smem_u32(&bars[wr])) && mbar_wait0(smem_u32(&bars[NGRP]));
   const int S = (int)((rowB + 127) / 128);
   if (ok && wr * 8 < rows) {
     const uint32_t base0 = sW + (uint32_t)(lrow0 * rowB) + (uint32_t)(j * 16);
+    const uint32_t a_k = (FMT == FMT_U4 || FMT == FMT_NF4) ? 2u : 1u;  // activation bytes per weight byte
 #pragma unroll 4
     for (int s = wk; s < S; s += WK) {
-      const size_t o = (size_t)s * 128 + (size_t)j * 16;
+      const uint32_t o = (uint32_t)s * 128u + (uint32_t)j * 16u;
       if (o >= rowB) break;
       uint4 wv[kR];
 #pragma unroll
       for (int r = 0; r < kR; r++) wv[r] = lds128(base0 + (uint32_t)(4 * r * rowB) + (uint32_t)(s * 128));
-      mac_chunk<FMT, MT, T>(wv, A, a_row, o, M, acc, neg, tb);
+      mac_chunk<FMT, MT, T>(wv, sA + a_k * o, (uint32_t)a_row, M, acc, neg, tb);
     }
   }
 
@@ -310,6 +313,7 @@ struct Cfg {
 
 // Row tile: as many channels per CTA as keep the staged block <= 48 KB (several CTAs per SM, so the
 // next launch's copies overlap this one under PDL) while the grid still covers the 148 SMs twice.
+// The activations (M x K) are staged beside it.
 Cfg choose(int fmt, int M, int K, int N) {
   Cfg c;
   c.mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
@@ -323,15 +327,13 @@ Cfg choose(int fmt, int M, int K, int N) {
 template <int FMT, int MT, int TR>
 cudaError_t launch_one(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cudaStream_t s, bool pdl,
                        const Tables &tb) {
-  const size_t smem = (size_t)TR * fmt_row_bytes(FMT, a.K);
+  const size_t smem = (size_t)TR * fmt_row_bytes(FMT, a.K) + (size_t)m * (FMT == FMT_F16 ? 2 : 1) * a.K;
   auto kern = gemv_kernel<FMT, MT, TR>;
-  if (smem > 48 * 1024) {
-    static int set_for = 0;  // opt in once to the largest size seen
-    if ((int)smem > set_for) {
-      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      set_for = (int)smem;
-    }
+  static bool attr_set = false;  // opt in once to the full dynamic budget (the static part adds ~1 KB)
+  if (!attr_set) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + TR - 1) / TR);

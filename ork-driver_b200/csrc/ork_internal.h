@@ -38,7 +38,9 @@ struct RunArgs {
 // Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M). A CTA stages
 // 8 whole weight rows in shared memory, which bounds the row size (gemv_supports).
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
-inline bool gemv_supports(int fmt, int K) { return fmt_row_bytes(fmt, K) * 8 <= 192 * 1024; }
+inline bool gemv_supports(int fmt, int K) {  // 8 weight rows + up to 8 activation rows in shared memory
+  return fmt_row_bytes(fmt, K) * 8 + (size_t)8 * K * (fmt == FMT_F16 ? 2 : 1) <= 196 * 1024;
+}
 unsigned int gemv_error_flag(bool reset);
 
 // Tensor-core path (tcgen05). Returns cudaErrorNotSupported when the shape/format has no TC kernel.
