@@ -20,6 +20,17 @@ int ork_i8_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t
 int ork_i4_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
 int ork_f16_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *dA, float *dC);
 
+/* No counterpart in ork-driver. ork_i8_mm_run for callers that cannot let a library allocate device
+ * memory at run time (an engine that reserved nearly all HBM for its own pool at start-up, a process
+ * under a hard device-memory cap, or code that must not trigger the device-wide synchronisation
+ * cudaMalloc / cudaFree can cause). Same arguments, checks and result as ork_i8_mm_run; A and C are
+ * staged through a fixed 4 MiB scratch area built into the library (held on every GPU that loads it)
+ * instead of buffers the context allocates, and the call allocates nothing. Limit: M*K rounded up to
+ * 256, plus 4*M*N, must fit in 4 MiB, else -1 with a message. The first call on a device looks up the
+ * scratch address (make it before any stream capture); calls that overlap on one GPU race on the
+ * shared scratch. */
+int ork_i8_mm_run_noalloc(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
+
 /* Wait for everything queued on the context's stream; 0 ok, -1 if the GPU reported an error. */
 int ork_b200_sync(ork_npu *ctx);
 /* The cudaStream_t the context queues on, and a way to substitute the caller's own stream (NULL restores

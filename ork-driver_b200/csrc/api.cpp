@@ -19,34 +19,32 @@
 #include "ork_b200.h"
 #include "ork_internal.h"
 #include "ork_npu.h"
+#include "ork_structs.h"
 #include "pack.h"
 
 using namespace orkb;
 
-struct ork_npu {
-  int device = 0;
-  cudaStream_t own_stream = nullptr;
-  cudaStream_t stream = nullptr;
-  void *dA = nullptr;
-  size_t capA = 0;
-  void *dC = nullptr;
-  size_t capC = 0;
-  bool pdl = true;
-  int force_route = -1;
-  uint64_t launches = 0;
-};
+namespace orkb {
 
-struct ork_w {
-  ork_npu *ctx = nullptr;
-  int K = 0, N = 0;
-  int fmt = FMT_I8;
-  int dtype = DT_I8;
-  int quant_kind = 0;
-  bool int4_store = false;  // an ork_i4a8 weight: carries bscale and dumps as O4N1
-  void *d = nullptr;
-  size_t bytes = 0;
-  float *bscale = nullptr;
-};
+// 0 = CUDA-core GEMV, 1 = tcgen05 GEMM, -1 = no kernel for this weight / shape.
+int route_for(const ork_npu *c, const ork_w *w, int M) {
+  const bool tc = gemm_tc_supports(w->fmt, M, w->K, w->N), gv = gemv_supports(w->fmt, w->K);
+  if (!tc && !gv) return -1;
+  if (c && c->force_route == 0) return gv ? 0 : 1;
+  if (c && c->force_route == 1) return tc ? 1 : 0;
+  // measured crossover: the CUDA-core GEMV wins up to M = 4 everywhere and up to M = 8 on small
+  // weights; the tensor-core kernel wins beyond
+  if (M <= 4 || (M <= 8 && (size_t)w->K * w->N <= ((size_t)4 << 20))) return gv ? 0 : 1;
+  return tc ? 1 : 0;
+}
+
+// Sticky device-side error flags (a bounded wait that expired); cleared when read.
+bool device_error() {
+  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true);
+  return (t | g) != 0;
+}
+
+}  // namespace orkb
 
 namespace {
 
@@ -116,24 +114,6 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
     return nullptr;
   }
   return w;
-}
-
-// 0 = CUDA-core GEMV, 1 = tcgen05 GEMM, -1 = no kernel for this weight / shape.
-int route_for(const ork_npu *c, const ork_w *w, int M) {
-  const bool tc = gemm_tc_supports(w->fmt, M, w->K, w->N), gv = gemv_supports(w->fmt, w->K);
-  if (!tc && !gv) return -1;
-  if (c && c->force_route == 0) return gv ? 0 : 1;
-  if (c && c->force_route == 1) return tc ? 1 : 0;
-  // measured crossover: the CUDA-core GEMV wins up to M = 4 everywhere and up to M = 8 on small
-  // weights; the tensor-core kernel wins beyond
-  if (M <= 4 || (M <= 8 && (size_t)w->K * w->N <= ((size_t)4 << 20))) return gv ? 0 : 1;
-  return tc ? 1 : 0;
-}
-
-// Sticky device-side error flags (a bounded wait that expired); cleared when read.
-bool device_error() {
-  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true);
-  return (t | g) != 0;
 }
 
 // Launch one matmul on device buffers (A, C already on the context's GPU).

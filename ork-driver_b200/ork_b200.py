@@ -48,6 +48,7 @@ SIGNATURES = [
     ("ork_i8_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_i8_mm_run_noalloc", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_b200_sync", _i, [_vp]),
     ("ork_b200_stream", _vp, [_vp]),
     ("ork_b200_set_stream", _i, [_vp, _vp]),
