@@ -162,25 +162,63 @@ __device__ __forceinline__ uint4 add4(uint4 a, uint4 b) {
 
 constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 128 ? 128 : 256; }
 
-template <bool F16, bool SWAP, int TN, int STAGES>
+// Nibble weights (FMT_U4 / FMT_NF4): the W tile arrives as nibbles ([rows][64 bytes] per 128-k block)
+// in a staging buffer and the four epilogue warps, idle during the main loop, expand it in registers
+// into the 128-byte-swizzled int8 tile the MMA reads, then publish it to the async proxy. Uniform codes
+// are sign-extended (x | (x & 8) * 0x1E per byte); NF4 indices go through two 8-entry prmt tables
+// (lut[8..15] and -lut[0..7], zero in the other half), negated bytewise without carries.
+struct Nf4Tables {
+  uint32_t neg0, neg1, pos0, pos1;
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// 8 nibbles (k = 8q .. 8q+7 in nibble order) -> 8 int8 codes in k order, as two words.
+template <int FMT>
+__device__ __forceinline__ uint2 expand8(uint32_t w, const Nf4Tables &tb) {
+  if constexpr (FMT == FMT_U4) {
+    uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;  // k even / k odd, 0..15
+    lo |= (lo & 0x08080808u) * 0x1Eu;                             // bit 3 set -> high nibble 0xF
+    hi |= (hi & 0x08080808u) * 0x1Eu;
+    return make_uint2(prmt(lo, hi, 0x5140), prmt(lo, hi, 0x7362));
+  } else {
+    const uint32_t x = w ^ 0x88888888u;
+    const uint32_t p0 = prmt(tb.pos0, tb.pos1, x), p1 = prmt(tb.pos0, tb.pos1, x >> 16);
+    const uint32_t n0 = prmt(tb.neg0, tb.neg1, w), n1 = prmt(tb.neg0, tb.neg1, w >> 16);
+    // bytes of n are 0..127: (0x80 - n) ^ 0x80 == -n per byte, with no borrow between bytes
+    return make_uint2(p0 | ((0x80808080u - n0) ^ 0x80808080u), p1 | ((0x80808080u - n1) ^ 0x80808080u));
+  }
+}
+
+template <int FMT, bool SWAP, int TN, int STAGES>
 __global__ void __launch_bounds__(192)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
-               void *__restrict__ Cout, int M, int N, int K) {
+               void *__restrict__ Cout, int M, int N, int K, Nf4Tables tb) {
+  constexpr bool F16 = FMT == FMT_F16;
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  constexpr int WROWS = SWAP ? BM : TN;                 // rows of the weight tile
   constexpr uint32_t R_BYTES = BM * BK_BYTES;
   constexpr uint32_t S_BYTES = TN * BK_BYTES;
-  constexpr int ESZ = F16 ? 2 : 1;
-  constexpr int KSTEPS = BK_BYTES / 32;  // 32-byte MMA K steps per stage (K=32 int8 / K=16 f16)
+  constexpr uint32_t NIB_BYTES = NIB ? WROWS * 64 : 0;  // nibble staging per stage
+  // bytes the TMA delivers per stage: the activation tile, and the weight tile (int8/f16) or nibbles
+  constexpr uint32_t TX_BYTES = NIB ? ((SWAP ? S_BYTES : R_BYTES) + NIB_BYTES) : (R_BYTES + S_BYTES);
+  constexpr int ESZ = F16 ? 2 : 1;                      // activation element size
+  constexpr int KSTEPS = BK_BYTES / 32;                 // 32-byte MMA K steps per stage
   constexpr int TCOLS = tmem_cols(TN);
-  // split-K partial tile in shared memory (reuses the drained stage ring): [128][TN+4] or, swapped,
-  // [TN][128+4] so that the reduced output is read in C's row-major order
   constexpr int PSTR = SWAP ? (BM + 4) : (TN + 4);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *sR = smem;
   uint8_t *sS = smem + STAGES * R_BYTES;
-  uint64_t *bars = (uint64_t *)(sS + STAGES * S_BYTES);  // full[STAGES], empty[STAGES], done
-  uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 1);
+  uint8_t *sN = sS + STAGES * S_BYTES;                   // nibble staging (NIB only)
+  uint64_t *bars = (uint64_t *)(sN + STAGES * NIB_BYTES);  // full[S], empty[S], conv[S], done
+  uint32_t *tmem_slot = (uint32_t *)(bars + 3 * STAGES + 1);
   uint32_t *P = (uint32_t *)smem;
+  uint8_t *sW = SWAP ? sR : sS;                          // where the MMA reads the weight tile
 
   asm volatile("griddepcontrol.launch_dependents;");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -188,13 +226,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
   const int SK = gridDim.z, ks = blockIdx.z;
   const int KB = (K * ESZ + BK_BYTES - 1) / BK_BYTES;
   const int kb0 = (int)((long long)KB * ks / SK), kb1 = (int)((long long)KB * (ks + 1) / SK);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), done = smem_u32(bars + 2 * STAGES);
-  const int rows_R = SWAP ? N : M, rows_S = SWAP ? M : N;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), conv0 = smem_u32(bars + 2 * STAGES),
+                 done = smem_u32(bars + 3 * STAGES);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
+      mbar_init(conv0 + 8 * s, 4);  // one arrival per converter warp
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -210,31 +249,40 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
+  // weight tile load of stage s for k block kb (int8/f16 straight into the MMA tile; nibbles to staging)
+  auto load_w = [&](int s, int kb) {
+    if constexpr (NIB) {
+      tma_load_2d(smem_u32(sN + s * NIB_BYTES), SWAP ? &mapR : &mapS, kb * 64, SWAP ? r0 : c0, full0 + 8 * s);
+    } else {
+      const int x = kb * (BK_BYTES / ESZ);
+      if (SWAP) tma_load_2d(smem_u32(sR + s * R_BYTES), &mapR, x, r0, full0 + 8 * s);
+      else tma_load_2d(smem_u32(sS + s * S_BYTES), &mapS, x, c0, full0 + 8 * s);
+    }
+  };
+  auto load_a = [&](int s, int kb) {
+    const int x = kb * (BK_BYTES / ESZ);
+    if (SWAP) tma_load_2d(smem_u32(sS + s * S_BYTES), &mapS, x, c0, full0 + 8 * s);
+    else tma_load_2d(smem_u32(sR + s * R_BYTES), &mapR, x, r0, full0 + 8 * s);
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       // the weight tiles do not depend on the previous kernel: the first ring's worth is requested
       // before waiting on it (programmatic dependent launch); activations only after the wait
       const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
       for (int i = 0; i < pre; i++) {
-        mbar_expect_tx(full0 + 8 * i, R_BYTES + S_BYTES);
-        const int x = (kb0 + i) * (BK_BYTES / ESZ);
-        if (SWAP) tma_load_2d(smem_u32(sR + i * R_BYTES), &mapR, x, r0, full0 + 8 * i);
-        else tma_load_2d(smem_u32(sS + i * S_BYTES), &mapS, x, c0, full0 + 8 * i);
+        mbar_expect_tx(full0 + 8 * i, TX_BYTES);
+        load_w(i, kb0 + i);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = 0; i < pre; i++) {
-        const int x = (kb0 + i) * (BK_BYTES / ESZ);
-        if (SWAP) tma_load_2d(smem_u32(sS + i * S_BYTES), &mapS, x, c0, full0 + 8 * i);
-        else tma_load_2d(smem_u32(sR + i * R_BYTES), &mapR, x, r0, full0 + 8 * i);
-      }
+      for (int i = 0; i < pre; i++) load_a(i, kb0 + i);
       for (int kb = kb0 + pre; kb < kb1; kb++) {
         const int i = kb - kb0, s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) break;
-        mbar_expect_tx(full0 + 8 * s, R_BYTES + S_BYTES);
-        const int x = kb * (BK_BYTES / ESZ);
-        tma_load_2d(smem_u32(sR + s * R_BYTES), &mapR, x, r0, full0 + 8 * s);
-        tma_load_2d(smem_u32(sS + s * S_BYTES), &mapS, x, c0, full0 + 8 * s);
+        mbar_expect_tx(full0 + 8 * s, TX_BYTES);
+        load_w(s, kb);
+        load_a(s, kb);
       }
     }
   } else if (warp == 1) {
@@ -243,7 +291,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
       for (int kb = kb0; kb < kb1; kb++) {
         const int i = kb - kb0, s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(full0 + 8 * s, ph)) break;
+        if (!mbar_wait((NIB ? conv0 : full0) + 8 * s, ph)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t rd = sw128_desc(smem_u32(sR + s * R_BYTES));
         const uint64_t sd = sw128_desc(smem_u32(sS + s * S_BYTES));
@@ -255,6 +303,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
       umma_commit(done);
     }
   } else {
+    const int ct = threadIdx.x - 64;  // 0..127 over warps 2..5
+    if constexpr (NIB) {
+      // converter: per stage, WROWS x 8 chunks of 16 output bytes (row r, k chunk c), written at the
+      // 128-byte-swizzle position (chunk c ^ (r & 7)) of the 1024-byte-aligned tile
+      bool cok = true;
+      for (int kb = kb0; kb < kb1 && cok; kb++) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        cok = mbar_wait(full0 + 8 * s, ph);
+        if (!cok) break;
+        const uint8_t *src = sN + s * NIB_BYTES;
+        uint8_t *dst = sW + s * (SWAP ? R_BYTES : S_BYTES);
+#pragma unroll 2
+        for (int t = ct; t < WROWS * 8; t += 128) {
+          const int r = t >> 3, c = t & 7;
+          const uint2 nb = *reinterpret_cast<const uint2 *>(src + r * 64 + c * 8);
+          const uint2 lo = expand8<FMT>(nb.x, tb), hi = expand8<FMT>(nb.y, tb);
+          *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(conv0 + 8 * s) : "memory");
+      }
+    }
     // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = tile row of R
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
@@ -318,8 +390,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
   }
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
-  (void)rows_R;
-  (void)rows_S;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -335,40 +405,56 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D map over a row-major [rows][cols] matrix of esz-byte elements; box = box_rows x 128 bytes, SW128.
-bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int esz, int box_rows) {
+// 2-D map over a row-major [rows][row_bytes] byte matrix (element = esz bytes) with a box of
+// box_rows x box_bytes; 128-byte swizzle for MMA operand tiles, none for the nibble staging tiles.
+bool make_map(CUtensorMap *map, const void *base, int rows, size_t row_bytes, int esz, int box_rows,
+              int box_bytes, bool swizzle) {
   auto fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)cols * esz};
-  const cuuint32_t box[2] = {(cuuint32_t)(BK_BYTES / esz), (cuuint32_t)box_rows};
+  const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / esz), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / esz), (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                         const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-template <bool F16, bool SWAP, int TN, int STAGES>
+uint32_t pack4(int a, int b, int c, int d) {
+  return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
+         ((uint32_t)(uint8_t)d << 24);
+}
+
+template <int FMT, bool SWAP, int TN, int STAGES>
 cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
-  constexpr int ESZ = F16 ? 2 : 1;
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  constexpr int ESZ = FMT == FMT_F16 ? 2 : 1;
+  constexpr int WROWS = SWAP ? BM : TN;
   CUtensorMap mR, mS;
-  const void *R = SWAP ? a.W : a.A, *S = SWAP ? a.A : a.W;
-  const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
-  if (!make_map(&mR, R, rowsR, a.K, ESZ, BM) || !make_map(&mS, S, rowsS, a.K, ESZ, TN)) return cudaErrorInvalidValue;
-  constexpr size_t ring = (size_t)STAGES * (BM + TN) * BK_BYTES;
+  const size_t a_row = (size_t)a.K * ESZ, w_row = fmt_row_bytes(FMT, a.K);
+  // the weight operand: its MMA tile (int8/f16, swizzled) or its nibble staging tile (64 B per row)
+  const bool okW = NIB ? make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, 1, WROWS, 64, false)
+                       : make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, ESZ, WROWS, BK_BYTES, true);
+  const bool okA = make_map(SWAP ? &mS : &mR, a.A, a.M, a_row, ESZ, SWAP ? TN : BM, BK_BYTES, true);
+  if (!okW || !okA) return cudaErrorInvalidValue;
+  constexpr size_t ring = (size_t)STAGES * ((BM + TN) * BK_BYTES + (NIB ? WROWS * 64 : 0));
   constexpr size_t part = (size_t)(SWAP ? TN * (BM + 4) : BM * (TN + 4)) * 4;
   static_assert(part <= ring, "partial tile must fit in the stage ring");
-  constexpr size_t smem = 1024 + ring + (2 * STAGES + 1) * 8 + 16;
+  constexpr size_t smem = 1024 + ring + (3 * STAGES + 1) * 8 + 16;
   static_assert(smem <= 232448, "shared memory budget");
-  auto kern = gemm_tc_kernel<F16, SWAP, TN, STAGES>;
+  auto kern = gemm_tc_kernel<FMT, SWAP, TN, STAGES>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
+  const int8_t *L = kNf4Lut;
+  const Nf4Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
+                     pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((rowsR + BM - 1) / BM, (rowsS + TN - 1) / TN, sk);
   cfg.blockDim = dim3(192);
@@ -383,7 +469,7 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].val.clusterDim.z = sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K);
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K, tb);
 }
 
 struct TcCfg {
@@ -399,13 +485,14 @@ struct TcCfg {
 // keeps at least one K block.
 TcCfg choose_tc(int fmt, int M, int K, int N) {
   TcCfg c;
+  const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
   c.swap = M <= 64;
   c.tn = c.swap ? (M <= 16 ? 16 : M <= 32 ? 32 : 64) : 128;
-  if (!c.swap && ((M + BM - 1) / BM) * ((N + 127) / 128) >= 192) c.tn = 256;
+  if (!nib && !c.swap && ((M + BM - 1) / BM) * ((N + 127) / 128) >= 192) c.tn = 256;
   // ORKB_TC_TN / ORKB_TC_SK: tuning overrides of the non-swapped tile width (128 or 256) and of the
   // split factor (1..8), read on every launch
   const char *env_tn = getenv("ORKB_TC_TN");
-  if (!c.swap && env_tn) c.tn = atoi(env_tn) == 256 ? 256 : 128;
+  if (!nib && !c.swap && env_tn) c.tn = atoi(env_tn) == 256 ? 256 : 128;
   const int tiles = c.swap ? (N + BM - 1) / BM : ((M + BM - 1) / BM) * ((N + c.tn - 1) / c.tn);
   const int KB = (K * (fmt == FMT_F16 ? 2 : 1) + BK_BYTES - 1) / BK_BYTES;
   const int max_sk = c.swap ? 8 : 4, target = c.swap ? 192 : 128;
@@ -419,24 +506,27 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
   return c;
 }
 
-template <bool F16>
+template <int FMT>
 cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl) {
-  // swapped (decode-sized M) tiles keep the ring at 72-80 KB so three CTAs fit on an SM: the next
-  // launch's CTAs then start streaming their weights while this one drains (programmatic launch)
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  // swapped (decode-sized M) tiles keep the ring at 72-84 KB so two or three CTAs fit on an SM: the
+  // next launch's CTAs then start streaming their weights while this one drains (programmatic launch)
   if (c.swap) {
-    if (c.tn == 16) return launch_tc<F16, true, 16, 4>(a, c.sk, s, pdl);
-    if (c.tn == 32) return launch_tc<F16, true, 32, 4>(a, c.sk, s, pdl);
-    return launch_tc<F16, true, 64, 3>(a, c.sk, s, pdl);
+    if (c.tn == 16) return launch_tc<FMT, true, 16, NIB ? 3 : 4>(a, c.sk, s, pdl);
+    if (c.tn == 32) return launch_tc<FMT, true, 32, NIB ? 3 : 4>(a, c.sk, s, pdl);
+    return launch_tc<FMT, true, 64, 3>(a, c.sk, s, pdl);
   }
-  if (c.tn == 256) return launch_tc<F16, false, 256, 4>(a, c.sk, s, pdl);
-  return launch_tc<F16, false, 128, 6>(a, c.sk, s, pdl);
+  if constexpr (!NIB) {
+    if (c.tn == 256) return launch_tc<FMT, false, 256, 4>(a, c.sk, s, pdl);
+  }
+  return launch_tc<FMT, false, 128, NIB ? 4 : 6>(a, c.sk, s, pdl);
 }
 
 }  // namespace
 
 bool gemm_tc_supports(int fmt, int M, int K, int N) {
   (void)K;
-  if (fmt != FMT_I8 && fmt != FMT_F16) return false;
+  if (fmt != FMT_I8 && fmt != FMT_F16 && fmt != FMT_U4 && fmt != FMT_NF4) return false;
   if (N % 16) return false;
   return M >= 1 && encode_fn() != nullptr;
 }
@@ -445,9 +535,13 @@ cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *laun
   if ((uintptr_t)a.A % 16 || (uintptr_t)a.W % 16 || (uintptr_t)a.C % 16) return cudaErrorMisalignedAddress;
   const TcCfg c = choose_tc(a.fmt, a.M, a.K, a.N);
   cudaError_t e;
-  if (a.fmt == FMT_I8) e = dispatch<false>(a, c, s, pdl);
-  else if (a.fmt == FMT_F16) e = dispatch<true>(a, c, s, pdl);
-  else return cudaErrorNotSupported;
+  switch (a.fmt) {
+    case FMT_I8: e = dispatch<FMT_I8>(a, c, s, pdl); break;
+    case FMT_F16: e = dispatch<FMT_F16>(a, c, s, pdl); break;
+    case FMT_U4: e = dispatch<FMT_U4>(a, c, s, pdl); break;
+    case FMT_NF4: e = dispatch<FMT_NF4>(a, c, s, pdl); break;
+    default: return cudaErrorNotSupported;
+  }
   if (e == cudaSuccess && launches) ++*launches;
   return e;
 }

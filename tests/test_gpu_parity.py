@@ -76,7 +76,7 @@ def test_i4a8_pack_run_exact(ctx, env_clean, nf4, use_im, K, N):
     assert np.array_equal(bs, obs) and np.array_equal(w.bscale(), obs)
     assert np.array_equal(w.resident(), blob[20 + 4 * N:])  # resident nibbles == O4N1 payload
     rng = np.random.default_rng(2)
-    for M in (1, 3, 8, 32):
+    for M in (1, 3, 8, 32, 100, 256):
         A = rand_i8(rng, (M, K))
         rc, Cm = ctx.run(w, A)
         assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), M
@@ -89,7 +89,7 @@ def test_w4a4_exact(ctx, K, N):
     B = rand_i8(rng, (K, N), -8, 8)
     w = ctx.i4_pack(B)
     assert w
-    for M in (1, 2, 7, 8, 32):
+    for M in (1, 2, 7, 8, 32, 256):
         A = rand_i8(rng, (M, K), -8, 8)
         rc, Cm = ctx.run(w, A)
         assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B)), M
@@ -303,6 +303,30 @@ def test_tensor_core_route_f16(ctx, K, N):
                 assert L.ork_b200_force_route(ctx.ctx, route) == 0
                 rc, Cm = ctx.run(w, A)
                 assert rc == 0 and np.abs(Cm - ref).max() <= f16_tol(A, B), (M, route)
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w.free()
+
+
+@pytest.mark.parametrize("nf4", [False, True])
+@pytest.mark.parametrize("K,N", [(288, 192), (2048, 1024)])
+def test_tensor_core_and_gemv_routes_agree_int4(ctx, env_clean, nf4, K, N):
+    """Nibble weights through both paths (the tensor-core one expands nibbles to int8 in shared memory)."""
+    if nf4:
+        env_clean.setenv("ORK_NF4", "1")
+    L = ork_b200.lib()
+    rng = np.random.default_rng(K + N + nf4)
+    f32 = rng.standard_normal((N, K), dtype=np.float32)
+    w, _ = ctx.i4a8_pack(f32)
+    codes, _, _ = of.i4a8_blob_codes(w.dump(), K, N)
+    try:
+        for M in (1, 5, 16, 24, 40, 64, 65, 128, 130):
+            A = rand_i8(rng, (M, K))
+            ref = of.gemm_i32(A, codes)
+            for route in (1, 0):
+                assert L.ork_b200_force_route(ctx.ctx, route) == 0
+                rc, Cm = ctx.run(w, A)
+                assert rc == 0 and np.array_equal(Cm, ref), (M, route)
     finally:
         L.ork_b200_force_route(ctx.ctx, -1)
         w.free()
