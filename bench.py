@@ -159,6 +159,78 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def other_configs(ctx, L, stream, ncopies=10, reps=10):
+    """The remaining BASELINE configs, timed like the breakdown (each config alone, CUDA graph of
+    `ncopies` calls over distinct weight copies): configs[0] fp16, configs[2] w4a8 (uniform and NF4, with
+    an imatrix) and W4A4. Algorithmic bytes per call: fp16 2KN+2MK+4MN, int4 KN/2+MK+4MN."""
+    import torch
+
+    import ork_b200
+
+    rng = np.random.default_rng(99)
+    out = {}
+
+    def timed(kind, w_list, K, N, M):
+        dtype_in = torch.float16 if kind == "f16" else torch.int8
+        dtype_out = torch.float32 if kind == "f16" else torch.int32
+        if kind == "f16":
+            A = [(torch.rand((M, K), device="cuda") * 2 - 1).to(torch.float16) for _ in range(ncopies)]
+        else:
+            lo, hi = (-7, 8) if kind == "i4" else (-127, 128)
+            A = [torch.randint(lo, hi, (M, K), dtype=dtype_in, device="cuda") for _ in range(ncopies)]
+        C = [torch.empty((M, N), dtype=dtype_out, device="cuda") for _ in range(ncopies)]
+        fn = {"f16": L.ork_f16_mm_run_async, "i8": L.ork_i8_mm_run_async, "i4": L.ork_i4_mm_run_async}[kind]
+        for i in range(ncopies):
+            assert fn(ctx.ctx, w_list[i].h, M, A[i].data_ptr(), C[i].data_ptr()) == 0
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(ncopies):
+                fn(ctx.ctx, w_list[i].h, M, A[i].data_ptr(), C[i].data_ptr())
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * ncopies), L.ork_b200_route(w_list[0].h, M)
+
+    def record(name, kind, ws, K, N, Ms, wbytes):
+        for M in Ms:
+            ms, route = timed(kind, ws, K, N, M)
+            abytes = M * K * (2 if kind == "f16" else 1)
+            by = wbytes + abytes + 4 * M * N
+            out[f"{name} {K}x{N} M{M}"] = {"us": ms * 1e3, "GB/s": by / (ms / 1e3) / 1e9,
+                                           "TOPS": 2 * M * K * N / (ms / 1e3) / 1e12, "route": route}
+
+    # configs[0]: fp16 K=2048 N=6144, M in {1, 64}; B ~ N(0, 0.02)
+    K, N = 2048, 6144
+    B = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+    ws = [ctx.f16_pack(B) for _ in range(ncopies)]
+    record("fp16", "f16", ws, K, N, (1, 64), 2 * K * N)
+    for w in ws:
+        w.free()
+    # configs[2]: w4a8 uniform / NF4 with imatrix ~ U(0.5, 2), and W4A4 with A ~ U[-7, 7]
+    for K, N in ((6144, 2048), (2048, 12288)):
+        f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        im = (rng.random(K, dtype=np.float32) * np.float32(1.5) + np.float32(0.5)).astype(np.float32)
+        for nf4 in (False, True):
+            blob = ork_b200.cpu_blob(f32, im, nf4=nf4)
+            ws = [ctx.i4a8_load(blob, K, N) for _ in range(ncopies)]
+            record("w4a8-" + ("nf4" if nf4 else "uniform"), "i8", ws, K, N, (1, 32, 256), K * N // 2)
+            for w in ws:
+                w.free()
+        B4 = rng.integers(-7, 8, size=(K, N), dtype=np.int8)
+        ws = [ctx.i4_pack(B4) for _ in range(ncopies)]
+        record("w4a4", "i4", ws, K, N, (1, 32, 256), K * N // 2)
+        for w in ws:
+            w.free()
+    return out
+
+
 def run_profile(spec):
     """One config, packed once, run 5 times with a synchronisation after each: a small, self-contained
     workload for `ncu -k <kernel> -s <skip> -c <count>` captures."""
@@ -203,6 +275,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-others", action="store_true", help="skip the other BASELINE configs' table")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
     args = ap.parse_args()
@@ -387,6 +460,8 @@ def main():
     e2e = {"value": world * STEP_BYTES * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps}
 
+    others = other_configs(ctx, L, stream) if (rank == 0 and not args.no_others) else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, cores, kind, sample, _ = cpu_reference_sweep(10.0)
@@ -408,7 +483,7 @@ def main():
             / (sum(breakdown[k]["ms"] for k in dec) / 1e3) / 1e9,
             "prefill_tops": sum(2 * np.prod([int(x) for x in k.replace("M", "").split("x")]) for k in pre)
             / (sum(breakdown[k]["ms"] for k in pre) / 1e3) / 1e12,
-            "breakdown": breakdown}
+            "breakdown": breakdown, "other_configs": others}
     if rank == 0:
         print(json.dumps(line), flush=True)
     for ws in weights.values():
