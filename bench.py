@@ -232,19 +232,35 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
 
 
 def run_profile(spec):
-    """One config, packed once, run 5 times with a synchronisation after each: a small, self-contained
-    workload for `ncu -k <kernel> -s <skip> -c <count>` captures."""
+    """`K,N,M[,route]`: one config, packed once, run 5 times with a synchronisation after each -- a small,
+    self-contained workload for `ncu -k <kernel> -s <skip> -c <count>` captures -- then 50 back-to-back
+    calls timed with events (a tuning aid). `all`: the 12 configs[1] calls once each, in sweep order,
+    synchronised (one launch per config, for per-config ncu metrics such as DRAM traffic)."""
     import torch
 
     import ork_b200
 
+    L = ork_b200.lib()
+    ctx = ork_b200.Context()
+    rng = np.random.default_rng(0)
+    if spec == "all":
+        for K, N in SHAPES:
+            f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+            w, _ = ctx.i8_pack_f32(f32)
+            for M in MS:
+                a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+                c = torch.empty((M, N), dtype=torch.int32, device="cuda")
+                torch.cuda.synchronize()
+                assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
+                assert L.ork_b200_sync(ctx.ctx) == 0
+            w.free()
+        print(json.dumps({"profile": "all", "configs": [f"{K}x{N}xM{M}" for K, N, M in CONFIGS]}))
+        ctx.close()
+        return
     parts = [int(x) for x in spec.split(",")]
     K, N, M = parts[:3]
     route = parts[3] if len(parts) > 3 else -1
-    L = ork_b200.lib()
-    ctx = ork_b200.Context()
     L.ork_b200_force_route(ctx.ctx, route)
-    rng = np.random.default_rng(0)
     f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
     w, _ = ctx.i8_pack_f32(f32)
     a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
@@ -276,6 +292,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-others", action="store_true", help="skip the other BASELINE configs' table")
+    ap.add_argument("--ncu-step", action="store_true",
+                    help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
+                         "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
     args = ap.parse_args()
@@ -360,6 +379,14 @@ def main():
     for s in range(args.warmup):
         graphs[s % NCOPIES].replay()
     barrier()
+    if args.ncu_step:
+        torch.cuda.cudart().cudaProfilerStart()
+        for s in range(NCOPIES):
+            graphs[s].replay()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps({"ncu_step": NCOPIES, "launches_per_step": launches_per_step}), flush=True)
+        return
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         with torch.cuda.stream(stream):
