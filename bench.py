@@ -231,6 +231,130 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
     return out
 
 
+# Llama-70B-shaped linear stack of BASELINE configs[4]: hidden 8192, FFN 28672, 80 layers, vocab 128256;
+# GQA 64 query / 8 key-value heads of 128 (QKV N = 8192 + 2*1024), gate and up fused into one N = 57344
+# weight. (K, N) per linear; the LM head runs once per pass.
+L70 = {"layers": 80, "linears": [("qkv", 8192, 10240), ("o", 8192, 8192), ("gate_up", 8192, 57344),
+                                 ("down", 28672, 8192)], "lm_head": (8192, 128256)}
+
+
+def run_70b(args):
+    """every weight NF4 (w4a8, B ~ N(0, 0.02)), column-sharded over the ranks; each matmul
+    runs on the local shard and its int32 C is all-gathered over NCCL. One step = one pass of M tokens
+    through the 80 layers' four linears and the LM head, captured as one CUDA graph (kernels and
+    collectives). Each rank quantizes its own channel slice once on the host and loads enough distinct
+    copies of a layer that its per-pass working set exceeds L2. value = tokens/s of the whole job."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ork_b200
+    import shard
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    L = ork_b200.lib()
+    ctx = ork_b200.Context()
+    stream = torch.cuda.Stream()
+    L.ork_b200_set_stream(ctx.ctx, stream.cuda_stream)
+    M = args.m
+    layer_bytes = sum(K * N // 2 for _, K, N in L70["linears"]) // world
+    ncopies = max(2, -(-400 * 2 ** 20 // layer_bytes))
+    rng = np.random.default_rng(4242 + rank)
+
+    def packed(K, N, copies):
+        n0, n1 = shard.shard_range(N, rank, world)
+        f32 = (rng.standard_normal((n1 - n0, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        blob = ork_b200.cpu_blob(f32, None, nf4=True)
+        del f32
+        return [ctx.i4a8_load(blob, K, n1 - n0) for _ in range(copies)]
+
+    lin = {name: (K, N, packed(K, N, ncopies)) for name, K, N in L70["linears"]}
+    Kh, Nv = L70["lm_head"]
+    # quantized in 3 channel blocks to bound host memory (same bytes and work); 128256 = 256 * 501, so 3
+    # blocks keep every rank's slice a multiple of 32 channels for 1, 2, 4 and 8 ranks
+    head_chunks = 3
+    head = [(Kh, Nv // head_chunks, packed(Kh, Nv // head_chunks, 1)[0]) for _ in range(head_chunks)]
+    A = {8192: torch.randint(-127, 128, (M, 8192), dtype=torch.int8, device="cuda"),
+         28672: torch.randint(-127, 128, (M, 28672), dtype=torch.int8, device="cuda")}
+    Cl = {name: torch.empty((M, N // world), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
+    Cf = {name: torch.empty((M, N), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
+    Chl = torch.empty((M, Nv // head_chunks // world), dtype=torch.int32, device="cuda")
+    Chf = torch.empty((M, Nv // head_chunks), dtype=torch.int32, device="cuda")
+
+    def run(w, a, cl, cf):
+        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), cl.data_ptr()) == 0
+        if world > 1:
+            shard.gather_columns(cl, dist, out=cf)
+
+    def one_pass():
+        for layer in range(L70["layers"]):
+            for name, K, N in L70["linears"]:
+                run(lin[name][2][layer % ncopies], A[K], Cl[name], Cf[name])
+        for K, N, w in head:
+            run(w, A[K], Chl, Chf)
+
+    with torch.cuda.stream(stream):
+        one_pass()  # eager warm-up: kernel attributes, tensor maps, NCCL communicator
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        l0 = ctx.launches()
+        with torch.cuda.graph(g, stream=stream):
+            one_pass()
+        launches_per_pass = ctx.launches() - l0
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        if dist.is_initialized():
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    del g
+    per_pass = ms / args.steps
+    rank_bytes = L70["layers"] * layer_bytes + Kh * Nv // 2 // world
+    line = {"metric": "70B-shape NF4 linear stack tok/s (configs[4])", "value": M / (per_pass / 1e3),
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_pass, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "Llama-70B-shaped linears, NF4 weights ~N(0,0.02), 80 layers x (QKV 8192x10240, "
+                                   "O 8192x8192, gate+up 8192x57344, down 28672x8192) + LM head 8192x128256, "
+                                   f"column-sharded over {world} GPU(s), NCCL all-gather of each int32 C",
+                       "M": M, "parallelism": f"column shard x{world}",
+                       "l2": f"inputs larger than L2: {ncopies} distinct copies of the per-rank layer weights "
+                             f"({ncopies * layer_bytes / 2**20:.0f} MiB) cycled over the 80 layers"},
+            "per_gpu_weight_GBs": rank_bytes / (per_pass / 1e3) / 1e9,
+            "weight_bytes_per_rank_per_pass": rank_bytes, "gpu_launches": int(launches_per_pass * args.steps),
+            "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for _, _, ws in lin.values():
+        for w in ws:
+            w.free()
+    for _, _, w in head:
+        w.free()
+    ctx.close()
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
 def run_profile(spec):
     """`K,N,M[,route]`: one config, packed once, run 5 times with a synchronisation after each -- a small,
     self-contained workload for `ncu -k <kernel> -s <skip> -c <count>` captures -- then 50 back-to-back
@@ -295,6 +419,9 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
+    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b"],
+                    help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack")
+    ap.add_argument("--m", type=int, default=1, help="70b workload: tokens per pass (1, 8 or 256)")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
     args = ap.parse_args()
@@ -303,6 +430,8 @@ def main():
         return run_reference(args)
     if args.profile:
         return run_profile(args.profile)
+    if args.workload == "70b":
+        return run_70b(args)
 
     import torch
 

@@ -1,0 +1,81 @@
+"""Column sharding of resident weights across the GPUs of one node (the 70B-shape configuration).
+
+Output channels are independent in every format of this library -- each channel has its own scale and
+its own K codes (ork-driver src/npu/i4/pack.c:63-80) -- so a weight B[K,N] splits by channel ranges with
+no change to any value: rank g packs channels [g*N/G, (g+1)*N/G) (a contiguous row block of the n-major
+f32 source) and produces C[:, its range]. The reference splits the same way across its NPU cores
+(src/npu.c:1356-1398). One collective per sharded matmul reassembles C: an all-gather of the int32
+shards over NCCL (NVLink / NVSwitch), then a channel-order view. Shard widths must keep the pack's
+alignment (N/G a multiple of 32, of 64 for W4A4).
+
+The module keeps the collective separate from the local matmul so the host-side logic (slicing, the
+gather and reassembly order) is testable on CPU ranks with any local product.
+"""
+import numpy as np
+
+
+def shard_range(N, rank, world, align=32):
+    """Channel range [n0, n1) of `rank` for an N-channel weight split over `world` ranks."""
+    if N % world or (N // world) % align:
+        raise ValueError(f"N={N} does not split into {world} shards of a multiple of {align} channels")
+    w = N // world
+    return rank * w, (rank + 1) * w
+
+
+def shard_rows_nk(f32_nk, rank, world, align=32):
+    """This rank's rows of an n-major [N][K] f32 weight (what ork_i8_mm_pack_f32 / ork_i4a8_mm_pack take)."""
+    n0, n1 = shard_range(f32_nk.shape[0], rank, world, align)
+    return np.ascontiguousarray(f32_nk[n0:n1])
+
+
+def shard_cols_kn(b_kn, rank, world, align=32):
+    """This rank's columns of a row-major [K][N] weight (what ork_i8_mm_pack / ork_i4_mm_pack take)."""
+    n0, n1 = shard_range(b_kn.shape[1], rank, world, align)
+    return np.ascontiguousarray(b_kn[:, n0:n1])
+
+
+def gather_columns(local, dist, group=None, out=None):
+    """All-gather the [M][N/G] shards of all ranks and return C [M][N] in channel order.
+
+    `local` is a torch tensor (int32 or float32) on the rank's device (CUDA with NCCL, CPU with gloo).
+    The collective gathers [G][M][N/G]; for M = 1 that is already [N], otherwise the rank axis moves next
+    to the channel axis (one strided copy)."""
+    import torch
+
+    world = dist.get_world_size(group)
+    M, w = local.shape
+    if world == 1:
+        return local
+    local = local.contiguous()
+    if dist.get_backend(group) == "nccl":
+        stacked = torch.empty((world, M, w), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(stacked, local, group=group)
+    else:
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local, group=group)
+        stacked = torch.stack(parts)
+    if M == 1:
+        full = stacked.view(1, world * w)
+    else:
+        full = stacked.permute(1, 0, 2).reshape(M, world * w)
+    if out is not None:
+        out.copy_(full)
+        return out
+    return full
+
+
+class ShardedLinear:
+    """One column-sharded resident weight on this rank, run through the library's async device-pointer
+    call, followed by the all-gather of C."""
+
+    def __init__(self, ctx, weight, N, rank, world):
+        self.ctx, self.w, self.N, self.rank, self.world = ctx, weight, N, rank, world
+        self.n0, self.n1 = shard_range(N, rank, world)
+
+    def forward(self, A_dev, C_local, dist, C_full=None):
+        L = self.ctx.L
+        M = A_dev.shape[0]
+        fn = L.ork_i4_mm_run_async if self.w.kind == "i4" else L.ork_i8_mm_run_async
+        if fn(self.ctx.ctx, self.w.h, M, A_dev.data_ptr(), C_local.data_ptr()) != 0:
+            raise RuntimeError("sharded matmul launch failed")
+        return gather_columns(C_local, dist, out=C_full)
