@@ -263,7 +263,7 @@ def run_70b(args):
     ctx = ork_b200.Context()
     stream = torch.cuda.Stream()
     L.ork_b200_set_stream(ctx.ctx, stream.cuda_stream)
-    M = args.m
+    M = args.tokens
     layer_bytes = sum(K * N // 2 for _, K, N in L70["linears"]) // world
     ncopies = max(2, -(-400 * 2 ** 20 // layer_bytes))
     rng = np.random.default_rng(4242 + rank)
@@ -421,7 +421,7 @@ def main():
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
     ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b"],
                     help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack")
-    ap.add_argument("--m", type=int, default=1, help="70b workload: tokens per pass (1, 8 or 256)")
+    ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
     args = ap.parse_args()
