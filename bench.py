@@ -355,6 +355,175 @@ def run_70b(args):
         dist.destroy_process_group()
 
 
+# Qwen3-1.7B shape of BASELINE configs[3]: 28 layers, hidden 2048, 16 query / 8 key-value heads of 128,
+# SwiGLU FFN 6144, vocab 151936, RMSNorm (eps 1e-6) incl. per-head q/k norms, RoPE theta 1e6.
+Q3 = {"H": 2048, "NH": 16, "NKV": 8, "D": 128, "FF": 6144, "layers": 28, "V": 151936, "theta": 1e6, "eps": 1e-6}
+
+
+def run_qwen3(args):
+    """random-init (~N(0,0.02)) Qwen3-1.7B-shaped w8a8 stack. Every linear projection (fused
+    QKV, O, fused gate/up, down, LM head) is ork_i8_mm_run on per-channel int8 weights packed by
+    ork_i8_mm_pack_f32, with per-row int8 activation quantization (absmax/127) before and the
+    as[m] * bscale[n] dequantization after; norms, RoPE, attention over the KV cache, SwiGLU and the
+    residual stream are PyTorch ops on the same stream. Prefill 128 tokens, then 256 greedy decode steps
+    of batch 1, each decode step one CUDA graph. Four distinct layer weight sets (200 MB, > L2) cycle
+    over the 28 layers. value = decode tokens/s; prefill tokens/s beside it."""
+    import torch
+    import torch.nn.functional as F
+
+    import ork_b200
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    L = ork_b200.lib()
+    ctx = ork_b200.Context()
+    stream = torch.cuda.Stream()
+    L.ork_b200_set_stream(ctx.ctx, stream.cuda_stream)
+    H, NH, NKV, D, FF, NLY, V = (Q3[k] for k in ("H", "NH", "NKV", "D", "FF", "layers", "V"))
+    PRE, DEC = 128, 256
+    MAXT = PRE + DEC
+    NDIST = 4
+    rng = np.random.default_rng(1234 + rank)
+    dev = "cuda"
+
+    def pack(N, K):
+        f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        w, bs = ctx.i8_pack_f32(f32)
+        assert w
+        return w, torch.from_numpy(bs).to(dev)
+
+    wsets = [{"qkv": pack((NH + 2 * NKV) * D, H), "o": pack(H, NH * D), "gu": pack(2 * FF, H),
+              "down": pack(H, FF)} for _ in range(NDIST)]
+    lm = pack(V, H)
+    g = torch.Generator(device=dev).manual_seed(5)
+    emb = (torch.randn((V, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    ones_h = torch.ones(H, device=dev)
+    ones_d = torch.ones(D, device=dev)
+    inv = 1.0 / (Q3["theta"] ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+    ang = torch.outer(torch.arange(MAXT, device=dev, dtype=torch.float32), inv)
+    cos_t, sin_t = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
+    kc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.bfloat16) for _ in range(NLY)]
+    vc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.bfloat16) for _ in range(NLY)]
+
+    def rmsnorm(x, w):
+        x = x.float()
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + Q3["eps"]) * w
+
+    def rope(x, cos, sin):  # x [..., T, D]
+        x1, x2 = x[..., : D // 2], x[..., D // 2:]
+        return x * cos + torch.cat([-x2, x1], -1) * sin
+
+    def linear(x, wb):  # x [M, K] float -> [M, N] float through the int8 library matmul
+        w, bs = wb
+        M = x.shape[0]
+        as_ = x.abs().amax(dim=1, keepdim=True).clamp_min(1e-9) / 127.0
+        xq = torch.clamp(torch.round(x / as_), -127, 127).to(torch.int8)
+        c = torch.empty((M, w.N), device=dev, dtype=torch.int32)
+        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, xq.data_ptr(), c.data_ptr()) == 0
+        return c.float() * as_ * bs
+
+    def layer(x, li, pos0, T, pos_t=None):  # x [T, H] fp32; decode: T = 1 at device position pos_t
+        ws = wsets[li % NDIST]
+        qkv = linear(rmsnorm(x, ones_h), ws["qkv"])
+        q = qkv[:, : NH * D].view(T, NH, D).transpose(0, 1)
+        k = qkv[:, NH * D: (NH + NKV) * D].view(T, NKV, D).transpose(0, 1)
+        v = qkv[:, (NH + NKV) * D:].view(T, NKV, D).transpose(0, 1)
+        q, k = rmsnorm(q, ones_d), rmsnorm(k, ones_d)
+        if pos_t is None:
+            cos, sin = cos_t[pos0:pos0 + T], sin_t[pos0:pos0 + T]
+            q, k = rope(q, cos, sin), rope(k, cos, sin)
+            kc[li][:, pos0:pos0 + T] = k.to(torch.bfloat16)
+            vc[li][:, pos0:pos0 + T] = v.to(torch.bfloat16)
+            o = F.scaled_dot_product_attention(q.to(torch.bfloat16), kc[li][:, :pos0 + T], vc[li][:, :pos0 + T],
+                                               is_causal=True, enable_gqa=True)
+        else:
+            cos, sin = cos_t.index_select(0, pos_t), sin_t.index_select(0, pos_t)
+            q, k = rope(q, cos, sin), rope(k, cos, sin)
+            kc[li].index_copy_(1, pos_t, k.to(torch.bfloat16))
+            vc[li].index_copy_(1, pos_t, v.to(torch.bfloat16))
+            mask = (torch.arange(MAXT, device=dev) <= pos_t).view(1, 1, MAXT)
+            o = F.scaled_dot_product_attention(q.to(torch.bfloat16), kc[li], vc[li], attn_mask=mask,
+                                               enable_gqa=True)
+        x = x + linear(o.transpose(0, 1).reshape(T, NH * D).float(), ws["o"])
+        gu = linear(rmsnorm(x, ones_h), ws["gu"])
+        x = x + linear(F.silu(gu[:, :FF]) * gu[:, FF:], ws["down"])
+        return x
+
+    def forward(tokens, pos0, pos_t=None):
+        x = emb.index_select(0, tokens).float()
+        for li in range(NLY):
+            x = layer(x, li, pos0, x.shape[0], pos_t)
+        return linear(rmsnorm(x[-1:], ones_h), lm)
+
+    prompt = torch.randint(0, V, (PRE,), device=dev, generator=g)
+    tok = torch.zeros(1, dtype=torch.long, device=dev)
+    pos = torch.zeros(1, dtype=torch.long, device=dev)
+
+    def decode_step():
+        logits = forward(tok, 0, pos)
+        tok.copy_(logits.argmax(-1))
+        pos.add_(1)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):  # warm-up prefill (kernel attributes, tensor maps, cuDNN/SDPA selection)
+            forward(prompt, 0)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = ctx.launches()
+        e0.record(stream)
+        logits = forward(prompt, 0)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        prefill_ms = e0.elapsed_time(e1)
+        prefill_launches = ctx.launches() - l0
+        tok.copy_(logits.argmax(-1))
+        pos.fill_(PRE)
+        decode_step()  # eager warm-up of the decode shapes
+        pos.fill_(PRE)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        l0 = ctx.launches()
+        with torch.cuda.graph(graph, stream=stream):
+            decode_step()
+        launches_per_token = ctx.launches() - l0
+        pos.fill_(PRE)
+        torch.cuda.synchronize()
+        with Clocks(local) as clk:
+            e0.record(stream)
+            for _ in range(DEC):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        decode_ms = e0.elapsed_time(e1)
+    del graph
+    weight_bytes = NLY * ((NH + 2 * NKV) * D * H + H * NH * D + 2 * FF * H + H * FF) + V * H
+    tps = DEC / (decode_ms / 1e3)
+    line = {"metric": "Qwen3-1.7B-shape w8a8 decode tok/s (configs[3])", "value": tps * world, "unit": "tok/s",
+            "n_gpus": world, "steps": DEC, "warmup": 1, "ms_per_step": decode_ms / DEC, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "Qwen3-1.7B-shaped w8a8 stack, random weights ~N(0,0.02): 28 layers, hidden 2048, "
+                                   "16/8 heads x 128, SwiGLU 6144, vocab 151936, q/k norms, RoPE 1e6; prefill 128 "
+                                   "then 256 greedy decode steps, batch 1",
+                       "linears": "every projection (fused QKV, O, fused gate/up, down, LM head) via ork_i8_mm_run; "
+                                  "norms/RoPE/attention/SwiGLU in PyTorch on the same stream",
+                       "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
+                       "parallelism": "replicas" if world > 1 else "single GPU"},
+            "prefill_tok_s": PRE / (prefill_ms / 1e3) * world, "prefill_ms": prefill_ms,
+            "decode_ms_per_token": decode_ms / DEC, "int8_weight_bytes_per_token": weight_bytes,
+            "linear_weight_GBs_decode": weight_bytes / (decode_ms / DEC / 1e3) / 1e9,
+            "gpu_launches": int(launches_per_token * DEC), "library_launches_per_token": launches_per_token,
+            "library_launches_prefill": prefill_launches, "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for ws in wsets:
+        for w, _ in ws.values():
+            w.free()
+    lm[0].free()
+    ctx.close()
+
+
 def run_profile(spec):
     """`K,N,M[,route]`: one config, packed once, run 5 times with a synchronisation after each -- a small,
     self-contained workload for `ncu -k <kernel> -s <skip> -c <count>` captures -- then 50 back-to-back
@@ -419,8 +588,9 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
-    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b"],
-                    help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack")
+    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3"],
+                    help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack; "
+                         "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack")
     ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
@@ -432,6 +602,8 @@ def main():
         return run_profile(args.profile)
     if args.workload == "70b":
         return run_70b(args)
+    if args.workload == "qwen3":
+        return run_qwen3(args)
 
     import torch
 
