@@ -194,22 +194,25 @@ __device__ __forceinline__ uint2 expand8(uint32_t w, const Nf4Tables &tb) {
   }
 }
 
-template <int FMT, bool SWAP, int TN, int STAGES>
+template <int FMT, bool SWAP, int TN, int STAGES, int NA>
 __global__ void __launch_bounds__(192)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
                void *__restrict__ Cout, int M, int N, int K, Nf4Tables tb) {
+  // NA accumulators of 128 rows stacked along the R side (TM = 128*NA): each K step issues NA MMAs that
+  // share the S tile, so S is fetched once per 128*NA rows (less operand traffic per output)
   constexpr bool F16 = FMT == FMT_F16;
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
-  constexpr int WROWS = SWAP ? BM : TN;                 // rows of the weight tile
-  constexpr uint32_t R_BYTES = BM * BK_BYTES;
+  constexpr int TM = BM * NA;
+  constexpr int WROWS = SWAP ? TM : TN;                 // rows of the weight tile
+  constexpr uint32_t R_BYTES = TM * BK_BYTES;
   constexpr uint32_t S_BYTES = TN * BK_BYTES;
   constexpr uint32_t NIB_BYTES = NIB ? WROWS * 64 : 0;  // nibble staging per stage
   // bytes the TMA delivers per stage: the activation tile, and the weight tile (int8/f16) or nibbles
   constexpr uint32_t TX_BYTES = NIB ? ((SWAP ? S_BYTES : R_BYTES) + NIB_BYTES) : (R_BYTES + S_BYTES);
   constexpr int ESZ = F16 ? 2 : 1;                      // activation element size
   constexpr int KSTEPS = BK_BYTES / 32;                 // 32-byte MMA K steps per stage
-  constexpr int TCOLS = tmem_cols(TN);
-  constexpr int PSTR = SWAP ? (BM + 4) : (TN + 4);
+  constexpr int TCOLS = tmem_cols(TN * NA);
+  constexpr int PSTR = SWAP ? (TM + 4) : (TN + 4);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *sR = smem;
@@ -222,7 +225,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
 
   asm volatile("griddepcontrol.launch_dependents;");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r0 = blockIdx.x * BM, c0 = blockIdx.y * TN;
+  const int r0 = blockIdx.x * TM, c0 = blockIdx.y * TN;
   const int SK = gridDim.z, ks = blockIdx.z;
   const int KB = (K * ESZ + BK_BYTES - 1) / BK_BYTES;
   const int kb0 = (int)((long long)KB * ks / SK), kb1 = (int)((long long)KB * (ks + 1) / SK);
@@ -297,7 +300,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         const uint64_t sd = sw128_desc(smem_u32(sS + s * S_BYTES));
 #pragma unroll
         for (int k = 0; k < KSTEPS; k++)  // advance 32 bytes (2 x 16-byte units) along K within the row
-          umma<F16>(tmem, rd + 2 * k, sd + 2 * k, id, (kb > kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+          for (int a = 0; a < NA; a++)    // accumulator a: R rows 128a.., TMEM columns a*TN..
+            umma<F16>(tmem + (uint32_t)(a * TN), rd + (uint64_t)(a * (BM * BK_BYTES >> 4)) + 2 * k, sd + 2 * k, id,
+                      (kb > kb0 || k > 0) ? 1u : 0u);
         umma_commit(empty0 + 8 * s);
       }
       umma_commit(done);
@@ -327,40 +333,44 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(conv0 + 8 * s) : "memory");
       }
     }
-    // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = tile row of R
+    // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = row of an R accumulator
     const int sub = warp & 3;
-    const int row = sub * 32 + lane;
     const bool ok = mbar_wait(done, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
 #pragma unroll 1
-      for (int cc = 0; cc < TN; cc += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)cc, r);
-        if (SK > 1) {  // stage the partial tile for the cluster reduction
-          if (SWAP) {
+      for (int a = 0; a < NA; a++) {
+        const int row = a * BM + sub * 32 + lane;  // tile row of R
+#pragma unroll 1
+        for (int cc = 0; cc < TN; cc += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(a * TN + cc), r);
+          if (SK > 1) {  // stage the partial tile for the cluster reduction
+            if (SWAP) {
 #pragma unroll
-            for (int q = 0; q < 16; q++) P[(cc + q) * PSTR + row] = r[q];
+              for (int q = 0; q < 16; q++) P[(cc + q) * PSTR + row] = r[q];
+            } else {
+#pragma unroll
+              for (int q = 0; q < 16; q += 4)
+                *reinterpret_cast<uint4 *>(P + row * PSTR + cc + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
+            }
+          } else if (SWAP) {  // D[n][m] -> C[m][n]: lanes are consecutive n, so each store is coalesced
+            const int n = r0 + row;
+            if (n < N) {
+              uint32_t *Cp = (uint32_t *)Cout;
+#pragma unroll
+              for (int q = 0; q < 16; q++)
+                if (c0 + cc + q < M) Cp[(size_t)(c0 + cc + q) * N + n] = r[q];
+            }
           } else {
+            const int m = r0 + row;
+            if (m < M) {
+              uint32_t *dst = (uint32_t *)Cout + (size_t)m * N + c0 + cc;
 #pragma unroll
-            for (int q = 0; q < 16; q += 4)
-              *reinterpret_cast<uint4 *>(P + row * PSTR + cc + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
-          }
-        } else if (SWAP) {  // D[n][m] -> C[m][n]: lanes are consecutive n, so each store is coalesced
-          const int n = r0 + row;
-          if (n < N) {
-            uint32_t *Cp = (uint32_t *)Cout;
-#pragma unroll
-            for (int q = 0; q < 16; q++)
-              if (c0 + cc + q < M) Cp[(size_t)(c0 + cc + q) * N + n] = r[q];
-          }
-        } else {
-          const int m = r0 + row;
-          if (m < M) {
-            uint32_t *dst = (uint32_t *)Cout + (size_t)m * N + c0 + cc;
-#pragma unroll
-            for (int q = 0; q < 16; q += 4)
-              if (c0 + cc + q < N) *reinterpret_cast<uint4 *>(dst + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
+              for (int q = 0; q < 16; q += 4)
+                if (c0 + cc + q < N)
+                  *reinterpret_cast<uint4 *>(dst + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
+            }
           }
         }
       }
@@ -371,17 +381,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
   if (SK > 1) {
     cluster_sync();  // every CTA's partial tile is in its shared memory
     // reduce: output items are (output row, 4-column vector) of the tile in C's row-major order
-    const int out_rows = SWAP ? min(TN, M - c0) : min(BM, M - r0);
-    const int out_cols = SWAP ? min(BM, N - r0) : min(TN, N - c0);
+    const int out_rows = SWAP ? min(TN, M - c0) : min(TM, M - r0);
+    const int out_cols = SWAP ? min(TM, N - r0) : min(TN, N - c0);
     const int vpr = out_cols / 4;  // N is a multiple of 16, tiles start at multiples of 16
     const int items = out_rows * vpr;
     const uint32_t pbase = smem_u32(P);
     uint32_t *Cp = (uint32_t *)Cout;
+    // every remote read of an item is issued before the first add, so the SK distributed-shared-memory
+    // latencies overlap instead of adding up
     for (int t = ks * 192 + (int)threadIdx.x; t < items; t += SK * 192) {
       const int orow = t / vpr, ov = t % vpr;
       const uint32_t off = (uint32_t)(orow * PSTR + 4 * ov) * 4u;
-      uint4 acc = ld_dsmem_v4(pbase + off, 0);
-      for (int q = 1; q < SK; q++) acc = add4<F16>(acc, ld_dsmem_v4(pbase + off, (uint32_t)q));
+      uint4 v[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        if (q < SK) v[q] = ld_dsmem_v4(pbase + off, (uint32_t)q);
+      uint4 acc = v[0];
+#pragma unroll
+      for (int q = 1; q < 8; q++)
+        if (q < SK) acc = add4<F16>(acc, v[q]);
       const int m = SWAP ? c0 + orow : r0 + orow;
       const int n = (SWAP ? r0 : c0) + 4 * ov;
       *reinterpret_cast<uint4 *>(Cp + (size_t)m * N + n) = acc;
@@ -427,24 +445,25 @@ uint32_t pack4(int a, int b, int c, int d) {
          ((uint32_t)(uint8_t)d << 24);
 }
 
-template <int FMT, bool SWAP, int TN, int STAGES>
+template <int FMT, bool SWAP, int TN, int STAGES, int NA = 1>
 cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
   constexpr int ESZ = FMT == FMT_F16 ? 2 : 1;
-  constexpr int WROWS = SWAP ? BM : TN;
+  constexpr int TM = BM * NA;
+  constexpr int WROWS = SWAP ? TM : TN;
   CUtensorMap mR, mS;
   const size_t a_row = (size_t)a.K * ESZ, w_row = fmt_row_bytes(FMT, a.K);
   // the weight operand: its MMA tile (int8/f16, swizzled) or its nibble staging tile (64 B per row)
   const bool okW = NIB ? make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, 1, WROWS, 64, false)
                        : make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, ESZ, WROWS, BK_BYTES, true);
-  const bool okA = make_map(SWAP ? &mS : &mR, a.A, a.M, a_row, ESZ, SWAP ? TN : BM, BK_BYTES, true);
+  const bool okA = make_map(SWAP ? &mS : &mR, a.A, a.M, a_row, ESZ, SWAP ? TN : TM, BK_BYTES, true);
   if (!okW || !okA) return cudaErrorInvalidValue;
-  constexpr size_t ring = (size_t)STAGES * ((BM + TN) * BK_BYTES + (NIB ? WROWS * 64 : 0));
-  constexpr size_t part = (size_t)(SWAP ? TN * (BM + 4) : BM * (TN + 4)) * 4;
+  constexpr size_t ring = (size_t)STAGES * ((TM + TN) * BK_BYTES + (NIB ? WROWS * 64 : 0));
+  constexpr size_t part = (size_t)(SWAP ? TN * (TM + 4) : TM * (TN + 4)) * 4;
   static_assert(part <= ring, "partial tile must fit in the stage ring");
   constexpr size_t smem = 1024 + ring + (3 * STAGES + 1) * 8 + 16;
   static_assert(smem <= 232448, "shared memory budget");
-  auto kern = gemm_tc_kernel<FMT, SWAP, TN, STAGES>;
+  auto kern = gemm_tc_kernel<FMT, SWAP, TN, STAGES, NA>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -456,7 +475,7 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
                      pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((rowsR + BM - 1) / BM, (rowsS + TN - 1) / TN, sk);
+  cfg.gridDim = dim3((rowsR + TM - 1) / TM, (rowsS + TN - 1) / TN, sk);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -475,32 +494,62 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
 struct TcCfg {
   bool swap;
   int tn, sk;
+  int na = 1;      // 128-row accumulators per CTA along the R side
+  int stages = 0;  // 0: the variant's default; 3: the 96 KB ring of the 128 x 128 tile
 };
 
-// Tile and split choice (measured on B200 over the BASELINE shapes): swapped operands with the
-// narrowest N-tile covering M for M <= 64, else 128 x 128 activation x weight tiles, widened to 256
-// once there are enough tiles to fill the GPU. Then K is split over a cluster: up to 8 ways for the
-// swapped (weight-streaming) tiles until ~192 CTAs, up to 4 ways for the MMA-heavy tiles until ~128
-// CTAs (beyond that the extra partial-tile traffic costs more than the parallelism gains); each CTA
-// keeps at least one K block.
+// Tile and split choice. Swapped operands with the narrowest N-tile covering M for M <= 64 (weight
+// streaming; K split over a cluster up to 8 ways until ~192 CTAs). For larger M the binding resource on
+// B200 is operand traffic from L2 to the SMs (~60 GB/s per SM, ~9-10 TB/s in all, measured): a tile of
+// TM x TN re-reads the weight ceil(M/TM) times and the activations ceil(N/TN) times. Each candidate
+// (TM = 128 or 256 rows of activations, TN = 128 or 256 weight rows; 512 TMEM columns at most) is costed
+// as that traffic plus the split-K partial tiles, over the SMs its grid occupies, and the cheapest wins.
 TcCfg choose_tc(int fmt, int M, int K, int N) {
   TcCfg c;
   const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
-  c.swap = M <= 64;
-  c.tn = c.swap ? (M <= 16 ? 16 : M <= 32 ? 32 : 64) : 128;
-  if (!nib && !c.swap && ((M + BM - 1) / BM) * ((N + 127) / 128) >= 192) c.tn = 256;
-  // ORKB_TC_TN / ORKB_TC_SK: tuning overrides of the non-swapped tile width (128 or 256) and of the
-  // split factor (1..8), read on every launch
-  const char *env_tn = getenv("ORKB_TC_TN");
-  if (!nib && !c.swap && env_tn) c.tn = atoi(env_tn) == 256 ? 256 : 128;
-  const int tiles = c.swap ? (N + BM - 1) / BM : ((M + BM - 1) / BM) * ((N + c.tn - 1) / c.tn);
   const int KB = (K * (fmt == FMT_F16 ? 2 : 1) + BK_BYTES - 1) / BK_BYTES;
-  const int max_sk = c.swap ? 8 : 4, target = c.swap ? 192 : 128;
-  c.sk = 1;
-  while (tiles * c.sk * 2 <= target && c.sk * 2 <= max_sk && c.sk * 2 <= KB) c.sk *= 2;
-  const char *env_sk = getenv("ORKB_TC_SK");
-  if (env_sk) {
-    const int v = atoi(env_sk);
+  c.swap = M <= 64;
+  if (c.swap) {
+    c.tn = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+    const int tiles = (N + BM - 1) / BM;
+    c.sk = 1;
+    while (tiles * c.sk * 2 <= 192 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
+  } else {
+    const double wbytes = (double)fmt_row_bytes(fmt, K) * N, abytes = (double)K * (fmt == FMT_F16 ? 2 : 1) * M;
+    struct Cand { int na, tn; size_t ring; };
+    const Cand cands[3] = {{1, 128, nib ? 4 * (size_t)(256 * 128 + 128 * 64) : 6 * (size_t)(256 * 128)},
+                           {2, 128, nib ? 3 * (size_t)(384 * 128 + 128 * 64) : 4 * (size_t)(384 * 128)},
+                           {1, 256, 4 * (size_t)(384 * 128)}};
+    double best = 1e30;
+    for (const Cand &cd : cands) {
+      if (nib && cd.tn == 256) continue;
+      const int tm = BM * cd.na;
+      const int tiles = ((M + tm - 1) / tm) * ((N + cd.tn - 1) / cd.tn);
+      const bool fits = (size_t)tm * (cd.tn + 4) * 4 <= cd.ring;
+      int sk = 1;
+      while (fits && tiles * sk * 2 <= 160 && sk * 2 <= 4 && sk * 2 <= KB) sk *= 2;
+      const int active = tiles * sk < 148 ? tiles * sk : 148;
+      const double traffic = wbytes * ((M + tm - 1) / tm) + abytes * ((N + cd.tn - 1) / cd.tn) +
+                             (sk > 1 ? (double)tiles * tm * cd.tn * 4 * (sk - 1) : 0.0);
+      const double t = traffic / (active * 60e9);
+      if (t < best) {
+        best = t;
+        c.na = cd.na;
+        c.tn = cd.tn;
+        c.sk = sk;
+      }
+    }
+  }
+  // tuning overrides, read on every launch: ORKB_TC_TN (128/256), ORKB_TC_NA (1/2), ORKB_TC_STAGES (3),
+  // ORKB_TC_SK (1..8)
+  if (!c.swap) {
+    if (const char *e = getenv("ORKB_TC_TN")) c.tn = (!nib && atoi(e) == 256) ? 256 : 128;
+    if (const char *e = getenv("ORKB_TC_NA")) c.na = atoi(e) == 2 ? 2 : 1;
+    if (c.na == 2) c.tn = 128;
+    if (const char *e = getenv("ORKB_TC_STAGES")) c.stages = atoi(e);
+  }
+  if (const char *e = getenv("ORKB_TC_SK")) {
+    const int v = atoi(e);
     if (v >= 1 && v <= 8 && v <= KB) c.sk = v;
   }
   return c;
@@ -509,15 +558,17 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
 template <int FMT>
 cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl) {
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
-  // swapped (decode-sized M) tiles keep the ring at 72-84 KB so two or three CTAs fit on an SM: the
+  // swapped (decode-sized M) tiles keep the ring at 72-98 KB so two or three CTAs fit on an SM: the
   // next launch's CTAs then start streaming their weights while this one drains (programmatic launch)
   if (c.swap) {
     if (c.tn == 16) return launch_tc<FMT, true, 16, NIB ? 3 : 4>(a, c.sk, s, pdl);
     if (c.tn == 32) return launch_tc<FMT, true, 32, NIB ? 3 : 4>(a, c.sk, s, pdl);
     return launch_tc<FMT, true, 64, 3>(a, c.sk, s, pdl);
   }
+  if (c.na == 2) return launch_tc<FMT, false, 128, NIB ? 3 : 4, 2>(a, c.sk, s, pdl);
   if constexpr (!NIB) {
     if (c.tn == 256) return launch_tc<FMT, false, 256, 4>(a, c.sk, s, pdl);
+    if (c.stages == 3) return launch_tc<FMT, false, 128, 3>(a, c.sk, s, pdl);
   }
   return launch_tc<FMT, false, 128, NIB ? 4 : 6>(a, c.sk, s, pdl);
 }

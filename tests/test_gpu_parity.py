@@ -330,3 +330,34 @@ def test_tensor_core_and_gemv_routes_agree_int4(ctx, env_clean, nf4, K, N):
     finally:
         L.ork_b200_force_route(ctx.ctx, -1)
         w.free()
+
+
+@pytest.mark.parametrize("na,tn,sk", [(1, 128, 1), (1, 128, 4), (2, 128, 1), (2, 128, 2), (2, 128, 4),
+                                      (1, 256, 1), (1, 256, 2)])
+def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
+    """Every non-swapped tile shape and split the router may pick (forced through its tuning variables),
+    over M / N / K tails, int8 and NF4 weights."""
+    env_clean.setenv("ORKB_TC_NA", str(na))
+    env_clean.setenv("ORKB_TC_TN", str(tn))
+    env_clean.setenv("ORKB_TC_SK", str(sk))
+    L = ork_b200.lib()
+    rng = np.random.default_rng(na * 100 + tn + sk)
+    K, N = 1056, 640
+    B = rand_i8(rng, (K, N))
+    w8 = ctx.i8_pack(B)
+    f32 = rng.standard_normal((N, K), dtype=np.float32)
+    env_clean.setenv("ORK_NF4", "1")
+    w4, _ = ctx.i4a8_pack(f32)
+    codes, _, _ = of.i4a8_blob_codes(w4.dump(), K, N)
+    try:
+        assert L.ork_b200_force_route(ctx.ctx, 1) == 0
+        for M in (65, 200, 256, 300, 512):
+            A = rand_i8(rng, (M, K))
+            rc, Cm = ctx.run(w8, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B)), ("i8", M)
+            rc, Cm = ctx.run(w4, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), ("nf4", M)
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w8.free()
+        w4.free()
