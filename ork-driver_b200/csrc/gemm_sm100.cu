@@ -122,15 +122,91 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// 32 lanes x 16 consecutive 32-bit TMEM columns into registers (one row per thread).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 32 lanes x 16 columns without waiting: several loads are put in flight and completed by one
+// tmem_wait_ld(), so the TMEM read latency is paid once per batch instead of once per 16 columns. The
+// destination registers must not be touched before the wait.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Epilogue store of a 32-row x 32-column block held one row per lane: the warp transposes it through
+// its own shared-memory tile (row stride 36 words: both the row-per-lane writes and the row-wise reads
+// are free of bank conflicts) so that every global store instruction writes four whole 128-byte rows
+// of C instead of 32 scattered 16-byte pieces.
+constexpr int kStgStride = 36;
+__device__ __forceinline__ void store_rows32(uint32_t *stg, const uint32_t (&lo)[16], const uint32_t (&hi)[16],
+                                             uint32_t *C, int M, int N, int m0, int n0, int lane) {
+#pragma unroll
+  for (int k = 0; k < 16; k += 4) {
+    *reinterpret_cast<uint4 *>(stg + lane * kStgStride + k) = make_uint4(lo[k], lo[k + 1], lo[k + 2], lo[k + 3]);
+    *reinterpret_cast<uint4 *>(stg + lane * kStgStride + 16 + k) = make_uint4(hi[k], hi[k + 1], hi[k + 2], hi[k + 3]);
+  }
+  __syncwarp();
+  const int ch = lane & 7, n = n0 + 4 * ch;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int r = 4 * j + (lane >> 3), m = m0 + r;
+    const uint4 x = *reinterpret_cast<const uint4 *>(stg + r * kStgStride + 4 * ch);
+    if (m < M && n < N) *reinterpret_cast<uint4 *>(C + (size_t)m * N + n) = x;
+  }
+  __syncwarp();
+}
+
+// Drains one warp's 32 TMEM lanes (TN accumulator columns from taddr) into C, or into the split-K
+// partial tile P. Loads are batched (up to 128 columns in flight, one wait). Non-swapped tiles hold a
+// row of C per lane and are stored through the warp's staging tile; swapped tiles hold a column of C
+// per lane (lanes along n), which stores coalesced as is. gr0 = global R row of lane 0, c0 = global
+// origin of the S columns, prow = this lane's row in the partial tile.
+template <bool SWAP, int TN, int PSTR>
+__device__ __forceinline__ void drain_rows(uint32_t taddr, int lane, bool split, uint32_t *P, int prow,
+                                           uint32_t *stg, uint32_t *C, int M, int N, int gr0, int c0) {
+  constexpr int CB = TN % 128 == 0 ? 128 : TN % 64 == 0 ? 64 : TN % 32 == 0 ? 32 : 16;  // divides TN
+  constexpr int NJ = CB / 16;
+#pragma unroll 1
+  for (int cb = 0; cb < TN; cb += CB) {
+    uint32_t v[NJ][16];
+#pragma unroll
+    for (int j = 0; j < NJ; j++) tmem_ld16_nowait(taddr + (uint32_t)(cb + 16 * j), v[j]);
+    tmem_wait_ld();
+    if (split) {
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const int cc = cb + 16 * j;
+        if constexpr (SWAP) {
+#pragma unroll
+          for (int q = 0; q < 16; q++) P[(cc + q) * PSTR + prow] = v[j][q];
+        } else {
+#pragma unroll
+          for (int q = 0; q < 16; q += 4)
+            *reinterpret_cast<uint4 *>(P + prow * PSTR + cc + q) =
+                make_uint4(v[j][q], v[j][q + 1], v[j][q + 2], v[j][q + 3]);
+        }
+      }
+    } else if constexpr (SWAP) {  // D[n][m] -> C[m][n]
+      const int n = gr0 + lane;
+      if (n < N) {
+#pragma unroll
+        for (int j = 0; j < NJ; j++)
+#pragma unroll
+          for (int q = 0; q < 16; q++) {
+            const int m = c0 + cb + 16 * j + q;
+            if (m < M) C[(size_t)m * N + n] = v[j][q];
+          }
+      }
+    } else {
+      static_assert(NJ % 2 == 0, "row stores go in 32-column blocks");
+#pragma unroll
+      for (int j = 0; j < NJ; j += 2) store_rows32(stg, v[j], v[j + 1], C, M, N, gr0, c0 + cb + 16 * j, lane);
+    }
+  }
 }
 
 __device__ __forceinline__ void cluster_sync() {
@@ -338,42 +414,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     const bool ok = mbar_wait(done, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
+      uint32_t *stg = (uint32_t *)smem + sub * 32 * kStgStride;  // the ring is idle once done fired
 #pragma unroll 1
-      for (int a = 0; a < NA; a++) {
-        const int row = a * BM + sub * 32 + lane;  // tile row of R
-#pragma unroll 1
-        for (int cc = 0; cc < TN; cc += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(a * TN + cc), r);
-          if (SK > 1) {  // stage the partial tile for the cluster reduction
-            if (SWAP) {
-#pragma unroll
-              for (int q = 0; q < 16; q++) P[(cc + q) * PSTR + row] = r[q];
-            } else {
-#pragma unroll
-              for (int q = 0; q < 16; q += 4)
-                *reinterpret_cast<uint4 *>(P + row * PSTR + cc + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
-            }
-          } else if (SWAP) {  // D[n][m] -> C[m][n]: lanes are consecutive n, so each store is coalesced
-            const int n = r0 + row;
-            if (n < N) {
-              uint32_t *Cp = (uint32_t *)Cout;
-#pragma unroll
-              for (int q = 0; q < 16; q++)
-                if (c0 + cc + q < M) Cp[(size_t)(c0 + cc + q) * N + n] = r[q];
-            }
-          } else {
-            const int m = r0 + row;
-            if (m < M) {
-              uint32_t *dst = (uint32_t *)Cout + (size_t)m * N + c0 + cc;
-#pragma unroll
-              for (int q = 0; q < 16; q += 4)
-                if (c0 + cc + q < N)
-                  *reinterpret_cast<uint4 *>(dst + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
-            }
-          }
-        }
-      }
+      for (int a = 0; a < NA; a++)
+        drain_rows<SWAP, TN, PSTR>(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(a * TN), lane, SK > 1, P,
+                                   a * BM + sub * 32 + lane, stg, (uint32_t *)Cout, M, N, r0 + a * BM + sub * 32,
+                                   c0);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -387,6 +433,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     const int items = out_rows * vpr;
     const uint32_t pbase = smem_u32(P);
     uint32_t *Cp = (uint32_t *)Cout;
+    // every remote read of an item is issued before the first add, so the SK distributed-shared-memory
+    // latencies overlap instead of adding up
     // every remote read of an item is issued before the first add, so the SK distributed-shared-memory
     // latencies overlap instead of adding up
     for (int t = ks * 192 + (int)threadIdx.x; t < items; t += SK * 192) {
@@ -408,6 +456,280 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
   }
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
+}
+
+// ---------------------------------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2). Two CTAs of a cluster (ranks 2j, 2j+1: the "pair") compute
+// one 256 x TN tile of D = R . S^T with M = 256 MMAs issued by the even CTA (the leader). Each CTA holds
+// its own 128 rows of R and its own TN/2 rows of S in shared memory and its own 128 rows of D (all TN
+// columns) in TMEM; the MMA reads the operand halves of both CTAs. Per output a CTA therefore loads
+// (128 + TN/2) rows instead of (128 + TN) -- the L2-to-SM operand stream, which bounds this kernel on
+// B200 (~45-60 GB/s per SM), shrinks by a third at TN = 256 compared with the one-CTA 128 x 256 tile.
+// Every load is issued by the CTA that owns the destination; there is no multicast.
+//   loads   int8/f16: both operands of both CTAs complete on the leader's full[s] barrier (the
+//           cta_group::2 form of the tiled TMA load, which may signal the peer CTA's barrier); the
+//           leader expects both CTAs' bytes. Nibble weights land in the owner's staging buffer and
+//           complete on its own wfull[s]; its converter warps then arrive on the leader's conv[s].
+//   mma     the leader waits full[s] (and conv[s]), issues the MMAs, and commits to the empty[s]
+//           barriers of both CTAs, and finally to both done barriers.
+//   epilog  each CTA drains its own TMEM rows; split-K partial tiles reduce across the SK CTAs that
+//           hold the same pair half (cluster ranks half + 2q) through distributed shared memory.
+// A cluster-wide barrier after initialisation guarantees that no peer signals a barrier or the MMA
+// writes a TMEM allocation that does not exist yet; another one before the end keeps both CTAs (their
+// shared memory and TMEM) alive until the pair is done.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  return remote;
+}
+
+// tiled load into this CTA's shared memory whose completion is counted on a barrier of either CTA of
+// the pair (bar: shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+template <bool F16>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id,
+                                          uint32_t accum) {
+  if constexpr (F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(id), "r"(accum));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(id), "r"(accum));
+  }
+}
+
+// completion of this thread's pair MMAs, signalled on one barrier (shared::cluster address, either CTA)
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// bounded wait with cluster-scope acquire (for arrivals made by the peer CTA's threads)
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_tc_error, 1u);
+      return false;
+    }
+  }
+}
+
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc_pair(int tn) {
+  return (idesc<F16>(tn) & ~(0x1Fu << 24)) | ((uint32_t)(256 >> 4) << 24);  // M = 256
+}
+
+template <int FMT, bool SWAP, int TN, int STAGES>
+__global__ void __launch_bounds__(192)
+gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
+                    void *__restrict__ Cout, int M, int N, int K, Nf4Tables tb) {
+  constexpr bool F16 = FMT == FMT_F16;
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  constexpr int HS = TN / 2;                             // S rows held by each CTA
+  constexpr int WROWS = SWAP ? BM : HS;                  // weight rows held by each CTA
+  constexpr uint32_t R_BYTES = BM * BK_BYTES;
+  constexpr uint32_t S_BYTES = HS * BK_BYTES;
+  constexpr uint32_t NIB_BYTES = NIB ? WROWS * 64 : 0;
+  constexpr uint32_t A_BYTES = SWAP ? S_BYTES : R_BYTES;  // activation tile per CTA and stage
+  // bytes counted on the leader's full[s] per stage (both CTAs): A and W, or A alone for nibbles
+  constexpr uint32_t FULL_TX = 2 * (NIB ? A_BYTES : (R_BYTES + S_BYTES));
+  constexpr int ESZ = F16 ? 2 : 1;
+  constexpr int KSTEPS = BK_BYTES / 32;
+  constexpr int TCOLS = tmem_cols(TN);
+  constexpr int PSTR = SWAP ? (BM + 4) : (TN + 4);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *sR = smem;
+  uint8_t *sS = smem + STAGES * R_BYTES;
+  uint8_t *sN = sS + STAGES * S_BYTES;
+  uint64_t *bars = (uint64_t *)(sN + STAGES * NIB_BYTES);  // full[S], empty[S], conv[S], wfull[S], done
+  uint32_t *tmem_slot = (uint32_t *)(bars + 4 * STAGES + 1);
+  uint32_t *P = (uint32_t *)smem;
+  uint8_t *sW = SWAP ? sR : sS;
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const uint32_t half = crank & 1u, leader_rank = crank & ~1u, peer_rank = crank ^ 1u;
+  const bool leader = half == 0;
+  const int r0 = (blockIdx.x >> 1) * (2 * BM), c0 = blockIdx.y * TN;  // pair tile origin
+  const int rr = r0 + (int)half * BM, sr = c0 + (int)half * HS;        // this CTA's R rows / S rows
+  const int SK = gridDim.z, ks = blockIdx.z;
+  const int KB = (K * ESZ + BK_BYTES - 1) / BK_BYTES;
+  const int kb0 = (int)((long long)KB * ks / SK), kb1 = (int)((long long)KB * (ks + 1) / SK);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), conv0 = smem_u32(bars + 2 * STAGES),
+                 wfull0 = smem_u32(bars + 3 * STAGES), done = smem_u32(bars + 4 * STAGES);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+      mbar_init(conv0 + 8 * s, 8);  // four converter warps in each CTA of the pair
+      mbar_init(wfull0 + 8 * s, 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapR) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapS) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync();  // both CTAs' barriers and TMEM exist before any peer signal or MMA
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  auto load_w = [&](int s, int kb) {
+    if constexpr (NIB) {
+      tma_load_2d(smem_u32(sN + s * NIB_BYTES), SWAP ? &mapR : &mapS, kb * 64, SWAP ? rr : sr, wfull0 + 8 * s);
+    } else {
+      const int x = kb * (BK_BYTES / ESZ);
+      if (SWAP) tma_load_2d_pair(smem_u32(sR + s * R_BYTES), &mapR, x, rr, mapa_u32(full0 + 8 * s, leader_rank));
+      else tma_load_2d_pair(smem_u32(sS + s * S_BYTES), &mapS, x, sr, mapa_u32(full0 + 8 * s, leader_rank));
+    }
+  };
+  auto load_a = [&](int s, int kb) {
+    const int x = kb * (BK_BYTES / ESZ);
+    if (SWAP) tma_load_2d_pair(smem_u32(sS + s * S_BYTES), &mapS, x, sr, mapa_u32(full0 + 8 * s, leader_rank));
+    else tma_load_2d_pair(smem_u32(sR + s * R_BYTES), &mapR, x, rr, mapa_u32(full0 + 8 * s, leader_rank));
+  };
+  auto expect = [&](int s) {
+    if (leader) mbar_expect_tx(full0 + 8 * s, FULL_TX);
+    if (NIB) mbar_expect_tx(wfull0 + 8 * s, NIB_BYTES);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+      for (int i = 0; i < pre; i++) {
+        expect(i);
+        load_w(i, kb0 + i);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int i = 0; i < pre; i++) load_a(i, kb0 + i);
+      for (int kb = kb0 + pre; kb < kb1; kb++) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) break;
+        expect(s);
+        load_w(s, kb);
+        load_a(s, kb);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t id = idesc_pair<F16>(TN);
+      for (int kb = kb0; kb < kb1; kb++) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        if (!mbar_wait(full0 + 8 * s, ph)) break;
+        if (NIB && !mbar_wait_cluster(conv0 + 8 * s, ph)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t rd = sw128_desc(smem_u32(sR + s * R_BYTES));
+        const uint64_t sd = sw128_desc(smem_u32(sS + s * S_BYTES));
+#pragma unroll
+        for (int k = 0; k < KSTEPS; k++)
+          umma_pair<F16>(tmem, rd + 2 * k, sd + 2 * k, id, (kb > kb0 || k > 0) ? 1u : 0u);
+        umma_commit_pair(empty0 + 8 * s);
+        umma_commit_pair(mapa_u32(empty0 + 8 * s, peer_rank));
+      }
+      umma_commit_pair(done);
+      umma_commit_pair(mapa_u32(done, peer_rank));
+    }
+  } else {
+    const int ct = threadIdx.x - 64;
+    if constexpr (NIB) {
+      bool cok = true;
+      for (int kb = kb0; kb < kb1 && cok; kb++) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        cok = mbar_wait(wfull0 + 8 * s, ph);
+        if (!cok) break;
+        const uint8_t *src = sN + s * NIB_BYTES;
+        uint8_t *dst = sW + s * (SWAP ? R_BYTES : S_BYTES);
+#pragma unroll 2
+        for (int t = ct; t < WROWS * 8; t += 128) {
+          const int r = t >> 3, c = t & 7;
+          const uint2 nb = *reinterpret_cast<const uint2 *>(src + r * 64 + c * 8);
+          const uint2 lo = expand8<FMT>(nb.x, tb), hi = expand8<FMT>(nb.y, tb);
+          *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_u32(conv0 + 8 * s, leader_rank));
+      }
+    }
+    const int sub = warp & 3;
+    const bool ok = mbar_wait(done, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok)
+      drain_rows<SWAP, TN, PSTR>(tmem + ((uint32_t)(sub * 32) << 16), lane, SK > 1, P, sub * 32 + lane,
+                                 (uint32_t *)smem + sub * 32 * kStgStride, (uint32_t *)Cout, M, N, rr + sub * 32, c0);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  if (SK > 1) {
+    cluster_sync();
+    // this CTA's slice of its half-tile: (output row, 4-column vector) items in C's row-major order,
+    // summed over the partials of cluster ranks half + 2q
+    const int out_rows = SWAP ? min(TN, M - c0) : min(BM, M - rr);
+    const int out_cols = SWAP ? min(BM, N - rr) : min(TN, N - c0);
+    const int vpr = out_cols / 4;
+    const int items = out_rows > 0 && out_cols > 0 ? out_rows * vpr : 0;
+    const uint32_t pbase = smem_u32(P);
+    uint32_t *Cp = (uint32_t *)Cout;
+    for (int t = ks * 192 + (int)threadIdx.x; t < items; t += SK * 192) {
+      const int orow = t / vpr, ov = t % vpr;
+      const uint32_t off = (uint32_t)(orow * PSTR + 4 * ov) * 4u;
+      uint4 v[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        if (q < SK) v[q] = ld_dsmem_v4(pbase + off, half + 2u * (uint32_t)q);
+      uint4 acc = v[0];
+#pragma unroll
+      for (int q = 1; q < 4; q++)
+        if (q < SK) acc = add4<F16>(acc, v[q]);
+      const int m = SWAP ? c0 + orow : rr + orow;
+      const int n = (SWAP ? rr : c0) + 4 * ov;
+      *reinterpret_cast<uint4 *>(Cp + (size_t)m * N + n) = acc;
+    }
+  }
+  cluster_sync();  // the pair (and every split-K partial) is finished before TMEM and shared memory go
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -491,19 +813,70 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K, tb);
 }
 
+// CTA-pair launch: grid x = 2 CTAs per 256 R rows, y = S tiles of TN, z = split-K; cluster (2, 1, sk).
+template <int FMT, bool SWAP, int TN, int STAGES>
+cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  constexpr int ESZ = FMT == FMT_F16 ? 2 : 1;
+  constexpr int HS = TN / 2;
+  constexpr int WROWS = SWAP ? BM : HS;
+  static_assert(TN % 32 == 0 && TN >= 64 && TN <= 256, "pair MMA N");
+  if (sk < 1 || sk > 4) return cudaErrorInvalidValue;
+  CUtensorMap mR, mS;
+  const size_t a_row = (size_t)a.K * ESZ, w_row = fmt_row_bytes(FMT, a.K);
+  const bool okW = NIB ? make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, 1, WROWS, 64, false)
+                       : make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, ESZ, WROWS, BK_BYTES, true);
+  const bool okA = make_map(SWAP ? &mS : &mR, a.A, a.M, a_row, ESZ, SWAP ? HS : BM, BK_BYTES, true);
+  if (!okW || !okA) return cudaErrorInvalidValue;
+  constexpr size_t ring = (size_t)STAGES * ((BM + HS) * BK_BYTES + (NIB ? WROWS * 64 : 0));
+  constexpr size_t part = (size_t)(SWAP ? TN * (BM + 4) : BM * (TN + 4)) * 4;
+  static_assert(part <= ring, "partial tile must fit in the stage ring");
+  constexpr size_t smem = 1024 + ring + (4 * STAGES + 1) * 8 + 16;
+  static_assert(smem <= 232448, "shared memory budget");
+  auto kern = gemm_tc_pair_kernel<FMT, SWAP, TN, STAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int8_t *L = kNf4Lut;
+  const Nf4Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
+                     pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * ((rowsR + 2 * BM - 1) / (2 * BM)), (rowsS + TN - 1) / TN, sk);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = sk;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K, tb);
+}
+
 struct TcCfg {
   bool swap;
   int tn, sk;
-  int na = 1;      // 128-row accumulators per CTA along the R side
-  int stages = 0;  // 0: the variant's default; 3: the 96 KB ring of the 128 x 128 tile
+  int na = 1;         // 128-row accumulators per CTA along the R side
+  int stages = 0;     // 0: the variant's default; 3: the 96 KB ring of the 128 x 128 tile
+  bool pair = false;  // CTA-pair (cta_group::2) tile of 256 x tn
 };
 
 // Tile and split choice. Swapped operands with the narrowest N-tile covering M for M <= 64 (weight
-// streaming; K split over a cluster up to 8 ways until ~192 CTAs). For larger M the binding resource on
-// B200 is operand traffic from L2 to the SMs (~60 GB/s per SM, ~9-10 TB/s in all, measured): a tile of
-// TM x TN re-reads the weight ceil(M/TM) times and the activations ceil(N/TN) times. Each candidate
-// (TM = 128 or 256 rows of activations, TN = 128 or 256 weight rows; 512 TMEM columns at most) is costed
-// as that traffic plus the split-K partial tiles, over the SMs its grid occupies, and the cheapest wins.
+// streaming; K split over a cluster up to 8 ways until ~192 CTAs). For larger M, measured on B200 over
+// configs of K in {2048, 6144}, N in {2048, 6144, 12288}, M in {128, 256, 512}: a CTA's time is set by
+// its own operand bytes in flight and its C tile, so the grid should cover the SMs once with the
+// narrowest tile that fits: 128-wide weight tiles, widened to 192 then 256 (int8 / f16) only while the
+// grid would exceed one wave of 148 CTAs; nibble weights past one wave use CTA-pair tiles of 256 x 192
+// (the converter work per CTA halves). Split-K (a cluster reduction through distributed shared memory)
+// pays for grids of up to 32 tiles, and for up to 64 tiles when K spans at least 32 blocks.
 TcCfg choose_tc(int fmt, int M, int K, int N) {
   TcCfg c;
   const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
@@ -515,42 +888,52 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
     c.sk = 1;
     while (tiles * c.sk * 2 <= 192 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
   } else {
-    const double wbytes = (double)fmt_row_bytes(fmt, K) * N, abytes = (double)K * (fmt == FMT_F16 ? 2 : 1) * M;
-    struct Cand { int na, tn; size_t ring; };
-    const Cand cands[3] = {{1, 128, nib ? 4 * (size_t)(256 * 128 + 128 * 64) : 6 * (size_t)(256 * 128)},
-                           {2, 128, nib ? 3 * (size_t)(384 * 128 + 128 * 64) : 4 * (size_t)(384 * 128)},
-                           {1, 256, 4 * (size_t)(384 * 128)}};
-    double best = 1e30;
-    for (const Cand &cd : cands) {
-      if (nib && cd.tn == 256) continue;
-      const int tm = BM * cd.na;
-      const int tiles = ((M + tm - 1) / tm) * ((N + cd.tn - 1) / cd.tn);
-      const bool fits = (size_t)tm * (cd.tn + 4) * 4 <= cd.ring;
-      int sk = 1;
-      while (fits && tiles * sk * 2 <= 160 && sk * 2 <= 4 && sk * 2 <= KB) sk *= 2;
-      const int active = tiles * sk < 148 ? tiles * sk : 148;
-      const double traffic = wbytes * ((M + tm - 1) / tm) + abytes * ((N + cd.tn - 1) / cd.tn) +
-                             (sk > 1 ? (double)tiles * tm * cd.tn * 4 * (sk - 1) : 0.0);
-      const double t = traffic / (active * 60e9);
-      if (t < best) {
-        best = t;
-        c.na = cd.na;
-        c.tn = cd.tn;
-        c.sk = sk;
+    const int mt = (M + BM - 1) / BM;
+    auto tiles = [&](int tn) { return mt * ((N + tn - 1) / tn); };
+    c.tn = 128;
+    if (tiles(128) > 148) {
+      if (nib) {
+        c.pair = true;
+        c.tn = ((M + 255) / 256) * ((N + 191) / 192) * 2 <= 148 ? 192 : 256;
+      } else {
+        c.tn = tiles(192) <= 148 ? 192 : 256;
       }
     }
+    const int t = c.pair ? 2 * ((M + 255) / 256) * ((N + c.tn - 1) / c.tn) : tiles(c.tn);
+    c.sk = 1;
+    if (t <= 32 && KB >= 8) c.sk = 4;
+    else if (t <= 64 && KB >= 32) c.sk = 2;
   }
-  // tuning overrides, read on every launch: ORKB_TC_TN (128/256), ORKB_TC_NA (1/2), ORKB_TC_STAGES (3),
+  // tuning overrides, read on every launch: ORKB_TC_TN (128/192/256), ORKB_TC_NA (1/2), ORKB_TC_STAGES (3),
   // ORKB_TC_SK (1..8)
   if (!c.swap) {
-    if (const char *e = getenv("ORKB_TC_TN")) c.tn = (!nib && atoi(e) == 256) ? 256 : 128;
+    if (const char *e = getenv("ORKB_TC_TN")) {
+      const int v = atoi(e);
+      c.tn = (!nib && (v == 256 || v == 192)) ? v : 128;
+    }
     if (const char *e = getenv("ORKB_TC_NA")) c.na = atoi(e) == 2 ? 2 : 1;
     if (c.na == 2) c.tn = 128;
     if (const char *e = getenv("ORKB_TC_STAGES")) c.stages = atoi(e);
   }
+  // ORKB_TC_PAIR: 1 = CTA-pair tiles (swapped operands for M <= 256), 2 = pair with A on the 256-row
+  // side, 3 = pair with the weight on the 256-row side (M <= 256)
+  if (const char *e = getenv("ORKB_TC_PAIR")) {
+    const int v = atoi(e);
+    if (v >= 1 && v <= 3 && !(v == 3 && M > 256)) {
+      c.pair = true;
+      c.na = 1;
+      c.swap = v == 3 || (v == 1 && M <= 256);
+      if (c.swap) c.tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+      else {
+        const int v = getenv("ORKB_TC_TN") ? atoi(getenv("ORKB_TC_TN")) : 256;
+        c.tn = (v == 64 || v == 128 || v == 192) ? v : 256;
+      }
+      if (c.sk > 4) c.sk = 4;
+    }
+  }
   if (const char *e = getenv("ORKB_TC_SK")) {
     const int v = atoi(e);
-    if (v >= 1 && v <= 8 && v <= KB) c.sk = v;
+    if (v >= 1 && v <= (c.pair ? 4 : 8) && v <= KB) c.sk = v;
   }
   return c;
 }
@@ -560,6 +943,17 @@ cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl)
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
   // swapped (decode-sized M) tiles keep the ring at 72-98 KB so two or three CTAs fit on an SM: the
   // next launch's CTAs then start streaming their weights while this one drains (programmatic launch)
+  if (c.pair) {
+    if (c.swap) {
+      if (c.tn == 64) return launch_tc_pair<FMT, true, 64, 6>(a, c.sk, s, pdl);
+      if (c.tn == 128) return launch_tc_pair<FMT, true, 128, NIB ? 5 : 6>(a, c.sk, s, pdl);
+      return launch_tc_pair<FMT, true, 256, NIB ? 4 : 6>(a, c.sk, s, pdl);
+    }
+    if (c.tn == 64) return launch_tc_pair<FMT, false, 64, 8>(a, c.sk, s, pdl);
+    if (c.tn == 128) return launch_tc_pair<FMT, false, 128, 6>(a, c.sk, s, pdl);
+    if (c.tn == 192) return launch_tc_pair<FMT, false, 192, NIB ? 4 : 6>(a, c.sk, s, pdl);
+    return launch_tc_pair<FMT, false, 256, NIB ? 4 : 6>(a, c.sk, s, pdl);
+  }
   if (c.swap) {
     if (c.tn == 16) return launch_tc<FMT, true, 16, NIB ? 3 : 4>(a, c.sk, s, pdl);
     if (c.tn == 32) return launch_tc<FMT, true, 32, NIB ? 3 : 4>(a, c.sk, s, pdl);
@@ -568,6 +962,7 @@ cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl)
   if (c.na == 2) return launch_tc<FMT, false, 128, NIB ? 3 : 4, 2>(a, c.sk, s, pdl);
   if constexpr (!NIB) {
     if (c.tn == 256) return launch_tc<FMT, false, 256, 4>(a, c.sk, s, pdl);
+    if (c.tn == 192) return launch_tc<FMT, false, 192, 4>(a, c.sk, s, pdl);
     if (c.stages == 3) return launch_tc<FMT, false, 128, 3>(a, c.sk, s, pdl);
   }
   return launch_tc<FMT, false, 128, NIB ? 4 : 6>(a, c.sk, s, pdl);

@@ -333,7 +333,7 @@ def test_tensor_core_and_gemv_routes_agree_int4(ctx, env_clean, nf4, K, N):
 
 
 @pytest.mark.parametrize("na,tn,sk", [(1, 128, 1), (1, 128, 4), (2, 128, 1), (2, 128, 2), (2, 128, 4),
-                                      (1, 256, 1), (1, 256, 2)])
+                                      (1, 256, 1), (1, 256, 2), (1, 192, 1), (1, 192, 4)])
 def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
     """Every non-swapped tile shape and split the router may pick (forced through its tuning variables),
     over M / N / K tails, int8 and NF4 weights."""
@@ -361,3 +361,48 @@ def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
         L.ork_b200_force_route(ctx.ctx, -1)
         w8.free()
         w4.free()
+
+
+@pytest.mark.parametrize("pair,tn,sk", [(2, 256, 1), (2, 256, 2), (2, 128, 1), (2, 128, 4), (2, 64, 1),
+                                        (2, 64, 2), (2, 192, 1), (2, 192, 4), (3, 0, 1), (3, 0, 2), (3, 0, 4)])
+def test_tensor_core_pair_tiles_exact(ctx, env_clean, pair, tn, sk):
+    """CTA-pair (cta_group::2) tiles forced through the tuning variables: pair = 2 puts the activations
+    on the 256-row side (M tails leave the second CTA of the last pair entirely out of range at
+    M = 300), pair = 3 the weight (N tails, narrow M). int8, NF4 and uniform int4 exact; f16 within
+    its tolerance."""
+    env_clean.setenv("ORKB_TC_PAIR", str(pair))
+    if tn:
+        env_clean.setenv("ORKB_TC_TN", str(tn))
+    env_clean.setenv("ORKB_TC_SK", str(sk))
+    L = ork_b200.lib()
+    rng = np.random.default_rng(pair * 1000 + tn + sk)
+    K, N = 1056, 640
+    B = rand_i8(rng, (K, N))
+    w8 = ctx.i8_pack(B)
+    f32 = rng.standard_normal((N, K), dtype=np.float32)
+    env_clean.setenv("ORK_NF4", "1")
+    wn, _ = ctx.i4a8_pack(f32)
+    env_clean.delenv("ORK_NF4")
+    wu, _ = ctx.i4a8_pack(f32)
+    cn, _, _ = of.i4a8_blob_codes(wn.dump(), K, N)
+    cu, _, _ = of.i4a8_blob_codes(wu.dump(), K, N)
+    Bh = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+    wh = ctx.f16_pack(Bh)
+    Ms = (65, 200, 256, 300, 512, 700) if pair == 2 else (40, 100, 128, 200, 256)
+    try:
+        assert L.ork_b200_force_route(ctx.ctx, 1) == 0
+        for M in Ms:
+            A = rand_i8(rng, (M, K))
+            rc, Cm = ctx.run(w8, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B)), ("i8", M)
+            rc, Cm = ctx.run(wn, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, cn)), ("nf4", M)
+            rc, Cm = ctx.run(wu, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, cu)), ("u4", M)
+            Ah = rng.uniform(-1, 1, size=(M, K)).astype(np.float16)
+            rc, Cm = ctx.run(wh, Ah)
+            assert rc == 0 and np.abs(Cm - of.gemm_f16(Ah, Bh)).max() <= f16_tol(Ah, Bh), ("f16", M)
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        for w in (w8, wn, wu, wh):
+            w.free()
