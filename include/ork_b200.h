@@ -31,6 +31,19 @@ int ork_f16_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *dA, float
  * shared scratch. */
 int ork_i8_mm_run_noalloc(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
 
+/* Grouped runs over device pointers (A, aScale, bScale, C on the context's GPU), enqueued like the
+ * async runs above; same arguments and checks as ork_i4_mm_run_grouped / ork_i8_mm_run_grouped. */
+int ork_i4_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
+                                const float *dbScale, float *dC);
+int ork_i8_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
+                                const float *dbScale, float *dC);
+
+/* The load-time header check of the .orkpack loaders, callable without a device: 0 when `blob` is a
+ * stamped blob of this build for (dtype, K, N), else ORK_PACKERR_SHORT / _UNSTAMPED / _FORMAT / _CAPS /
+ * _SHAPE, checked in that order (ork-driver src/npu/core/packhdr.c). And the caps id this build stamps. */
+int ork_b200_pack_check(const void *blob, size_t n, int dtype, int K, int N);
+uint32_t ork_b200_pack_capid(void);
+
 /* Wait for everything queued on the context's stream; 0 ok, -1 if the GPU reported an error. */
 int ork_b200_sync(ork_npu *ctx);
 /* The cudaStream_t the context queues on, and a way to substitute the caller's own stream (NULL restores

@@ -96,6 +96,76 @@ size_t ork_i4a8_pack_cpu_blob(ork_npu *ctx, int K, int N, const float *f32, cons
 size_t ork_i4a8_pack_cpu_blob_qerr(ork_npu *ctx, int K, int N, const float *f32, const float *imatrix,
                                    int nf4, void *out, size_t cap, float *qerr_out);
 
+/* ---- persisted tiled weights (.orkpack entries; ork-driver include/ork/weights.h:159-269) --------
+ * Every blob from ork_w_dump / ork_*_w_dump_cpu starts with this one-page header and every
+ * ork_*_mm_load* refuses a blob whose stamp disagrees with this build (src/npu/core/packhdr.c). The
+ * header layout, magic, refusal order and codes are the reference's; `capid` identifies THIS build's
+ * caps (B200, K-major resident rows) and `soc` reads "b200", so a blob tiled for an RK35xx NPU is
+ * refused with ORK_PACKERR_CAPS here and a B200 blob is refused the same way by an NPU build. After the
+ * header the payload is the weight's resident layout: int8 [N][K] (int4 stores inflated to their int8
+ * codes), fp16 [N][K], or W4A4 nibbles [N][K/2] with the low nibble holding the even k. */
+#define ORK_PACK_MAGIC 0x4b50414fu /* "OAPK" */
+#define ORK_PACK_HDR_BYTES 4096u
+typedef struct {
+  uint32_t magic;     /* ORK_PACK_MAGIC */
+  uint32_t fmt;       /* ork_pack_format_version() at dump time */
+  uint32_t capid;     /* resolved-caps identity of the dumping build */
+  uint32_t dtype;     /* 0 fp16, 1 int8, 2 int4 (ork-driver include/ork/run.h:42) */
+  int32_t K, N;
+  uint32_t hdr_bytes; /* == ORK_PACK_HDR_BYTES */
+  uint32_t flags;     /* reserved, 0 */
+  char soc[16];       /* device id at dump time, for the diagnostic */
+} ork_pack_hdr;       /* zero-padded to ORK_PACK_HDR_BYTES */
+#define ORK_PACKERR_SHORT (-1)
+#define ORK_PACKERR_UNSTAMPED (-2)
+#define ORK_PACKERR_FORMAT (-3)
+#define ORK_PACKERR_CAPS (-4)
+#define ORK_PACKERR_SHAPE (-5)
+/* include/ork/weights.h:199. == ORK_PACK_HDR_BYTES. */
+size_t ork_pack_hdr_bytes(void);
+/* include/ork/weights.h:203. Header + the weight's resident bytes; out == NULL returns the size, 0 on a
+ * short cap or a NULL weight. An int4-store weight (ork_i4a8_*) dumps as int8 (its inflated codes), as
+ * the reference's resident int8 tiles do, and reloads with ork_i8_mm_load. */
+size_t ork_w_dump(const ork_w *w, void *out, size_t cap);
+/* include/ork/weights.h:210. The exact bytes ork_i8_mm_pack(B) + ork_w_dump would give, computed on the
+ * host with no device (ctx may be NULL). B row-major int8 [K][N]; K%32, N%32. out == NULL -> size. */
+size_t ork_i8_w_dump_cpu(ork_npu *ctx, int K, int N, const int8_t *B, void *out, size_t cap);
+/* include/ork/weights.h:213. The NPU's full-K companion tiling has no counterpart in the K-major B200
+ * layout (every weight is already full-K): always 0, the reference's "no companion" answer. */
+size_t ork_i8_w_dump_bf_cpu(ork_npu *ctx, int K, int N, const int8_t *B, void *out, size_t cap);
+/* include/ork/weights.h:219. The exact bytes ork_i4_mm_pack(B) + ork_w_dump would give (W4A4, dtype 2),
+ * host only (ctx may be NULL). K%32, N%64. out == NULL -> size. */
+size_t ork_i4_w_dump_cpu(ork_npu *ctx, int K, int N, const int8_t *B, void *out, size_t cap);
+/* include/ork/weights.h:226, :229, :265. Reload a stamped blob of that dtype and (K,N); NULL on any header
+ * refusal (the cause is printed once) or a size that is not header + payload exactly. */
+ork_w *ork_f16_mm_load(ork_npu *ctx, int K, int N, const void *blob, size_t n);
+ork_w *ork_i8_mm_load(ork_npu *ctx, int K, int N, const void *blob, size_t n);
+ork_w *ork_i4_mm_load(ork_npu *ctx, int K, int N, const void *blob, size_t n);
+/* include/ork/weights.h:243. Load a W4A4 blob (ork_i4_w_dump_cpu / ork_w_dump of an int4 weight) as an
+ * int8-compute weight: the int4 values are its int8 codes (sign-extended), it runs with ork_i8_mm_run,
+ * and with G > 0 dividing K it is tagged for ork_i8_mm_run_grouped. Carries no scales. */
+ork_w *ork_i4a8_mm_load_tiled(ork_npu *ctx, int K, int N, const void *blob, size_t n, int G);
+
+/* ---- per-group scales (ork-driver include/ork/weights.h:126-132, include/ork/run.h:121-125) ------- */
+
+/* include/ork/weights.h:128. W4A4 weight with K split into groups of G: G%32, K%G, G <= 10752, plus the
+ * ork_i4_mm_pack rules (K%32, N%64). Runs with ork_i4_mm_run_grouped (and ork_i4_mm_run). */
+ork_w *ork_i4_mm_pack_grouped(ork_npu *ctx, int K, int N, const int8_t *B, int G);
+/* include/ork/weights.h:132 (src/npu.c:1191). Tag an int4 or int8 weight with group size G (0 clears);
+ * -1 for fp16 / NULL weights or a G that does not divide K. */
+int ork_w_set_group(ork_w *w, int G);
+/* include/ork/run.h:121 and include/ork/weights.h:253. C fp32 [M][N] = sum over K-groups g (ascending)
+ * of ((float)dot_g(A[m], B[:,n]) * aScale[m*(K/G)+g]) * bScale[g*N+n], the int32 group dot exact and
+ * every fp32 multiply and add rounded separately -- bit-identical to ork-driver's CPU accumulate
+ * (src/npu/core/buf.c:501-520). _i4_: W4A4 weight, A int4 values in int8; _i8_: any int8-compute weight
+ * (int8, int4 store or tiled-loaded) with a group size, A int8. Group sizes: G%16 for int8 weights,
+ * G%32 for int4 weights. 0 ok; -1 on bad arguments, an ungrouped weight, overlapping A/C, or a device
+ * error. */
+int ork_i4_mm_run_grouped(ork_npu *ctx, ork_w *w, int M, const int8_t *A, const float *aScale,
+                          const float *bScale, float *C);
+int ork_i8_mm_run_grouped(ork_npu *ctx, ork_w *w, int M, const int8_t *A, const float *aScale,
+                          const float *bScale, float *C);
+
 /* include/ork/weights.h:141. Frees a weight's host bookkeeping. Unlike the reference (which leaves the
  * NPU window to teardown), device memory is released here as well: HBM has no IOVA window to protect. */
 void ork_w_free(ork_w *w);

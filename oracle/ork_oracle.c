@@ -24,6 +24,43 @@
 #define ORC_API __attribute__((visibility("default")))
 
 /* ---------------------------------------------------------------------------------------------------
+ * Grouped (per-K-group scaled) GEMM. src/npu/core/buf.c:501-520 (orki_cpu_gemm_grouped), shared by
+ * ork_i4_mm_run_grouped and ork_i8_mm_run_grouped offline: Sk = K/G; for each row m the fp32 row starts
+ * at 0 and, for g ascending, gains ((float)acc * aScale[m*Sk+g]) * bScale[g*N+n] where acc is the exact
+ * int32 dot of A[m][gG..gG+G) with B[gG..gG+G)[n] (B row-major [K][N]). Every multiply and add is a
+ * separately rounded fp32 operation (-ffp-contract=off). Returns -1 on bad arguments, as the reference. */
+ORC_API int orc_gemm_grouped(int M, int K, int N, int G, const int8_t *A, const int8_t *B, const float *aScale,
+                             const float *bScale, float *C)
+{
+    if (M < 1 || K < 1 || N < 1 || G < 1 || (K % G) || !A || !B || !aScale || !bScale || !C) return -1;
+    const int Sk = K / G;
+#pragma omp parallel for schedule(static) if (M > 1)
+    for (int m = 0; m < M; m++) {
+        float *crow = C + (size_t)m * N;
+        int32_t *acc = malloc((size_t)N * sizeof *acc);
+        for (int n = 0; n < N; n++) crow[n] = 0.0f;
+        if (!acc) continue;
+        for (int g = 0; g < Sk; g++) {
+            const float as = aScale[(size_t)m * Sk + g];
+            const float *bs = bScale + (size_t)g * N;
+            for (int n = 0; n < N; n++) acc[n] = 0;
+            for (int k = g * G; k < (g + 1) * G; k++) {
+                const int32_t a = A[(size_t)m * K + k];
+                if (!a) continue;
+                const int8_t *brow = B + (size_t)k * N;
+                for (int n = 0; n < N; n++) acc[n] += a * (int32_t)brow[n];
+            }
+            for (int n = 0; n < N; n++) {
+                const float t = (float)acc[n] * as;
+                crow[n] += t * bs[n];
+            }
+        }
+        free(acc);
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------------
  * Integer GEMM. src/npu/core/buf.c:428-477 (orki_cpu_gemm_i32): C[M][N] int32 = A[M][K] int8 x B[K][N]
  * int8 (B row-major), k-outer AXPY into a zeroed C row, exact int32 accumulation. Parallel over M. */
 ORC_API void orc_gemm_i32(int M, int K, int N, const int8_t *A, const int8_t *B, int32_t *C)

@@ -44,25 +44,18 @@ bool device_error() {
   return (t | g) != 0;
 }
 
-}  // namespace orkb
-
-namespace {
-
 void log_err(const char *what, cudaError_t e) {
   fprintf(stderr, "[ork] ERROR %s: %s\n", what, cudaGetErrorString(e));
 }
 
-struct DeviceGuard {  // run a call with the context's device current, restoring the caller's
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
+DeviceGuard::DeviceGuard(int dev) {
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  if (prev != dev) cudaSetDevice(dev);
+}
+DeviceGuard::~DeviceGuard() {
+  int cur = -1;
+  if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+}
 
 bool grow(void **p, size_t *cap, size_t need) {
   if (*cap >= need) return true;
@@ -76,6 +69,11 @@ bool grow(void **p, size_t *cap, size_t need) {
   }
   *cap = sz;
   return true;
+}
+
+bool overlaps(const void *a, size_t an, const void *b, size_t bn) {
+  const uintptr_t a0 = (uintptr_t)a, a1 = a0 + an, b0 = (uintptr_t)b, b1 = b0 + bn;
+  return a0 < b1 && b0 < a1;
 }
 
 // Device memory of the context's GPU (or managed memory) can be used in place.
@@ -116,6 +114,10 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
   return w;
 }
 
+}  // namespace orkb
+
+namespace {
+
 // Launch one matmul on device buffers (A, C already on the context's GPU).
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
   RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt};
@@ -132,11 +134,6 @@ int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
     return -1;
   }
   return 0;
-}
-
-bool overlaps(const void *a, size_t an, const void *b, size_t bn) {
-  const uintptr_t a0 = (uintptr_t)a, a1 = a0 + an, b0 = (uintptr_t)b, b1 = b0 + bn;
-  return a0 < b1 && b0 < a1;
 }
 
 // The synchronous run shared by the three public run functions.
@@ -227,6 +224,7 @@ void ork_npu_free(ork_npu *c) {
     cudaStreamSynchronize(c->stream);
     if (c->dA) cudaFree(c->dA);
     if (c->dC) cudaFree(c->dC);
+    if (c->dS) cudaFree(c->dS);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;

@@ -307,6 +307,127 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
   }
 }
 
+// Grouped variant (per-K-group scales): same staging and arithmetic as gemv_kernel, but each warp walks
+// a contiguous range of 128-byte weight segments and flushes its lane partials into a shared-memory
+// table P[group][channel][row] with integer atomics whenever the lane's chunk moves into the next K
+// group -- exact int32 per group whatever the lane order. After a block barrier one thread per
+// (channel, row) combines the groups in ascending order in fp32 with explicitly rounded multiplies and
+// adds (no contraction), the arithmetic of ork-driver's orki_cpu_gemm_grouped (src/npu/core/buf.c:
+// 501-520): c = 0; for g: c += ((float)P_g * aScale[m][g]) * bScale[g][n].
+template <int FMT, int MT, int TR>
+__global__ void __launch_bounds__(kWarps * 32)
+gemv_grouped_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, const float *__restrict__ aS,
+                    const float *__restrict__ bS, float *__restrict__ C, int M, int K, int N, int G, Tables tb) {
+  static_assert(FMT != FMT_F16, "grouped scales apply to integer weights");
+  constexpr int WR = TR / (4 * kR);
+  constexpr int WK = kWarps / WR;
+  constexpr int V = kR * MT;
+  constexpr int NGRP = TR / 8;
+  constexpr int KPB = (FMT == FMT_I8) ? 1 : 2;  // k values per weight byte
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[NGRP + 1];
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 3, j = lane & 7;
+  const int wr = warp / WK, wk = warp % WK;
+  const int n0 = blockIdx.x * TR;
+  const int rows = min(TR, N - n0);
+  const size_t rowB = (size_t)K / KPB;
+  const size_t a_row = (size_t)K;
+  const int Sk = K / G;
+  const int gbytes = G / KPB;  // weight bytes per group (a multiple of the 16-byte lane chunk)
+  const uint32_t sW = smem_u32(smem);
+  const uint32_t sA = sW + (uint32_t)(TR * rowB);
+  int *P = reinterpret_cast<int *>(smem + TR * rowB + ((M * a_row + 15) & ~(size_t)15));
+
+  if (threadIdx.x == 0) {
+    for (int q = 0; q <= NGRP; q++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[q])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const uint8_t *src = W + (size_t)n0 * rowB;
+    for (int q = 0; q < NGRP; q++) {
+      const int r0 = q * 8, nr = min(8, rows - r0);
+      const uint32_t bar = smem_u32(&bars[q]);
+      const uint32_t bytes = nr > 0 ? (uint32_t)(nr * rowB) : 0u;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+      if (nr > 0)
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         sW + (uint32_t)(r0 * rowB)),
+                     "l"(src + (size_t)r0 * rowB), "r"(bytes), "r"(bar)
+                     : "memory");
+    }
+  }
+  for (int t = threadIdx.x; t < Sk * TR * MT; t += kWarps * 32) P[t] = 0;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) {
+    const uint32_t bar = smem_u32(&bars[NGRP]), bytes = (uint32_t)(M * a_row);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sA),
+                 "l"(A), "r"(bytes), "r"(bar)
+                 : "memory");
+  }
+  __syncthreads();  // barrier init and the zeroed table visible to every thread
+
+  using T = int;
+  T acc[V];
+  T neg[(FMT == FMT_NF4) ? V : 1];
+#pragma unroll
+  for (int i = 0; i < V; i++) acc[i] = 0;
+#pragma unroll
+  for (int i = 0; i < ((FMT == FMT_NF4) ? V : 1); i++) neg[i] = 0;
+
+  const int lrow0 = wr * 8 + gq;
+  const bool ok = mbar_wait0(smem_u32(&bars[wr])) && mbar_wait0(smem_u32(&bars[NGRP]));
+  const int S = (int)((rowB + 127) / 128);
+  const int s0 = (int)((long long)S * wk / WK), s1 = (int)((long long)S * (wk + 1) / WK);
+  if (ok && wr * 8 < rows) {
+    const uint32_t base0 = sW + (uint32_t)(lrow0 * rowB) + (uint32_t)(j * 16);
+    const uint32_t a_k = (uint32_t)KPB;
+    for (int s = s0; s < s1; s++) {
+      const uint32_t o = (uint32_t)s * 128u + (uint32_t)j * 16u;
+      const bool live = o < rowB;
+      if (live) {
+        uint4 wv[kR];
+#pragma unroll
+        for (int r = 0; r < kR; r++) wv[r] = lds128(base0 + (uint32_t)(4 * r * rowB) + (uint32_t)(s * 128));
+        mac_chunk<FMT, MT, T>(wv, sA + a_k * o, (uint32_t)a_row, M, acc, neg, tb);
+      }
+      // flush at the end of the lane's group (or of its range)
+      const int grp = (int)(o / (uint32_t)gbytes);
+      const uint32_t on = o + 128u;
+      const bool last = (s + 1 >= s1) || on >= rowB || (int)(on / (uint32_t)gbytes) != grp;
+      if (live && last) {
+#pragma unroll
+        for (int r = 0; r < kR; r++) {
+          const int lr = lrow0 + 4 * r;
+#pragma unroll
+          for (int m = 0; m < MT; m++) {
+            T v = acc[r * MT + m];
+            if constexpr (FMT == FMT_U4) v >>= 4;
+            if constexpr (FMT == FMT_NF4) v -= neg[r * MT + m];
+            if (m < M && lr < rows && v != 0) atomicAdd(&P[(grp * TR + lr) * MT + m], v);
+            acc[r * MT + m] = 0;
+            if constexpr (FMT == FMT_NF4) neg[r * MT + m] = 0;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < TR * MT; t += kWarps * 32) {
+    const int m = t / TR, lr = t % TR;
+    if (m < M && lr < rows) {
+      const int n = n0 + lr;
+      float c = 0.0f;
+      for (int g = 0; g < Sk; g++)
+        c = __fadd_rn(c, __fmul_rn(__fmul_rn((float)P[(g * TR + lr) * MT + m], aS[(size_t)m * Sk + g]),
+                                   bS[(size_t)g * N + n]));
+      C[(size_t)m * N + n] = c;
+    }
+  }
+}
+
 struct Cfg {
   int mt, tr;
 };
@@ -366,6 +487,49 @@ uint32_t pack4(int a, int b, int c, int d) {
          ((uint32_t)(uint8_t)d << 24);
 }
 
+template <int FMT, int MT, int TR>
+cudaError_t launch_grouped_one(const GroupedArgs &a, const uint8_t *Ab, const float *aSb, float *Cb, int m,
+                               cudaStream_t s, bool pdl, const Tables &tb) {
+  const size_t rowB = fmt_row_bytes(FMT, a.K);
+  const size_t smem = (size_t)TR * rowB + (((size_t)m * a.K + 15) & ~(size_t)15) + (size_t)(a.K / a.G) * TR * MT * 4;
+  auto kern = gemv_grouped_kernel<FMT, MT, TR>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + TR - 1) / TR);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t *)a.W, Ab, aSb, a.bS, Cb, m, a.K, a.N, a.G, tb);
+}
+
+// shared memory of one grouped CTA: staged weight rows, activations, the group table
+size_t grouped_smem(int fmt, int K, int G, int mt, int tr) {
+  return (size_t)tr * fmt_row_bytes(fmt, K) + (((size_t)mt * K + 15) & ~(size_t)15) + (size_t)(K / G) * tr * mt * 4;
+}
+
+template <int FMT>
+cudaError_t dispatch_grouped(const GroupedArgs &a, int mt, int tr, const uint8_t *Ab, const float *aSb, float *Cb,
+                             int m, cudaStream_t s, bool pdl, const Tables &tb) {
+#define ORKB_GG_CASE(MT_, TR_) \
+  if (mt == MT_ && tr == TR_) return launch_grouped_one<FMT, MT_, TR_>(a, Ab, aSb, Cb, m, s, pdl, tb);
+  ORKB_GG_CASE(1, 8) ORKB_GG_CASE(1, 16) ORKB_GG_CASE(1, 32)
+  ORKB_GG_CASE(2, 8) ORKB_GG_CASE(2, 16) ORKB_GG_CASE(2, 32)
+  ORKB_GG_CASE(4, 8) ORKB_GG_CASE(4, 16) ORKB_GG_CASE(4, 32)
+  ORKB_GG_CASE(8, 8) ORKB_GG_CASE(8, 16) ORKB_GG_CASE(8, 32)
+#undef ORKB_GG_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
 }  // namespace
 
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches) {
@@ -402,6 +566,52 @@ unsigned int gemv_error_flag(bool reset) {
     cudaMemcpyToSymbol(g_gemv_error, &z, sizeof z);
   }
   return v;
+}
+
+}  // namespace orkb
+
+namespace orkb {
+
+bool grouped_supports(int fmt, int K, int G) {
+  if (G <= 0 || K % G) return false;
+  if (fmt == FMT_I8) {
+    if (G % 16) return false;
+  } else if (fmt == FMT_U4 || fmt == FMT_NF4) {
+    if (G % 32) return false;
+  } else {
+    return false;
+  }
+  return grouped_smem(fmt, K, G, 8, 8) <= 196 * 1024;
+}
+
+cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, int *launches) {
+  if ((uintptr_t)a.W % 16 || (uintptr_t)a.A % 16 || (uintptr_t)a.C % 4) return cudaErrorMisalignedAddress;
+  if (!grouped_supports(a.fmt, a.K, a.G)) return cudaErrorInvalidValue;
+  if ((size_t)a.K % 16) return cudaErrorMisalignedAddress;  // activation rows stay 16-byte aligned
+  const int8_t *L = kNf4Lut;
+  const Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
+                  pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const int Sk = a.K / a.G;
+  for (int m0 = 0; m0 < a.M; m0 += 8) {
+    const int m = a.M - m0 < 8 ? a.M - m0 : 8;
+    const int mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+    int tr = 8;
+    for (int t : {16, 32})
+      if (grouped_smem(a.fmt, a.K, a.G, mt, t) <= 196 * 1024 && (a.N + t - 1) / t >= 2 * 148) tr = t;
+    const uint8_t *Ab = (const uint8_t *)a.A + (size_t)m0 * a.K;
+    const float *aSb = a.aS + (size_t)m0 * Sk;
+    float *Cb = a.C + (size_t)m0 * a.N;
+    cudaError_t e;
+    switch (a.fmt) {
+      case FMT_I8: e = dispatch_grouped<FMT_I8>(a, mt, tr, Ab, aSb, Cb, m, s, pdl, tb); break;
+      case FMT_U4: e = dispatch_grouped<FMT_U4>(a, mt, tr, Ab, aSb, Cb, m, s, pdl, tb); break;
+      case FMT_NF4: e = dispatch_grouped<FMT_NF4>(a, mt, tr, Ab, aSb, Cb, m, s, pdl, tb); break;
+      default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+    if (launches) ++*launches;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace orkb

@@ -43,6 +43,21 @@ inline bool gemv_supports(int fmt, int K) {  // 8 weight rows + up to 8 activati
 }
 unsigned int gemv_error_flag(bool reset);
 
+// Grouped (per-K-group scaled) matmul, ork-driver src/npu/core/buf.c:501-520: C[m][n] fp32 = sum over
+// groups g, ascending, of ((float)P_g[m][n] * aScale[m*Sk+g]) * bScale[g*N+n], P_g the exact int32 dot
+// over the group's G columns; Sk = K/G. Weight formats FMT_I8 (G % 16 == 0), FMT_U4 / FMT_NF4
+// (G % 32 == 0). Device pointers; M any (launched 8 rows at a time).
+struct GroupedArgs {
+  const void *W;
+  const void *A;       // [M][K] int8
+  const float *aS;     // [M][K/G]
+  const float *bS;     // [K/G][N]
+  float *C;            // [M][N]
+  int M, K, N, fmt, G;
+};
+cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, int *launches);
+bool grouped_supports(int fmt, int K, int G);
+
 // Tensor-core path (tcgen05). Returns cudaErrorNotSupported when the shape/format has no TC kernel.
 cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
 bool gemm_tc_supports(int fmt, int M, int K, int N);

@@ -16,6 +16,8 @@ struct ork_npu {
   size_t capA = 0;
   void *dC = nullptr;
   size_t capC = 0;
+  void *dS = nullptr;  // staging for the scale tables of grouped runs
+  size_t capS = 0;
   bool pdl = true;
   int force_route = -1;
   uint64_t launches = 0;
@@ -28,6 +30,7 @@ struct ork_w {
   int dtype = orkb::DT_I8;
   int quant_kind = 0;
   bool int4_store = false;  // an ork_i4a8 weight: carries bscale and dumps as O4N1
+  int gsize = 0;            // K-group size of a grouped weight (ork_i4_mm_pack_grouped, _load_tiled, set_group)
   void *d = nullptr;
   size_t bytes = 0;
   float *bscale = nullptr;
@@ -38,4 +41,19 @@ namespace orkb {
 int route_for(const ork_npu *c, const ork_w *w, int M);
 // Sticky device-side error flags (a bounded wait that expired); cleared when read.
 bool device_error();
+
+void log_err(const char *what, cudaError_t e);
+// Makes the context's device current for a call and restores the caller's device afterwards.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev);
+  ~DeviceGuard();
+};
+// Grows a device staging buffer to at least `need` bytes (1 MiB minimum).
+bool grow(void **p, size_t *cap, size_t need);
+// Memory of the context's GPU (or managed memory) that a kernel can use in place.
+bool is_device_ptr(const void *p, int device);
+bool overlaps(const void *a, size_t an, const void *b, size_t bn);
+// A new resident weight: device memory of `bytes`, filled from host memory in the resident format.
+ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host_resident, size_t bytes);
 }  // namespace orkb

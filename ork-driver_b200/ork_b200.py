@@ -49,6 +49,23 @@ SIGNATURES = [
     ("ork_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_noalloc", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_pack_hdr_bytes", _sz, []),
+    ("ork_w_dump", _sz, [_vp, _vp, _sz]),
+    ("ork_i8_w_dump_cpu", _sz, [_vp, _i, _i, _vp, _vp, _sz]),
+    ("ork_i8_w_dump_bf_cpu", _sz, [_vp, _i, _i, _vp, _vp, _sz]),
+    ("ork_i4_w_dump_cpu", _sz, [_vp, _i, _i, _vp, _vp, _sz]),
+    ("ork_f16_mm_load", _vp, [_vp, _i, _i, _vp, _sz]),
+    ("ork_i8_mm_load", _vp, [_vp, _i, _i, _vp, _sz]),
+    ("ork_i4_mm_load", _vp, [_vp, _i, _i, _vp, _sz]),
+    ("ork_i4a8_mm_load_tiled", _vp, [_vp, _i, _i, _vp, _sz, _i]),
+    ("ork_i4_mm_pack_grouped", _vp, [_vp, _i, _i, _vp, _i]),
+    ("ork_w_set_group", _i, [_vp, _i]),
+    ("ork_i4_mm_run_grouped", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_i8_mm_run_grouped", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_i4_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_i8_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_b200_pack_check", _i, [_vp, _sz, _i, _i, _i]),
+    ("ork_b200_pack_capid", C.c_uint32, []),
     ("ork_b200_sync", _i, [_vp]),
     ("ork_b200_stream", _vp, [_vp]),
     ("ork_b200_set_stream", _i, [_vp, _vp]),
@@ -139,6 +156,41 @@ class Context:
         blob = np.ascontiguousarray(blob, np.uint8)
         return Weight(self, self.L.ork_i4a8_mm_load(self.ctx, K, N, _p(blob), blob.nbytes), K, N, "i8")
 
+    def i4_pack_grouped(self, B_kn, G):
+        B_kn = np.ascontiguousarray(B_kn, np.int8)
+        K, N = B_kn.shape
+        return Weight(self, self.L.ork_i4_mm_pack_grouped(self.ctx, K, N, _p(B_kn), G), K, N, "i4")
+
+    def load(self, blob, K, N, kind):
+        """ork_{i8,i4,f16}_mm_load of a stamped .orkpack blob."""
+        blob = np.ascontiguousarray(blob, np.uint8)
+        fn = {"i8": self.L.ork_i8_mm_load, "i4": self.L.ork_i4_mm_load, "f16": self.L.ork_f16_mm_load}[kind]
+        return Weight(self, fn(self.ctx, K, N, _p(blob), blob.nbytes), K, N, kind)
+
+    def i4a8_load_tiled(self, blob, K, N, G):
+        blob = np.ascontiguousarray(blob, np.uint8)
+        return Weight(self, self.L.ork_i4a8_mm_load_tiled(self.ctx, K, N, _p(blob), blob.nbytes, G), K, N, "i8")
+
+    def dump_cpu(self, B_kn, kind):
+        """ork_i8_w_dump_cpu / ork_i4_w_dump_cpu: the stamped blob, built on the host."""
+        B_kn = np.ascontiguousarray(B_kn, np.int8)
+        K, N = B_kn.shape
+        fn = self.L.ork_i8_w_dump_cpu if kind == "i8" else self.L.ork_i4_w_dump_cpu
+        need = fn(self.ctx, K, N, _p(B_kn), None, 0)
+        out = np.zeros(need, np.uint8)
+        assert need and fn(self.ctx, K, N, _p(B_kn), _p(out), need) == need
+        return out
+
+    def run_grouped(self, w, A, aS, bS):
+        """ork_i4_mm_run_grouped / ork_i8_mm_run_grouped (by w's kind); returns (rc, C fp32)."""
+        A = np.ascontiguousarray(A, np.int8)
+        aS = np.ascontiguousarray(aS, np.float32)
+        bS = np.ascontiguousarray(bS, np.float32)
+        M = A.shape[0]
+        Cm = np.zeros((M, w.N), np.float32)
+        fn = self.L.ork_i4_mm_run_grouped if w.kind == "i4" else self.L.ork_i8_mm_run_grouped
+        return fn(self.ctx, w.h, M, _p(A), _p(aS), _p(bS), _p(Cm)), Cm
+
     # ---- run (synchronous, host numpy buffers) ---------------------------------------------------
     def run(self, w, A, M=None):
         """C = A . B through the run function matching w's dtype; returns (rc, C)."""
@@ -185,6 +237,18 @@ class Weight:
         need = self.ctx.L.ork_b200_weight_read(self.h, None, 0)
         out = np.zeros(need, np.uint8)
         assert self.ctx.L.ork_b200_weight_read(self.h, _p(out), need) == need
+        return out
+
+    def set_group(self, G):
+        return self.ctx.L.ork_w_set_group(self.h, G)
+
+    def pack_dump(self):
+        """ork_w_dump: the stamped .orkpack entry of this weight."""
+        need = self.ctx.L.ork_w_dump(self.h, None, 0)
+        if need == 0:
+            return None
+        out = np.zeros(need, np.uint8)
+        assert self.ctx.L.ork_w_dump(self.h, _p(out), need) == need
         return out
 
     def dump(self):

@@ -3,7 +3,8 @@
 Runs ork-driver's offline CPU path (oracle/_ref/libork_ref.so, built by `make -C oracle ref` from the
 reference sources) on small seeded inputs and records what it produced: O4N1 blob hashes and qerr of
 ork_i4a8_pack_cpu_blob_qerr for every quantizer mode, the per-channel int8 scales of orki_chan_scales_f32,
-and the W4A4 int32 result checksum of ork_i4_mm_pack + ork_i4_mm_run on an offline context. The fixture
+the W4A4 int32 result checksum of ork_i4_mm_pack + ork_i4_mm_run on an offline context, and the fp32
+results of the grouped-scale path (ork_i4_mm_pack_grouped + ork_i4_mm_run_grouped, orki_cpu_gemm_grouped). The fixture
 pins the restated oracle (oracle/ork_oracle.c) where the reference tree is absent (the GPU box).
 
     python tests/golden/make_fixtures.py            # rewrites reference_fixtures.json
@@ -49,6 +50,20 @@ def seeded_weights(seed, N, K, scale=0.02):
 def seeded_imatrix(seed, K):
     rng = np.random.default_rng(seed + 1000)
     return (rng.random(K, dtype=np.float32) * np.float32(1.5) + np.float32(0.5)).astype(np.float32)
+
+
+# grouped scales: (M, K, N, G, activation range) -- W4A4 (A int4) and W4A8 (A int8) over int4 weights
+GROUPED_CASES = [(1, 1024, 128, 32, 8), (3, 2048, 192, 128, 8), (8, 1024, 64, 256, 128), (5, 4096, 128, 64, 128)]
+
+
+def grouped_inputs(seed, M, K, N, G, a_range):
+    """A [M][K] in [-a_range, a_range), int4 weights B [K][N], aScale [M][K/G], bScale [K/G][N]."""
+    rng = np.random.default_rng(seed)
+    A = rng.integers(-a_range, a_range, size=(M, K), dtype=np.int8)
+    B = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    aS = rng.uniform(1e-3, 3e-2, size=(M, K // G)).astype(np.float32)
+    bS = rng.uniform(1e-3, 3e-2, size=(K // G, N)).astype(np.float32)
+    return A, B, aS, bS
 
 
 def sha(a):
@@ -106,6 +121,21 @@ def main():
         assert ref.ork_i4_mm_run(ctx, w, M, of._p(A), of._p(Cm)) == 0
         ref.ork_w_free(w)
         fx["w4a4"][f"{M}x{K}x{N}"] = {"seed": seed, "M": M, "K": K, "N": N, "c_fnv64": of.fnv64(Cm)}
+    # grouped scales: ork_i4_mm_pack_grouped + ork_i4_mm_run_grouped (W4A4, A int4) on the offline context,
+    # and orki_cpu_gemm_grouped with int8 activations (the W4A8 grouped tier shares it)
+    fx["grouped"] = {}
+    for i, (M, K, N, G, ar) in enumerate(GROUPED_CASES):
+        seed = 300 + i
+        A, B, aS, bS = grouped_inputs(seed, M, K, N, G, ar)
+        Cm = np.zeros((M, N), np.float32)
+        if ar == 8:
+            w = ref.ork_i4_mm_pack_grouped(ctx, K, N, of._p(B), G)
+            assert w and ref.ork_i4_mm_run_grouped(ctx, w, M, of._p(A), of._p(aS), of._p(bS), of._p(Cm)) == 0
+            ref.ork_w_free(w)
+        else:
+            assert ref.orki_cpu_gemm_grouped(M, K, N, G, of._p(A), of._p(B), of._p(aS), of._p(bS), of._p(Cm)) == 0
+        fx["grouped"][f"{M}x{K}x{N}_G{G}_a{ar}"] = {"seed": seed, "M": M, "K": K, "N": N, "G": G, "a_range": ar,
+                                                    "c_sha256": sha(Cm)}
     ref.ork_npu_free(ctx)
     with open(OUT, "w") as f:
         json.dump(fx, f, indent=1, sort_keys=True)

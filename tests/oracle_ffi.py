@@ -45,6 +45,9 @@ def restated():
         lib.orc_gen_rnd_f16.argtypes = [C.POINTER(C.c_uint32), C.c_void_p, C.c_size_t]
         lib.orc_nf4_lut.argtypes = [C.c_void_p]
         lib.orc_threads.restype = C.c_int
+        lib.orc_gemm_grouped.restype = C.c_int
+        lib.orc_gemm_grouped.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p]
         _restated = lib
     return _restated
 
@@ -80,6 +83,26 @@ def reference():
         lib.ork_w_codes.argtypes = [C.c_void_p]
         lib.ork_w_free.argtypes = [C.c_void_p]
         lib.ork_i8_mm_run_cpu.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        # grouped scales (src/npu/core/buf.c:501, src/npu/i4/pack.c:686, src/npu/i4/run.c:367,
+        # src/npu/i4/pack.c:265, src/npu/i8/run.c:45) and the persisted-weight header (src/npu/core/packhdr.c)
+        lib.orki_cpu_gemm_grouped.restype = C.c_int
+        lib.orki_cpu_gemm_grouped.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                              C.c_void_p, C.c_void_p, C.c_void_p]
+        lib.ork_i4_mm_pack_grouped.restype = C.c_void_p
+        lib.ork_i4_mm_pack_grouped.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int]
+        for name in ("ork_i4_mm_run_grouped", "ork_i8_mm_run_grouped"):
+            getattr(lib, name).restype = C.c_int
+            getattr(lib, name).argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_void_p]
+        for name in ("ork_i8_w_dump_cpu", "ork_i4_w_dump_cpu"):
+            getattr(lib, name).restype = C.c_size_t
+            getattr(lib, name).argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t]
+        lib.ork_i4a8_mm_load_tiled.restype = C.c_void_p
+        lib.ork_i4a8_mm_load_tiled.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_int]
+        lib.orki_pack_check.restype = C.c_int
+        lib.orki_pack_check.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int]
+        lib.orki_pack_capid.restype = C.c_uint
+        lib.orki_pack_capid.argtypes = [C.c_void_p]
         _reference = lib
     return _reference
 
@@ -121,6 +144,20 @@ def gemm_f16(A, B_kn):
     N = B_kn.shape[1]
     Cm = np.empty((M, N), np.float32)
     restated().orc_gemm_f16(M, K, N, _p(A), _p(B_kn), _p(Cm))
+    return Cm
+
+
+def gemm_grouped(A, B_kn, G, aS, bS):
+    """C fp32 = sum over K-groups of ((float)int32 dot * aS[m][g]) * bS[g][n], g ascending
+    (src/npu/core/buf.c:501-520)."""
+    A = np.ascontiguousarray(A, np.int8)
+    B_kn = np.ascontiguousarray(B_kn, np.int8)
+    aS = np.ascontiguousarray(aS, np.float32)
+    bS = np.ascontiguousarray(bS, np.float32)
+    M, K = A.shape
+    N = B_kn.shape[1]
+    Cm = np.empty((M, N), np.float32)
+    assert restated().orc_gemm_grouped(M, K, N, G, _p(A), _p(B_kn), _p(aS), _p(bS), _p(Cm)) == 0
     return Cm
 
 
