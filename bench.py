@@ -524,6 +524,167 @@ def run_qwen3(args):
     ctx.close()
 
 
+# grouped scales (per-K-group aScale/bScale, fp32 C): the reference's own grouped W4A8 test shapes
+# (examples/test_grouped_i8.c:84-87, G = 512 / 1024) plus a G = 128 decode shape, at M = 1 and 8
+GROUPED_SHAPES = [(2048, 4096, 512), (2048, 16384, 512), (4096, 20480, 1024), (3072, 12288, 1024), (4096, 4096, 128)]
+GROUPED_MS = [1, 8]
+
+
+def grouped_bytes(K, N, G, M):
+    """Algorithmic bytes of one grouped run: int4 weight + bScale + A + aScale + fp32 C."""
+    return K * N // 2 + (K // G) * N * 4 + M * K + M * (K // G) * 4 + 4 * M * N
+
+
+def run_grouped(args):
+    """Grouped-scale W4A8 decode: int4 weights written by ork_i4_w_dump_cpu, loaded with
+    ork_i4a8_mm_load_tiled(G), run by ork_i8_mm_run_grouped(_async) with int8 activations, fp32 C. One step
+    = every (shape, M) once; 3 distinct weight copies (>= 240 MB) cycle so no call finds its weight in L2.
+    value = algorithmic GB/s of the step (device-resident inputs, one CUDA graph, events); e2e = the
+    synchronous host-buffer call; cpu_baseline = the reference's orki_cpu_gemm_grouped (oracle/_ref) on a
+    bounded sample of the same calls."""
+    import torch
+
+    import ork_b200
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_ffi as of
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    ctx = ork_b200.Context()
+    L = ctx.L
+    stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+    NC = 3
+    rng = np.random.default_rng(77 + rank)
+    calls, host, weights = [], [], []
+    for K, N, G in GROUPED_SHAPES:
+        B = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+        blob = ctx.dump_cpu(B, "i4")
+        ws = [ctx.i4a8_load_tiled(blob, K, N, G) for _ in range(NC)]
+        assert all(ws)
+        weights += ws
+        for M in GROUPED_MS:
+            A = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+            aS = rng.uniform(1e-3, 3e-2, size=(M, K // G)).astype(np.float32)
+            bS = rng.uniform(1e-3, 3e-2, size=(K // G, N)).astype(np.float32)
+            host.append((K, N, G, M, A, B, aS, bS))
+            for ci in range(NC):
+                dev = [torch.from_numpy(x).cuda() for x in (A, aS, bS)]
+                dC = torch.empty((M, N), dtype=torch.float32, device="cuda")
+                calls.append((ci, (K, N, G, M), ws[ci], dev, dC))
+    step_bytes = sum(grouped_bytes(K, N, G, M) for K, N, G, M, *_ in host)
+
+    def enqueue(sel):
+        for _, _, w, (dA, daS, dbS), dC in sel:
+            assert L.ork_i8_mm_run_grouped_async(ctx.ctx, w.h, dA.shape[0], dA.data_ptr(), daS.data_ptr(),
+                                                 dbS.data_ptr(), dC.data_ptr()) == 0
+
+    def graph_of(sel):
+        enqueue(sel)
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            enqueue(sel)
+        return g
+
+    def timed(g, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3
+
+    # correctness of the timed calls (first copy) against the restated oracle, before timing
+    for ci, key, w, (dA, daS, dbS), dC in calls:
+        if ci == 0:
+            K, N, G, M = key
+            hA, haS, hbS = dA.cpu().numpy(), daS.cpu().numpy(), dbS.cpu().numpy()
+            B = next(h[5] for h in host if h[:4] == key)
+            enqueue([(ci, key, w, (dA, daS, dbS), dC)])
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            assert np.array_equal(dC.cpu().numpy().view(np.uint32),
+                                  of.gemm_grouped(hA, B, G, haS, hbS).view(np.uint32)), key
+    g_all = graph_of(calls)
+    for _ in range(max(args.warmup, 3)):
+        g_all.replay()
+    torch.cuda.synchronize()
+    reps = max(1, args.steps // NC)
+    with Clocks(local) as clk:
+        t = timed(g_all, reps)
+    ms_per_step = t / (reps * NC) * 1e3
+    value = step_bytes / (ms_per_step / 1e3) / 1e9
+    breakdown, dom = {}, None
+    for K, N, G, M, *_ in host:
+        sel = [c for c in calls if c[1] == (K, N, G, M)]
+        g = graph_of(sel)
+        for _ in range(3):
+            g.replay()
+        tt = timed(g, 20) / (20 * NC)
+        gbs = grouped_bytes(K, N, G, M) / tt / 1e9
+        name = f"{K}x{N}_G{G}_M{M}"
+        breakdown[name] = {"us": tt * 1e6, "GB/s": gbs}
+        if dom is None or tt > breakdown[dom]["us"] / 1e6:
+            dom = name
+        del g
+    # e2e: the synchronous public call over host buffers, one pass of the step per iteration
+    pinned = [(torch.from_numpy(A).pin_memory().numpy(), torch.from_numpy(aS).pin_memory().numpy(),
+               torch.from_numpy(bS).pin_memory().numpy(), np.zeros((M, N), np.float32), K, N, G, M)
+              for K, N, G, M, A, B, aS, bS in host]
+    hw = {key: [c[2] for c in calls if c[1] == key and c[0] == 0][0] for key in {c[1] for c in calls}}
+    t0 = time.perf_counter()
+    e2e_reps = 5
+    for _ in range(e2e_reps):
+        for A, aS, bS, Cm, K, N, G, M in pinned:
+            assert L.ork_i8_mm_run_grouped(ctx.ctx, hw[(K, N, G, M)].h, M, of._p(A), of._p(aS), of._p(bS),
+                                           of._p(Cm)) == 0
+    e2e_t = (time.perf_counter() - t0) / e2e_reps
+    h2d = sum(A.nbytes + aS.nbytes + bS.nbytes for A, aS, bS, *_ in pinned)
+    d2h = sum(Cm.nbytes for _, _, _, Cm, *_ in pinned)
+    hbm, _, src = peaks()
+    line = {"metric": "grouped-scale W4A8 decode algorithmic HBM GB/s", "value": value * world, "unit": "GB/s",
+            "n_gpus": world, "steps": reps * NC, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "grouped W4A8: ork_i4_w_dump_cpu -> ork_i4a8_mm_load_tiled(G) -> "
+                                   "ork_i8_mm_run_grouped, fp32 C; (K,N,G) in "
+                                   + ", ".join(f"({K},{N},{G})" for K, N, G in GROUPED_SHAPES)
+                                   + " (examples/test_grouped_i8.c shapes + G=128), M in {1,8}",
+                       "l2": f"{NC} distinct weight copies cycled", "step_bytes": step_bytes,
+                       "parallelism": "replicas" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": breakdown[dom]["GB/s"], "peak": hbm, "unit": "GB/s",
+                         "frac": breakdown[dom]["GB/s"] / hbm, "traffic": None, "kernel": dom,
+                         "peak_source": src},
+            "e2e": {"value": step_bytes / e2e_t / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_t * 1e3},
+            "clocks": clk.summary(), "gpu_launches": int(len(calls) * reps),
+            "breakdown": breakdown}
+    if rank == 0 and not args.no_cpu:
+        ref = of.reference()
+        fn = ref.orki_cpu_gemm_grouped if ref is not None else of.restated().orc_gemm_grouped
+        sample = [h for h in host if h[3] == 1]
+        t0, n = time.perf_counter(), 0
+        while n == 0 or (time.perf_counter() - t0 < 10 and n < 3):
+            for K, N, G, M, A, B, aS, bS in sample:
+                Cm = np.zeros((M, N), np.float32)
+                assert fn(M, K, N, G, of._p(A), of._p(B), of._p(aS), of._p(bS), of._p(Cm)) == 0
+            n += 1
+        tc = (time.perf_counter() - t0) / n
+        line["cpu_baseline"] = {"value": sum(grouped_bytes(K, N, G, M) for K, N, G, M, *_ in sample) / tc / 1e9,
+                                "unit": "GB/s", "cores": of.restated().orc_threads(),
+                                "kind": "reference" if ref is not None else "port",
+                                "sample": f"{n} pass(es) of the M=1 calls of the step ({tc * n:.2f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del g_all
+    for w in weights:
+        w.free()
+    ctx.close()
+
+
 def run_profile(spec):
     """`K,N,M[,route]`: one config, packed once, run 5 times with a synchronisation after each -- a small,
     self-contained workload for `ncu -k <kernel> -s <skip> -c <count>` captures -- then 50 back-to-back
@@ -550,12 +711,20 @@ def run_profile(spec):
         print(json.dumps({"profile": "all", "configs": [f"{K}x{N}xM{M}" for K, N, M in CONFIGS]}))
         ctx.close()
         return
-    parts = [int(x) for x in spec.split(",")]
+    fields = spec.split(",")
+    fmt = fields[4] if len(fields) > 4 else "i8"  # i8 | u4 | nf4 (int4 stores of ork_i4a8_mm_pack)
+    parts = [int(x) for x in fields[:4]]
     K, N, M = parts[:3]
     route = parts[3] if len(parts) > 3 else -1
     L.ork_b200_force_route(ctx.ctx, route)
     f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
-    w, _ = ctx.i8_pack_f32(f32)
+    if fmt == "i8":
+        w, _ = ctx.i8_pack_f32(f32)
+    else:
+        if fmt == "nf4":
+            os.environ["ORK_NF4"] = "1"
+        w, _ = ctx.i4a8_pack(f32)
+        os.environ.pop("ORK_NF4", None)
     a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
     c = torch.empty((M, N), dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
@@ -588,12 +757,12 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
-    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3"],
+    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped"],
                     help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack; "
-                         "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack")
+                         "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack; grouped: grouped-scale W4A8 decode")
     ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
     ap.add_argument("--profile", default=None,
-                    help="K,N,M[,route]: run one w8a8 config a few times eagerly (for ncu captures)")
+                    help="K,N,M[,route[,fmt]]: run one config a few times eagerly (for ncu captures); fmt i8|u4|nf4")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -604,6 +773,8 @@ def main():
         return run_70b(args)
     if args.workload == "qwen3":
         return run_qwen3(args)
+    if args.workload == "grouped":
+        return run_grouped(args)
 
     import torch
 

@@ -27,6 +27,7 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "nibble.cuh"
 #include "ork_internal.h"
 
 namespace orkb {
@@ -240,36 +241,8 @@ constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 1
 
 // Nibble weights (FMT_U4 / FMT_NF4): the W tile arrives as nibbles ([rows][64 bytes] per 128-k block)
 // in a staging buffer and the four epilogue warps, idle during the main loop, expand it in registers
-// into the 128-byte-swizzled int8 tile the MMA reads, then publish it to the async proxy. Uniform codes
-// are sign-extended (x | (x & 8) * 0x1E per byte); NF4 indices go through two 8-entry prmt tables
-// (lut[8..15] and -lut[0..7], zero in the other half), negated bytewise without carries.
-struct Nf4Tables {
-  uint32_t neg0, neg1, pos0, pos1;
-};
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
-// 8 nibbles (k = 8q .. 8q+7 in nibble order) -> 8 int8 codes in k order, as two words.
-template <int FMT>
-__device__ __forceinline__ uint2 expand8(uint32_t w, const Nf4Tables &tb) {
-  if constexpr (FMT == FMT_U4) {
-    uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;  // k even / k odd, 0..15
-    lo |= (lo & 0x08080808u) * 0x1Eu;                             // bit 3 set -> high nibble 0xF
-    hi |= (hi & 0x08080808u) * 0x1Eu;
-    return make_uint2(prmt(lo, hi, 0x5140), prmt(lo, hi, 0x7362));
-  } else {
-    const uint32_t x = w ^ 0x88888888u;
-    const uint32_t p0 = prmt(tb.pos0, tb.pos1, x), p1 = prmt(tb.pos0, tb.pos1, x >> 16);
-    const uint32_t n0 = prmt(tb.neg0, tb.neg1, w), n1 = prmt(tb.neg0, tb.neg1, w >> 16);
-    // bytes of n are 0..127: (0x80 - n) ^ 0x80 == -n per byte, with no borrow between bytes
-    return make_uint2(p0 | ((0x80808080u - n0) ^ 0x80808080u), p1 | ((0x80808080u - n1) ^ 0x80808080u));
-  }
-}
-
+// (expand8, nibble.cuh) into the 128-byte-swizzled int8 tile the MMA reads, then publish it to the async
+// proxy.
 template <int FMT, bool SWAP, int TN, int STAGES, int NA>
 __global__ void __launch_bounds__(192)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
@@ -762,10 +735,6 @@ bool make_map(CUtensorMap *map, const void *base, int rows, size_t row_bytes, in
   return r == CUDA_SUCCESS;
 }
 
-uint32_t pack4(int a, int b, int c, int d) {
-  return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
-         ((uint32_t)(uint8_t)d << 24);
-}
 
 template <int FMT, bool SWAP, int TN, int STAGES, int NA = 1>
 cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
@@ -792,9 +761,7 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  const int8_t *L = kNf4Lut;
-  const Nf4Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
-                     pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const Nf4Tables tb = nf4_tables();
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((rowsR + TM - 1) / TM, (rowsS + TN - 1) / TN, sk);
@@ -840,9 +807,7 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  const int8_t *L = kNf4Lut;
-  const Nf4Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
-                     pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const Nf4Tables tb = nf4_tables();
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((rowsR + 2 * BM - 1) / (2 * BM)), (rowsS + TN - 1) / TN, sk);
@@ -870,8 +835,9 @@ struct TcCfg {
 };
 
 // Tile and split choice. Swapped operands with the narrowest N-tile covering M for M <= 64 (weight
-// streaming; K split over a cluster up to 8 ways until ~192 CTAs). For larger M, measured on B200 over
-// configs of K in {2048, 6144}, N in {2048, 6144, 12288}, M in {128, 256, 512}: a CTA's time is set by
+// streaming; K split over a cluster up to 8 ways while the grid stays within ~320 CTAs, two per SM).
+// For larger M, measured on B200 over configs of K in {2048, 6144}, N in {2048, 6144, 12288},
+// M in {128, 256, 512}: a CTA's time is set by
 // its own operand bytes in flight and its C tile, so the grid should cover the SMs once with the
 // narrowest tile that fits: 128-wide weight tiles, widened to 192 then 256 (int8 / f16) only while the
 // grid would exceed one wave of 148 CTAs; nibble weights past one wave use CTA-pair tiles of 256 x 192
@@ -886,7 +852,7 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
     c.tn = M <= 16 ? 16 : M <= 32 ? 32 : 64;
     const int tiles = (N + BM - 1) / BM;
     c.sk = 1;
-    while (tiles * c.sk * 2 <= 192 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
+    while (tiles * c.sk * 2 <= 320 && c.sk * 2 <= 8 && c.sk * 2 <= KB) c.sk *= 2;
   } else {
     const int mt = (M + BM - 1) / BM;
     auto tiles = [&](int tn) { return mt * ((N + tn - 1) / tn); };

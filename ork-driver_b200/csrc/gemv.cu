@@ -13,22 +13,26 @@
 //
 // Arithmetic, in registers:
 //   int8  : 4 x dp4a per 16 weight bytes and activation row;
-//   int4  : the nibble is moved to the top of a byte ((w<<4)&0xF0F0F0F0 / w&0xF0F0F0F0), so each byte
-//           holds 16*code; dp4a then accumulates 16*dot exactly and the lane's sum is shifted right by 4
-//           before the cross-lane reduction (exact: every partial is a multiple of 16);
-//   NF4   : the nibble indexes two 8-entry byte tables with prmt -- pos = lut[8..15] (selected when bit 3
-//           is set) and neg = -lut[0..7] (selected when bit 3 is clear; prmt's sign-replicate mode
-//           yields 0 for the other half because every table byte is >= 0), dot = dp4a(pos) - dp4a(neg);
+//   int4  : each 16-byte chunk of nibbles (32 k) is expanded once to its int8 codes (expand8,
+//           nibble.cuh: sign-extended uniform codes, or the NF4 table through prmt) and then multiplied
+//           with dp4a like int8 -- the expansion is shared by all MT activation rows;
 //   fp16  : converted to fp32 and accumulated with FFMA.
 // Every integer result is exact int32, identical to ork-driver's CPU oracle (src/npu/core/buf.c:428).
 //
-// Work mapping: eight lanes cover one channel, 16 bytes each, so one warp-wide shared-memory read moves
+// A second, direct-load kernel (gemv_direct_kernel) serves the shapes where staging whole rows per CTA
+// does not pay: a warp streams its CPW channel rows through a register ring of 128-bit loads and reads
+// the activations through L1 (see choose() for where each kernel is used).
+//
+// Work mapping (staged kernel): eight lanes cover one channel, 16 bytes each, so one warp-wide shared-memory read moves
 // 4 channels x 128 contiguous bytes and the activation chunk it multiplies is shared by the 4 channel
 // groups; each lane holds R = 2 channels (8 per warp) to reuse every activation load twice. The WK warps
 // that share a channel group split K; partials are reduced with a butterfly shuffle across the 8 lanes,
 // then across the K-split warps in shared memory.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+
+#include "nibble.cuh"
 #include "ork_internal.h"
 
 namespace orkb {
@@ -52,14 +56,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 }
 
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
-
-// prmt.b32 in its default mode. Emitted directly because the selector's bit 3 (replicate the sign of
-// the selected byte) is part of the NF4 lookup, and __byte_perm only honours the low 3 bits.
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
 
 // Bounded mbarrier wait (parity 0: each barrier completes exactly once per launch).
 __device__ __forceinline__ bool mbar_wait0(uint32_t bar) {
@@ -100,16 +96,28 @@ __device__ __forceinline__ void bfly_step(T *v, int lane) {
   }
 }
 
-struct Tables {
-  uint32_t neg0, neg1, pos0, pos1;
-};
+using Tables = Nf4Tables;
 
 // acc[r*MT+m] += <activation chunk of row m, weight chunk of channel r> for one 16-byte weight chunk per
 // channel. `sa` is the shared-memory address of activation row 0 at the chunk's first k, `a_row` the
 // activation row pitch in bytes.
 template <int FMT, int MT, typename T>
-__device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], uint32_t sa, uint32_t a_row, int M, T *acc, T *neg,
+__device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], uint32_t sa, uint32_t a_row, int M, T *acc,
                                           const Tables &tb) {
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  uint32_t wx[NIB ? kR : 1][8];  // nibble chunks expanded once to int8 codes in k order
+  if constexpr (NIB) {
+#pragma unroll
+    for (int r = 0; r < kR; r++) {
+      const uint32_t ww[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint2 e = expand8<FMT>(ww[q], tb);
+        wx[r][2 * q] = e.x;
+        wx[r][2 * q + 1] = e.y;
+      }
+    }
+  }
 #pragma unroll
   for (int m = 0; m < MT; m++) {
     if (m >= M) break;
@@ -124,41 +132,14 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], uint32_t sa, ui
         c = dp4a(a.z, wv[r].z, c);
         c = dp4a(a.w, wv[r].w, c);
       }
-    } else if constexpr (FMT == FMT_U4) {
-      const uint4 a0 = lds128(arow), a1 = lds128(arow + 16);
-      const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      uint32_t ev[4], od[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        ev[q] = prmt(aw[2 * q], aw[2 * q + 1], 0x6420);  // k = 8q + {0,2,4,6}
-        od[q] = prmt(aw[2 * q], aw[2 * q + 1], 0x7531);  // k = 8q + {1,3,5,7}
-      }
-#pragma unroll
-      for (int r = 0; r < kR; r++) {
-        const uint32_t ww[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
-        T &c = acc[r * MT + m];
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          c = dp4a(ev[q], (ww[q] << 4) & 0xF0F0F0F0u, c);
-          c = dp4a(od[q], ww[q] & 0xF0F0F0F0u, c);
-        }
-      }
-    } else if constexpr (FMT == FMT_NF4) {
-      const uint4 a0 = lds128(arow), a1 = lds128(arow + 16);
+    } else if constexpr (FMT == FMT_U4 || FMT == FMT_NF4) {
+      const uint4 a0 = lds128(arow), a1 = lds128(arow + 16);  // 32 activations, k order
       const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
       for (int r = 0; r < kR; r++) {
-        const uint32_t ww[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
         T &c = acc[r * MT + m];
-        T &d = neg[r * MT + m];
 #pragma unroll
-        for (int q = 0; q < 4; q++) {  // nibble i of word q is k = 8q + i
-          const uint32_t w = ww[q], x = ww[q] ^ 0x88888888u;
-          c = dp4a(aw[2 * q], prmt(tb.pos0, tb.pos1, x), c);
-          c = dp4a(aw[2 * q + 1], prmt(tb.pos0, tb.pos1, x >> 16), c);
-          d = dp4a(aw[2 * q], prmt(tb.neg0, tb.neg1, w), d);
-          d = dp4a(aw[2 * q + 1], prmt(tb.neg0, tb.neg1, w >> 16), d);
-        }
+        for (int q = 0; q < 8; q++) c = dp4a(aw[q], wx[r][q], c);
       }
     } else {  // FMT_F16
       const uint4 a = lds128(arow);
@@ -235,11 +216,8 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
   __syncthreads();  // barrier init visible to every thread
 
   T acc[V];
-  T neg[(FMT == FMT_NF4) ? V : 1];
 #pragma unroll
   for (int i = 0; i < V; i++) acc[i] = T(0);
-#pragma unroll
-  for (int i = 0; i < ((FMT == FMT_NF4) ? V : 1); i++) neg[i] = T(0);
 
   // this lane's channels: local rows wr*8 + g + 4r, r < kR (the warp-row group is one copy group)
   const int lrow0 = wr * 8 + g;
@@ -255,17 +233,10 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
       uint4 wv[kR];
 #pragma unroll
       for (int r = 0; r < kR; r++) wv[r] = lds128(base0 + (uint32_t)(4 * r * rowB) + (uint32_t)(s * 128));
-      mac_chunk<FMT, MT, T>(wv, sA + a_k * o, (uint32_t)a_row, M, acc, neg, tb);
+      mac_chunk<FMT, MT, T>(wv, sA + a_k * o, (uint32_t)a_row, M, acc, tb);
     }
   }
 
-  if constexpr (FMT == FMT_U4) {
-#pragma unroll
-    for (int i = 0; i < V; i++) acc[i] >>= 4;
-  } else if constexpr (FMT == FMT_NF4) {
-#pragma unroll
-    for (int i = 0; i < V; i++) acc[i] -= neg[i];
-  }
   bfly_step<V, 4>(acc, lane);
   bfly_step<(V / 2 > 1 ? V / 2 : 1), 2>(acc, lane);
   bfly_step<(V / 4 > 1 ? V / 4 : 1), 1>(acc, lane);
@@ -337,6 +308,7 @@ gemv_grouped_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A
   const size_t a_row = (size_t)K;
   const int Sk = K / G;
   const int gbytes = G / KPB;  // weight bytes per group (a multiple of the 16-byte lane chunk)
+  const int share = gbytes % 128 == 0 ? 8 : (128 % gbytes == 0 ? gbytes / 16 : 1);
   const uint32_t sW = smem_u32(smem);
   const uint32_t sA = sW + (uint32_t)(TR * rowB);
   int *P = reinterpret_cast<int *>(smem + TR * rowB + ((M * a_row + 15) & ~(size_t)15));
@@ -371,14 +343,12 @@ gemv_grouped_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A
 
   using T = int;
   T acc[V];
-  T neg[(FMT == FMT_NF4) ? V : 1];
 #pragma unroll
   for (int i = 0; i < V; i++) acc[i] = 0;
-#pragma unroll
-  for (int i = 0; i < ((FMT == FMT_NF4) ? V : 1); i++) neg[i] = 0;
 
   const int lrow0 = wr * 8 + gq;
-  const bool ok = mbar_wait0(smem_u32(&bars[wr])) && mbar_wait0(smem_u32(&bars[NGRP]));
+  // warp-uniform (the group flush below shuffles across the warp)
+  const bool ok = __all_sync(0xffffffffu, mbar_wait0(smem_u32(&bars[wr])) && mbar_wait0(smem_u32(&bars[NGRP])));
   const int S = (int)((rowB + 127) / 128);
   const int s0 = (int)((long long)S * wk / WK), s1 = (int)((long long)S * (wk + 1) / WK);
   if (ok && wr * 8 < rows) {
@@ -391,24 +361,43 @@ gemv_grouped_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A
         uint4 wv[kR];
 #pragma unroll
         for (int r = 0; r < kR; r++) wv[r] = lds128(base0 + (uint32_t)(4 * r * rowB) + (uint32_t)(s * 128));
-        mac_chunk<FMT, MT, T>(wv, sA + a_k * o, (uint32_t)a_row, M, acc, neg, tb);
+        mac_chunk<FMT, MT, T>(wv, sA + a_k * o, (uint32_t)a_row, M, acc, tb);
       }
-      // flush at the end of the lane's group (or of its range)
+      // Flush the lane partials into P at the end of a group. When the lanes of a channel group share
+      // groups in aligned power-of-two sets (share = 2, 4 or 8 lanes: a group of 32 or 64 bytes, or whole
+      // 128-byte segments), the set is first reduced with xor-shuffles -- its flush points are the same
+      // for the whole warp -- and one lane per set adds; otherwise every lane adds its own partial.
       const int grp = (int)(o / (uint32_t)gbytes);
-      const uint32_t on = o + 128u;
-      const bool last = (s + 1 >= s1) || on >= rowB || (int)(on / (uint32_t)gbytes) != grp;
-      if (live && last) {
+      if (share > 1) {
+        const bool last = share < 8 || (s + 1 >= s1) || (uint32_t)(s + 1) * 128u >= rowB ||
+                          (int)((uint32_t)(s + 1) * 128u / (uint32_t)gbytes) != grp;
+        if (last) {
 #pragma unroll
-        for (int r = 0; r < kR; r++) {
-          const int lr = lrow0 + 4 * r;
+          for (int r = 0; r < kR; r++) {
+            const int lr = lrow0 + 4 * r;
 #pragma unroll
-          for (int m = 0; m < MT; m++) {
-            T v = acc[r * MT + m];
-            if constexpr (FMT == FMT_U4) v >>= 4;
-            if constexpr (FMT == FMT_NF4) v -= neg[r * MT + m];
-            if (m < M && lr < rows && v != 0) atomicAdd(&P[(grp * TR + lr) * MT + m], v);
-            acc[r * MT + m] = 0;
-            if constexpr (FMT == FMT_NF4) neg[r * MT + m] = 0;
+            for (int m = 0; m < MT; m++) {
+              T v = acc[r * MT + m];
+              for (int off = 1; off < share; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+              if (live && (j & (share - 1)) == 0 && m < M && lr < rows && v != 0)
+                atomicAdd(&P[(grp * TR + lr) * MT + m], v);
+              acc[r * MT + m] = 0;
+            }
+          }
+        }
+      } else {
+        const uint32_t on = o + 128u;
+        const bool last = (s + 1 >= s1) || on >= rowB || (int)(on / (uint32_t)gbytes) != grp;
+        if (live && last) {
+#pragma unroll
+          for (int r = 0; r < kR; r++) {
+            const int lr = lrow0 + 4 * r;
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+              const T v = acc[r * MT + m];
+              if (m < M && lr < rows && v != 0) atomicAdd(&P[(grp * TR + lr) * MT + m], v);
+              acc[r * MT + m] = 0;
+            }
           }
         }
       }
@@ -428,20 +417,206 @@ gemv_grouped_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A
   }
 }
 
+// Direct-load decode kernel. One warp owns CPW consecutive output channels and their whole K row; lane
+// l reads 16-byte chunks l, l+32, l+64, ... of every row (each warp load is 512 contiguous bytes) with
+// 128-bit loads that bypass L1, keeping U chunks per channel in flight in a register ring -- the first U
+// are issued before griddepcontrol.wait, so under programmatic launch they overlap the previous kernel.
+// Activations come through the L1 read-only path (every warp of an SM reads the same M x K block).
+// Partials are reduced across the 32 lanes with halving butterflies.
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ldg_a(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Sum NV values (a power of two <= 32) over the 32 lanes: while more than one value is left, lanes OFF
+// apart trade halves; afterwards lane l holds the total of value (l * NV) >> 5, and lanes l with
+// l % (32 / NV) == 0 are the unique holders.
+template <int NV, int OFF, typename T>
+__device__ __forceinline__ void bfly32(T *v, int lane) {
+  if constexpr (OFF >= 1) {
+    if constexpr (NV > 1) {
+      constexpr int H = NV / 2;
+      const bool up = (lane & OFF) != 0;
+#pragma unroll
+      for (int i = 0; i < H; i++) {
+        const T send = up ? v[i] : v[i + H];
+        const T keep = up ? v[i + H] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+      }
+      bfly32<H, OFF / 2>(v, lane);
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], OFF);
+      bfly32<1, OFF / 2>(v, lane);
+    }
+  }
+}
+
+// acc[r*MT+m] += <activation row m at k of chunk `ch`, weight chunk of channel r>, activations read from
+// global memory (L1).
+template <int FMT, int MT, int CPW, typename T>
+__device__ __forceinline__ void mac_regs(const uint4 (&wv)[CPW], const uint8_t *__restrict__ a0, size_t a_row, int M,
+                                         T *acc, const Tables &tb) {
+  constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
+  uint32_t wx[NIB ? CPW : 1][8];
+  if constexpr (NIB) {
+#pragma unroll
+    for (int r = 0; r < CPW; r++) {
+      const uint32_t ww[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint2 e = expand8<FMT>(ww[q], tb);
+        wx[r][2 * q] = e.x;
+        wx[r][2 * q + 1] = e.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    if (m >= M) break;
+    const uint8_t *ar = a0 + (size_t)m * a_row;
+    if constexpr (FMT == FMT_I8) {
+      const uint4 a = ldg_a(ar);
+#pragma unroll
+      for (int r = 0; r < CPW; r++) {
+        T &c = acc[r * MT + m];
+        c = dp4a(a.x, wv[r].x, c);
+        c = dp4a(a.y, wv[r].y, c);
+        c = dp4a(a.z, wv[r].z, c);
+        c = dp4a(a.w, wv[r].w, c);
+      }
+    } else if constexpr (NIB) {
+      const uint4 x0 = ldg_a(ar), x1 = ldg_a(ar + 16);
+      const uint32_t aw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int r = 0; r < CPW; r++) {
+        T &c = acc[r * MT + m];
+#pragma unroll
+        for (int q = 0; q < 8; q++) c = dp4a(aw[q], wx[r][q], c);
+      }
+    } else {  // FMT_F16
+      const uint4 a = ldg_a(ar);
+      const __half2 *ah = reinterpret_cast<const __half2 *>(&a);
+      float2 af[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) af[q] = __half22float2(ah[q]);
+#pragma unroll
+      for (int r = 0; r < CPW; r++) {
+        const __half2 *wh = reinterpret_cast<const __half2 *>(&wv[r]);
+        T &c = acc[r * MT + m];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float2 wf = __half22float2(wh[q]);
+          c = fmaf(af[q].x, wf.x, c);
+          c = fmaf(af[q].y, wf.y, c);
+        }
+      }
+    }
+  }
+}
+
+constexpr int kDirectWarps = 8;
+
+template <int FMT, int MT, int CPW, int U>
+__global__ void __launch_bounds__(kDirectWarps * 32)
+gemv_direct_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M,
+                   int K, int N, Tables tb) {
+  using T = typename Acc<FMT>::T;
+  constexpr int V = CPW * MT;
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int lane = threadIdx.x & 31;
+  const int n0 = ((int)blockIdx.x * kDirectWarps + (int)(threadIdx.x >> 5)) * CPW;
+  const size_t rowB = (FMT == FMT_F16) ? (size_t)K * 2 : (FMT == FMT_I8) ? (size_t)K : (size_t)K / 2;
+  const size_t a_row = (FMT == FMT_F16) ? (size_t)K * 2 : (size_t)K;
+  const uint32_t a_k = (FMT == FMT_U4 || FMT == FMT_NF4) ? 2u : 1u;  // activation bytes per weight byte
+  const int nch = (int)(rowB / 16);
+  const bool active = n0 < N;
+  const uint8_t *wrow[CPW];
+#pragma unroll
+  for (int r = 0; r < CPW; r++) wrow[r] = W + (size_t)min(n0 + r, N - 1) * rowB;  // clamped rows read, unused
+
+  uint4 ring[U][CPW];
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+    const int ch = lane + 32 * u;
+#pragma unroll
+    for (int r = 0; r < CPW; r++)
+      if (active && ch < nch) ring[u][r] = ldg_stream(wrow[r] + (size_t)ch * 16);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!active) return;
+
+  T acc[V];
+#pragma unroll
+  for (int i = 0; i < V; i++) acc[i] = T(0);
+  for (int base = lane; base < nch; base += 32 * U) {
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int ch = base + 32 * u;
+      if (ch < nch) {
+        uint4 wv[CPW];
+#pragma unroll
+        for (int r = 0; r < CPW; r++) wv[r] = ring[u][r];
+        const int nx = ch + 32 * U;  // refill this slot with the chunk U steps ahead
+        if (nx < nch) {
+#pragma unroll
+          for (int r = 0; r < CPW; r++) ring[u][r] = ldg_stream(wrow[r] + (size_t)nx * 16);
+        }
+        mac_regs<FMT, MT, CPW, T>(wv, A + (size_t)ch * 16 * a_k, a_row, M, acc, tb);
+      }
+    }
+  }
+  bfly32<V, 16>(acc, lane);
+  if (lane % (32 / V) == 0) {
+    const int idx = (lane * V) >> 5, r = idx / MT, m = idx % MT;
+    if (m < M && n0 + r < N) reinterpret_cast<T *>(Cout)[(size_t)m * N + n0 + r] = acc[0];
+  }
+}
+
 struct Cfg {
   int mt, tr;
+  bool direct = false;  // the direct-load kernel (cpw channels per warp) instead of the staged one
+  int cpw = 2;
 };
 
-// Row tile: as many channels per CTA as keep the staged block <= 48 KB (several CTAs per SM, so the
-// next launch's copies overlap this one under PDL) while the grid still covers the 148 SMs twice.
-// The activations (M x K) are staged beside it.
+// Kernel and tile choice, measured on B200 over K in {2048, 6144, 8192}, N in {2048 .. 28672},
+// M in {1, 4, 8}, int8 / uniform int4 / NF4 (weights cycled through more than L2):
+// - the staged kernel with 8-channel CTAs (the smallest block, so the most CTAs share an SM and the
+//   next launch's copies overlap this one) is best or within ~5% on most shapes;
+// - the direct-load kernel wins where each staged CTA would carry a large activation block (M = 8 with
+//   K >= 8192: up to 2x), on nibble weights with short rows (K <= 2048, N <= 8192: 5-20%), and is the
+//   only one for rows that do not fit the staged kernel's shared memory (any K).
 Cfg choose(int fmt, int M, int K, int N) {
   Cfg c;
   c.mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
   const size_t rowB = fmt_row_bytes(fmt, K);
+  const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
   c.tr = 8;
-  for (int tr : {16, 32})
-    if ((size_t)tr * rowB <= 48 * 1024 && (N + tr - 1) / tr >= 2 * 148) c.tr = tr;
+  const bool staged_fits = rowB * 8 + (size_t)8 * K * (fmt == FMT_F16 ? 2 : 1) <= 196 * 1024;
+  if (!staged_fits || (c.mt == 8 && K >= 8192)) {
+    c.direct = true;
+    c.cpw = (!staged_fits || (c.mt == 8 && fmt != FMT_NF4)) ? 4 : 2;
+  } else if (nib && K <= 2048 && N <= 8192) {
+    c.direct = true;
+    c.cpw = 2;
+  }
+  if (const char *e = getenv("ORKB_GEMV_KIND")) c.direct = atoi(e) == 1 || !staged_fits;  // tuning overrides
+  if (const char *e = getenv("ORKB_GEMV_CPW")) {
+    const int v = atoi(e);
+    if (v == 1 || v == 2 || v == 4) c.cpw = v;
+  }
+  if (const char *e = getenv("ORKB_GEMV_TR")) {
+    const int v = atoi(e);
+    if ((v == 8 || v == 16 || v == 32) && (size_t)v * rowB + (size_t)c.mt * K * 2 <= 196 * 1024) c.tr = v;
+  }
   return c;
 }
 
@@ -482,10 +657,6 @@ cudaError_t dispatch_fmt(const RunArgs &a, const Cfg &c, const uint8_t *Ab, void
   return cudaErrorInvalidConfiguration;
 }
 
-uint32_t pack4(int a, int b, int c, int d) {
-  return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
-         ((uint32_t)(uint8_t)d << 24);
-}
 
 template <int FMT, int MT, int TR>
 cudaError_t launch_grouped_one(const GroupedArgs &a, const uint8_t *Ab, const float *aSb, float *Cb, int m,
@@ -530,13 +701,42 @@ cudaError_t dispatch_grouped(const GroupedArgs &a, int mt, int tr, const uint8_t
   return cudaErrorInvalidConfiguration;
 }
 
+template <int FMT, int MT, int CPW, int U>
+cudaError_t launch_direct(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cudaStream_t s, bool pdl,
+                          const Tables &tb) {
+  cudaLaunchConfig_t cfg = {};
+  const int warps = (a.N + CPW - 1) / CPW;
+  cfg.gridDim = dim3((warps + kDirectWarps - 1) / kDirectWarps);
+  cfg.blockDim = dim3(kDirectWarps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_direct_kernel<FMT, MT, CPW, U>, (const uint8_t *)a.W, Ab, Cb, m, a.K, a.N,
+                            tb);
+}
+
+template <int FMT>
+cudaError_t dispatch_direct(const RunArgs &a, int mt, int cpw, const uint8_t *Ab, void *Cb, int m, cudaStream_t s,
+                            bool pdl, const Tables &tb) {
+#define ORKB_GD_CASE(MT_, CPW_, U_) \
+  if (mt == MT_ && cpw == CPW_) return launch_direct<FMT, MT_, CPW_, U_>(a, Ab, Cb, m, s, pdl, tb);
+  ORKB_GD_CASE(1, 1, 8) ORKB_GD_CASE(1, 2, 4) ORKB_GD_CASE(1, 4, 2)
+  ORKB_GD_CASE(2, 1, 8) ORKB_GD_CASE(2, 2, 4) ORKB_GD_CASE(2, 4, 2)
+  ORKB_GD_CASE(4, 1, 4) ORKB_GD_CASE(4, 2, 4) ORKB_GD_CASE(4, 4, 2)
+  ORKB_GD_CASE(8, 1, 4) ORKB_GD_CASE(8, 2, 2) ORKB_GD_CASE(8, 4, 2)
+#undef ORKB_GD_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
 }  // namespace
 
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches) {
   if ((uintptr_t)a.W % 16 || (uintptr_t)a.A % 16) return cudaErrorMisalignedAddress;
-  const int8_t *L = kNf4Lut;
-  const Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
-                  pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const Tables tb = nf4_tables();
   const size_t a_row = (a.fmt == FMT_F16) ? (size_t)a.K * 2 : (size_t)a.K;
   const size_t c_row = (size_t)a.N * 4;
   for (int m0 = 0; m0 < a.M; m0 += 8) {
@@ -545,6 +745,18 @@ cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launche
     const uint8_t *Ab = (const uint8_t *)a.A + (size_t)m0 * a_row;
     void *Cb = (uint8_t *)a.C + (size_t)m0 * c_row;
     cudaError_t e;
+    if (c.direct) {
+      switch (a.fmt) {
+        case FMT_I8: e = dispatch_direct<FMT_I8>(a, c.mt, c.cpw, Ab, Cb, m, s, pdl, tb); break;
+        case FMT_U4: e = dispatch_direct<FMT_U4>(a, c.mt, c.cpw, Ab, Cb, m, s, pdl, tb); break;
+        case FMT_NF4: e = dispatch_direct<FMT_NF4>(a, c.mt, c.cpw, Ab, Cb, m, s, pdl, tb); break;
+        case FMT_F16: e = dispatch_direct<FMT_F16>(a, c.mt, c.cpw, Ab, Cb, m, s, pdl, tb); break;
+        default: return cudaErrorInvalidValue;
+      }
+      if (e != cudaSuccess) return e;
+      if (launches) ++*launches;
+      continue;
+    }
     switch (a.fmt) {
       case FMT_I8: e = dispatch_fmt<FMT_I8>(a, c, Ab, Cb, m, s, pdl, tb); break;
       case FMT_U4: e = dispatch_fmt<FMT_U4>(a, c, Ab, Cb, m, s, pdl, tb); break;
@@ -588,16 +800,16 @@ cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, 
   if ((uintptr_t)a.W % 16 || (uintptr_t)a.A % 16 || (uintptr_t)a.C % 4) return cudaErrorMisalignedAddress;
   if (!grouped_supports(a.fmt, a.K, a.G)) return cudaErrorInvalidValue;
   if ((size_t)a.K % 16) return cudaErrorMisalignedAddress;  // activation rows stay 16-byte aligned
-  const int8_t *L = kNf4Lut;
-  const Tables tb{pack4(-L[0], -L[1], -L[2], -L[3]), pack4(-L[4], -L[5], -L[6], -L[7]),
-                  pack4(L[8], L[9], L[10], L[11]), pack4(L[12], L[13], L[14], L[15])};
+  const Tables tb = nf4_tables();
   const int Sk = a.K / a.G;
   for (int m0 = 0; m0 < a.M; m0 += 8) {
     const int m = a.M - m0 < 8 ? a.M - m0 : 8;
     const int mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
-    int tr = 8;
+    int tr = 8;  // as the plain decode kernel: staged rows <= 48 KB so several CTAs share an SM
     for (int t : {16, 32})
-      if (grouped_smem(a.fmt, a.K, a.G, mt, t) <= 196 * 1024 && (a.N + t - 1) / t >= 2 * 148) tr = t;
+      if ((size_t)t * fmt_row_bytes(a.fmt, a.K) <= 48 * 1024 && grouped_smem(a.fmt, a.K, a.G, mt, t) <= 196 * 1024 &&
+          (a.N + t - 1) / t >= 2 * 148)
+        tr = t;
     const uint8_t *Ab = (const uint8_t *)a.A + (size_t)m0 * a.K;
     const float *aSb = a.aS + (size_t)m0 * Sk;
     float *Cb = a.C + (size_t)m0 * a.N;

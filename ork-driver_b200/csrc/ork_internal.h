@@ -35,12 +35,11 @@ struct RunArgs {
   int fmt;
 };
 
-// Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M). A CTA stages
-// 8 whole weight rows in shared memory, which bounds the row size (gemv_supports).
+// Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M). Two kernels:
+// staged (a CTA copies 8 whole weight rows into shared memory) and direct-load (a warp streams its rows
+// through registers); the direct one has no row-size limit, so every K is supported.
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
-inline bool gemv_supports(int fmt, int K) {  // 8 weight rows + up to 8 activation rows in shared memory
-  return fmt_row_bytes(fmt, K) * 8 + (size_t)8 * K * (fmt == FMT_F16 ? 2 : 1) <= 196 * 1024;
-}
+inline bool gemv_supports(int fmt, int K) { return K > 0 && fmt >= FMT_F16 && fmt <= FMT_NF4; }
 unsigned int gemv_error_flag(bool reset);
 
 // Grouped (per-K-group scaled) matmul, ork-driver src/npu/core/buf.c:501-520: C[m][n] fp32 = sum over

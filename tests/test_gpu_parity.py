@@ -406,3 +406,44 @@ def test_tensor_core_pair_tiles_exact(ctx, env_clean, pair, tn, sk):
         L.ork_b200_force_route(ctx.ctx, -1)
         for w in (w8, wn, wu, wh):
             w.free()
+
+
+@pytest.mark.parametrize("kind,cpw", [("staged", 0), ("direct", 1), ("direct", 2), ("direct", 4)])
+def test_decode_kernels_exact_all_formats(ctx, env_clean, kind, cpw):
+    """Both decode kernels, forced through the tuning variables, on every weight format and M = 1..8,
+    including a row far beyond the staged kernel's shared memory (K = 24576: always the direct kernel)."""
+    L = ork_b200.lib()
+    if kind == "direct":
+        env_clean.setenv("ORKB_GEMV_KIND", "1")
+        env_clean.setenv("ORKB_GEMV_CPW", str(cpw))
+    else:
+        env_clean.setenv("ORKB_GEMV_KIND", "0")
+    rng = np.random.default_rng(cpw + 40)
+    try:
+        assert L.ork_b200_force_route(ctx.ctx, 0) == 0
+        for K, N in ((2048, 96), (24576, 64)):
+            B = rand_i8(rng, (K, N))
+            f32 = rng.standard_normal((N, K), dtype=np.float32)
+            w8 = ctx.i8_pack(B)
+            wu, _ = ctx.i4a8_pack(f32)
+            env_clean.setenv("ORK_NF4", "1")
+            wn, _ = ctx.i4a8_pack(f32)
+            env_clean.delenv("ORK_NF4")
+            cu, _, _ = of.i4a8_blob_codes(wu.dump(), K, N)
+            cn, _, _ = of.i4a8_blob_codes(wn.dump(), K, N)
+            Bh = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+            wh = ctx.f16_pack(Bh)
+            try:
+                for M in (1, 2, 3, 5, 8, 11):
+                    A = rand_i8(rng, (M, K))
+                    for w, codes, tag in ((w8, B, "i8"), (wu, cu, "u4"), (wn, cn, "nf4")):
+                        rc, Cm = ctx.run(w, A)
+                        assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), (tag, K, M)
+                    Ah = rng.uniform(-1, 1, size=(M, K)).astype(np.float16)
+                    rc, Cm = ctx.run(wh, Ah)
+                    assert rc == 0 and np.abs(Cm - of.gemm_f16(Ah, Bh)).max() <= f16_tol(Ah, Bh), ("f16", K, M)
+            finally:
+                for w in (w8, wu, wn, wh):
+                    w.free()
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)

@@ -140,9 +140,11 @@ def test_loads_refuse_foreign_or_mismatched_blobs(ctx):
     assert not L.ork_i4a8_mm_load_tiled(ctx.ctx, K, N, _p(b8), b8.nbytes, 32)
 
 
-@pytest.mark.parametrize("G", [32, 128, 1024])
-def test_i4_grouped_exact(ctx, G):
-    K, N = 2048, 320
+@pytest.mark.parametrize("K,G", [(2048, 32), (2048, 128), (2048, 1024), (2016, 96), (3072, 384)])
+def test_i4_grouped_exact(ctx, K, G):
+    """Group sizes whose nibble bytes are one lane chunk (32), half a segment (128), several segments
+    (1024), straddle lane sets (96 -> 48 bytes) or segments (384 -> 192 bytes)."""
+    N = 320
     rng = np.random.default_rng(G)
     B = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
     w = ctx.i4_pack_grouped(B, G)
@@ -184,14 +186,14 @@ def test_i8_grouped_on_tiled_load_exact(ctx, G):
         w.free()
 
 
-@pytest.mark.parametrize("kind", ["i8", "nf4"])
+@pytest.mark.parametrize("kind", ["i8", "i8_g48", "nf4"])
 def test_set_group_on_int8_compute_weights(ctx, env_clean, kind):
-    K, N = 1024, 128
+    K, N = (1056, 128) if kind == "i8_g48" else (1024, 128)
     rng = np.random.default_rng(7)
-    if kind == "i8":
+    if kind.startswith("i8"):
         B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
         w = ctx.i8_pack(B)
-        codes_kn, G = B, 16
+        codes_kn, G = B, (48 if kind == "i8_g48" else 16)
     else:
         env_clean.setenv("ORK_NF4", "1")
         w, _ = ctx.i4a8_pack(rng.standard_normal((N, K), dtype=np.float32))
