@@ -685,6 +685,135 @@ def run_grouped(args):
     ctx.close()
 
 
+def run_moe(args):
+    """Batches of independent matmuls (ork_i8_mm_run_chain_async): an MoE decode layer of 64 experts, each a
+    2048 x 1408 w4a8 NF4 weight (ork_i4a8_mm_pack with ORK_NF4) seeing 1-4 tokens, as one batch; 4 distinct
+    expert sets (>= 180 MB of nibbles) cycle so no batch finds its weights in L2. value = algorithmic GB/s of
+    the batch (device-resident inputs, one CUDA graph per step, events); breakdown: the same 64 matmuls
+    issued as 64 separate ork_i8_mm_run_async launches; e2e: the synchronous ork_i8_mm_run_chain over host
+    buffers; cpu_baseline: the reference's own chain semantics (orki_cpu_gemm_i32 per task, oracle/_ref)."""
+    import torch
+
+    import ork_b200
+    from ork_b200 import TaskI8
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_ffi as of
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    ctx = ork_b200.Context()
+    L = ctx.L
+    stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+    E, K, N, NSET = 64, 2048, 1408, 4
+    rng = np.random.default_rng(99 + rank)
+    os.environ["ORK_NF4"] = "1"
+    sets, host = [], []
+    for si in range(NSET):
+        ws, tasks, keep = [], [], []
+        for e in range(E):
+            f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+            w, _ = ctx.i4a8_pack(f32)
+            M = 1 + (e * 7 + si) % 4
+            A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+            Cd = torch.empty((M, N), dtype=torch.int32, device="cuda")
+            ws.append(w)
+            keep += [A, Cd]
+            tasks.append(TaskI8(w.h, M, A.data_ptr(), Cd.data_ptr(), 0))
+            if si == 0:
+                codes, _, _ = of.i4a8_blob_codes(w.dump(), K, N)
+                host.append((w, M, A.cpu().numpy(), codes, Cd))
+        sets.append((ws, (TaskI8 * E)(*tasks), keep))
+    os.environ.pop("ORK_NF4", None)
+    step_bytes = sum(K * N // 2 + t.M * K + 4 * t.M * N for t in sets[0][1])
+
+    # correctness of the batched launch against the oracle, before timing
+    assert L.ork_i8_mm_run_chain_async(ctx.ctx, E, sets[0][1]) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    for w, M, A, codes, Cd in host:
+        assert np.array_equal(Cd.cpu().numpy(), of.gemm_i32(A, codes))
+
+    def graph(fn):
+        fn()
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        return g
+
+    def batched():
+        for ws, arr, _ in sets:
+            assert L.ork_i8_mm_run_chain_async(ctx.ctx, E, arr) == 0
+
+    def separate():
+        for ws, arr, _ in sets:
+            for t in arr:
+                assert L.ork_i8_mm_run_async(ctx.ctx, t.w, t.M, t.A, t.C) == 0
+
+    def timed(g, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / (reps * NSET)
+
+    gb, gs = graph(batched), graph(separate)
+    reps = max(1, args.steps // NSET)
+    with Clocks(local) as clk:
+        t_b = timed(gb, reps)
+    t_s = timed(gs, reps)
+    # e2e: the synchronous public call with host buffers (staged A in, C out, one launch for the batch)
+    hA = [np.ascontiguousarray(A) for _, _, A, _, _ in host]
+    hC = [np.zeros((M, N), np.int32) for _, M, _, _, _ in host]
+    harr = (TaskI8 * E)(*[TaskI8(w.h, M, a.ctypes.data, c.ctypes.data, 0)
+                          for (w, M, _, _, _), a, c in zip(host, hA, hC)])
+    t0 = time.perf_counter()
+    for _ in range(10):
+        assert L.ork_i8_mm_run_chain(ctx.ctx, E, harr) == 0
+    t_e2e = (time.perf_counter() - t0) / 10
+    hbm, _, src = peaks()
+    line = {"metric": "MoE batch (64 experts, w4a8 NF4 decode) algorithmic HBM GB/s", "value": step_bytes / t_b / 1e9 * world,
+            "unit": "GB/s", "n_gpus": world, "steps": reps * NSET, "warmup": 3, "ms_per_step": t_b * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"ork_i8_mm_run_chain(_async): {E} experts of K={K}, N={N} NF4 (ork_i4a8_mm_pack), "
+                                   "1-4 tokens each", "l2": f"{NSET} distinct expert sets cycled",
+                       "step_bytes": step_bytes, "parallelism": "replicas" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": step_bytes / t_b / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": step_bytes / t_b / 1e9 / hbm, "traffic": None, "kernel": "gemv_batched_kernel",
+                         "peak_source": src},
+            "e2e": {"value": step_bytes / t_e2e / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": int(sum(a.nbytes for a in hA)),
+                    "d2h_bytes_per_step": int(sum(c.nbytes for c in hC)), "ms_per_step": t_e2e * 1e3},
+            "breakdown": {"batched_one_launch_us": t_b * 1e6, "separate_64_launches_us": t_s * 1e6,
+                          "separate_GBs": step_bytes / t_s / 1e9},
+            "clocks": clk.summary(), "gpu_launches": int(reps * NSET)}
+    if rank == 0 and not args.no_cpu:
+        ref = of.reference()
+        fn = ref.ork_i8_mm_run_cpu if ref is not None else of.restated().orc_gemm_i32
+        Cm = [np.zeros((M, N), np.int32) for _, M, _, _, _ in host]
+        t0 = time.perf_counter()
+        for (w, M, A, codes, _), c in zip(host, Cm):
+            fn(M, K, N, of._p(A), of._p(np.ascontiguousarray(codes)), of._p(c))
+        tc = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": step_bytes / tc / 1e9, "unit": "GB/s", "cores": of.restated().orc_threads(),
+                                "kind": "reference" if ref is not None else "port",
+                                "sample": f"one batch of {E} expert matmuls on inflated int8 codes ({tc:.2f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del gb, gs
+    for ws, _, _ in sets:
+        for w in ws:
+            w.free()
+    ctx.close()
+
+
 def run_profile(spec):
     """`K,N,M[,route]`: one config, packed once, run 5 times with a synchronisation after each -- a small,
     self-contained workload for `ncu -k <kernel> -s <skip> -c <count>` captures -- then 50 back-to-back
@@ -757,9 +886,10 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
-    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped"],
+    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped", "moe"],
                     help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack; "
-                         "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack; grouped: grouped-scale W4A8 decode")
+                         "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack; grouped: grouped-scale W4A8 decode; "
+                         "moe: a batch of 64 NF4 expert matmuls through ork_i8_mm_run_chain")
     ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route[,fmt]]: run one config a few times eagerly (for ncu captures); fmt i8|u4|nf4")
@@ -775,6 +905,8 @@ def main():
         return run_qwen3(args)
     if args.workload == "grouped":
         return run_grouped(args)
+    if args.workload == "moe":
+        return run_moe(args)
 
     import torch
 

@@ -38,6 +38,11 @@ int ork_i4_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA,
 int ork_i8_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
                                 const float *dbScale, float *dC);
 
+/* ork_i8_mm_run_chain over device pointers (every A and C on the context's GPU), enqueued without waiting:
+ * the batch's decode-sized tasks go into one launch, as in the synchronous form. A task with a C row
+ * stride other than N must be decode-sized (M <= 8). Capturable in a CUDA graph. */
+int ork_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
+
 /* The load-time header check of the .orkpack loaders, callable without a device: 0 when `blob` is a
  * stamped blob of this build for (dtype, K, N), else ORK_PACKERR_SHORT / _UNSTAMPED / _FORMAT / _CAPS /
  * _SHAPE, checked in that order (ork-driver src/npu/core/packhdr.c). And the caps id this build stamps. */

@@ -166,6 +166,41 @@ int ork_i4_mm_run_grouped(ork_npu *ctx, ork_w *w, int M, const int8_t *A, const 
 int ork_i8_mm_run_grouped(ork_npu *ctx, ork_w *w, int M, const int8_t *A, const float *aScale,
                           const float *bScale, float *C);
 
+/* ---- batches of independent matmuls (ork-driver include/ork/dynamic.h:14-30, include/ork/chain.h:
+ * 110-120, include/ork/run.h:119-120) --------------------------------------------------------------- */
+
+/* include/ork/dynamic.h:14-28. One matmul of a batch: C = A . w with the run rules of ork_i8_mm_run /
+ * ork_i4_mm_run; cstride (int8 tasks) is C's row stride in elements, 0 = w's N. */
+typedef struct {
+  ork_w *w;
+  int M;
+  const int8_t *A;
+  int32_t *C;
+  int cstride;
+} ork_mm_task_i8;
+typedef struct {
+  ork_w *w;
+  int M;
+  const int8_t *A;
+  int32_t *C;
+} ork_mm_task_i4;
+/* include/ork/dynamic.h:30, include/ork/chain.h:120 (stream), :110 (int4 chain), include/ork/dynamic.h:33
+ * (experts; nc, the NPU core count, is ignored). Run S independent matmuls as one batch: decode-sized
+ * tasks (M <= 8) of one weight format share ONE kernel launch, larger tasks follow on the same stream;
+ * synchronous, every C complete on return. 0 ok; -1 on bad arguments (a NULL or wrong-dtype weight,
+ * M < 1, NULL A/C, cstride < N, A/C overlap) or a device error. S = 0 is a no-op. */
+int ork_i8_mm_run_chain(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
+int ork_i8_mm_run_stream(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
+int ork_i4_mm_run_chain(ork_npu *ctx, int S, const ork_mm_task_i4 *tasks);
+int ork_i4_mm_run_experts(ork_npu *ctx, const ork_mm_task_i4 *ex, int ntask, int nc);
+/* include/ork/run.h:119-120. Asynchronous submit of one matmul (any weight dtype; A int8/int4 or fp16 as
+ * the weight's run function takes, copied at submit) into a ring of 8 in-flight slots; returns a ticket
+ * >= 0, or -1 when the arguments are bad or all slots are in flight (collect first). ork_mm_collect waits
+ * for that ticket's matmul, writes C (int32 or fp32 [M][N]) and frees the slot: 0 ok, -1 for an unknown or
+ * already collected ticket or a device error. */
+int ork_mm_submit(ork_npu *ctx, ork_w *w, int M, const void *A);
+int ork_mm_collect(ork_npu *ctx, int ticket, void *C);
+
 /* include/ork/weights.h:141. Frees a weight's host bookkeeping. Unlike the reference (which leaves the
  * NPU window to teardown), device memory is released here as well: HBM has no IOVA window to protect. */
 void ork_w_free(ork_w *w);

@@ -114,10 +114,6 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
   return w;
 }
 
-}  // namespace orkb
-
-namespace {
-
 // Launch one matmul on device buffers (A, C already on the context's GPU).
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
   RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt};
@@ -135,6 +131,10 @@ int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
   }
   return 0;
 }
+
+}  // namespace orkb
+
+namespace {
 
 // The synchronous run shared by the three public run functions.
 int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype, const char *name) {
@@ -225,6 +225,7 @@ void ork_npu_free(ork_npu *c) {
     if (c->dA) cudaFree(c->dA);
     if (c->dC) cudaFree(c->dC);
     if (c->dS) cudaFree(c->dS);
+    ring_free(c);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;

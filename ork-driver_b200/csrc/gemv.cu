@@ -163,10 +163,12 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], uint32_t sa, ui
 }
 
 // TR channels per CTA (8 per warp-row group), WK = 4 / (TR / 8) warps split K.
+// One CTA's work of the staged kernel: channels [n0, n0 + TR) of the weight at W (N channels of K), the
+// activations A (M rows), C rows at a stride of cstride elements.
 template <int FMT, int MT, int TR>
-__global__ void __launch_bounds__(kWarps * 32)
-gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M, int K,
-            int N, Tables tb) {
+__device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A,
+                                           void *__restrict__ Cout, int M, int K, int N, int n0, int cstride,
+                                           const Tables &tb) {
   using T = typename Acc<FMT>::T;
   constexpr int WR = TR / (4 * kR);  // warp-row groups
   constexpr int WK = kWarps / WR;    // warps splitting K
@@ -180,7 +182,6 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 3, j = lane & 7;
   const int wr = warp / WK, wk = warp % WK;
-  const int n0 = blockIdx.x * TR;
   const int rows = min(TR, N - n0);
   const size_t rowB = (FMT == FMT_F16) ? (size_t)K * 2 : (FMT == FMT_I8) ? (size_t)K : (size_t)K / 2;
   const size_t a_row = (FMT == FMT_F16) ? (size_t)K * 2 : (size_t)K;
@@ -254,7 +255,7 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
       for (int i = 0; i < HELD; i++) {
         const int idx = base + i, r = idx / MT, m = idx % MT;
         const int lr = lrow0 + 4 * r;
-        if (m < M && lr < rows) C[(size_t)m * N + n0 + lr] = acc[i];
+        if (m < M && lr < rows) C[(size_t)m * cstride + n0 + lr] = acc[i];
       }
     }
   } else {
@@ -272,10 +273,45 @@ gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *
         T s = red[0][lr][m];
 #pragma unroll
         for (int q = 1; q < WK; q++) s += red[q][lr][m];
-        C[(size_t)m * N + n0 + lr] = s;
+        C[(size_t)m * cstride + n0 + lr] = s;
       }
     }
   }
+}
+
+template <int FMT, int MT, int TR>
+__global__ void __launch_bounds__(kWarps * 32)
+gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M, int K,
+            int N, Tables tb) {
+  gemv_block<FMT, MT, TR>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb);
+}
+
+// Batched (chain / MoE) variant: many independent matmuls of one weight format in one launch. Task t
+// owns CTAs [block0[t], block0[t + 1]); each CTA finds its task by binary search and runs the staged
+// kernel's block for it. The task table travels as a kernel parameter.
+constexpr int kMaxBatch = 96;
+struct BatchTask {
+  const uint8_t *W;
+  const uint8_t *A;
+  void *C;
+  int M, K, N, cstride, block0;
+};
+struct BatchTable {
+  BatchTask t[kMaxBatch];
+  int n;
+};
+
+template <int FMT, int MT, int TR>
+__global__ void __launch_bounds__(kWarps * 32) gemv_batched_kernel(const __grid_constant__ BatchTable bt, Tables tb) {
+  int lo = 0, hi = bt.n - 1;
+  const int b = (int)blockIdx.x;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (bt.t[mid].block0 <= b) lo = mid;
+    else hi = mid - 1;
+  }
+  const BatchTask &t = bt.t[lo];
+  gemv_block<FMT, MT, TR>(t.W, t.A, t.C, t.M, t.K, t.N, (b - t.block0) * TR, t.cstride, tb);
 }
 
 // Grouped variant (per-K-group scales): same staging and arithmetic as gemv_kernel, but each warp walks
@@ -732,6 +768,40 @@ cudaError_t dispatch_direct(const RunArgs &a, int mt, int cpw, const uint8_t *Ab
   return cudaErrorInvalidConfiguration;
 }
 
+template <int FMT, int MT>
+cudaError_t launch_batched_one(const BatchTable &bt, int blocks, size_t smem, cudaStream_t s, bool pdl,
+                               const Tables &tb) {
+  auto kern = gemv_batched_kernel<FMT, MT, 8>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, bt, tb);
+}
+
+template <int FMT>
+cudaError_t dispatch_batched(const BatchTable &bt, int mt, int blocks, size_t smem, cudaStream_t s, bool pdl,
+                             const Tables &tb) {
+  switch (mt) {
+    case 1: return launch_batched_one<FMT, 1>(bt, blocks, smem, s, pdl, tb);
+    case 2: return launch_batched_one<FMT, 2>(bt, blocks, smem, s, pdl, tb);
+    case 4: return launch_batched_one<FMT, 4>(bt, blocks, smem, s, pdl, tb);
+    default: return launch_batched_one<FMT, 8>(bt, blocks, smem, s, pdl, tb);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches) {
@@ -818,6 +888,48 @@ cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, 
       case FMT_I8: e = dispatch_grouped<FMT_I8>(a, mt, tr, Ab, aSb, Cb, m, s, pdl, tb); break;
       case FMT_U4: e = dispatch_grouped<FMT_U4>(a, mt, tr, Ab, aSb, Cb, m, s, pdl, tb); break;
       case FMT_NF4: e = dispatch_grouped<FMT_NF4>(a, mt, tr, Ab, aSb, Cb, m, s, pdl, tb); break;
+      default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+    if (launches) ++*launches;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace orkb
+
+namespace orkb {
+
+bool batched_supports(int fmt, int M, int K) {
+  return M >= 1 && M <= 8 && K > 0 && fmt_row_bytes(fmt, K) * 8 + (size_t)M * K * (fmt == FMT_F16 ? 2 : 1) <= 196 * 1024;
+}
+
+cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool pdl, int *launches) {
+  const Tables tb = nf4_tables();
+  for (int i0 = 0; i0 < n; i0 += kMaxBatch) {
+    const int cnt = n - i0 < kMaxBatch ? n - i0 : kMaxBatch;
+    BatchTable bt;
+    bt.n = cnt;
+    int blocks = 0, mmax = 1;
+    size_t smem = 0;
+    const int fmt = t[i0].fmt;
+    for (int j = 0; j < cnt; j++) {
+      const ChainTask &c = t[i0 + j];
+      if (c.fmt != fmt || !batched_supports(c.fmt, c.M, c.K)) return cudaErrorInvalidValue;
+      if ((uintptr_t)c.W % 16 || (uintptr_t)c.A % 16) return cudaErrorMisalignedAddress;
+      bt.t[j] = BatchTask{(const uint8_t *)c.W, (const uint8_t *)c.A, c.C, c.M, c.K, c.N, c.cstride, blocks};
+      blocks += (c.N + 7) / 8;
+      mmax = c.M > mmax ? c.M : mmax;
+      const size_t sm = fmt_row_bytes(c.fmt, c.K) * 8 + (size_t)c.M * c.K * (c.fmt == FMT_F16 ? 2 : 1);
+      smem = sm > smem ? sm : smem;
+    }
+    const int mt = mmax <= 1 ? 1 : mmax <= 2 ? 2 : mmax <= 4 ? 4 : 8;
+    cudaError_t e;
+    switch (fmt) {
+      case FMT_I8: e = dispatch_batched<FMT_I8>(bt, mt, blocks, smem, s, pdl, tb); break;
+      case FMT_U4: e = dispatch_batched<FMT_U4>(bt, mt, blocks, smem, s, pdl, tb); break;
+      case FMT_NF4: e = dispatch_batched<FMT_NF4>(bt, mt, blocks, smem, s, pdl, tb); break;
+      case FMT_F16: e = dispatch_batched<FMT_F16>(bt, mt, blocks, smem, s, pdl, tb); break;
       default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;

@@ -55,6 +55,18 @@ struct GroupedArgs {
   int M, K, N, fmt, G;
 };
 cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, int *launches);
+
+// Batched decode: independent matmuls of one weight format in one launch of the staged decode kernel
+// (the chain / MoE entry points); each task M <= 8 with rows that fit the staged kernel
+// (batched_supports). C of task t is written at a row stride of cstride elements.
+struct ChainTask {
+  const void *W;
+  const void *A;
+  void *C;
+  int M, K, N, cstride, fmt;
+};
+bool batched_supports(int fmt, int M, int K);
+cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool pdl, int *launches);
 bool grouped_supports(int fmt, int K, int G);
 
 // Tensor-core path (tcgen05). Returns cudaErrorNotSupported when the shape/format has no TC kernel.

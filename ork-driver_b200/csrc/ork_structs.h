@@ -18,6 +18,7 @@ struct ork_npu {
   size_t capC = 0;
   void *dS = nullptr;  // staging for the scale tables of grouped runs
   size_t capS = 0;
+  void *ring = nullptr;  // in-flight slots of ork_mm_submit / ork_mm_collect (chain.cpp)
   bool pdl = true;
   int force_route = -1;
   uint64_t launches = 0;
@@ -54,6 +55,10 @@ bool grow(void **p, size_t *cap, size_t need);
 // Memory of the context's GPU (or managed memory) that a kernel can use in place.
 bool is_device_ptr(const void *p, int device);
 bool overlaps(const void *a, size_t an, const void *b, size_t bn);
+// Releases the ork_mm_submit ring of a context (chain.cpp).
+void ring_free(ork_npu *c);
+// Launch one matmul on device buffers of the context's GPU (the route of route_for); 0 or -1.
+int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC);
 // A new resident weight: device memory of `bytes`, filled from host memory in the resident format.
 ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host_resident, size_t bytes);
 }  // namespace orkb

@@ -64,6 +64,13 @@ SIGNATURES = [
     ("ork_i8_mm_run_grouped", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     ("ork_i4_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     ("ork_i8_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_i8_mm_run_chain", _i, [_vp, _i, _vp]),
+    ("ork_i8_mm_run_stream", _i, [_vp, _i, _vp]),
+    ("ork_i8_mm_run_chain_async", _i, [_vp, _i, _vp]),
+    ("ork_i4_mm_run_chain", _i, [_vp, _i, _vp]),
+    ("ork_i4_mm_run_experts", _i, [_vp, _vp, _i, _i]),
+    ("ork_mm_submit", _i, [_vp, _vp, _i, _vp]),
+    ("ork_mm_collect", _i, [_vp, _i, _vp]),
     ("ork_b200_pack_check", _i, [_vp, _sz, _i, _i, _i]),
     ("ork_b200_pack_capid", C.c_uint32, []),
     ("ork_b200_sync", _i, [_vp]),
@@ -208,6 +215,16 @@ class Context:
 
     def launches(self):
         return int(self.L.ork_b200_launches(self.ctx))
+
+
+class TaskI8(C.Structure):
+    """ork_mm_task_i8 (include/ork_npu.h)."""
+    _fields_ = [("w", C.c_void_p), ("M", C.c_int), ("A", C.c_void_p), ("C", C.c_void_p), ("cstride", C.c_int)]
+
+
+class TaskI4(C.Structure):
+    """ork_mm_task_i4 (include/ork_npu.h)."""
+    _fields_ = [("w", C.c_void_p), ("M", C.c_int), ("A", C.c_void_p), ("C", C.c_void_p)]
 
 
 class Weight:
