@@ -379,3 +379,136 @@ ORC_API int orc_threads(void)
     return 1;
 #endif
 }
+
+/* ---------------------------------------------------------------------------------------------------
+ * Whole decode layer. src/npu/i8/chain.c:106-122 (ork_i8_mm_layer, direct path) over the glue kernels of
+ * src/spine_kernels.h:19-38, restated: RMSNorm y = x * (1/sqrtf(sum(x^2)/D + eps)) * g (sum sequential);
+ * per-tensor int8 quantization s = 127 / max(1e-6, max|x|), q = clamp(lrintf(x*s), +-127), dequant int32/s;
+ * RoPE NeoX on pairs (i, i+D/2), theta = pos * powf(base, -2i/D); M = 1 attention with a running max,
+ * exp-sum and sequential weighted sum; SwiGLU silu(g) * u with silu(g) = g / (1 + expf(-g)). The k and v
+ * projections are computed as in the reference; kv_ext (this library's decode extension) additionally
+ * normalises + rotates the token's k (k_norm may be NULL), writes k and v at slot nkv of the caches
+ * (head stride `hstride` tokens) and attends over nkv + 1 keys. dims = {D, H, Hkv, dk, dv, Nff, nkv, pos}.
+ * Weights are int8 codes B [K][N] row-major. */
+static void orc_rms(const float *x, const float *g, int n, float *y)
+{
+    float ss = 0.0f;
+    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    const float r = 1.0f / sqrtf(ss / n + 1e-6f);
+    for (int i = 0; i < n; i++) y[i] = x[i] * r * g[i];
+}
+
+static float orc_q8(const float *x, int n, int8_t *q)
+{
+    float mx = 1e-6f;
+    for (int i = 0; i < n; i++) {
+        const float a = fabsf(x[i]);
+        if (a > mx) mx = a;
+    }
+    const float s = 127.0f / mx;
+    for (int i = 0; i < n; i++) {
+        const int v = (int)lrintf(x[i] * s);
+        q[i] = (int8_t)(v > 127 ? 127 : (v < -127 ? -127 : v));
+    }
+    return s;
+}
+
+static void orc_rope(float *x, int n, int pos, float base)
+{
+    const int h = n / 2;
+    for (int i = 0; i < h; i++) {
+        const float th = pos * powf(base, -2.0f * i / n), c = cosf(th), s = sinf(th);
+        const float a = x[i], b = x[i + h];
+        x[i] = a * c - b * s;
+        x[i + h] = a * s + b * c;
+    }
+}
+
+static void orc_attn1(const float *q, const float *Kh, const float *Vh, int nk, int dk, int dv, float scale, float *o)
+{
+    float *s = malloc((size_t)nk * sizeof *s);
+    float mx = -1e30f;
+    for (int j = 0; j < nk; j++) {
+        float a = 0.0f;
+        for (int d = 0; d < dk; d++) a += q[d] * Kh[(size_t)j * dk + d];
+        s[j] = a * scale;
+        if (s[j] > mx) mx = s[j];
+    }
+    float z = 0.0f;
+    for (int j = 0; j < nk; j++) {
+        s[j] = expf(s[j] - mx);
+        z += s[j];
+    }
+    for (int d = 0; d < dv; d++) {
+        float acc = 0.0f;
+        for (int j = 0; j < nk; j++) acc += s[j] * Vh[(size_t)j * dv + d];
+        o[d] = acc / z;
+    }
+    free(s);
+}
+
+static void orc_gemv1(int K, int N, const int8_t *a, const int8_t *B, int32_t *c) { orc_gemm_i32(1, K, N, a, B, c); }
+
+ORC_API int orc_layer_i8(const uint32_t *dm, double attn_scale, double rope_base, const int8_t *Bq, const int8_t *Bk,
+                         const int8_t *Bv, const int8_t *Bo, const int8_t *Bg, const int8_t *Bu, const int8_t *Bd,
+                         const float *attn_norm, const float *q_norm, const float *ffn_norm, const float *x,
+                         float *Kc, float *Vc, float *x_out, int kv_ext, const float *k_norm, int hstride)
+{
+    const int D = (int)dm[0], H = (int)dm[1], Hkv = (int)dm[2], dk = (int)dm[3], dv = (int)dm[4], F = (int)dm[5],
+              nkv = (int)dm[6], pos = (int)dm[7];
+    if (dk != dv || Hkv < 1 || H % Hkv) return -3;
+    const int Nq = H * dk, Nk = Hkv * dk, grp = H / Hkv, hs = kv_ext ? hstride : nkv;
+    int32_t *cq = malloc((size_t)Nq * 4), *ck = malloc((size_t)Nk * 4), *cv = malloc((size_t)Nk * 4),
+            *co = malloc((size_t)D * 4), *cg = malloc((size_t)F * 4), *cu = malloc((size_t)F * 4),
+            *cd = malloc((size_t)D * 4);
+    int8_t *a8 = malloc((size_t)(Nq > F ? (Nq > D ? Nq : D) : (F > D ? F : D)));
+    float *t = malloc((size_t)D * 4), *qf = malloc((size_t)Nq * 4), *ao = malloc((size_t)Nq * 4),
+          *x1 = malloc((size_t)D * 4), *g = malloc((size_t)F * 4), *u = malloc((size_t)F * 4),
+          *kf = malloc((size_t)dk * 4);
+    int rc = -1;
+    if (cq && ck && cv && co && cg && cu && cd && a8 && t && qf && ao && x1 && g && u && kf) {
+        orc_rms(x, attn_norm, D, t);
+        const float sx = orc_q8(t, D, a8);
+        orc_gemv1(D, Nq, a8, Bq, cq);
+        orc_gemv1(D, Nk, a8, Bk, ck);
+        orc_gemv1(D, Nk, a8, Bv, cv);
+        if (kv_ext) {  /* the token's own k (normed, rotated) and v join the caches at slot nkv */
+            for (int hk = 0; hk < Hkv; hk++) {
+                for (int d = 0; d < dk; d++) kf[d] = ck[hk * dk + d] / sx;
+                if (k_norm) orc_rms(kf, k_norm, dk, kf);
+                orc_rope(kf, dk, pos, (float)rope_base);
+                for (int d = 0; d < dk; d++) {
+                    Kc[((size_t)hk * hs + nkv) * dk + d] = kf[d];
+                    Vc[((size_t)hk * hs + nkv) * dv + d] = cv[hk * dk + d] / sx;
+                }
+            }
+        }
+        const int nk = kv_ext ? nkv + 1 : nkv;
+        for (int i = 0; i < Nq; i++) qf[i] = cq[i] / sx;
+        for (int h = 0; h < H; h++) {
+            float *qh = qf + (size_t)h * dk;
+            orc_rms(qh, q_norm, dk, qh);
+            orc_rope(qh, dk, pos, (float)rope_base);
+            orc_attn1(qh, Kc + (size_t)(h / grp) * hs * dk, Vc + (size_t)(h / grp) * hs * dv, nk, dk, dv,
+                      (float)attn_scale, ao + (size_t)h * dv);
+        }
+        const float sa = orc_q8(ao, Nq, a8);
+        orc_gemv1(Nq, D, a8, Bo, co);
+        for (int i = 0; i < D; i++) x1[i] = x[i] + co[i] / sa;
+        orc_rms(x1, ffn_norm, D, t);
+        const float sf = orc_q8(t, D, a8);
+        orc_gemv1(D, F, a8, Bg, cg);
+        orc_gemv1(D, F, a8, Bu, cu);
+        for (int i = 0; i < F; i++) {
+            const float gi = cg[i] / sf, ui = cu[i] / sf;
+            g[i] = (gi / (1.0f + expf(-gi))) * ui;
+        }
+        const float sg = orc_q8(g, F, a8);
+        orc_gemv1(F, D, a8, Bd, cd);
+        for (int i = 0; i < D; i++) x_out[i] = x1[i] + cd[i] / sg;
+        rc = 0;
+    }
+    free(cq); free(ck); free(cv); free(co); free(cg); free(cu); free(cd);
+    free(a8); free(t); free(qf); free(ao); free(x1); free(g); free(u); free(kf);
+    return rc;
+}

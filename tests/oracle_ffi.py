@@ -45,6 +45,9 @@ def restated():
         lib.orc_gen_rnd_f16.argtypes = [C.POINTER(C.c_uint32), C.c_void_p, C.c_size_t]
         lib.orc_nf4_lut.argtypes = [C.c_void_p]
         lib.orc_threads.restype = C.c_int
+        lib.orc_layer_i8.restype = C.c_int
+        lib.orc_layer_i8.argtypes = [C.c_void_p, C.c_double, C.c_double] + [C.c_void_p] * 7 + [C.c_void_p] * 7 + \
+            [C.c_int, C.c_void_p, C.c_int]
         lib.orc_gemm_grouped.restype = C.c_int
         lib.orc_gemm_grouped.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_void_p]
@@ -101,6 +104,8 @@ def reference():
         lib.ork_i4a8_mm_load_tiled.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_int]
         lib.orki_pack_check.restype = C.c_int
         lib.orki_pack_check.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int]
+        lib.ref_layer_i8.restype = C.c_int
+        lib.ref_layer_i8.argtypes = [C.c_void_p, C.c_double, C.c_double] + [C.c_void_p] * 7 + [C.c_void_p] * 7
         lib.orki_pack_capid.restype = C.c_uint
         lib.orki_pack_capid.argtypes = [C.c_void_p]
         _reference = lib
@@ -159,6 +164,41 @@ def gemm_grouped(A, B_kn, G, aS, bS):
     Cm = np.empty((M, N), np.float32)
     assert restated().orc_gemm_grouped(M, K, N, G, _p(A), _p(B_kn), _p(aS), _p(bS), _p(Cm)) == 0
     return Cm
+
+
+LAYER_KEYS = ("D", "H", "Hkv", "dk", "dv", "Nff", "nkv", "pos")
+
+
+def layer_inputs(seed, D, H, Hkv, dk, Nff, nkv, pos, hstride=None):
+    """Seeded inputs of one decode layer: weight codes B [K][N] (q, k, v, o, gate, up, down), norm gains,
+    x, and K/V caches [Hkv][hstride][dk] (hstride >= nkv + 1 leaves room for the token's own k/v)."""
+    rng = np.random.default_rng(seed)
+    Nq, Nk = H * dk, Hkv * dk
+    shapes = [(D, Nq), (D, Nk), (D, Nk), (Nq, D), (D, Nff), (D, Nff), (Nff, D)]
+    Bs = [rng.integers(-127, 128, size=s, dtype=np.int8) for s in shapes]
+    norms = [rng.uniform(0.5, 1.5, size=n).astype(np.float32) for n in (D, dk, D, dk)]  # attn, q, ffn, k
+    x = rng.standard_normal(D).astype(np.float32)
+    hs = hstride or nkv
+    Kc = np.zeros((Hkv, hs, dk), np.float32)
+    Vc = np.zeros((Hkv, hs, dk), np.float32)
+    Kc[:, :nkv] = rng.standard_normal((Hkv, nkv, dk)).astype(np.float32)
+    Vc[:, :nkv] = rng.standard_normal((Hkv, nkv, dk)).astype(np.float32)
+    return Bs, norms, x, Kc, Vc
+
+
+def layer(dims, attn_scale, rope_base, Bs, norms, x, Kc, Vc, kv_ext=False, hstride=0, k_norm=True):
+    """The restated decode layer (src/npu/i8/chain.c:106-122); with kv_ext the token's k/v are written into
+    copies of the caches at slot nkv first. Returns (x_out, Kc, Vc)."""
+    dm = np.array([dims[k] for k in LAYER_KEYS], np.uint32)
+    Kc, Vc = Kc.copy(), Vc.copy()
+    out = np.zeros(dims["D"], np.float32)
+    Bs = [np.ascontiguousarray(b) for b in Bs]
+    kn = norms[3] if k_norm else None
+    rc = restated().orc_layer_i8(_p(dm), attn_scale, rope_base, *[_p(b) for b in Bs], _p(norms[0]), _p(norms[1]),
+                                 _p(norms[2]), _p(x), _p(Kc), _p(Vc), _p(out), int(kv_ext),
+                                 None if kn is None else _p(kn), hstride)
+    assert rc == 0
+    return out, Kc, Vc
 
 
 def i8_quant_f32(f32_nk):
