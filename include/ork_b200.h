@@ -43,6 +43,26 @@ int ork_i8_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA,
  * stride other than N must be decode-sized (M <= 8). Capturable in a CUDA graph. */
 int ork_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
 
+/* ork_i8_mm_layer over device pointers, enqueued without waiting (the first layer call on a context
+ * allocates its workspace: make one before capturing a CUDA graph), with an optional decode extension:
+ *   k_norm   RMSNorm gain applied to the token's k per head (Qwen3's k-norm; NULL: none);
+ *   append   non-zero: the token's k (dequantized, k-normed, rotated at pos) and v are written into Kc / Vc
+ *            at slot nkv of each kv head, and attention covers nkv + 1 keys (the token attends to itself);
+ *   hstride  kv-head stride of the caches in tokens (their capacity; 0 = nkv);
+ *   dpos     non-NULL: pos and nkv are both read from this device int when the kernels run (cached tokens
+ *            = position of the token), so a captured CUDA graph replays across decode steps.
+ * kv = NULL is ork_i8_mm_layer's behaviour. Same return codes. */
+typedef struct ork_b200_layer_kv {
+  const float *k_norm;
+  int append;
+  int hstride;
+  const int *dpos;
+} ork_b200_layer_kv;
+int ork_i8_mm_layer_async(ork_npu *ctx, const struct ork_layer_dims *d, ork_w *wq, ork_w *wk, ork_w *wv, ork_w *wo,
+                          ork_w *wg, ork_w *wu, ork_w *wd, const float *attn_norm, const float *q_norm,
+                          const float *ffn_norm, const float *x, float *Kc, float *Vc, float *x_out,
+                          const ork_b200_layer_kv *kv);
+
 /* The load-time header check of the .orkpack loaders, callable without a device: 0 when `blob` is a
  * stamped blob of this build for (dtype, K, N), else ORK_PACKERR_SHORT / _UNSTAMPED / _FORMAT / _CAPS /
  * _SHAPE, checked in that order (ork-driver src/npu/core/packhdr.c). And the caps id this build stamps. */

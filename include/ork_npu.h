@@ -201,6 +201,23 @@ int ork_i4_mm_run_experts(ork_npu *ctx, const ork_mm_task_i4 *ex, int ntask, int
 int ork_mm_submit(ork_npu *ctx, ork_w *w, int M, const void *A);
 int ork_mm_collect(ork_npu *ctx, int ticket, void *C);
 
+/* include/ork/chain.h:105-110. One decode token through a Llama/Qwen-style layer: x fp32 [D] ->
+ * RMSNorm(attn_norm) -> per-tensor int8 -> q, k, v projections -> per head: RMSNorm(q_norm), RoPE NeoX at
+ * `pos` (base rope_base), attention over the nkv cached keys/values (Kc, Vc fp32 [Hkv][nkv][dk], grouped
+ * query heads) -> int8 -> o projection -> residual -> RMSNorm(ffn_norm) -> int8 -> gate, up -> SwiGLU ->
+ * int8 -> down -> residual = x_out [D]. The arithmetic of src/npu/i8/chain.c:106-122 with the glue of
+ * src/spine_kernels.h; the k and v projections are computed as in the reference but the caches are only
+ * read (see ork_i8_mm_layer_async in ork_b200.h for the appending form). Weights: int8-compute weights
+ * (wq D x H*dk, wk / wv D x Hkv*dk, wo H*dk x D, wg / wu D x Nff, wd Nff x D). dv must equal dk. Host or
+ * device pointers; synchronous. 0 ok, -3 on bad arguments or shapes, -1 on a device error. */
+struct ork_layer_dims {
+  uint32_t D, H, Hkv, dk, dv, Nff, nkv, pos;
+  double attn_scale, rope_base;
+};
+int ork_i8_mm_layer(ork_npu *ctx, const struct ork_layer_dims *d, ork_w *wq, ork_w *wk, ork_w *wv, ork_w *wo,
+                    ork_w *wg, ork_w *wu, ork_w *wd, const float *attn_norm, const float *q_norm,
+                    const float *ffn_norm, const float *x, const float *Kc, const float *Vc, float *x_out);
+
 /* include/ork/weights.h:141. Frees a weight's host bookkeeping. Unlike the reference (which leaves the
  * NPU window to teardown), device memory is released here as well: HBM has no IOVA window to protect. */
 void ork_w_free(ork_w *w);

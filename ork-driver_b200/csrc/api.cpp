@@ -226,6 +226,7 @@ void ork_npu_free(ork_npu *c) {
     if (c->dC) cudaFree(c->dC);
     if (c->dS) cudaFree(c->dS);
     ring_free(c);
+    if (c->dL) cudaFree(c->dL);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "ork_internal.h"
+#include "ork_b200.h"
 
 struct ork_npu {
   int device = 0;
@@ -19,6 +20,8 @@ struct ork_npu {
   void *dS = nullptr;  // staging for the scale tables of grouped runs
   size_t capS = 0;
   void *ring = nullptr;  // in-flight slots of ork_mm_submit / ork_mm_collect (chain.cpp)
+  void *dL = nullptr;    // workspace of the decode layer (layer.cu)
+  size_t capL = 0;
   bool pdl = true;
   int force_route = -1;
   uint64_t launches = 0;
@@ -55,6 +58,10 @@ bool grow(void **p, size_t *cap, size_t need);
 // Memory of the context's GPU (or managed memory) that a kernel can use in place.
 bool is_device_ptr(const void *p, int device);
 bool overlaps(const void *a, size_t an, const void *b, size_t bn);
+// Enqueues one decode layer on device pointers (layer.cu); W = {q, k, v, o, gate, up, down}.
+int layer_enqueue(ork_npu *c, const struct ork_layer_dims *d, ork_w *const *W, const float *attn_norm,
+                  const float *q_norm, const float *ffn_norm, const float *x, const float *Kc, const float *Vc,
+                  float *x_out, const struct ork_b200_layer_kv *kv);
 // Releases the ork_mm_submit ring of a context (chain.cpp).
 void ring_free(ork_npu *c);
 // Launch one matmul on device buffers of the context's GPU (the route of route_for); 0 or -1.

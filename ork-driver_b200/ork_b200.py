@@ -71,6 +71,8 @@ SIGNATURES = [
     ("ork_i4_mm_run_experts", _i, [_vp, _vp, _i, _i]),
     ("ork_mm_submit", _i, [_vp, _vp, _i, _vp]),
     ("ork_mm_collect", _i, [_vp, _i, _vp]),
+    ("ork_i8_mm_layer", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7),
+    ("ork_i8_mm_layer_async", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7 + [_vp]),
     ("ork_b200_pack_check", _i, [_vp, _sz, _i, _i, _i]),
     ("ork_b200_pack_capid", C.c_uint32, []),
     ("ork_b200_sync", _i, [_vp]),
@@ -225,6 +227,17 @@ class TaskI8(C.Structure):
 class TaskI4(C.Structure):
     """ork_mm_task_i4 (include/ork_npu.h)."""
     _fields_ = [("w", C.c_void_p), ("M", C.c_int), ("A", C.c_void_p), ("C", C.c_void_p)]
+
+
+class LayerDims(C.Structure):
+    """struct ork_layer_dims (include/ork_npu.h)."""
+    _fields_ = [(k, C.c_uint32) for k in ("D", "H", "Hkv", "dk", "dv", "Nff", "nkv", "pos")] + \
+        [("attn_scale", C.c_double), ("rope_base", C.c_double)]
+
+
+class LayerKV(C.Structure):
+    """ork_b200_layer_kv (include/ork_b200.h)."""
+    _fields_ = [("k_norm", C.c_void_p), ("append", C.c_int), ("hstride", C.c_int), ("dpos", C.c_void_p)]
 
 
 class Weight:

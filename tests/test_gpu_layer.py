@@ -1,0 +1,138 @@
+"""The decode layer (ork_i8_mm_layer, ork-driver include/ork/chain.h:105-110) on the B200 against the
+restated layer of oracle/ork_oracle.c, itself pinned bit for bit to the reference's own glue kernels
+(tests/test_layer_host.py).
+
+The matmuls are exact int32 on both sides; the fp32 glue differs only in summation order (tree vs
+sequential) and in CUDA's expf/sinf/cosf/powf against the host's, a few ulps each. Those ulps can move a
+value across an int8 rounding boundary in the three intermediate quantizations, which changes that one
+code by 1 and the layer output by about |w| / s -- far below 1 % of the output's scale. The bound below
+(3e-3 of max|x_out|) admits a few such flips and nothing larger.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle_ffi as of
+import ork_b200
+from ork_b200 import LayerDims, LayerKV
+
+pytestmark = pytest.mark.gpu
+_p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+TOL = 3e-3
+
+DIMS = [dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=17, pos=17),
+        dict(D=2048, H=16, Hkv=8, dk=128, dv=128, Nff=6144, nkv=100, pos=100)]
+
+
+def _pack(ctx, Bs):
+    return [ctx.i8_pack(b) for b in Bs]
+
+
+def _dims(d, scale, base):
+    return LayerDims(*[d[k] for k in of.LAYER_KEYS], scale, base)
+
+
+def _close(got, want):
+    err = np.abs(got - want).max()
+    return err <= TOL * np.abs(want).max(), err
+
+
+@pytest.mark.parametrize("d", DIMS)
+def test_layer_matches_oracle(ctx, d):
+    Bs, norms, x, Kc, Vc = of.layer_inputs(21, d["D"], d["H"], d["Hkv"], d["dk"], d["Nff"], d["nkv"], d["pos"])
+    scale, base = 1.0 / np.sqrt(d["dk"]), 1e6
+    want, _, _ = of.layer(d, scale, base, Bs, norms, x, Kc, Vc)
+    ws = _pack(ctx, Bs)
+    out = np.zeros(d["D"], np.float32)
+    dims = _dims(d, scale, base)
+    rc = ctx.L.ork_i8_mm_layer(ctx.ctx, C.byref(dims), *[w.h for w in ws], _p(norms[0]), _p(norms[1]),
+                               _p(norms[2]), _p(x), _p(Kc), _p(Vc), _p(out))
+    for w in ws:
+        w.free()
+    assert rc == 0
+    ok, err = _close(out, want)
+    print("max|err|", err, "scale", np.abs(want).max())
+    assert ok, err
+
+
+def test_layer_decode_extension_graph_replay(ctx):
+    """Three decode steps captured once in a CUDA graph: each step appends its k/v at the device position
+    and attends over it, the position advancing on the device; compared step by step with the oracle."""
+    import torch
+
+    L = ork_b200.lib()
+    d = dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=5, pos=5)
+    cap = 16
+    Bs, norms, x0, Kc, Vc = of.layer_inputs(22, 256, 4, 2, 64, 512, 5, 5, hstride=cap)
+    scale, base = 0.125, 1e4
+    ws = _pack(ctx, Bs)
+    dev = torch.device("cuda", L.ork_b200_device(ctx.ctx))
+    t = {k: torch.from_numpy(v).to(dev) for k, v in dict(an=norms[0], qn=norms[1], fn=norms[2], kn=norms[3],
+                                                         x=x0, K=Kc, V=Vc).items()}
+    xo = torch.zeros(256, dtype=torch.float32, device=dev)
+    pos = torch.tensor([5], dtype=torch.int32, device=dev)
+    kv = LayerKV(t["kn"].data_ptr(), 1, cap, pos.data_ptr())
+    dims = _dims(d, scale, base)
+    stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+
+    def step():
+        assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
+                                       t["qn"].data_ptr(), t["fn"].data_ptr(), t["x"].data_ptr(),
+                                       t["K"].data_ptr(), t["V"].data_ptr(), xo.data_ptr(), C.byref(kv)) == 0
+        t["x"].copy_(xo)  # the next step's input is this step's output
+        pos.add_(1)
+
+    # one eager call sizes the layer workspace before capture (its result is discarded: a scratch cache)
+    sK, sV, sp = t["K"].clone(), t["V"].clone(), pos.clone()
+    kv0 = LayerKV(t["kn"].data_ptr(), 1, cap, sp.data_ptr())
+    assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
+                                   t["qn"].data_ptr(), t["fn"].data_ptr(), t["x"].data_ptr(), sK.data_ptr(),
+                                   sV.data_ptr(), xo.data_ptr(), C.byref(kv0)) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    # the capture ran nothing: replay three steps from position 5
+    refK, refV, x = Kc.copy(), Vc.copy(), x0.copy()
+    for s in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        ds = dict(d, nkv=5 + s, pos=5 + s)
+        want, refK, refV = of.layer(ds, scale, base, Bs, norms, x, refK, refV, kv_ext=True, hstride=cap)
+        got = xo.cpu().numpy()
+        ok, err = _close(got, want)
+        assert ok, (s, err)
+        gotK = t["K"].cpu().numpy()
+        assert np.abs(gotK[:, 5 + s] - refK[:, 5 + s]).max() <= 1e-3 * np.abs(refK[:, 5 + s]).max(), s
+        x = want
+    assert int(pos.item()) == 8
+    for w in ws:
+        w.free()
+
+
+def test_layer_refusals(ctx):
+    d = DIMS[0]
+    Bs, norms, x, Kc, Vc = of.layer_inputs(23, d["D"], d["H"], d["Hkv"], d["dk"], d["Nff"], d["nkv"], d["pos"])
+    ws = _pack(ctx, Bs)
+    out = np.zeros(d["D"], np.float32)
+    L = ctx.L
+
+    def call(dd, wl=None, xx=x):
+        dims = _dims(dd, 0.125, 1e4)
+        wl = wl or ws
+        return L.ork_i8_mm_layer(ctx.ctx, C.byref(dims), *[w.h if w else None for w in wl], _p(norms[0]),
+                                 _p(norms[1]), _p(norms[2]), None if xx is None else _p(xx), _p(Kc), _p(Vc), _p(out))
+
+    assert call(dict(d, dv=32)) == -3          # dv != dk
+    assert call(dict(d, Hkv=3)) == -3          # H % Hkv
+    assert call(dict(d, nkv=0)) == -3          # nothing to attend to
+    assert call(d, wl=[ws[1]] + ws[1:]) == -3  # q weight of the wrong shape
+    assert call(d, xx=None) == -3
+    wf = ctx.f16_pack(np.zeros((d["D"], 256), np.float16))
+    assert call(d, wl=[wf] + ws[1:]) == -3     # not an int8-compute weight
+    wf.free()
+    assert call(d) == 0
+    for w in ws:
+        w.free()
