@@ -361,17 +361,22 @@ Q3 = {"H": 2048, "NH": 16, "NKV": 8, "D": 128, "FF": 6144, "layers": 28, "V": 15
 
 
 def run_qwen3(args):
-    """random-init (~N(0,0.02)) Qwen3-1.7B-shaped w8a8 stack. Every linear projection (fused
-    QKV, O, fused gate/up, down, LM head) is ork_i8_mm_run on per-channel int8 weights packed by
-    ork_i8_mm_pack_f32, with per-row int8 activation quantization (absmax/127) before and the
-    as[m] * bscale[n] dequantization after; norms, RoPE, attention over the KV cache, SwiGLU and the
-    residual stream are PyTorch ops on the same stream. Prefill 128 tokens, then 256 greedy decode steps
-    of batch 1, each decode step one CUDA graph. Four distinct layer weight sets (200 MB, > L2) cycle
-    over the 28 layers. value = decode tokens/s; prefill tokens/s beside it."""
+    """random-init (~N(0,0.02)) Qwen3-1.7B-shaped w8a8 stack; every projection's weight is
+    packed per output channel by ork_i8_mm_pack_f32. Decode (the headline): each of the 28 layers is one
+    ork_i8_mm_layer_async call -- the library's decode layer: RMSNorm + int8 quantization, q/k/v in one
+    batched launch, q/k RMSNorm + RoPE + attention over the fp32 KV cache (the token's k/v appended at the
+    device-side position), o, residual + RMSNorm + quantization, gate/up in one launch, SwiGLU +
+    quantization, down, residual -- then the final norm and the LM head (ork_i8_mm_run_async) and a greedy
+    argmax; a whole token is one CUDA graph. Prefill of the 128-token prompt runs the same model with
+    PyTorch glue around ork_i8_mm_run (per-row activation quantization). Four distinct layer weight sets
+    (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s; prefill tokens/s beside it."""
+    import ctypes as C
+
     import torch
     import torch.nn.functional as F
 
     import ork_b200
+    from ork_b200 import LayerDims, LayerKV
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     rank = int(os.environ.get("RANK", "0"))
@@ -394,8 +399,9 @@ def run_qwen3(args):
         assert w
         return w, torch.from_numpy(bs).to(dev)
 
-    wsets = [{"qkv": pack((NH + 2 * NKV) * D, H), "o": pack(H, NH * D), "gu": pack(2 * FF, H),
-              "down": pack(H, FF)} for _ in range(NDIST)]
+    names = ("q", "k", "v", "o", "g", "u", "d")
+    wsets = [dict(zip(names, (pack(NH * D, H), pack(NKV * D, H), pack(NKV * D, H), pack(H, NH * D),
+                              pack(FF, H), pack(FF, H), pack(H, FF)))) for _ in range(NDIST)]
     lm = pack(V, H)
     g = torch.Generator(device=dev).manual_seed(5)
     emb = (torch.randn((V, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
@@ -404,8 +410,8 @@ def run_qwen3(args):
     inv = 1.0 / (Q3["theta"] ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
     ang = torch.outer(torch.arange(MAXT, device=dev, dtype=torch.float32), inv)
     cos_t, sin_t = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
-    kc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.bfloat16) for _ in range(NLY)]
-    vc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.bfloat16) for _ in range(NLY)]
+    kc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.float32) for _ in range(NLY)]
+    vc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.float32) for _ in range(NLY)]
 
     def rmsnorm(x, w):
         x = x.float()
@@ -424,63 +430,65 @@ def run_qwen3(args):
         assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, xq.data_ptr(), c.data_ptr()) == 0
         return c.float() * as_ * bs
 
-    def layer(x, li, pos0, T, pos_t=None):  # x [T, H] fp32; decode: T = 1 at device position pos_t
+    def prefill_layer(x, li, T):  # x [T, H] fp32, positions 0..T-1; fills the fp32 caches
         ws = wsets[li % NDIST]
-        qkv = linear(rmsnorm(x, ones_h), ws["qkv"])
-        q = qkv[:, : NH * D].view(T, NH, D).transpose(0, 1)
-        k = qkv[:, NH * D: (NH + NKV) * D].view(T, NKV, D).transpose(0, 1)
-        v = qkv[:, (NH + NKV) * D:].view(T, NKV, D).transpose(0, 1)
+        xn = rmsnorm(x, ones_h)
+        q = linear(xn, ws["q"]).view(T, NH, D).transpose(0, 1)
+        k = linear(xn, ws["k"]).view(T, NKV, D).transpose(0, 1)
+        v = linear(xn, ws["v"]).view(T, NKV, D).transpose(0, 1)
         q, k = rmsnorm(q, ones_d), rmsnorm(k, ones_d)
-        if pos_t is None:
-            cos, sin = cos_t[pos0:pos0 + T], sin_t[pos0:pos0 + T]
-            q, k = rope(q, cos, sin), rope(k, cos, sin)
-            kc[li][:, pos0:pos0 + T] = k.to(torch.bfloat16)
-            vc[li][:, pos0:pos0 + T] = v.to(torch.bfloat16)
-            o = F.scaled_dot_product_attention(q.to(torch.bfloat16), kc[li][:, :pos0 + T], vc[li][:, :pos0 + T],
-                                               is_causal=True, enable_gqa=True)
-        else:
-            cos, sin = cos_t.index_select(0, pos_t), sin_t.index_select(0, pos_t)
-            q, k = rope(q, cos, sin), rope(k, cos, sin)
-            kc[li].index_copy_(1, pos_t, k.to(torch.bfloat16))
-            vc[li].index_copy_(1, pos_t, v.to(torch.bfloat16))
-            mask = (torch.arange(MAXT, device=dev) <= pos_t).view(1, 1, MAXT)
-            o = F.scaled_dot_product_attention(q.to(torch.bfloat16), kc[li], vc[li], attn_mask=mask,
-                                               enable_gqa=True)
-        x = x + linear(o.transpose(0, 1).reshape(T, NH * D).float(), ws["o"])
-        gu = linear(rmsnorm(x, ones_h), ws["gu"])
-        x = x + linear(F.silu(gu[:, :FF]) * gu[:, FF:], ws["down"])
+        cos, sin = cos_t[:T], sin_t[:T]
+        q, k = rope(q, cos, sin), rope(k, cos, sin)
+        kc[li][:, :T] = k
+        vc[li][:, :T] = v
+        o = F.scaled_dot_product_attention(q, kc[li][:, :T], vc[li][:, :T], is_causal=True, enable_gqa=True)
+        x = x + linear(o.transpose(0, 1).reshape(T, NH * D), ws["o"])
+        xn = rmsnorm(x, ones_h)
+        x = x + linear(F.silu(linear(xn, ws["g"])) * linear(xn, ws["u"]), ws["d"])
         return x
 
-    def forward(tokens, pos0, pos_t=None):
+    def prefill(tokens):
         x = emb.index_select(0, tokens).float()
         for li in range(NLY):
-            x = layer(x, li, pos0, x.shape[0], pos_t)
+            x = prefill_layer(x, li, x.shape[0])
         return linear(rmsnorm(x[-1:], ones_h), lm)
 
     prompt = torch.randint(0, V, (PRE,), device=dev, generator=g)
     tok = torch.zeros(1, dtype=torch.long, device=dev)
-    pos = torch.zeros(1, dtype=torch.long, device=dev)
+    pos = torch.zeros(1, dtype=torch.int32, device=dev)
+    xa = torch.zeros(H, dtype=torch.float32, device=dev)
+    xb = torch.zeros(H, dtype=torch.float32, device=dev)
+    dims = LayerDims(H, NH, NKV, D, D, FF, PRE, PRE, 1.0 / float(np.sqrt(D)), Q3["theta"])
+    kv = LayerKV(ones_d.data_ptr(), 1, MAXT, pos.data_ptr())
 
     def decode_step():
-        logits = forward(tok, 0, pos)
+        xa.copy_(emb.index_select(0, tok).float().view(-1))
+        bufs = (xa, xb)
+        for li in range(NLY):
+            ws = wsets[li % NDIST]
+            xi, xo = bufs[li % 2], bufs[(li + 1) % 2]
+            assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[ws[n][0].h for n in names],
+                                           ones_h.data_ptr(), ones_d.data_ptr(), ones_h.data_ptr(), xi.data_ptr(),
+                                           kc[li].data_ptr(), vc[li].data_ptr(), xo.data_ptr(), C.byref(kv)) == 0
+        logits = linear(rmsnorm(bufs[NLY % 2].view(1, -1), ones_h), lm)
         tok.copy_(logits.argmax(-1))
         pos.add_(1)
 
     with torch.cuda.stream(stream):
-        for _ in range(2):  # warm-up prefill (kernel attributes, tensor maps, cuDNN/SDPA selection)
-            forward(prompt, 0)
+        for _ in range(2):  # warm-up prefill (kernel attributes, tensor maps, SDPA selection)
+            prefill(prompt)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0 = ctx.launches()
         e0.record(stream)
-        logits = forward(prompt, 0)
+        logits = prefill(prompt)
         e1.record(stream)
         torch.cuda.synchronize()
         prefill_ms = e0.elapsed_time(e1)
         prefill_launches = ctx.launches() - l0
         tok.copy_(logits.argmax(-1))
         pos.fill_(PRE)
-        decode_step()  # eager warm-up of the decode shapes
+        decode_step()  # eager warm-up of the decode shapes (sizes the layer workspace before capture)
         pos.fill_(PRE)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
@@ -497,19 +505,26 @@ def run_qwen3(args):
             e1.record(stream)
             torch.cuda.synchronize()
         decode_ms = e0.elapsed_time(e1)
+        assert int(pos.item()) == PRE + DEC
     del graph
     weight_bytes = NLY * ((NH + 2 * NKV) * D * H + H * NH * D + 2 * FF * H + H * FF) + V * H
     tps = DEC / (decode_ms / 1e3)
+    hbm, _, src = peaks()
+    roof_tps = hbm * 1e9 / weight_bytes
     line = {"metric": "Qwen3-1.7B-shape w8a8 decode tok/s (configs[3])", "value": tps * world, "unit": "tok/s",
             "n_gpus": world, "steps": DEC, "warmup": 1, "ms_per_step": decode_ms / DEC, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "Qwen3-1.7B-shaped w8a8 stack, random weights ~N(0,0.02): 28 layers, hidden 2048, "
                                    "16/8 heads x 128, SwiGLU 6144, vocab 151936, q/k norms, RoPE 1e6; prefill 128 "
                                    "then 256 greedy decode steps, batch 1",
-                       "linears": "every projection (fused QKV, O, fused gate/up, down, LM head) via ork_i8_mm_run; "
-                                  "norms/RoPE/attention/SwiGLU in PyTorch on the same stream",
+                       "linears": "decode: every layer through ork_i8_mm_layer_async (the library's decode layer: "
+                                  "its own glue kernels around its matmuls), LM head through ork_i8_mm_run_async; "
+                                  "prefill: PyTorch glue around ork_i8_mm_run_async",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
                        "parallelism": "replicas" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": tps * weight_bytes / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": tps / roof_tps, "traffic": None, "kernel": "decode token (weights once)",
+                         "peak_source": src},
             "prefill_tok_s": PRE / (prefill_ms / 1e3) * world, "prefill_ms": prefill_ms,
             "decode_ms_per_token": decode_ms / DEC, "int8_weight_bytes_per_token": weight_bytes,
             "linear_weight_GBs_decode": weight_bytes / (decode_ms / DEC / 1e3) / 1e9,

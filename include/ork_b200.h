@@ -48,9 +48,11 @@ int ork_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
  *   k_norm   RMSNorm gain applied to the token's k per head (Qwen3's k-norm; NULL: none);
  *   append   non-zero: the token's k (dequantized, k-normed, rotated at pos) and v are written into Kc / Vc
  *            at slot nkv of each kv head, and attention covers nkv + 1 keys (the token attends to itself);
- *   hstride  kv-head stride of the caches in tokens (their capacity; 0 = nkv);
+ *   hstride  kv-head stride of the caches in tokens (their capacity; 0 = nkv, allowed only without append
+ *            and dpos);
  *   dpos     non-NULL: pos and nkv are both read from this device int when the kernels run (cached tokens
- *            = position of the token), so a captured CUDA graph replays across decode steps.
+ *            = position of the token), so a captured CUDA graph replays across decode steps. A position
+ *            whose keys do not fit hstride skips attention and is reported as an execution error.
  * kv = NULL is ork_i8_mm_layer's behaviour. Same return codes. */
 typedef struct ork_b200_layer_kv {
   const float *k_norm;

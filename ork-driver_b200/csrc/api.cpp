@@ -40,8 +40,8 @@ int route_for(const ork_npu *c, const ork_w *w, int M) {
 
 // Sticky device-side error flags (a bounded wait that expired); cleared when read.
 bool device_error() {
-  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true);
-  return (t | g) != 0;
+  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true), l = layer_error_flag(true);
+  return (t | g | l) != 0;
 }
 
 void log_err(const char *what, cudaError_t e) {
@@ -419,7 +419,7 @@ int ork_b200_sync(ork_npu *c) {
     return -1;
   }
   if (device_error()) {
-    fprintf(stderr, "[ork] ERROR ork_b200_sync: a kernel's bounded pipeline wait timed out\n");
+    fprintf(stderr, "[ork] ERROR ork_b200_sync: a kernel reported an error (a bounded wait timed out, or a decode position outside the caches)\n");
     return -1;
   }
   return 0;

@@ -6,14 +6,17 @@
 // dependent launch so the next matmul streams its weights while the glue runs:
 //   1 norm_quant      RMSNorm(x) * attn_norm -> per-tensor int8 (s = 127 / max|.|)        1 CTA
 //   2 matmul batch    q, k, v projections in one batched decode launch
-//   3 attention       per query head: dequant, RMSNorm(q_norm), RoPE NeoX, softmax(q.K) V; the last
-//                     head's CTA quantizes all heads' output (global max)                   H CTAs
+//   3 attention       split-KV: per query head and chunk of keys, dequant, RMSNorm(q_norm), RoPE NeoX,
+//                     the chunk's softmax partials; the last CTA of a head merges its chunks, the last
+//                     head's CTA quantizes all heads' output (global max)          H x S CTAs
 //   4 matmul          o projection
 //   5 norm_quant      x1 = x + Co / sa, RMSNorm(x1) * ffn_norm -> int8                     1 CTA
 //   6 matmul batch    gate, up
 //   7 swiglu_quant    silu(Cg / sf) * (Cu / sf) -> int8                                    1 CTA
 //   8 matmul          down
 //   9 residual        x_out = x1 + Cd / sac
+// Folding the glue into the matmuls' prologues was measured slower: each matmul CTA would recompute the
+// whole row's norm or SwiGLU, and at M = 1 the matmuls are latency- not bandwidth-bound.
 // The glue uses the same formulas and operation order as the reference element by element; sums and
 // maxima are tree reductions and expf/sinf/cosf/powf are CUDA's, so results agree with the reference to
 // rounding (a quantization code can flip where a value sits on a rounding boundary).
@@ -22,6 +25,7 @@
 // read from device memory so a captured graph replays across tokens.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <vector>
 
@@ -35,7 +39,7 @@ namespace orkb {
 namespace {
 
 constexpr int kGlueThreads = 1024;
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 
 __device__ __forceinline__ void pdl_start() { asm volatile("griddepcontrol.launch_dependents;"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -58,7 +62,7 @@ __device__ float block_max(float v, float *red) {
   __syncthreads();
   if (l == 0) red[w] = v;
   __syncthreads();
-  v = l < nw ? red[l] : 0.0f;
+  v = l < nw ? red[l] : -3.0e38f;
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
@@ -79,15 +83,30 @@ norm_quant_kernel(const float *__restrict__ x, const int32_t *__restrict__ Co, c
   pdl_start();
   pdl_wait();
   const float sa = Co ? *sa_in : 1.0f;
+  const int bd = blockDim.x;
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = x[i];
-    if (Co) {
-      v = v + Co[i] / sa;
-      x1[i] = v;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * bd) {  // four elements per thread in flight
+    float xv[4];
+    int32_t cv[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int i = i0 + k * bd;
+      xv[k] = i < n ? x[i] : 0.0f;
+      cv[k] = (Co && i < n) ? Co[i] : 0;
     }
-    row[i] = v;
-    ss += v * v;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int i = i0 + k * bd;
+      if (i < n) {
+        float v = xv[k];
+        if (Co) {
+          v = v + cv[k] / sa;
+          x1[i] = v;
+        }
+        row[i] = v;
+        ss += v * v;
+      }
+    }
   }
   ss = block_sum(ss, red);
   const float r = 1.0f / sqrtf(ss / n + 1e-6f);
@@ -112,12 +131,26 @@ swiglu_quant_kernel(const int32_t *__restrict__ Cg, const int32_t *__restrict__ 
   pdl_start();
   pdl_wait();
   const float sf = *sf_in;
+  const int bd = blockDim.x;
   float mx = 1e-6f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float gi = Cg[i] / sf, ui = Cu[i] / sf;
-    const float a = (gi / (1.0f + expf(-gi))) * ui;
-    row[i] = a;
-    mx = fmaxf(mx, fabsf(a));
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * bd) {  // four elements per thread in flight
+    int32_t gv[4], uv[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int i = i0 + k * bd;
+      gv[k] = i < n ? Cg[i] : 0;
+      uv[k] = i < n ? Cu[i] : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int i = i0 + k * bd;
+      if (i < n) {
+        const float gi = gv[k] / sf, ui = uv[k] / sf;
+        const float a = (gi / (1.0f + expf(-gi))) * ui;
+        row[i] = a;
+        mx = fmaxf(mx, fabsf(a));
+      }
+    }
   }
   mx = block_max(mx, red);
   const float s = 127.0f / mx;
@@ -134,6 +167,13 @@ residual_kernel(const float *__restrict__ x1, const int32_t *__restrict__ Cd, co
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = x1[i] + Cd[i] / s;
 }
 
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+// Sticky flag: a layer launch met a position outside its caches (the device-read position of a captured
+// graph); its attention is skipped and the error reported by the next synchronising call.
+__device__ unsigned int g_layer_error = 0;
+constexpr int kMaxSplit = 256;  // split-KV CTAs per head at most
+
 struct AttnArgs {
   const int32_t *Cq, *Ck, *Cv;
   const float *sx;
@@ -142,15 +182,18 @@ struct AttnArgs {
   float *Kw, *Vw;        // extension: where the token's k / v are written (the caches), or null
   int H, Hkv, dk, nkv, pos, hstride;
   const int *dpos;  // extension: position (= cached tokens) read on the device, or null
+  int kpc;          // most keys per split CTA (a multiple of 32): gridDim.y * kpc covers the most keys
   float scale, base;
-  float *ao;           // [H][dk] fp32 attention output
-  unsigned int *gmax;  // bits of the running max |ao| (non-negative floats order as their bits)
-  unsigned int *count;
+  float *pm, *pz, *po;  // split partials: max [H][gridDim.y], exp-sum [H][gridDim.y], V rows [H][gridDim.y][dk]
+  float *ao;            // [H][dk] fp32 attention output
+  unsigned int *gmax;   // bits of the running max |ao| (non-negative floats order as their bits)
+  unsigned int *hcount; // [H] split CTAs done per head, left at zero
+  unsigned int *count;  // heads done, left at zero
   int8_t *ao8;
   float *sa;
 };
 
-// RMSNorm (gain g) + RoPE NeoX of one head vector held in shared memory (dk values, dk <= blockDim)
+// RMSNorm (gain g) + RoPE NeoX of one head vector held in shared memory (dk values, dk / 2 <= blockDim)
 __device__ void norm_rope(float *v, const float *g, int dk, int pos, float base, float *red) {
   const int t = threadIdx.x;
   float sq = 0.0f;
@@ -178,80 +221,160 @@ __device__ void norm_rope(float *v, const float *g, int dk, int pos, float base,
   __syncthreads();
 }
 
+// Split-KV decode attention. The nk keys of a head are cut into S <= gridDim.y chunks of kpc keys, kpc the
+// smallest multiple of 32 that covers nk (nk may be read on the device, so S is decided there and CTAs
+// past it return at once); CTA (h, sp) scores its chunk with
+// one warp per key (lanes across dk, four keys per warp in flight), and writes the chunk's max, exp-sum and
+// exp-weighted V row. The last CTA of a head merges the S partials rescaled to the head's max, and the last
+// head quantizes all heads' output with the global max.
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
-  extern __shared__ float sm[];  // q[dk], k[dk], v[dk], scores[nk]
+  extern __shared__ float sm[];  // q[dk], k[dk], v[dk], scores[kpc], partial rows [warps][dk], weights[kMaxSplit]
   __shared__ float red[32];
-  __shared__ bool last;
+  __shared__ bool last_split, last_head;
   pdl_start();
   pdl_wait();
-  const int h = blockIdx.x, t = threadIdx.x, dk = a.dk;
+  const int h = blockIdx.x, sp = blockIdx.y, t = threadIdx.x, dk = a.dk, Sg = gridDim.y;
   const int grp = a.H / a.Hkv, hk = h / grp;
   const bool ext = a.Kw != nullptr;
   const int pos = a.dpos ? *a.dpos : a.pos;
   const int nkv = a.dpos ? *a.dpos : a.nkv;
   const int nk = ext ? nkv + 1 : nkv;
-  float *q = sm, *kn = sm + dk, *vn = sm + 2 * dk, *sc = sm + 3 * dk;
+  const int kpc = max(32, (nk + 32 * Sg - 1) / (32 * Sg) * 32);  // <= a.kpc, the shared-memory size
+  if (nk < 1 || kpc > a.kpc || (ext && nkv >= a.hstride)) {
+    if (h == 0 && sp == 0 && t == 0) atomicOr(&g_layer_error, 1u);
+    return;
+  }
+  const int S = (nk + kpc - 1) / kpc;
+  if (sp >= S) return;
+  const int j0 = sp * kpc, j1 = min(nk, j0 + kpc), n = j1 - j0;
+  const bool own = ext && j0 <= nkv && nkv < j1;  // the token's own key falls in this chunk
+  float *q = sm, *kn = sm + dk, *vn = sm + 2 * dk, *sc = sm + 3 * dk, *part = sc + a.kpc, *wts = part + kAttnWarps * dk;
+  const int lane = t & 31, wp = t >> 5, per = dk / 32;
   const float sx = *a.sx;
   for (int d = t; d < dk; d += blockDim.x) q[d] = a.Cq[h * dk + d] / sx;
   __syncthreads();
   norm_rope(q, a.q_norm, dk, pos, a.base, red);
-  if (ext) {  // the token's own k and v (every head of the group computes them; the first one stores them)
+  if (own) {
     for (int d = t; d < dk; d += blockDim.x) {
       kn[d] = a.Ck[hk * dk + d] / sx;
       vn[d] = a.Cv[hk * dk + d] / sx;
     }
     __syncthreads();
     norm_rope(kn, a.k_norm, dk, pos, a.base, red);
-    if (h % grp == 0)
+    if (h % grp == 0)  // the group's first query head stores the token's k and v
       for (int d = t; d < dk; d += blockDim.x) {
         a.Kw[((size_t)hk * a.hstride + nkv) * dk + d] = kn[d];
         a.Vw[((size_t)hk * a.hstride + nkv) * dk + d] = vn[d];
       }
   }
   const float *Kh = a.Kc + (size_t)hk * a.hstride * dk, *Vh = a.Vc + (size_t)hk * a.hstride * dk;
-  // scores: one warp per key, lanes across dk
-  const int lane = t & 31, wp = t >> 5, nw = blockDim.x >> 5;
-  for (int j = wp; j < nk; j += nw) {
-    const float *kr = (ext && j == nkv) ? kn : Kh + (size_t)j * dk;
-    float s = 0.0f;
-    for (int d = lane; d < dk; d += 32) s += q[d] * kr[d];
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) sc[j] = s * a.scale;
+  float qr[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) qr[i] = i < per ? q[lane + 32 * i] : 0.0f;
+  for (int jb = j0; jb < j1; jb += 4 * kAttnWarps) {
+    float kr[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = jb + wp + kAttnWarps * u;
+      const float *row = j >= j1 ? nullptr : (own && j == nkv) ? kn : Kh + (size_t)j * dk;
+#pragma unroll
+      for (int i = 0; i < 8; i++) kr[u][i] = (row && i < per) ? row[lane + 32 * i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      float sv = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) sv += qr[i] * kr[u][i];
+      for (int o = 16; o; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+      const int j = jb + wp + kAttnWarps * u;
+      if (lane == 0 && j < j1) sc[j - j0] = sv * a.scale;
+    }
   }
   __syncthreads();
-  float mx = -1e30f;
-  for (int j = t; j < nk; j += blockDim.x) mx = fmaxf(mx, sc[j]);
-  mx = block_max(mx, red);
+  float m = -3.0e38f;
+  for (int j = t; j < n; j += blockDim.x) m = fmaxf(m, sc[j]);
+  m = block_max(m, red);
   float z = 0.0f;
-  for (int j = t; j < nk; j += blockDim.x) {
-    const float e = expf(sc[j] - mx);
+  for (int j = t; j < n; j += blockDim.x) {
+    const float e = expf(sc[j] - m);
     sc[j] = e;
     z += e;
   }
-  z = block_sum(z, red);
+  z = block_sum(z, red);  // its barriers also publish sc
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i] = 0.0f;
+  for (int jb = j0; jb < j1; jb += 4 * kAttnWarps) {
+    float vr[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = jb + wp + kAttnWarps * u;
+      const float *row = j >= j1 ? nullptr : (own && j == nkv) ? vn : Vh + (size_t)j * dk;
+#pragma unroll
+      for (int i = 0; i < 8; i++) vr[u][i] = (row && i < per) ? row[lane + 32 * i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = jb + wp + kAttnWarps * u;
+      const float e = j < j1 ? sc[j - j0] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) acc[i] += e * vr[u][i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+    if (i < per) part[wp * dk + lane + 32 * i] = acc[i];
   __syncthreads();
+  for (int d = t; d < dk; d += blockDim.x) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) sum += part[w * dk + d];
+    a.po[((size_t)h * Sg + sp) * dk + d] = sum;
+  }
+  if (t == 0) {
+    a.pm[h * Sg + sp] = m;
+    a.pz[h * Sg + sp] = z;
+  }
+  __threadfence();
+  __syncthreads();
+  if (t == 0) last_split = atomicAdd(a.hcount + h, 1u) == (unsigned int)S - 1;
+  __syncthreads();
+  if (!last_split) return;
+  // merge the head's S partials: weights exp(m_i - M), normalizer sum z_i exp(m_i - M)
+  __threadfence();
+  float M = -3.0e38f;
+  for (int i = t; i < S; i += blockDim.x) M = fmaxf(M, __ldcg(a.pm + h * Sg + i));
+  M = block_max(M, red);
+  float Z = 0.0f;
+  for (int i = t; i < S; i += blockDim.x) {
+    const float w = expf(__ldcg(a.pm + h * Sg + i) - M);
+    wts[i] = w;
+    Z += __ldcg(a.pz + h * Sg + i) * w;
+  }
+  Z = block_sum(Z, red);
   float om = 0.0f;
   for (int d = t; d < dk; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int j = 0; j < nk; j++) acc += sc[j] * ((ext && j == nkv) ? vn[d] : Vh[(size_t)j * dk + d]);
-    const float o = acc / z;
+    float o = 0.0f;
+    for (int i = 0; i < S; i++) o += __ldcg(a.po + ((size_t)h * Sg + i) * dk + d) * wts[i];
+    o /= Z;
     a.ao[h * dk + d] = o;
     om = fmaxf(om, fabsf(o));
   }
   om = block_max(om, red);
-  // the last head's CTA quantizes every head's output with the global maximum
+  __threadfence();
   if (t == 0) {
+    a.hcount[h] = 0u;
     atomicMax(a.gmax, __float_as_uint(om));
     __threadfence();
-    last = atomicAdd(a.count, 1u) == (unsigned int)gridDim.x - 1;
+    last_head = atomicAdd(a.count, 1u) == (unsigned int)a.H - 1;
   }
   __syncthreads();
-  if (last) {
+  if (last_head) {
     __threadfence();
-    const float m = fmaxf(1e-6f, __uint_as_float(atomicAdd(a.gmax, 0u)));
-    const float s = 127.0f / m;
-    const int n = a.H * dk;
-    for (int i = t; i < n; i += blockDim.x) a.ao8[i] = q8(__ldcg(a.ao + i), s);
+    const float mx = fmaxf(1e-6f, __uint_as_float(atomicAdd(a.gmax, 0u)));
+    const float s = 127.0f / mx;
+    const int nq = a.H * dk;
+    for (int i = t; i < nq; i += blockDim.x) a.ao8[i] = q8(__ldcg(a.ao + i), s);
     if (t == 0) {
       *a.sa = s;
       *a.gmax = 0u;
@@ -283,34 +406,64 @@ struct LayerWs {
   int8_t *xn8, *ao8, *xf8, *ac8;
   int32_t *Cq, *Ck, *Cv, *Co, *Cg, *Cu, *Cd;
   float *ao, *x1, *sc;  // sc: sx, sa, sf, sac
-  unsigned int *gmax, *count;
+  float *pm, *pz, *po;  // attention split partials
+  unsigned int *gmax, *count, *hcount;
 };
 
-// The attention kernel's running maximum and CTA counter sit in the first 256 bytes, a fixed place that
-// is zeroed once at allocation and left at zero by every launch (the last CTA resets them), whatever the
-// dimensions of the calls that share the workspace. The first call on a context allocates the workspace,
-// so it must precede any CUDA-graph capture.
-static bool layer_ws(ork_npu *c, int D, int Nq, int Nk, int F, LayerWs *w) {
-  const size_t parts[] = {up256(D), up256(Nq), up256(D), up256(F), up256((size_t)Nq * 4), up256((size_t)Nk * 4),
-                          up256((size_t)Nk * 4), up256((size_t)D * 4), up256((size_t)F * 4), up256((size_t)F * 4),
-                          up256((size_t)D * 4), up256((size_t)Nq * 4), up256((size_t)D * 4), 256};
-  size_t total = 256;
+constexpr int kMaxHeads = 4096;
+constexpr size_t kCounterBytes = 256 + kMaxHeads * 4;
+
+// Split-KV CTAs per head for attention over at most maxk keys: enough chunks of 32 keys to fill about one
+// wave of the GPU's resident CTAs across the H heads.
+static int attn_splits(int H, int maxk) {
+  const int cap = std::max(1, std::min(kMaxSplit, 148 * (2048 / kAttnThreads) / H));
+  return std::max(1, std::min(cap, (maxk + 31) / 32));
+}
+static int attn_kpc(int maxk, int Sg) { return std::max(32, (maxk + 32 * Sg - 1) / (32 * Sg) * 32); }
+static size_t attn_smem(int dk, int kpc) { return (size_t)(3 * dk + kpc + kAttnWarps * dk + kMaxSplit) * 4; }
+
+// The attention kernel's running maximum and CTA counters sit in a fixed region at the start of the
+// allocation, zeroed once at allocation and left at zero by every launch (the last CTAs reset them),
+// whatever the dimensions of the calls that share the workspace. The first call on a context allocates
+// the workspace, so it must precede any CUDA-graph capture.
+static bool layer_ws(ork_npu *c, int D, int H, int Nq, int Nk, int F, int dk, int Sg, LayerWs *w) {
+  const size_t parts[] = {up256(D),
+                          up256(Nq),
+                          up256(D),
+                          up256(F),
+                          up256((size_t)Nq * 4),
+                          up256((size_t)Nk * 4),
+                          up256((size_t)Nk * 4),
+                          up256((size_t)D * 4),
+                          up256((size_t)F * 4),
+                          up256((size_t)F * 4),
+                          up256((size_t)D * 4),
+                          up256((size_t)Nq * 4),
+                          up256((size_t)D * 4),
+                          256,
+                          up256((size_t)H * Sg * 4),
+                          up256((size_t)H * Sg * 4),
+                          up256((size_t)H * Sg * dk * 4)};
+  constexpr int np = sizeof(parts) / sizeof(parts[0]);
+  size_t total = kCounterBytes;
   for (size_t p : parts) total += p;
   if (c->capL < total) {
     if (c->dL) cudaFree(c->dL);
     c->dL = nullptr;
     c->capL = 0;
     if (cudaMalloc(&c->dL, total) != cudaSuccess) return false;
-    if (cudaMemset(c->dL, 0, total) != cudaSuccess) return false;  // gmax / count start at zero
+    if (cudaMemset(c->dL, 0, total) != cudaSuccess) return false;  // the counters start at zero
     c->capL = total;
   }
   w->gmax = (unsigned int *)c->dL;
   w->count = w->gmax + 1;
-  uint8_t *p = (uint8_t *)c->dL + 256;
-  void **dst[] = {(void **)&w->xn8, (void **)&w->ao8, (void **)&w->xf8, (void **)&w->ac8, (void **)&w->Cq,
-                  (void **)&w->Ck,  (void **)&w->Cv,  (void **)&w->Co,  (void **)&w->Cg,  (void **)&w->Cu,
-                  (void **)&w->Cd,  (void **)&w->ao,  (void **)&w->x1,  (void **)&w->sc};
-  for (int i = 0; i < 14; i++) {
+  w->hcount = w->gmax + 64;
+  uint8_t *p = (uint8_t *)c->dL + kCounterBytes;
+  void **dst[np] = {(void **)&w->xn8, (void **)&w->ao8, (void **)&w->xf8, (void **)&w->ac8, (void **)&w->Cq,
+                    (void **)&w->Ck,  (void **)&w->Cv,  (void **)&w->Co,  (void **)&w->Cg,  (void **)&w->Cu,
+                    (void **)&w->Cd,  (void **)&w->ao,  (void **)&w->x1,  (void **)&w->sc,  (void **)&w->pm,
+                    (void **)&w->pz,  (void **)&w->po};
+  for (int i = 0; i < np; i++) {
     *dst[i] = p;
     p += parts[i];
   }
@@ -324,8 +477,20 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
                   const ork_b200_layer_kv *kv) {
   const int D = (int)d->D, H = (int)d->H, Hkv = (int)d->Hkv, dk = (int)d->dk, F = (int)d->Nff;
   const int Nq = H * dk, Nk = Hkv * dk;
+  const bool ext = kv && kv->append;
+  // keys attention may cover: the cache capacity when the position is read on the device
+  const int maxk = (kv && kv->dpos) ? kv->hstride : (int)d->nkv + (ext ? 1 : 0);
+  const int Sg = attn_splits(H, maxk), kpc = attn_kpc(maxk, Sg);
   LayerWs ws;
-  if (!layer_ws(c, D, Nq, Nk, F, &ws)) return -1;
+  if (!layer_ws(c, D, H, Nq, Nk, F, dk, Sg, &ws)) return -1;
+  static bool attrs = false;  // the glue kernels may use up to 200 KB of dynamic shared memory
+  if (!attrs) {
+    const void *k[] = {(const void *)norm_quant_kernel, (const void *)swiglu_quant_kernel,
+                       (const void *)attention_kernel};
+    for (const void *f : k)
+      if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) return -1;
+    attrs = true;
+  }
   const bool pdl = c->pdl;
   cudaStream_t s = c->stream;
   int nl = 0;
@@ -355,7 +520,7 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
     int n = D;
     void *args[] = {(void *)&xx, (void *)&no, (void *)&nsa, (void *)&nx1, (void *)&attn_norm, (void *)&n,
                     (void *)&ws.xn8, (void *)&ws.sc};
-    e = launch_pdl((const void *)norm_quant_kernel, 1, kGlueThreads, (size_t)D * 4, s, pdl, args);
+    e = launch_pdl((const void *)norm_quant_kernel, dim3(1), kGlueThreads, (size_t)D * 4, s, pdl, args);
     if (e != cudaSuccess) goto fail;
     nl++;
   }
@@ -371,7 +536,6 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
     a.k_norm = kv ? kv->k_norm : nullptr;
     a.Kc = Kc;
     a.Vc = Vc;
-    const bool ext = kv && kv->append;
     a.Kw = ext ? const_cast<float *>(Kc) : nullptr;
     a.Vw = ext ? const_cast<float *>(Vc) : nullptr;
     a.H = H;
@@ -381,16 +545,20 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
     a.pos = (int)d->pos;
     a.hstride = (kv && kv->hstride > 0) ? kv->hstride : (int)d->nkv;
     a.dpos = kv ? kv->dpos : nullptr;
-    const int maxk = (kv && kv->hstride > 0) ? kv->hstride : (int)d->nkv + 1;
+    a.kpc = kpc;
     a.scale = (float)d->attn_scale;
     a.base = (float)d->rope_base;
+    a.pm = ws.pm;
+    a.pz = ws.pz;
+    a.po = ws.po;
     a.ao = ws.ao;
     a.gmax = ws.gmax;
+    a.hcount = ws.hcount;
     a.count = ws.count;
     a.ao8 = ws.ao8;
     a.sa = ws.sc + 1;
     void *args[] = {(void *)&a};
-    e = launch_pdl((const void *)attention_kernel, H, kAttnThreads, (size_t)(3 * dk + maxk) * 4, s, pdl, args);
+    e = launch_pdl((const void *)attention_kernel, dim3(H, Sg), kAttnThreads, attn_smem(dk, kpc), s, pdl, args);
     if (e != cudaSuccess) goto fail;
     nl++;
   }
@@ -405,7 +573,7 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
     float *sf = ws.sc + 2;
     void *args[] = {(void *)&xx, (void *)&co, (void *)&sa, (void *)&x1, (void *)&ffn_norm, (void *)&n,
                     (void *)&ws.xf8, (void *)&sf};
-    e = launch_pdl((const void *)norm_quant_kernel, 1, kGlueThreads, (size_t)D * 4, s, pdl, args);
+    e = launch_pdl((const void *)norm_quant_kernel, dim3(1), kGlueThreads, (size_t)D * 4, s, pdl, args);
     if (e != cudaSuccess) goto fail;
     nl++;
   }
@@ -416,7 +584,7 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
     float *sac = ws.sc + 3;
     int n = F;
     void *args[] = {(void *)&ws.Cg, (void *)&ws.Cu, (void *)&sf, (void *)&n, (void *)&ws.ac8, (void *)&sac};
-    e = launch_pdl((const void *)swiglu_quant_kernel, 1, kGlueThreads, (size_t)F * 4, s, pdl, args);
+    e = launch_pdl((const void *)swiglu_quant_kernel, dim3(1), kGlueThreads, (size_t)F * 4, s, pdl, args);
     if (e != cudaSuccess) goto fail;
     nl++;
   }
@@ -426,7 +594,7 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
     const float *x1 = ws.x1, *sac = ws.sc + 3;
     int n = D;
     void *args[] = {(void *)&x1, (void *)&ws.Cd, (void *)&sac, (void *)&n, (void *)&x_out};
-    e = launch_pdl((const void *)residual_kernel, (D + 255) / 256, 256, 0, s, pdl, args);
+    e = launch_pdl((const void *)residual_kernel, dim3((D + 255) / 256), 256, 0, s, pdl, args);
     if (e != cudaSuccess) goto fail;
     nl++;
   }
@@ -435,6 +603,16 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
 fail:
   log_err("ork_i8_mm_layer", e);
   return -1;
+}
+
+unsigned int layer_error_flag(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_layer_error, sizeof v);
+  if (reset && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_layer_error, &z, sizeof z);
+  }
+  return v;
 }
 
 }  // namespace orkb
@@ -448,8 +626,12 @@ bool dims_ok(const ork_layer_dims *d, ork_w *const *W, const ork_b200_layer_kv *
   const long D = d->D, H = d->H, Hkv = d->Hkv, dk = d->dk, F = d->Nff;
   if (D < 32 || H < 1 || Hkv < 1 || H % Hkv || dk < 2 || dk % 2 || dk > 256 || d->dv != d->dk || F < 32) return false;
   if (D * 4 > 200 * 1024 || F * 4 > 200 * 1024) return false;
-  const long keys = (kv && kv->hstride > 0) ? kv->hstride : (long)d->nkv + 1;
-  if ((3 * dk + keys) * 4 > 200 * 1024) return false;
+  // the caches' capacity must be given where the token is appended or the position is read on the device
+  if (H > kMaxHeads || dk % 32 || (kv && (kv->dpos || kv->append) && kv->hstride <= 0)) return false;
+  const long keys = (kv && kv->dpos) ? kv->hstride : (long)d->nkv + ((kv && kv->append) ? 1 : 0);
+  if (keys < 1 || keys > (1 << 24)) return false;
+  const int Sg = attn_splits((int)H, (int)keys);
+  if (attn_smem((int)dk, attn_kpc((int)keys, Sg)) > 200 * 1024) return false;
   if (kv && kv->append && kv->hstride > 0 && !kv->dpos && (long)d->nkv + 1 > kv->hstride) return false;
   if (!(kv && kv->append) && d->nkv < 1) return false;
   const long Nq = H * dk, Nk = Hkv * dk;

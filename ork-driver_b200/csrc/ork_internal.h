@@ -41,6 +41,7 @@ struct RunArgs {
 cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launches);
 inline bool gemv_supports(int fmt, int K) { return K > 0 && fmt >= FMT_F16 && fmt <= FMT_NF4; }
 unsigned int gemv_error_flag(bool reset);
+unsigned int layer_error_flag(bool reset);  // layer.cu: a position outside the caches
 
 // Grouped (per-K-group scaled) matmul, ork-driver src/npu/core/buf.c:501-520: C[m][n] fp32 = sum over
 // groups g, ascending, of ((float)P_g[m][n] * aScale[m*Sk+g]) * bScale[g*N+n], P_g the exact int32 dot

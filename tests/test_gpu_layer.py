@@ -21,8 +21,15 @@ pytestmark = pytest.mark.gpu
 _p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
 TOL = 3e-3
 
+# attention splits each head's keys over CTAs in chunks of at least 32: one chunk, several, and (9000 keys)
+# more chunks than a head may have CTAs, so chunks of 64. The 9000-key case rotates at position 100: at
+# position 9000 the RoPE angle pos * base^(-2i/dk) is so ill-conditioned that a one-ulp change of the base
+# alone moves the oracle's own output by 0.8 % (5e-7 at position 100), so CUDA's powf / cosf against the
+# host's would be measured there, not the kernel.
 DIMS = [dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=17, pos=17),
-        dict(D=2048, H=16, Hkv=8, dk=128, dv=128, Nff=6144, nkv=100, pos=100)]
+        dict(D=2048, H=16, Hkv=8, dk=128, dv=128, Nff=6144, nkv=100, pos=100),
+        dict(D=512, H=8, Hkv=2, dk=128, dv=128, Nff=1024, nkv=3000, pos=3000),
+        dict(D=512, H=8, Hkv=2, dk=128, dv=128, Nff=1024, nkv=9000, pos=100)]
 
 
 def _pack(ctx, Bs):
@@ -56,22 +63,24 @@ def test_layer_matches_oracle(ctx, d):
     assert ok, err
 
 
-def test_layer_decode_extension_graph_replay(ctx):
+@pytest.mark.parametrize("p0,cap", [(5, 16), (95, 160)])
+def test_layer_decode_extension_graph_replay(ctx, p0, cap):
     """Three decode steps captured once in a CUDA graph: each step appends its k/v at the device position
-    and attends over it, the position advancing on the device; compared step by step with the oracle."""
+    and attends over it, the position advancing on the device; compared step by step with the oracle.
+    From position 95 the token's own key sits in the last of several key chunks, and the steps cross a
+    chunk boundary (96 keys -> 97)."""
     import torch
 
     L = ork_b200.lib()
-    d = dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=5, pos=5)
-    cap = 16
-    Bs, norms, x0, Kc, Vc = of.layer_inputs(22, 256, 4, 2, 64, 512, 5, 5, hstride=cap)
+    d = dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=p0, pos=p0)
+    Bs, norms, x0, Kc, Vc = of.layer_inputs(22, 256, 4, 2, 64, 512, p0, p0, hstride=cap)
     scale, base = 0.125, 1e4
     ws = _pack(ctx, Bs)
     dev = torch.device("cuda", L.ork_b200_device(ctx.ctx))
     t = {k: torch.from_numpy(v).to(dev) for k, v in dict(an=norms[0], qn=norms[1], fn=norms[2], kn=norms[3],
                                                          x=x0, K=Kc, V=Vc).items()}
     xo = torch.zeros(256, dtype=torch.float32, device=dev)
-    pos = torch.tensor([5], dtype=torch.int32, device=dev)
+    pos = torch.tensor([p0], dtype=torch.int32, device=dev)
     kv = LayerKV(t["kn"].data_ptr(), 1, cap, pos.data_ptr())
     dims = _dims(d, scale, base)
     stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
@@ -94,20 +103,54 @@ def test_layer_decode_extension_graph_replay(ctx):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
         step()
-    # the capture ran nothing: replay three steps from position 5
+    # the capture ran nothing: replay three steps from position p0
     refK, refV, x = Kc.copy(), Vc.copy(), x0.copy()
     for s in range(3):
         g.replay()
         torch.cuda.synchronize()
-        ds = dict(d, nkv=5 + s, pos=5 + s)
+        ds = dict(d, nkv=p0 + s, pos=p0 + s)
         want, refK, refV = of.layer(ds, scale, base, Bs, norms, x, refK, refV, kv_ext=True, hstride=cap)
         got = xo.cpu().numpy()
         ok, err = _close(got, want)
         assert ok, (s, err)
         gotK = t["K"].cpu().numpy()
-        assert np.abs(gotK[:, 5 + s] - refK[:, 5 + s]).max() <= 1e-3 * np.abs(refK[:, 5 + s]).max(), s
+        assert np.abs(gotK[:, p0 + s] - refK[:, p0 + s]).max() <= 1e-3 * np.abs(refK[:, p0 + s]).max(), s
         x = want
-    assert int(pos.item()) == 8
+    assert int(pos.item()) == p0 + 3
+    for w in ws:
+        w.free()
+
+
+def test_layer_device_position_past_capacity_is_an_error(ctx):
+    """A device-read position whose token would not fit the caches: the kernel's own check skips attention
+    (no cache access), the sync reports the error once, and the context keeps working."""
+    import torch
+
+    L = ork_b200.lib()
+    cap = 8
+    d = dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=cap, pos=cap)
+    Bs, norms, x0, Kc, Vc = of.layer_inputs(24, 256, 4, 2, 64, 512, 4, 4, hstride=cap)
+    ws = _pack(ctx, Bs)
+    dev = torch.device("cuda", L.ork_b200_device(ctx.ctx))
+    t = {k: torch.from_numpy(v).to(dev) for k, v in dict(an=norms[0], qn=norms[1], fn=norms[2], kn=norms[3],
+                                                         x=x0, K=Kc, V=Vc).items()}
+    K0 = t["K"].clone()
+    xo = torch.zeros(256, dtype=torch.float32, device=dev)
+    dims = _dims(d, 0.125, 1e4)
+
+    def call(p):
+        pos = torch.tensor([p], dtype=torch.int32, device=dev)
+        kv = LayerKV(t["kn"].data_ptr(), 1, cap, pos.data_ptr())
+        torch.cuda.synchronize()
+        assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
+                                       t["qn"].data_ptr(), t["fn"].data_ptr(), t["x"].data_ptr(),
+                                       t["K"].data_ptr(), t["V"].data_ptr(), xo.data_ptr(), C.byref(kv)) == 0
+        return L.ork_b200_sync(ctx.ctx)
+
+    assert call(cap) == -1                      # slot cap is past the caches
+    assert torch.equal(t["K"], K0)              # nothing was written
+    assert call(cap - 1) == 0                   # the last slot is fine, and the flag was cleared
+    assert not torch.equal(t["K"], K0)
     for w in ws:
         w.free()
 
