@@ -40,8 +40,9 @@ int route_for(const ork_npu *c, const ork_w *w, int M) {
 
 // Sticky device-side error flags (a bounded wait that expired); cleared when read.
 bool device_error() {
-  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true), l = layer_error_flag(true);
-  return (t | g | l) != 0;
+  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true), l = layer_error_flag(true),
+                     f = fused_error_flag(true);
+  return (t | g | l | f) != 0;
 }
 
 void log_err(const char *what, cudaError_t e) {

@@ -27,8 +27,10 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <vector>
 
+#include "glue.cuh"
 #include "ork_b200.h"
 #include "ork_internal.h"
 #include "ork_npu.h"
@@ -67,10 +69,7 @@ __device__ float block_max(float v, float *red) {
   return v;
 }
 
-__device__ __forceinline__ int8_t q8(float v, float s) {
-  const int q = __float2int_rn(v * s);  // lrintf in the default rounding mode: nearest, ties to even
-  return (int8_t)(q > 127 ? 127 : (q < -127 ? -127 : q));
-}
+using glue::q8;
 
 // RMSNorm + per-tensor int8 quantization of one row of n values (spine_rmsnorm + spine_quant). With Co
 // given, the row is first formed as x1 = x + Co / *sa_in and stored to x1.
@@ -109,7 +108,7 @@ norm_quant_kernel(const float *__restrict__ x, const int32_t *__restrict__ Co, c
     }
   }
   ss = block_sum(ss, red);
-  const float r = 1.0f / sqrtf(ss / n + 1e-6f);
+  const float r = glue::rms_recip(ss, n);
   float mx = 1e-6f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float y = row[i] * r * g[i];
@@ -117,7 +116,7 @@ norm_quant_kernel(const float *__restrict__ x, const int32_t *__restrict__ Co, c
     mx = fmaxf(mx, fabsf(y));
   }
   mx = block_max(mx, red);
-  const float s = 127.0f / mx;
+  const float s = glue::qscale(mx);
   for (int i = threadIdx.x; i < n; i += blockDim.x) q[i] = q8(row[i], s);
   if (threadIdx.x == 0) *s_out = s;
 }
@@ -146,14 +145,14 @@ swiglu_quant_kernel(const int32_t *__restrict__ Cg, const int32_t *__restrict__ 
       const int i = i0 + k * bd;
       if (i < n) {
         const float gi = gv[k] / sf, ui = uv[k] / sf;
-        const float a = (gi / (1.0f + expf(-gi))) * ui;
+        const float a = glue::silu_mul(gi, ui);
         row[i] = a;
         mx = fmaxf(mx, fabsf(a));
       }
     }
   }
   mx = block_max(mx, red);
-  const float s = 127.0f / mx;
+  const float s = glue::qscale(mx);
   for (int i = threadIdx.x; i < n; i += blockDim.x) q[i] = q8(row[i], s);
   if (threadIdx.x == 0) *s_out = s;
 }
@@ -200,14 +199,14 @@ __device__ void norm_rope(float *v, const float *g, int dk, int pos, float base,
   for (int d = t; d < dk; d += blockDim.x) sq += v[d] * v[d];
   if (g) {
     sq = block_sum(sq, red);
-    const float r = 1.0f / sqrtf(sq / dk + 1e-6f);
+    const float r = glue::rms_recip(sq, dk);
     for (int d = t; d < dk; d += blockDim.x) v[d] = v[d] * r * g[d];
     __syncthreads();
   }
   const int h = dk / 2;
   float a = 0.0f, b = 0.0f, c = 0.0f, s = 0.0f;
   if (t < h) {
-    const float th = pos * powf(base, -2.0f * t / dk);
+    const float th = glue::rope_angle(pos, base, t, dk);
     c = cosf(th);
     s = sinf(th);
     a = v[t];
@@ -240,7 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   const int nkv = a.dpos ? *a.dpos : a.nkv;
   const int nk = ext ? nkv + 1 : nkv;
   const int kpc = max(32, (nk + 32 * Sg - 1) / (32 * Sg) * 32);  // <= a.kpc, the shared-memory size
-  if (nk < 1 || kpc > a.kpc || (ext && nkv >= a.hstride)) {
+  if (nk < 1 || kpc > a.kpc || nkv > a.hstride || (ext && nkv >= a.hstride)) {
     if (h == 0 && sp == 0 && t == 0) atomicOr(&g_layer_error, 1u);
     return;
   }
@@ -371,8 +370,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   __syncthreads();
   if (last_head) {
     __threadfence();
-    const float mx = fmaxf(1e-6f, __uint_as_float(atomicAdd(a.gmax, 0u)));
-    const float s = 127.0f / mx;
+    const float s = glue::qscale(__uint_as_float(atomicAdd(a.gmax, 0u)));
     const int nq = a.H * dk;
     for (int i = t; i < nq; i += blockDim.x) a.ao8[i] = q8(__ldcg(a.ao + i), s);
     if (t == 0) {
@@ -407,10 +405,13 @@ struct LayerWs {
   int32_t *Cq, *Ck, *Cv, *Co, *Cg, *Cu, *Cd;
   float *ao, *x1, *sc;  // sc: sx, sa, sf, sac
   float *pm, *pz, *po;  // attention split partials
+  uint64_t *ll;         // persistent layer: the epoch-tagged words its CTAs exchange
   unsigned int *gmax, *count, *hcount;
+  unsigned int *epoch, *sync;  // persistent layer: launch epoch, arrival counts
 };
 
 constexpr int kMaxHeads = 4096;
+constexpr int kMaxGrid = 1024;  // CTAs of a persistent layer launch at most (one per SM)
 constexpr size_t kCounterBytes = 256 + kMaxHeads * 4;
 
 // Split-KV CTAs per head for attention over at most maxk keys: enough chunks of 32 keys to fill about one
@@ -422,9 +423,16 @@ static int attn_splits(int H, int maxk) {
 static int attn_kpc(int maxk, int Sg) { return std::max(32, (maxk + 32 * Sg - 1) / (32 * Sg) * 32); }
 static size_t attn_smem(int dk, int kpc) { return (size_t)(3 * dk + kpc + kAttnWarps * dk + kMaxSplit) * 4; }
 
+// Epoch-tagged words of the persistent layer: q, k, v, o, chunk maxima and sums, chunk rows, ao, head
+// maxima, h, CTA maxima.
+static size_t ll_words(int D, int H, int Nq, int Nk, int F, int dk, int Sg) {
+  return (size_t)Nq + 2 * (size_t)Nk + D + 2 * (size_t)H * Sg + (size_t)H * Sg * dk + Nq + H + F + kMaxGrid;
+}
+
 // The attention kernel's running maximum and CTA counters sit in a fixed region at the start of the
 // allocation, zeroed once at allocation and left at zero by every launch (the last CTAs reset them),
-// whatever the dimensions of the calls that share the workspace. The first call on a context allocates
+// whatever the dimensions of the calls that share the workspace; so do the persistent layer's launch
+// epoch (which only grows) and its arrival counts (left at zero). The first call on a context allocates
 // the workspace, so it must precede any CUDA-graph capture.
 static bool layer_ws(ork_npu *c, int D, int H, int Nq, int Nk, int F, int dk, int Sg, LayerWs *w) {
   const size_t parts[] = {up256(D),
@@ -443,7 +451,8 @@ static bool layer_ws(ork_npu *c, int D, int H, int Nq, int Nk, int F, int dk, in
                           256,
                           up256((size_t)H * Sg * 4),
                           up256((size_t)H * Sg * 4),
-                          up256((size_t)H * Sg * dk * 4)};
+                          up256((size_t)H * Sg * dk * 4),
+                          up256(ll_words(D, H, Nq, Nk, F, dk, Sg) * 8)};
   constexpr int np = sizeof(parts) / sizeof(parts[0]);
   size_t total = kCounterBytes;
   for (size_t p : parts) total += p;
@@ -457,12 +466,14 @@ static bool layer_ws(ork_npu *c, int D, int H, int Nq, int Nk, int F, int dk, in
   }
   w->gmax = (unsigned int *)c->dL;
   w->count = w->gmax + 1;
+  w->epoch = w->gmax + 2;
+  w->sync = w->gmax + 4;
   w->hcount = w->gmax + 64;
   uint8_t *p = (uint8_t *)c->dL + kCounterBytes;
   void **dst[np] = {(void **)&w->xn8, (void **)&w->ao8, (void **)&w->xf8, (void **)&w->ac8, (void **)&w->Cq,
                     (void **)&w->Ck,  (void **)&w->Cv,  (void **)&w->Co,  (void **)&w->Cg,  (void **)&w->Cu,
                     (void **)&w->Cd,  (void **)&w->ao,  (void **)&w->x1,  (void **)&w->sc,  (void **)&w->pm,
-                    (void **)&w->pz,  (void **)&w->po};
+                    (void **)&w->pz,  (void **)&w->po,  (void **)&w->ll};
   for (int i = 0; i < np; i++) {
     *dst[i] = p;
     p += parts[i];
@@ -480,9 +491,58 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
   const bool ext = kv && kv->append;
   // keys attention may cover: the cache capacity when the position is read on the device
   const int maxk = (kv && kv->dpos) ? kv->hstride : (int)d->nkv + (ext ? 1 : 0);
-  const int Sg = attn_splits(H, maxk), kpc = attn_kpc(maxk, Sg);
+  // the persistent one-launch layer (layer_fused.cu) when the seven weights share an int8-compute format
+  // and its plan fits; ORKB_LAYER_FUSED=0 selects the multi-launch form
+  FusedArgs fa = {};
+  const int G = fused_grid(c->device);
+  bool fused = G > 0 && G <= kMaxGrid;
+  for (int i = 0; i < 7 && fused; i++) fused = W[i]->fmt == W[0]->fmt;
+  if (const char *e = getenv("ORKB_LAYER_FUSED")) fused = fused && atoi(e) != 0;
+  if (fused) {
+    fa.D = D, fa.H = H, fa.Hkv = Hkv, fa.dk = dk, fa.F = F;
+    fa.Sg = fused_splits(H, maxk, G);
+    fa.kpc = fused_kpc(maxk, fa.Sg);
+    fused = fused_plan(&fa, W[0]->fmt, G);
+  }
+  const int Sg = fused ? fa.Sg : attn_splits(H, maxk), kpc = attn_kpc(maxk, Sg);
   LayerWs ws;
   if (!layer_ws(c, D, H, Nq, Nk, F, dk, Sg, &ws)) return -1;
+  if (fused) {
+    for (int i = 0; i < 7; i++) fa.W[i] = (const uint8_t *)W[i]->d;
+    fa.attn_norm = attn_norm;
+    fa.q_norm = q_norm;
+    fa.k_norm = kv ? kv->k_norm : nullptr;
+    fa.ffn_norm = ffn_norm;
+    fa.x = x;
+    fa.Kc = Kc;
+    fa.Vc = Vc;
+    fa.Kw = ext ? const_cast<float *>(Kc) : nullptr;
+    fa.Vw = ext ? const_cast<float *>(Vc) : nullptr;
+    fa.x_out = x_out;
+    fa.nkv = (int)d->nkv;
+    fa.pos = (int)d->pos;
+    fa.hstride = (kv && kv->hstride > 0) ? kv->hstride : (int)d->nkv;
+    fa.dpos = kv ? kv->dpos : nullptr;
+    fa.scale = (float)d->attn_scale;
+    fa.base = (float)d->rope_base;
+    uint64_t *l = ws.ll;
+    auto take = [&](size_t n) {
+      uint64_t *r = l;
+      l += n;
+      return r;
+    };
+    fa.q = take(Nq), fa.k = take(Nk), fa.v = take(Nk), fa.o = take(D);
+    fa.pm = take((size_t)H * Sg), fa.pz = take((size_t)H * Sg), fa.po = take((size_t)H * Sg * dk);
+    fa.ao = take(Nq), fa.amax = take(H), fa.h = take(F), fa.hmax = take(kMaxGrid);
+    fa.epoch = ws.epoch, fa.sync = ws.sync;
+    const cudaError_t e = launch_layer_fused(fa, W[0]->fmt, G, c->stream);
+    if (e != cudaSuccess) {
+      log_err("ork_i8_mm_layer (persistent)", e);
+      return -1;
+    }
+    c->launches += 1;
+    return 0;
+  }
   static bool attrs = false;  // the glue kernels may use up to 200 KB of dynamic shared memory
   if (!attrs) {
     const void *k[] = {(const void *)norm_quant_kernel, (const void *)swiglu_quant_kernel,
@@ -632,7 +692,7 @@ bool dims_ok(const ork_layer_dims *d, ork_w *const *W, const ork_b200_layer_kv *
   if (keys < 1 || keys > (1 << 24)) return false;
   const int Sg = attn_splits((int)H, (int)keys);
   if (attn_smem((int)dk, attn_kpc((int)keys, Sg)) > 200 * 1024) return false;
-  if (kv && kv->append && kv->hstride > 0 && !kv->dpos && (long)d->nkv + 1 > kv->hstride) return false;
+  if (kv && kv->hstride > 0 && !kv->dpos && (long)d->nkv + (kv->append ? 1 : 0) > kv->hstride) return false;
   if (!(kv && kv->append) && d->nkv < 1) return false;
   const long Nq = H * dk, Nk = Hkv * dk;
   const long shape[7][2] = {{D, Nq}, {D, Nk}, {D, Nk}, {Nq, D}, {D, F}, {D, F}, {F, D}};

@@ -77,4 +77,37 @@ bool gemm_tc_supports(int fmt, int M, int K, int N);
 // then exits without a result). Read after a synchronisation; reset clears it.
 unsigned int tc_error_flag(bool reset);
 
+// Persistent decode layer (layer_fused.cu): one cooperative launch of one CTA per SM runs a whole
+// ork_i8_mm_layer. The caller fills everything above `slot`; launch_layer_fused plans the shared memory
+// (fused_plan: false when the layer's rows or activations do not fit it) and launches.
+struct FusedArgs {
+  const uint8_t *W[7];  // q, k, v, o, gate, up, down: resident rows of one int8-compute format
+  const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *x;
+  const float *Kc, *Vc;
+  float *Kw, *Vw;  // the caches when the token's k / v are appended, else null
+  float *x_out;
+  int D, H, Hkv, dk, F, nkv, pos, hstride;
+  const int *dpos;
+  float scale, base;
+  // values exchanged between CTAs: 64-bit words, the value's bits in the low half and the launch's epoch
+  // in the high half, so a reader polls the data itself (no barrier, no fence)
+  uint64_t *q, *k, *v, *o;   // projections [H*dk], [Hkv*dk], [Hkv*dk], [D] (int32)
+  uint64_t *pm, *pz, *po;    // attention chunk partials [H][Sg], [H][Sg], [H][Sg][dk] (float)
+  uint64_t *ao, *amax;       // merged attention output [H][dk] and max |.| per head (float)
+  uint64_t *h, *hmax;        // SwiGLU row [F] and max |h| per CTA [grid] (float)
+  unsigned int *epoch;       // launch epoch (advanced by the last CTA to finish)
+  unsigned int *sync;        // arrivals: [0] heads merged, [1] CTAs past o, [2] CTAs past SwiGLU,
+                             // [3] CTAs finished (all zeroed by the last CTA to finish)
+  int Sg, kpc;               // attention chunks per head, most keys per chunk
+  uint32_t slot;             // -- planned: ring slot bytes, slots, shared-memory layout
+  int nslots;
+  uint32_t off_a8, off_x, off_y, off_loc, smem;
+};
+int fused_grid(int device);                  // CTAs of the persistent launch: the device's SM count
+int fused_splits(int H, int maxk, int G);    // attention chunks per head
+int fused_kpc(int maxk, int Sg);             // most keys per chunk (a multiple of 32)
+bool fused_plan(FusedArgs *a, int fmt, int G);
+cudaError_t launch_layer_fused(const FusedArgs &a, int fmt, int G, cudaStream_t s);
+unsigned int fused_error_flag(bool reset);
+
 }  // namespace orkb

@@ -1,6 +1,8 @@
 """The decode layer (ork_i8_mm_layer, ork-driver include/ork/chain.h:105-110) on the B200 against the
 restated layer of oracle/ork_oracle.c, itself pinned bit for bit to the reference's own glue kernels
-(tests/test_layer_host.py).
+(tests/test_layer_host.py). Every case runs in both of the library's forms: the persistent one-launch
+kernel (layer_fused.cu, the default where the seven weights share a format) and the multi-launch form
+(layer.cu, ORKB_LAYER_FUSED=0).
 
 The matmuls are exact int32 on both sides; the fp32 glue differs only in summation order (tree vs
 sequential) and in CUDA's expf/sinf/cosf/powf against the host's, a few ulps each. Those ulps can move a
@@ -32,6 +34,12 @@ DIMS = [dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=17, pos=17),
         dict(D=512, H=8, Hkv=2, dk=128, dv=128, Nff=1024, nkv=9000, pos=100)]
 
 
+@pytest.fixture(params=["fused", "multi"])
+def path(request, monkeypatch):
+    monkeypatch.setenv("ORKB_LAYER_FUSED", "1" if request.param == "fused" else "0")
+    return request.param
+
+
 def _pack(ctx, Bs):
     return [ctx.i8_pack(b) for b in Bs]
 
@@ -45,26 +53,63 @@ def _close(got, want):
     return err <= TOL * np.abs(want).max(), err
 
 
+def _run(ctx, d, ws, norms, x, Kc, Vc, scale, base):
+    out = np.zeros(d["D"], np.float32)
+    dims = _dims(d, scale, base)
+    l0 = ctx.launches()
+    rc = ctx.L.ork_i8_mm_layer(ctx.ctx, C.byref(dims), *[w.h for w in ws], _p(norms[0]), _p(norms[1]),
+                               _p(norms[2]), _p(x), _p(Kc), _p(Vc), _p(out))
+    assert rc == 0
+    return out, ctx.launches() - l0
+
+
 @pytest.mark.parametrize("d", DIMS)
-def test_layer_matches_oracle(ctx, d):
+def test_layer_matches_oracle(ctx, path, d):
     Bs, norms, x, Kc, Vc = of.layer_inputs(21, d["D"], d["H"], d["Hkv"], d["dk"], d["Nff"], d["nkv"], d["pos"])
     scale, base = 1.0 / np.sqrt(d["dk"]), 1e6
     want, _, _ = of.layer(d, scale, base, Bs, norms, x, Kc, Vc)
     ws = _pack(ctx, Bs)
-    out = np.zeros(d["D"], np.float32)
-    dims = _dims(d, scale, base)
-    rc = ctx.L.ork_i8_mm_layer(ctx.ctx, C.byref(dims), *[w.h for w in ws], _p(norms[0]), _p(norms[1]),
-                               _p(norms[2]), _p(x), _p(Kc), _p(Vc), _p(out))
+    out, launches = _run(ctx, d, ws, norms, x, Kc, Vc, scale, base)
     for w in ws:
         w.free()
-    assert rc == 0
     ok, err = _close(out, want)
     print("max|err|", err, "scale", np.abs(want).max())
     assert ok, err
+    assert launches == 1 if path == "fused" else launches >= 9
+
+
+@pytest.mark.parametrize("fmt", ["u4", "nf4", "mixed"])
+def test_layer_int4_weights(ctx, env_clean, path, fmt):
+    """int4-weight / int8-activation stores (uniform and NF4 codes): the oracle runs the same layer on the
+    int8 codes the stores hold. A mix of formats takes the multi-launch form in both settings."""
+    d = DIMS[1]
+    Bs, norms, x, Kc, Vc = of.layer_inputs(25, d["D"], d["H"], d["Hkv"], d["dk"], d["Nff"], d["nkv"], d["pos"])
+    rng = np.random.default_rng(26)
+    ws, codes = [], []
+    for i, B in enumerate(Bs):
+        K, N = B.shape
+        if fmt == "mixed" and i % 2:
+            ws.append(ctx.i8_pack(B))
+            codes.append(B)
+            continue
+        if fmt == "nf4" or (fmt == "mixed" and i == 2):
+            env_clean.setenv("ORK_NF4", "1")
+        w, _ = ctx.i4a8_pack(rng.standard_normal((N, K), dtype=np.float32))
+        env_clean.delenv("ORK_NF4", raising=False)
+        ws.append(w)
+        codes.append(of.i4a8_blob_codes(w.dump(), K, N)[0])
+    scale, base = 1.0 / np.sqrt(d["dk"]), 1e6
+    want, _, _ = of.layer(d, scale, base, codes, norms, x, Kc, Vc)
+    out, launches = _run(ctx, d, ws, norms, x, Kc, Vc, scale, base)
+    for w in ws:
+        w.free()
+    ok, err = _close(out, want)
+    assert ok, err
+    assert launches == 1 if (path == "fused" and fmt != "mixed") else launches >= 9
 
 
 @pytest.mark.parametrize("p0,cap", [(5, 16), (95, 160)])
-def test_layer_decode_extension_graph_replay(ctx, p0, cap):
+def test_layer_decode_extension_graph_replay(ctx, path, p0, cap):
     """Three decode steps captured once in a CUDA graph: each step appends its k/v at the device position
     and attends over it, the position advancing on the device; compared step by step with the oracle.
     From position 95 the token's own key sits in the last of several key chunks, and the steps cross a
@@ -121,7 +166,7 @@ def test_layer_decode_extension_graph_replay(ctx, p0, cap):
         w.free()
 
 
-def test_layer_device_position_past_capacity_is_an_error(ctx):
+def test_layer_device_position_past_capacity_is_an_error(ctx, path):
     """A device-read position whose token would not fit the caches: the kernel's own check skips attention
     (no cache access), the sync reports the error once, and the context keeps working."""
     import torch
@@ -155,7 +200,7 @@ def test_layer_device_position_past_capacity_is_an_error(ctx):
         w.free()
 
 
-def test_layer_refusals(ctx):
+def test_layer_refusals(ctx, path):
     d = DIMS[0]
     Bs, norms, x, Kc, Vc = of.layer_inputs(23, d["D"], d["H"], d["Hkv"], d["dk"], d["Nff"], d["nkv"], d["pos"])
     ws = _pack(ctx, Bs)
