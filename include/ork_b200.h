@@ -43,6 +43,14 @@ int ork_i8_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA,
  * stride other than N must be decode-sized (M <= 8). Capturable in a CUDA graph. */
 int ork_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
 
+/* The fused output stages (ork_i8_mm_run_out8 / _out16 / _ewmul) over device pointers, enqueued without
+ * waiting. Decode-sized runs (M <= 8) requantize inside the matmul kernel; larger M use a context scratch
+ * for the int32 sums (allocated on first use: make one call before capturing a CUDA graph). */
+int ork_i8_mm_run_out8_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int8_t *dC, int mult, int shift);
+int ork_i8_mm_run_out16_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, short *dC, int mult, int shift);
+int ork_i8_mm_run_ewmul_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const int8_t *dG, int8_t *dC,
+                              int mult, int shift);
+
 /* ork_i8_mm_layer over device pointers, enqueued without waiting (the first layer call on a context
  * allocates its workspace: make one before capturing a CUDA graph), with an optional decode extension:
  *   k_norm   RMSNorm gain applied to the token's k per head (Qwen3's k-norm; NULL: none);

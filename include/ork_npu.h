@@ -243,6 +243,24 @@ int ork_i8_mm_run(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
 /* include/ork/run.h:111. W4A4: C int32 = A (int4 values in int8) x B; exact int32 accumulation. */
 int ork_i4_mm_run(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
 
+/* Fused output stages (include/ork/run.h:48-108). The int8 matmul's int32 sum requantized in the output
+ * stage: out = clamp(rne(acc * mult / 2^shift)) with rne = round half to even (the reference's own model
+ * of its NPU stage, examples/test_mm_i8_out8.c:24-33), clamped to int8 (out8) or int16 (out16); ewmul
+ * multiplies by G (int8 [M][N], e.g. silu(gate)) first: C = clamp_i8(rne(acc * G * mult / 2^shift)), the
+ * up projection of a fused SwiGLU. Weights: int8-compute (ork_i8_mm_pack(_f32), int4 stores). Returns 0;
+ * -2 for another weight kind, K not a multiple of 512 or above 4096, N not a multiple of 32 (the
+ * reference's limits, kept for identical refusals), or a negative mult / shift; -1 on NULL or overlapping
+ * buffers or a device error. M <= 0 does nothing and returns 0. Host or device buffers. */
+int ork_i8_mm_run_out8(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int8_t *C, int mult, int shift);
+int ork_i8_mm_run_out16(ork_npu *ctx, ork_w *w, int M, const int8_t *A, short *C, int mult, int shift);
+int ork_i8_mm_run_ewmul(ork_npu *ctx, ork_w *w, int M, const int8_t *A, const int8_t *G, int8_t *C, int mult,
+                        int shift);
+/* include/ork/sdp.h:45-52. Standalone element-wise multiply: out[m][n] = clamp_i8(rne(up * silu * mult /
+ * 2^shift)). -2 outside M 1..8176, N 16..8192 (multiple of 16), mult 0..0x7fff, shift 0..31; -1 on NULL
+ * or overlapping buffers. us (may be NULL) receives the kernel's device time in microseconds. */
+int ork_i8_npu_ewmul(ork_npu *ctx, const int8_t *up, const int8_t *silu, int M, int N, int mult, int shift,
+                     int8_t *out, double *us);
+
 /* include/ork/run.h:132. The API's explicit CPU int8 matmul (B row-major raw codes). It exists for
  * callers who want to time the CPU side of a routing decision; no run function above ever calls it. */
 void ork_i8_mm_run_cpu(int M, int K, int N, const int8_t *A, const int8_t *B, int32_t *C);

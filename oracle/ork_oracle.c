@@ -24,6 +24,34 @@
 #define ORC_API __attribute__((visibility("default")))
 
 /* ---------------------------------------------------------------------------------------------------
+ * Fused output stages (include/ork/run.h:48-108 ork_i8_mm_run_out8 / _out16 / _ewmul, include/ork/sdp.h:45-52
+ * ork_i8_npu_ewmul). The reference's model of the NPU's requant stage, which its own test compares the
+ * silicon against bit for bit (examples/test_mm_i8_out8.c:24-33 requant_i8): v = acc * mult in 64 bits,
+ * q = v >> shift (arithmetic floor), +1 when the remainder exceeds half or equals half with q odd (round
+ * half to even), then clamp. ewmul multiplies by the second operand before the stage; the standalone
+ * element-wise multiply is the same stage on up * silu (the operands of sdp.h:45). shift 0 keeps v. */
+static int64_t orc_rne_shift(int64_t v, int shift)
+{
+    if (shift <= 0) return v;
+    const int64_t q = v >> shift, rem = v - (q << shift), half = (int64_t)1 << (shift - 1);
+    return (rem > half || (rem == half && (q & 1))) ? q + 1 : q;
+}
+
+/* out[i] = clamp(rne((in[i] * (g ? g[i] : 1)) * mult / 2^shift)) for i < n; bits 8 -> int8, 16 -> int16 */
+ORC_API void orc_requant(size_t n, const int32_t *in, const int8_t *g, int mult, int shift, int bits, void *out)
+{
+    const int64_t hi = bits == 16 ? 32767 : 127, lo = -hi - 1;
+    for (size_t i = 0; i < n; i++) {
+        int64_t v = (int64_t)in[i] * mult;
+        if (g) v *= g[i];
+        int64_t q = orc_rne_shift(v, shift);
+        q = q > hi ? hi : q < lo ? lo : q;
+        if (bits == 16) ((int16_t *)out)[i] = (int16_t)q;
+        else ((int8_t *)out)[i] = (int8_t)q;
+    }
+}
+
+/* ---------------------------------------------------------------------------------------------------
  * Grouped (per-K-group scaled) GEMM. src/npu/core/buf.c:501-520 (orki_cpu_gemm_grouped), shared by
  * ork_i4_mm_run_grouped and ork_i8_mm_run_grouped offline: Sk = K/G; for each row m the fp32 row starts
  * at 0 and, for g ascending, gains ((float)acc * aScale[m*Sk+g]) * bScale[g*N+n] where acc is the exact

@@ -32,8 +32,11 @@
 
 #include <cstdlib>
 
+#include <type_traits>
+
 #include "nibble.cuh"
 #include "ork_internal.h"
+#include "requant.cuh"
 
 namespace orkb {
 
@@ -165,10 +168,30 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[kR], uint32_t sa, ui
 // TR channels per CTA (8 per warp-row group), WK = 4 / (TR / 8) warps split K.
 // One CTA's work of the staged kernel: channels [n0, n0 + TR) of the weight at W (N channels of K), the
 // activations A (M rows), C rows at a stride of cstride elements.
+// One result to C: the raw sum, or for int8-compute formats the requantized output stage.
+template <typename T>
+__device__ __forceinline__ void store_out(void *C, const OutStage &os, size_t idx, T v) {
+  if constexpr (std::is_floating_point<T>::value) {  // fp16 weights: fp32 sums, no output stage
+    reinterpret_cast<float *>(C)[idx] = v;
+  } else {
+    if (os.mode == OUT_I32) {
+      reinterpret_cast<int32_t *>(C)[idx] = v;
+      return;
+    }
+    int64_t p = (int64_t)v * os.mult;
+    if (os.mode == OUT_EWMUL) p *= os.G[idx];
+    const int64_t q = requant_rne(p, os.shift);
+    if (os.mode == OUT_I16)
+      reinterpret_cast<int16_t *>(C)[idx] = (int16_t)(q > 32767 ? 32767 : q < -32768 ? -32768 : q);
+    else
+      reinterpret_cast<int8_t *>(C)[idx] = (int8_t)(q > 127 ? 127 : q < -128 ? -128 : q);
+  }
+}
+
 template <int FMT, int MT, int TR>
 __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A,
                                            void *__restrict__ Cout, int M, int K, int N, int n0, int cstride,
-                                           const Tables &tb) {
+                                           const Tables &tb, const OutStage &os) {
   using T = typename Acc<FMT>::T;
   constexpr int WR = TR / (4 * kR);  // warp-row groups
   constexpr int WK = kWarps / WR;    // warps splitting K
@@ -248,14 +271,13 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
   if (V >= 8 && (j & 1)) base += V / 8;
   const bool writer = (V >= 8) || (V == 4 && !(j & 1)) || (V == 2 && !(j & 3)) || (V == 1 && j == 0);
 
-  T *C = reinterpret_cast<T *>(Cout);
   if constexpr (WK == 1) {
     if (writer) {
 #pragma unroll
       for (int i = 0; i < HELD; i++) {
         const int idx = base + i, r = idx / MT, m = idx % MT;
         const int lr = lrow0 + 4 * r;
-        if (m < M && lr < rows) C[(size_t)m * cstride + n0 + lr] = acc[i];
+        if (m < M && lr < rows) store_out<T>(Cout, os, (size_t)m * cstride + n0 + lr, acc[i]);
       }
     }
   } else {
@@ -273,7 +295,7 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
         T s = red[0][lr][m];
 #pragma unroll
         for (int q = 1; q < WK; q++) s += red[q][lr][m];
-        C[(size_t)m * cstride + n0 + lr] = s;
+        store_out<T>(Cout, os, (size_t)m * cstride + n0 + lr, s);
       }
     }
   }
@@ -283,7 +305,7 @@ template <int FMT, int MT, int TR>
 __global__ void __launch_bounds__(kWarps * 32)
 gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M, int K,
             int N, Tables tb) {
-  gemv_block<FMT, MT, TR>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb);
+  gemv_block<FMT, MT, TR>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb, OutStage{});
 }
 
 // Batched (chain / MoE) variant: many independent matmuls of one weight format in one launch. Task t
@@ -295,6 +317,7 @@ struct BatchTask {
   const uint8_t *A;
   void *C;
   int M, K, N, cstride, block0;
+  OutStage os;
 };
 struct BatchTable {
   BatchTask t[kMaxBatch];
@@ -311,7 +334,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_batched_kernel(const __grid_
     else hi = mid - 1;
   }
   const BatchTask &t = bt.t[lo];
-  gemv_block<FMT, MT, TR>(t.W, t.A, t.C, t.M, t.K, t.N, (b - t.block0) * TR, t.cstride, tb);
+  gemv_block<FMT, MT, TR>(t.W, t.A, t.C, t.M, t.K, t.N, (b - t.block0) * TR, t.cstride, tb, t.os);
 }
 
 // Grouped variant (per-K-group scales): same staging and arithmetic as gemv_kernel, but each warp walks
@@ -917,7 +940,8 @@ cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool 
       const ChainTask &c = t[i0 + j];
       if (c.fmt != fmt || !batched_supports(c.fmt, c.M, c.K)) return cudaErrorInvalidValue;
       if ((uintptr_t)c.W % 16 || (uintptr_t)c.A % 16) return cudaErrorMisalignedAddress;
-      bt.t[j] = BatchTask{(const uint8_t *)c.W, (const uint8_t *)c.A, c.C, c.M, c.K, c.N, c.cstride, blocks};
+      if (c.os.mode != OUT_I32 && c.fmt == FMT_F16) return cudaErrorInvalidValue;
+      bt.t[j] = BatchTask{(const uint8_t *)c.W, (const uint8_t *)c.A, c.C, c.M, c.K, c.N, c.cstride, blocks, c.os};
       blocks += (c.N + 7) / 8;
       mmax = c.M > mmax ? c.M : mmax;
       const size_t sm = fmt_row_bytes(c.fmt, c.K) * 8 + (size_t)c.M * c.K * (c.fmt == FMT_F16 ? 2 : 1);

@@ -60,13 +60,27 @@ cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, 
 // Batched decode: independent matmuls of one weight format in one launch of the staged decode kernel
 // (the chain / MoE entry points); each task M <= 8 with rows that fit the staged kernel
 // (batched_supports). C of task t is written at a row stride of cstride elements.
+// Output stage of an int8-compute matmul (the reference's fused requant outputs, include/ork/run.h:48-108):
+// OUT_I32 the raw int32 sums; OUT_I8 / OUT_I16 clamp(rne(acc * mult / 2^shift)) to int8 / int16;
+// OUT_EWMUL clamp_i8(rne(acc * G * mult / 2^shift)) with G int8 laid out like C. rne = round half to even.
+enum { OUT_I32 = 0, OUT_I8 = 1, OUT_I16 = 2, OUT_EWMUL = 3 };
+struct OutStage {
+  int mode, mult, shift;
+  const int8_t *G;
+};
 struct ChainTask {
   const void *W;
   const void *A;
   void *C;
   int M, K, N, cstride, fmt;
+  OutStage os;  // zero: raw int32 C
 };
 bool batched_supports(int fmt, int M, int K);
+// Elementwise output stages over n values (outstage.cu): requant of int32 sums, and the int8 x int8
+// element-wise multiply of ork_i8_npu_ewmul.
+cudaError_t launch_requant(const int32_t *C, size_t n, const OutStage &os, void *out, cudaStream_t s);
+cudaError_t launch_ewmul_i8(const int8_t *a, const int8_t *b, size_t n, int mult, int shift, int8_t *out,
+                            cudaStream_t s);
 cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool pdl, int *launches);
 bool grouped_supports(int fmt, int K, int G);
 

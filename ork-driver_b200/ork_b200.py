@@ -46,6 +46,13 @@ SIGNATURES = [
     ("ork_i4_mm_run", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_cpu", None, [_i, _i, _i, _vp, _vp, _vp]),
     ("ork_i8_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_i8_mm_run_out8", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+    ("ork_i8_mm_run_out16", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+    ("ork_i8_mm_run_ewmul", _i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
+    ("ork_i8_mm_run_out8_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+    ("ork_i8_mm_run_out16_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+    ("ork_i8_mm_run_ewmul_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
+    ("ork_i8_npu_ewmul", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, C.POINTER(C.c_double)]),
     ("ork_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_noalloc", _i, [_vp, _vp, _i, _vp, _vp]),

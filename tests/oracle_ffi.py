@@ -49,6 +49,8 @@ def restated():
         lib.orc_layer_i8.argtypes = [C.c_void_p, C.c_double, C.c_double] + [C.c_void_p] * 7 + [C.c_void_p] * 7 + \
             [C.c_int, C.c_void_p, C.c_int]
         lib.orc_gemm_grouped.restype = C.c_int
+        lib.orc_requant.argtypes = [C.c_size_t, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
+        lib.orc_requant.restype = None
         lib.orc_gemm_grouped.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_void_p]
         _restated = lib
@@ -264,3 +266,17 @@ class Lcg:
 
     def skip(self, n):
         self.sd = C.c_uint32(restated().orc_lcg_skip(self.sd.value, n))
+
+
+def requant(acc, mult, shift, bits=8, g=None):
+    """The fused output stage on int32 sums (optionally times g first): the reference's requant model
+    (examples/test_mm_i8_out8.c:24-33), restated in oracle/ork_oracle.c."""
+    acc = np.ascontiguousarray(acc, np.int32)
+    out = np.empty(acc.shape, np.int16 if bits == 16 else np.int8)
+    gp = None
+    if g is not None:
+        g = np.ascontiguousarray(g, np.int8)
+        assert g.shape == acc.shape
+        gp = _p(g)
+    restated().orc_requant(acc.size, _p(acc), gp, int(mult), int(shift), bits, _p(out))
+    return out
