@@ -283,22 +283,40 @@ def run_70b(args):
     head = [(Kh, Nv // head_chunks, packed(Kh, Nv // head_chunks, 1)[0]) for _ in range(head_chunks)]
     A = {8192: torch.randint(-127, 128, (M, 8192), dtype=torch.int8, device="cuda"),
          28672: torch.randint(-127, 128, (M, 28672), dtype=torch.int8, device="cuda")}
-    Cl = {name: torch.empty((M, N // world), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
-    Cf = {name: torch.empty((M, N), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
-    Chl = torch.empty((M, Nv // head_chunks // world), dtype=torch.int32, device="cuda")
-    Chf = torch.empty((M, Nv // head_chunks), dtype=torch.int32, device="cuda")
+    p2p = world > 1 and args.gather == "p2p"
+    if p2p:
+        # the gather fused into the matmul: each rank's decode kernel stores its columns into every rank's C
+        # over NVLink and signals; a bounded wait on the stream makes C complete before the next matmul
+        peers = shard.PeerGroup(ctx, dist)
+        tab = {name: peers.table(M, N, N // world)[0] for name, K, N in L70["linears"]}
+        tab_head = peers.table(M, Nv // head_chunks, Nv // head_chunks // world)[0]
+    else:
+        Cl = {name: torch.empty((M, N // world), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
+        Cf = {name: torch.empty((M, N), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
+        Chl = torch.empty((M, Nv // head_chunks // world), dtype=torch.int32, device="cuda")
+        Chf = torch.empty((M, Nv // head_chunks), dtype=torch.int32, device="cuda")
 
     def run(w, a, cl, cf):
         assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), cl.data_ptr()) == 0
         if world > 1:
             shard.gather_columns(cl, dist, out=cf)
 
+    def run_p2p(w, a, t):
+        assert L.ork_i8_mm_run_peers_async(ctx.ctx, w.h, M, a.data_ptr(), t) == 0
+        assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
+
     def one_pass():
         for layer in range(L70["layers"]):
             for name, K, N in L70["linears"]:
-                run(lin[name][2][layer % ncopies], A[K], Cl[name], Cf[name])
+                if p2p:
+                    run_p2p(lin[name][2][layer % ncopies], A[K], tab[name])
+                else:
+                    run(lin[name][2][layer % ncopies], A[K], Cl[name], Cf[name])
         for K, N, w in head:
-            run(w, A[K], Chl, Chf)
+            if p2p:
+                run_p2p(w, A[K], tab_head)
+            else:
+                run(w, A[K], Chl, Chf)
 
     with torch.cuda.stream(stream):
         one_pass()  # eager warm-up: kernel attributes, tensor maps, NCCL communicator
@@ -336,7 +354,9 @@ def run_70b(args):
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": "Llama-70B-shaped linears, NF4 weights ~N(0,0.02), 80 layers x (QKV 8192x10240, "
                                    "O 8192x8192, gate+up 8192x57344, down 28672x8192) + LM head 8192x128256, "
-                                   f"column-sharded over {world} GPU(s), NCCL all-gather of each int32 C",
+                                   f"column-sharded over {world} GPU(s), "
+                                   + ("gather fused into each matmul over NVLink peer memory (P2P stores + "
+                                      "bounded signal wait)" if p2p else "NCCL all-gather of each int32 C"),
                        "M": M, "parallelism": f"column shard x{world}",
                        "l2": f"inputs larger than L2: {ncopies} distinct copies of the per-rank layer weights "
                              f"({ncopies * layer_bytes / 2**20:.0f} MiB) cycled over the 80 layers"},
@@ -350,6 +370,8 @@ def run_70b(args):
             w.free()
     for _, _, w in head:
         w.free()
+    if p2p:
+        peers.close()
     ctx.close()
     if dist.is_initialized():
         dist.destroy_process_group()
@@ -362,8 +384,8 @@ Q3 = {"H": 2048, "NH": 16, "NKV": 8, "D": 128, "FF": 6144, "layers": 28, "V": 15
 
 def run_qwen3(args):
     """random-init (~N(0,0.02)) Qwen3-1.7B-shaped w8a8 stack; every projection's weight is
-    packed per output channel by ork_i8_mm_pack_f32. Decode (the headline): each of the 28 layers is one
-    ork_i8_mm_layer_async call -- the library's decode layer: RMSNorm + int8 quantization, q/k/v in one
+    packed per output channel by ork_i8_mm_pack_f32. Decode (the headline): the 28 layers are one
+    ork_i8_mm_layers_async call (one persistent launch) -- the library's decode layer: RMSNorm + int8 quantization, q/k/v in one
     batched launch, q/k RMSNorm + RoPE + attention over the fp32 KV cache (the token's k/v appended at the
     device-side position), o, residual + RMSNorm + quantization, gate/up in one launch, SwiGLU +
     quantization, down, residual -- then the final norm and the LM head (ork_i8_mm_run_async) and a greedy
@@ -376,7 +398,7 @@ def run_qwen3(args):
     import torch.nn.functional as F
 
     import ork_b200
-    from ork_b200 import LayerDims, LayerKV
+    from ork_b200 import LayerDims, LayerKV, LayerW
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     rank = int(os.environ.get("RANK", "0"))
@@ -461,16 +483,16 @@ def run_qwen3(args):
     dims = LayerDims(H, NH, NKV, D, D, FF, PRE, PRE, 1.0 / float(np.sqrt(D)), Q3["theta"])
     kv = LayerKV(ones_d.data_ptr(), 1, MAXT, pos.data_ptr())
 
+    # the 28 layers as one ork_i8_mm_layers_async call (one persistent launch per token)
+    stack = (LayerW * NLY)(*[LayerW(*[wsets[li % NDIST][n][0].h for n in names], ones_h.data_ptr(), ones_d.data_ptr(),
+                                    ones_h.data_ptr(), ones_d.data_ptr(), kc[li].data_ptr(), vc[li].data_ptr())
+                             for li in range(NLY)])
+
     def decode_step():
         xa.copy_(emb.index_select(0, tok).float().view(-1))
-        bufs = (xa, xb)
-        for li in range(NLY):
-            ws = wsets[li % NDIST]
-            xi, xo = bufs[li % 2], bufs[(li + 1) % 2]
-            assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[ws[n][0].h for n in names],
-                                           ones_h.data_ptr(), ones_d.data_ptr(), ones_h.data_ptr(), xi.data_ptr(),
-                                           kc[li].data_ptr(), vc[li].data_ptr(), xo.data_ptr(), C.byref(kv)) == 0
-        logits = linear(rmsnorm(bufs[NLY % 2].view(1, -1), ones_h), lm)
+        assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NLY, stack, xa.data_ptr(), xb.data_ptr(),
+                                        C.byref(kv)) == 0
+        logits = linear(rmsnorm(xb.view(1, -1), ones_h), lm)
         tok.copy_(logits.argmax(-1))
         pos.add_(1)
 
@@ -517,8 +539,8 @@ def run_qwen3(args):
             "config": {"workload": "Qwen3-1.7B-shaped w8a8 stack, random weights ~N(0,0.02): 28 layers, hidden 2048, "
                                    "16/8 heads x 128, SwiGLU 6144, vocab 151936, q/k norms, RoPE 1e6; prefill 128 "
                                    "then 256 greedy decode steps, batch 1",
-                       "linears": "decode: every layer through ork_i8_mm_layer_async (the library's decode layer: "
-                                  "its own glue kernels around its matmuls), LM head through ork_i8_mm_run_async; "
+                       "linears": "decode: the 28 layers as one ork_i8_mm_layers_async call (the library's decode "
+                                  "layer, one persistent launch), LM head through ork_i8_mm_run_async; "
                                   "prefill: PyTorch glue around ork_i8_mm_run_async",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
                        "parallelism": "replicas" if world > 1 else "single GPU"},
@@ -906,6 +928,8 @@ def main():
                          "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack; grouped: grouped-scale W4A8 decode; "
                          "moe: a batch of 64 NF4 expert matmuls through ork_i8_mm_run_chain")
     ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="70b workload at N > 1: the C gather fused into the matmul over peer memory, or NCCL")
     ap.add_argument("--profile", default=None,
                     help="K,N,M[,route[,fmt]]: run one config a few times eagerly (for ncu captures); fmt i8|u4|nf4")
     args = ap.parse_args()

@@ -73,6 +73,48 @@ int ork_i8_mm_layer_async(ork_npu *ctx, const struct ork_layer_dims *d, ork_w *w
                           const float *ffn_norm, const float *x, float *Kc, float *Vc, float *x_out,
                           const ork_b200_layer_kv *kv);
 
+/* Several consecutive decode layers in one call: layer l's output is layer l+1's input, x feeds the first
+ * and x_out receives the last. Same dims (d) and one int8-compute weight format for all layers; kv's
+ * append / hstride / dpos apply to every layer, each layer's k-norm is its own (k_norm, may be NULL; kv's
+ * k_norm is not used). When the layers fit the persistent kernel the whole stack is ONE launch whose
+ * weight stream runs across layer boundaries; otherwise the multi-launch form runs layer by layer. The
+ * first call with a given list of layers uploads its pointer table (make it before capturing a CUDA graph).
+ * Returns as ork_i8_mm_layer_async. */
+typedef struct ork_b200_layer_w {
+  ork_w *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+  const float *attn_norm, *q_norm, *ffn_norm, *k_norm;
+  float *Kc, *Vc;
+} ork_b200_layer_w;
+int ork_i8_mm_layers_async(ork_npu *ctx, const struct ork_layer_dims *d, int nlayers, const ork_b200_layer_w *layers,
+                           const float *x, float *x_out, const ork_b200_layer_kv *kv);
+
+/* Column-sharded runs with the gather fused into the matmul (one process per GPU, NVLink peer memory).
+ * Rank g of R holds output channels [col0, col0 + ncols) of a weight; its run writes those columns of C
+ * into EVERY rank's C buffer ([M][ldc] int32) and signals every rank once per CTA; a rank that needs C
+ * waits with ork_b200_peers_wait_async (bounded: an expired wait reports an error at the next sync).
+ * Buffers come from ork_b200_sym_alloc (device memory + its CUDA IPC handle, ORK_B200_IPC_HANDLE_BYTES
+ * bytes, exchanged by the caller over any transport) and ork_b200_sym_open (a peer's buffer mapped here).
+ * flags[r] is rank r's signal block (at least 4 * R bytes of a symmetric buffer, zero at allocation).
+ * M <= 8 runs are one kernel (matmul + peer stores + signal); larger M add one scatter kernel. Rule: read
+ * C before starting the next peer run on this rank (a peer rewrites C only after a later signal of ours).
+ * Returns 0 / NULL-free on success, -1 (NULL) on bad arguments or CUDA errors. No counterpart in
+ * ork-driver, which gathers its cores' column slices on the host (src/npu.c:1356-1398). */
+#define ORK_B200_IPC_HANDLE_BYTES 64
+typedef struct ork_b200_peers ork_b200_peers;
+void *ork_b200_sym_alloc(ork_npu *ctx, size_t bytes, void *handle_out);
+int ork_b200_sym_free(ork_npu *ctx, void *p);
+void *ork_b200_sym_open(ork_npu *ctx, const void *handle);
+int ork_b200_sym_close(ork_npu *ctx, void *peer);
+ork_b200_peers *ork_b200_peers_create(ork_npu *ctx, int nranks, int rank, void *const *C, void *const *flags, int ldc,
+                                      int col0, int ncols);
+void ork_b200_peers_destroy(ork_b200_peers *p);
+int ork_i8_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
+int ork_i4_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
+int ork_b200_peers_wait_async(ork_npu *ctx, ork_b200_peers *p);
+/* Copy `bytes` between any two host / device addresses, ordered after the context's queued work, and wait
+ * for it (for callers without a CUDA binding of their own, e.g. to read a symmetric buffer). 0 or -1. */
+int ork_b200_copy(ork_npu *ctx, void *dst, const void *src, size_t bytes);
+
 /* The load-time header check of the .orkpack loaders, callable without a device: 0 when `blob` is a
  * stamped blob of this build for (dtype, K, N), else ORK_PACKERR_SHORT / _UNSTAMPED / _FORMAT / _CAPS /
  * _SHAPE, checked in that order (ork-driver src/npu/core/packhdr.c). And the caps id this build stamps. */

@@ -41,8 +41,8 @@ int route_for(const ork_npu *c, const ork_w *w, int M) {
 // Sticky device-side error flags (a bounded wait that expired); cleared when read.
 bool device_error() {
   const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true), l = layer_error_flag(true),
-                     f = fused_error_flag(true);
-  return (t | g | l | f) != 0;
+                     f = fused_error_flag(true), p = peer_error_flag(true);
+  return (t | g | l | f | p) != 0;
 }
 
 void log_err(const char *what, cudaError_t e) {
@@ -227,7 +227,9 @@ void ork_npu_free(ork_npu *c) {
     if (c->dC) cudaFree(c->dC);
     if (c->dS) cudaFree(c->dS);
     ring_free(c);
+    layer_tabs_free(c);
     if (c->dL) cudaFree(c->dL);
+    if (c->dX) cudaFree(c->dX);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;

@@ -28,6 +28,8 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <new>
 #include <vector>
 
 #include "glue.cuh"
@@ -424,9 +426,9 @@ static int attn_kpc(int maxk, int Sg) { return std::max(32, (maxk + 32 * Sg - 1)
 static size_t attn_smem(int dk, int kpc) { return (size_t)(3 * dk + kpc + kAttnWarps * dk + kMaxSplit) * 4; }
 
 // Epoch-tagged words of the persistent layer: q, k, v, o, chunk maxima and sums, chunk rows, ao, head
-// maxima, h, CTA maxima.
+// maxima, h, CTA maxima, the residual stream between layers.
 static size_t ll_words(int D, int H, int Nq, int Nk, int F, int dk, int Sg) {
-  return (size_t)Nq + 2 * (size_t)Nk + D + 2 * (size_t)H * Sg + (size_t)H * Sg * dk + Nq + H + F + kMaxGrid;
+  return (size_t)Nq + 2 * (size_t)Nk + D + 2 * (size_t)H * Sg + (size_t)H * Sg * dk + Nq + H + F + kMaxGrid + D;
 }
 
 // The attention kernel's running maximum and CTA counters sit in a fixed region at the start of the
@@ -481,6 +483,106 @@ static bool layer_ws(ork_npu *c, int D, int H, int Nq, int Nk, int F, int dk, in
   return true;
 }
 
+// Device copies of persistent-layer tables, one per distinct list of layer pointers, uploaded when first
+// seen (outside CUDA-graph capture) and kept for the context's life.
+struct LayerTabs {
+  std::vector<std::pair<std::vector<FusedLayerW>, FusedLayerW *>> e;
+};
+
+void layer_tabs_free(ork_npu *c) {
+  LayerTabs *t = (LayerTabs *)c->ltabs;
+  if (!t) return;
+  for (auto &p : t->e) cudaFree(p.second);
+  delete t;
+  c->ltabs = nullptr;
+}
+
+static const FusedLayerW *layer_tab(ork_npu *c, const FusedLayerW *lw, int n) {
+  if (!c->ltabs) c->ltabs = new (std::nothrow) LayerTabs;
+  LayerTabs *t = (LayerTabs *)c->ltabs;
+  if (!t) return nullptr;
+  for (auto &p : t->e)
+    if ((int)p.first.size() == n && !memcmp(p.first.data(), lw, sizeof(FusedLayerW) * n)) return p.second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    fprintf(stderr, "[ork] ERROR ork_i8_mm_layer: a new list of layers during CUDA-graph capture; make one call "
+                    "with these layers before capturing\n");
+    return nullptr;
+  }
+  if (t->e.size() >= 4096) {  // bound the cache: drop everything (no graph may still use an old table...)
+    fprintf(stderr, "[ork] ERROR ork_i8_mm_layer: more than 4096 distinct layer lists on one context\n");
+    return nullptr;
+  }
+  FusedLayerW *d = nullptr;
+  if (cudaMalloc(&d, sizeof(FusedLayerW) * n) != cudaSuccess) return nullptr;
+  if (cudaMemcpy(d, lw, sizeof(FusedLayerW) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(d);
+    return nullptr;
+  }
+  t->e.emplace_back(std::vector<FusedLayerW>(lw, lw + n), d);
+  return d;
+}
+
+// Enqueue n consecutive layers as one persistent launch (layer_fused.cu). W = the first layer's seven
+// weights (dims and format are shared by all layers). Returns 0 when enqueued, -1 on an error, 1 when
+// the persistent form does not apply (another format in the list, a plan that does not fit, or
+// ORKB_LAYER_FUSED=0) and the caller must run the multi-launch form.
+int fused_enqueue(ork_npu *c, const ork_layer_dims *d, const FusedLayerW *lw, int n, int fmt, ork_w *const *W,
+                  const float *x, float *x_out, const ork_b200_layer_kv *kv) {
+  const int D = (int)d->D, H = (int)d->H, Hkv = (int)d->Hkv, dk = (int)d->dk, F = (int)d->Nff;
+  const int Nq = H * dk, Nk = Hkv * dk;
+  const bool ext = kv && kv->append;
+  const int maxk = (kv && kv->dpos) ? kv->hstride : (int)d->nkv + (ext ? 1 : 0);
+  const int G = fused_grid(c->device);
+  if (G < 1 || G > kMaxGrid) return 1;
+  for (int i = 0; i < 7; i++)
+    if (W[i]->fmt != fmt) return 1;
+  if (const char *e = getenv("ORKB_LAYER_FUSED"))
+    if (atoi(e) == 0) return 1;
+  FusedArgs fa = {};
+  fa.D = D, fa.H = H, fa.Hkv = Hkv, fa.dk = dk, fa.F = F;
+  fa.Sg = fused_splits(H, maxk, G);
+  fa.kpc = fused_kpc(maxk, fa.Sg);
+  if (!fused_plan(&fa, fmt, G)) return 1;
+  const int Sg = fa.Sg;
+  LayerWs ws;
+  if (!layer_ws(c, D, H, Nq, Nk, F, dk, Sg, &ws)) return -1;
+  if (n == 1) {  // one layer: its pointers travel in the kernel parameters (any capture may use them)
+    fa.lw = nullptr;
+    fa.lw0 = *lw;
+  } else {
+    fa.lw = layer_tab(c, lw, n);
+    if (!fa.lw) return -1;
+  }
+  fa.nl = n;
+  fa.ext = ext ? 1 : 0;
+  fa.x = x;
+  fa.x_out = x_out;
+  fa.nkv = (int)d->nkv;
+  fa.pos = (int)d->pos;
+  fa.hstride = (kv && kv->hstride > 0) ? kv->hstride : (int)d->nkv;
+  fa.dpos = kv ? kv->dpos : nullptr;
+  fa.scale = (float)d->attn_scale;
+  fa.base = (float)d->rope_base;
+  uint64_t *l = ws.ll;
+  auto take = [&](size_t m) {
+    uint64_t *r = l;
+    l += m;
+    return r;
+  };
+  fa.q = take(Nq), fa.k = take(Nk), fa.v = take(Nk), fa.o = take(D);
+  fa.pm = take((size_t)H * Sg), fa.pz = take((size_t)H * Sg), fa.po = take((size_t)H * Sg * dk);
+  fa.ao = take(Nq), fa.amax = take(H), fa.h = take(F), fa.hmax = take(kMaxGrid), fa.xl = take(D);
+  fa.epoch = ws.epoch, fa.sync = ws.sync;
+  const cudaError_t e = launch_layer_fused(fa, fmt, G, c->stream);
+  if (e != cudaSuccess) {
+    log_err("ork_i8_mm_layer (persistent)", e);
+    return -1;
+  }
+  c->launches += 1;
+  return 0;
+}
+
 // Enqueue one layer on the context's stream; every pointer is device memory. kv may be null (the
 // reference's behaviour: caches read only, nkv keys).
 int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const float *attn_norm, const float *q_norm,
@@ -493,56 +595,15 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
   const int maxk = (kv && kv->dpos) ? kv->hstride : (int)d->nkv + (ext ? 1 : 0);
   // the persistent one-launch layer (layer_fused.cu) when the seven weights share an int8-compute format
   // and its plan fits; ORKB_LAYER_FUSED=0 selects the multi-launch form
-  FusedArgs fa = {};
-  const int G = fused_grid(c->device);
-  bool fused = G > 0 && G <= kMaxGrid;
-  for (int i = 0; i < 7 && fused; i++) fused = W[i]->fmt == W[0]->fmt;
-  if (const char *e = getenv("ORKB_LAYER_FUSED")) fused = fused && atoi(e) != 0;
-  if (fused) {
-    fa.D = D, fa.H = H, fa.Hkv = Hkv, fa.dk = dk, fa.F = F;
-    fa.Sg = fused_splits(H, maxk, G);
-    fa.kpc = fused_kpc(maxk, fa.Sg);
-    fused = fused_plan(&fa, W[0]->fmt, G);
-  }
-  const int Sg = fused ? fa.Sg : attn_splits(H, maxk), kpc = attn_kpc(maxk, Sg);
+  FusedLayerW lw;
+  for (int i = 0; i < 7; i++) lw.W[i] = (const uint8_t *)W[i]->d;
+  lw.attn_norm = attn_norm, lw.q_norm = q_norm, lw.k_norm = kv ? kv->k_norm : nullptr, lw.ffn_norm = ffn_norm;
+  lw.Kc = const_cast<float *>(Kc), lw.Vc = const_cast<float *>(Vc);
+  const int fr = fused_enqueue(c, d, &lw, 1, W[0]->fmt, W, x, x_out, kv);
+  if (fr != 1) return fr;  // 0 done, -1 error; 1: not eligible, run the multi-launch form
+  const int Sg = attn_splits(H, maxk), kpc = attn_kpc(maxk, Sg);
   LayerWs ws;
   if (!layer_ws(c, D, H, Nq, Nk, F, dk, Sg, &ws)) return -1;
-  if (fused) {
-    for (int i = 0; i < 7; i++) fa.W[i] = (const uint8_t *)W[i]->d;
-    fa.attn_norm = attn_norm;
-    fa.q_norm = q_norm;
-    fa.k_norm = kv ? kv->k_norm : nullptr;
-    fa.ffn_norm = ffn_norm;
-    fa.x = x;
-    fa.Kc = Kc;
-    fa.Vc = Vc;
-    fa.Kw = ext ? const_cast<float *>(Kc) : nullptr;
-    fa.Vw = ext ? const_cast<float *>(Vc) : nullptr;
-    fa.x_out = x_out;
-    fa.nkv = (int)d->nkv;
-    fa.pos = (int)d->pos;
-    fa.hstride = (kv && kv->hstride > 0) ? kv->hstride : (int)d->nkv;
-    fa.dpos = kv ? kv->dpos : nullptr;
-    fa.scale = (float)d->attn_scale;
-    fa.base = (float)d->rope_base;
-    uint64_t *l = ws.ll;
-    auto take = [&](size_t n) {
-      uint64_t *r = l;
-      l += n;
-      return r;
-    };
-    fa.q = take(Nq), fa.k = take(Nk), fa.v = take(Nk), fa.o = take(D);
-    fa.pm = take((size_t)H * Sg), fa.pz = take((size_t)H * Sg), fa.po = take((size_t)H * Sg * dk);
-    fa.ao = take(Nq), fa.amax = take(H), fa.h = take(F), fa.hmax = take(kMaxGrid);
-    fa.epoch = ws.epoch, fa.sync = ws.sync;
-    const cudaError_t e = launch_layer_fused(fa, W[0]->fmt, G, c->stream);
-    if (e != cudaSuccess) {
-      log_err("ork_i8_mm_layer (persistent)", e);
-      return -1;
-    }
-    c->launches += 1;
-    return 0;
-  }
   static bool attrs = false;  // the glue kernels may use up to 200 KB of dynamic shared memory
   if (!attrs) {
     const void *k[] = {(const void *)norm_quant_kernel, (const void *)swiglu_quant_kernel,
@@ -757,6 +818,45 @@ int ork_i8_mm_layer_async(ork_npu *c, const struct ork_layer_dims *d, ork_w *wq,
   if (!c || !attn_norm || !q_norm || !ffn_norm || !x || !Kc || !Vc || !x_out || !dims_ok(d, W, kv)) return -3;
   DeviceGuard dg(c->device);
   return layer_enqueue(c, d, W, attn_norm, q_norm, ffn_norm, x, Kc, Vc, x_out, kv);
+}
+
+int ork_i8_mm_layers_async(ork_npu *c, const struct ork_layer_dims *d, int n, const ork_b200_layer_w *L,
+                           const float *x, float *x_out, const ork_b200_layer_kv *kv) {
+  if (!c || !L || !x || !x_out || n < 1 || n > 1024) return -3;
+  for (int l = 0; l < n; l++) {
+    const ork_b200_layer_w &y = L[l];
+    ork_w *W[7] = {y.wq, y.wk, y.wv, y.wo, y.wg, y.wu, y.wd};
+    if (!y.attn_norm || !y.q_norm || !y.ffn_norm || !y.Kc || !y.Vc || !dims_ok(d, W, kv)) return -3;
+    if (y.wq->fmt != L[0].wq->fmt) return -3;
+    for (int i = 1; i < 7; i++)
+      if (W[i]->fmt != W[0]->fmt) return -3;
+  }
+  DeviceGuard dg(c->device);
+  std::vector<FusedLayerW> tab(n);
+  for (int l = 0; l < n; l++) {
+    const ork_b200_layer_w &y = L[l];
+    ork_w *W[7] = {y.wq, y.wk, y.wv, y.wo, y.wg, y.wu, y.wd};
+    for (int i = 0; i < 7; i++) tab[l].W[i] = (const uint8_t *)W[i]->d;
+    tab[l].attn_norm = y.attn_norm, tab[l].q_norm = y.q_norm, tab[l].k_norm = y.k_norm;
+    tab[l].ffn_norm = y.ffn_norm, tab[l].Kc = y.Kc, tab[l].Vc = y.Vc;
+  }
+  ork_w *W0[7] = {L[0].wq, L[0].wk, L[0].wv, L[0].wo, L[0].wg, L[0].wu, L[0].wd};
+  const int fr = fused_enqueue(c, d, tab.data(), n, W0[0]->fmt, W0, x, x_out, kv);
+  if (fr != 1) return fr;
+  // the multi-launch form, layer by layer, the residual stream through two context buffers
+  const size_t xb = ((size_t)d->D * 4 + 255) & ~(size_t)255;
+  if (n > 1 && !grow(&c->dX, &c->capX, 2 * xb)) return -1;
+  const float *xi = x;
+  for (int l = 0; l < n; l++) {
+    const ork_b200_layer_w &y = L[l];
+    ork_w *W[7] = {y.wq, y.wk, y.wv, y.wo, y.wg, y.wu, y.wd};
+    float *xo = l == n - 1 ? x_out : (float *)((uint8_t *)c->dX + (l & 1) * xb);
+    ork_b200_layer_kv k1 = kv ? *kv : ork_b200_layer_kv{nullptr, 0, 0, nullptr};
+    k1.k_norm = y.k_norm;
+    if (layer_enqueue(c, d, W, y.attn_norm, y.q_norm, y.ffn_norm, xi, y.Kc, y.Vc, xo, &k1)) return -1;
+    xi = xo;
+  }
+  return 0;
 }
 
 }  // extern "C"

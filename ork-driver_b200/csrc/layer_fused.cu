@@ -239,13 +239,15 @@ __device__ void produce(const FusedArgs &a, uint32_t ring, uint32_t full0, uint3
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   uint32_t k = 0, s = 0, use = 0;
-  for (int p = 0; p < 4; p++) {
+  for (int lp = 0; lp < 4 * a.nl; lp++) {  // every layer's phases in order: the stream never pauses
+    const int p = lp & 3;
+    const FusedLayerW *lw = a.lw ? a.lw + (lp >> 2) : &a.lw0;
     Range r[3];
     const int n = ranges(a, p, blockIdx.x, G, r);
     for (int i = 0; i < n; i++) {
       const uint32_t rowB = row_bytes<FMT>(wK(a, r[i].w));
       const int rps = (int)(a.slot / rowB);
-      const uint8_t *W = a.W[r[i].w];
+      const uint8_t *W = lw->W[r[i].w];
       for (int r0 = r[i].r0; r0 < r[i].r1; r0 += rps, k++) {
         const int nr = min(rps, r[i].r1 - r0);
         if (use > 0) mbar_wait(empty0 + 8 * s, (use - 1) & 1);  // the slot's previous rows consumed
@@ -343,7 +345,8 @@ struct Plan {
   uint64_t *C[3];  // phase 0: q, k, v (by weight); phase 1: o
   int *loc;       // phase 2: this CTA's gate results, then its up results (nf each)
   int f0, nf;
-  float *out;     // phase 3: x_out = x1 + v / s
+  float *out;     // phase 3: x_out = x1 + v / s (the last layer), or
+  uint64_t *xl;   // phase 3: the next layer's x as tagged words
   const float *x1;
   float s;
 };
@@ -382,8 +385,10 @@ __device__ __noinline__ uint32_t consume(const FusedArgs &a, const Plan &pl, int
             ll_put(C + row, (uint32_t)v, ep);
           else if (p == 2)
             pl.loc[(w == 4 ? 0 : pl.nf) + row - pl.f0] = v;
-          else
+          else if (pl.out)
             pl.out[row] = pl.x1[row] + v / pl.s;
+          else
+            ll_putf(pl.xl + row, pl.x1[row] + v / pl.s, ep);
         }
       }
       __syncwarp();
@@ -425,15 +430,15 @@ __device__ __forceinline__ void head_vec(const uint32_t (&c)[PER], float sx, con
 // j0 + w + 16 u with an online softmax (running max, rescaled sums); the CTA then combines its warps'
 // maxima, sums and V rows into the item's partials. y: scratch, [kCW][dk] rows then 2 * kCW floats.
 template <int PER>
-__device__ void attend(const FusedArgs &a, int h, int sp, int kpc, int nkv, int nk, int pos, float sx, float *y,
-                       uint32_t ep) {
+__device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp, int kpc, int nkv, int nk, int pos,
+                       float sx, float *y, uint32_t ep) {
   constexpr int dk = 32 * PER;
   const int t = threadIdx.x, lane = t & 31, wp = t >> 5;
   const int grp = a.H / a.Hkv, hk = h / grp, Sg = a.Sg;
-  const bool ext = a.Kw != nullptr;
+  const bool ext = a.ext != 0;
   const int j0 = sp * kpc, j1 = min(nk, j0 + kpc);
   const bool own = ext && j0 <= nkv && nkv < j1;
-  const float *Kh = a.Kc + (size_t)hk * a.hstride * dk, *Vh = a.Vc + (size_t)hk * a.hstride * dk;
+  const float *Kh = lw.Kc + (size_t)hk * a.hstride * dk, *Vh = lw.Vc + (size_t)hk * a.hstride * dk;
   // the raw q (and the token's own k, v): one round of polls
   uint32_t cq[PER], ck[PER], cv[PER];
   ll_get_n<PER>(a.q + h * dk, lane, 32, dk, ep, cq);
@@ -442,16 +447,16 @@ __device__ void attend(const FusedArgs &a, int h, int sp, int kpc, int nkv, int 
     ll_get_n<PER>(a.v + hk * dk, lane, 32, dk, ep, cv);
   }
   float q[PER], kn[PER], vn[PER];
-  head_vec<PER>(cq, sx, a.q_norm, pos, a.base, lane, q);
+  head_vec<PER>(cq, sx, lw.q_norm, pos, a.base, lane, q);
   if (own) {
-    head_vec<PER>(ck, sx, a.k_norm, pos, a.base, lane, kn);
+    head_vec<PER>(ck, sx, lw.k_norm, pos, a.base, lane, kn);
 #pragma unroll
     for (int i = 0; i < PER; i++) vn[i] = (int32_t)cv[i] / sx;
     if (h % grp == 0 && wp == 0)  // the group's first query head stores the token's k and v
 #pragma unroll
       for (int i = 0; i < PER; i++) {
-        a.Kw[((size_t)hk * a.hstride + nkv) * dk + lane + 32 * i] = kn[i];
-        a.Vw[((size_t)hk * a.hstride + nkv) * dk + lane + 32 * i] = vn[i];
+        lw.Kc[((size_t)hk * a.hstride + nkv) * dk + lane + 32 * i] = kn[i];
+        lw.Vc[((size_t)hk * a.hstride + nkv) * dk + lane + 32 * i] = vn[i];
       }
   }
   float m = -3.0e38f, z = 0.0f, acc[PER];
@@ -575,182 +580,200 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int t = threadIdx.x;
   const int D = a.D, F = a.F, Nq = a.H * dk;
-  const uint32_t ep = *(volatile unsigned int *)a.epoch + 1u;  // this launch's epoch
+  const uint32_t ep0 = *(volatile unsigned int *)a.epoch + 1u;  // the first layer's tag; layer l: ep0 + l
   const uint32_t a8 = ring + a.off_a8;
   int8_t *a8p = reinterpret_cast<int8_t *>(sm + a.off_a8);
-  float *xs = reinterpret_cast<float *>(sm + a.off_x);  // x, ao, then x1 (kept to the end)
+  float *xs = reinterpret_cast<float *>(sm + a.off_x);  // x, ao, then x1 (kept to the end of the layer)
   float *ys = reinterpret_cast<float *>(sm + a.off_y);  // norm gains / attention scratch / h
   int *loc = reinterpret_cast<int *>(sm + a.off_loc);   // this CTA's gate and up results
   uint32_t kc = 0;
-  if (t == 0) {  // phase A's plan
-    plan.n = ranges(a, 0, blockIdx.x, G, plan.r);
-    plan.C[0] = a.q, plan.C[1] = a.k, plan.C[2] = a.v;
-  }
-
-  // ---- A: RMSNorm + quant of x; q, k, v ----
-  float ss = 0.0f;
-  for (int i0 = t; i0 < D; i0 += kLB * kCT) {  // kLB elements per thread in flight: loads, then stores
-    float v[kLB], g[kLB];
-#pragma unroll
-    for (int u = 0; u < kLB; u++) {
-      const int i = i0 + u * kCT;
-      v[u] = i < D ? a.x[i] : 0.0f;
-      g[u] = i < D ? a.attn_norm[i] : 0.0f;
-    }
-#pragma unroll
-    for (int u = 0; u < kLB; u++) {
-      const int i = i0 + u * kCT;
-      if (i < D) {
-        xs[i] = v[u];
-        ys[i] = g[u];
-        ss += v[u] * v[u];
-      }
-    }
-  }
-  ss = c_sum(ss, red);
-  float r = glue::rms_recip(ss, D);
-  float mx = 1e-6f;
-  for (int i = t; i < D; i += kCT) mx = fmaxf(mx, fabsf(xs[i] * r * ys[i]));
-  mx = c_max(mx, red);
-  const float sx = glue::qscale(mx);
-  for (int i = t; i < D; i += kCT) a8p[i] = q8(xs[i] * r * ys[i], sx);
-  cbar();
-  kc = consume<FMT>(a, plan, 0, kc, ring, full0, empty0, a8, tb, ep);
-
-  // ---- B: attention items, then the merge of head h by CTA h ----
-  const bool ext = a.Kw != nullptr;
+  const bool ext = a.ext != 0;
   const int pos = a.dpos ? *a.dpos : a.pos;
   const int nkv = a.dpos ? *a.dpos : a.nkv;
   const int nk = ext ? nkv + 1 : nkv;
   const int Sg = a.Sg;
   const int kpc = max(32, (nk + 32 * Sg - 1) / (32 * Sg) * 32);
   const bool bad = nk < 1 || kpc > a.kpc || nkv > a.hstride || (ext && nkv >= a.hstride);
-  if (bad) {  // no attention: ao is zero (the error is reported), so the phases after still complete
-    if (blockIdx.x == 0 && t == 0) atomicOr(&g_fused_error, 4u);
-    for (int h = blockIdx.x; h < a.H; h += G) {
-      for (int d = t; d < dk; d += kCT) ll_putf(a.ao + h * dk + d, 0.0f, ep);
-      if (t == 0) ll_putf(a.amax + h, 0.0f, ep);
-      arrive(a.sync + 0);
-    }
-  } else {
-    const int S = (nk + kpc - 1) / kpc;
-    for (int it = blockIdx.x; it < a.H * S; it += G)
-      attend<PER>(a, it % a.H, it / a.H, kpc, nkv, nk, pos, sx, ys, ep);
-    for (int h = blockIdx.x; h < a.H; h += G) merge_head<PER>(a, h, S, red, ep);
-  }
-
-  // ---- C: ao and the head maxima, quantization; o ----
-  await_count(a.sync + 0, (unsigned int)a.H);
-  float om = 0.0f;
-  for (int i0 = t; i0 < a.H; i0 += kLB * kCT) {
-    uint32_t v[kLB];
-    ll_get_n<kLB>(a.amax, i0, kCT, a.H, ep, v);
-#pragma unroll
-    for (int u = 0; u < kLB; u++)
-      if (i0 + u * kCT < a.H) om = fmaxf(om, __uint_as_float(v[u]));
-  }
-  for (int e0 = t; e0 < Nq; e0 += kLB * kCT) {
-    uint32_t v[kLB];
-    ll_get_n<kLB>(a.ao, e0, kCT, Nq, ep, v);
-#pragma unroll
-    for (int u = 0; u < kLB; u++)
-      if (e0 + u * kCT < Nq) xs[e0 + u * kCT] = __uint_as_float(v[u]);
-  }
-  om = c_max(om, red);
-  const float sa = glue::qscale(om);
-  for (int e = t; e < Nq; e += kCT) a8p[e] = q8(xs[e], sa);
-  if (t == 0) {
-    plan.n = ranges(a, 1, blockIdx.x, G, plan.r);
-    plan.C[0] = a.o;
-  }
-  cbar();
-  kc = consume<FMT>(a, plan, 1, kc, ring, full0, empty0, a8, tb, ep);
-  arrive(a.sync + 1);
-
-  // ---- D: x1 = x + Co / sa, RMSNorm + quant; gate and up; SwiGLU ----
-  await_count(a.sync + 1, (unsigned int)G);
-  ss = 0.0f;
-  for (int i0 = t; i0 < D; i0 += kLB * kCT) {
-    float v[kLB], g[kLB];
-    uint32_t c[kLB];
-#pragma unroll
-    for (int u = 0; u < kLB; u++) {
-      const int i = i0 + u * kCT;
-      v[u] = i < D ? a.x[i] : 0.0f;
-      g[u] = i < D ? a.ffn_norm[i] : 0.0f;
-    }
-    ll_get_n<kLB>(a.o, i0, kCT, D, ep, c);
-#pragma unroll
-    for (int u = 0; u < kLB; u++) {
-      const int i = i0 + u * kCT;
-      if (i < D) {
-        const float x1 = v[u] + (int32_t)c[u] / sa;
-        xs[i] = x1;
-        ys[i] = g[u];
-        ss += x1 * x1;
-      }
-    }
-  }
-  ss = c_sum(ss, red);
-  r = glue::rms_recip(ss, D);
-  mx = 1e-6f;
-  for (int i = t; i < D; i += kCT) mx = fmaxf(mx, fabsf(xs[i] * r * ys[i]));
-  mx = c_max(mx, red);
-  const float sf = glue::qscale(mx);
-  for (int i = t; i < D; i += kCT) a8p[i] = q8(xs[i] * r * ys[i], sf);
+  const int S = bad ? 1 : (nk + kpc - 1) / kpc;
+  if (bad && blockIdx.x == 0 && t == 0) atomicOr(&g_fused_error, 4u);
   int f0, f1;
   share(F, blockIdx.x, G, f0, f1);
   const int nf = f1 - f0;
-  if (t == 0) {
-    plan.n = ranges(a, 2, blockIdx.x, G, plan.r);
-    plan.loc = loc, plan.f0 = f0, plan.nf = nf;
-  }
-  cbar();
-  kc = consume<FMT>(a, plan, 2, kc, ring, full0, empty0, a8, tb, ep);
-  cbar();
-  float hm = 0.0f;
-  for (int i = t; i < nf; i += kCT) {
-    const float hv = glue::silu_mul(loc[i] / sf, loc[nf + i] / sf);
-    ll_putf(a.h + f0 + i, hv, ep);
-    hm = fmaxf(hm, fabsf(hv));
-  }
-  hm = c_max(hm, red);
-  if (t == 0) ll_putf(a.hmax + blockIdx.x, hm, ep);
-  arrive(a.sync + 2);
 
-  // ---- E: quantization of h; down with the residual ----
-  await_count(a.sync + 2, (unsigned int)G);
-  hm = 0.0f;
-  for (int i0 = t; i0 < G; i0 += kLB * kCT) {
-    uint32_t v[kLB];
-    ll_get_n<kLB>(a.hmax, i0, kCT, G, ep, v);
-#pragma unroll
-    for (int u = 0; u < kLB; u++)
-      if (i0 + u * kCT < G) hm = fmaxf(hm, __uint_as_float(v[u]));
-  }
-  for (int i0 = t; i0 < F; i0 += kLB * kCT) {
-    uint32_t v[kLB];
-    ll_get_n<kLB>(a.h, i0, kCT, F, ep, v);
-#pragma unroll
-    for (int u = 0; u < kLB; u++)
-      if (i0 + u * kCT < F) ys[i0 + u * kCT] = __uint_as_float(v[u]);
-  }
-  hm = c_max(hm, red);
-  const float sc = glue::qscale(hm);
-  for (int i = t; i < F; i += kCT) a8p[i] = q8(ys[i], sc);
-  if (t == 0) {
-    plan.n = ranges(a, 3, blockIdx.x, G, plan.r);
-    plan.out = a.x_out, plan.x1 = xs, plan.s = sc;
-  }
-  cbar();
-  consume<FMT>(a, plan, 3, kc, ring, full0, empty0, a8, tb, ep);
+  for (int l = 0; l < a.nl; l++) {
+    const FusedLayerW &lw = a.lw ? a.lw[l] : a.lw0;
+    const uint32_t ep = ep0 + (uint32_t)l;
+    const bool first = l == 0, last = l == a.nl - 1;
+    if (t == 0) {  // phase A's plan
+      plan.n = ranges(a, 0, blockIdx.x, G, plan.r);
+      plan.C[0] = a.q, plan.C[1] = a.k, plan.C[2] = a.v;
+    }
 
-  // the last CTA to finish clears the counts and advances the epoch for the next launch
+    // ---- A: RMSNorm + quant of x (the previous layer's output after its hand-off); q, k, v ----
+    if (!first) await_count(a.sync + 4, (unsigned int)(l * G));
+    float ss = 0.0f;
+    for (int i0 = t; i0 < D; i0 += kLB * kCT) {  // kLB elements per thread in flight: loads, then stores
+      float v[kLB], g[kLB];
+      if (first) {
+#pragma unroll
+        for (int u = 0; u < kLB; u++) v[u] = i0 + u * kCT < D ? a.x[i0 + u * kCT] : 0.0f;
+      } else {
+        uint32_t w[kLB];
+        ll_get_n<kLB>(a.xl, i0, kCT, D, ep - 1u, w);
+#pragma unroll
+        for (int u = 0; u < kLB; u++) v[u] = __uint_as_float(w[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kLB; u++) g[u] = i0 + u * kCT < D ? lw.attn_norm[i0 + u * kCT] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < kLB; u++) {
+        const int i = i0 + u * kCT;
+        if (i < D) {
+          xs[i] = v[u];
+          ys[i] = g[u];
+          ss += v[u] * v[u];
+        }
+      }
+    }
+    ss = c_sum(ss, red);
+    float r = glue::rms_recip(ss, D);
+    float mx = 1e-6f;
+    for (int i = t; i < D; i += kCT) mx = fmaxf(mx, fabsf(xs[i] * r * ys[i]));
+    mx = c_max(mx, red);
+    const float sx = glue::qscale(mx);
+    for (int i = t; i < D; i += kCT) a8p[i] = q8(xs[i] * r * ys[i], sx);
+    cbar();
+    kc = consume<FMT>(a, plan, 0, kc, ring, full0, empty0, a8, tb, ep);
+
+    // ---- B: attention items, then the merge of head h by CTA h ----
+    if (bad) {  // no attention: ao is zero (the error is reported), so the phases after still complete
+      for (int h = blockIdx.x; h < a.H; h += G) {
+        for (int d = t; d < dk; d += kCT) ll_putf(a.ao + h * dk + d, 0.0f, ep);
+        if (t == 0) ll_putf(a.amax + h, 0.0f, ep);
+        arrive(a.sync + 0);
+      }
+    } else {
+      for (int it = blockIdx.x; it < a.H * S; it += G)
+        attend<PER>(a, lw, it % a.H, it / a.H, kpc, nkv, nk, pos, sx, ys, ep);
+      for (int h = blockIdx.x; h < a.H; h += G) merge_head<PER>(a, h, S, red, ep);
+    }
+
+    // ---- C: ao and the head maxima, quantization; o ----
+    await_count(a.sync + 0, (unsigned int)((l + 1) * a.H));
+    float om = 0.0f;
+    for (int i0 = t; i0 < a.H; i0 += kLB * kCT) {
+      uint32_t v[kLB];
+      ll_get_n<kLB>(a.amax, i0, kCT, a.H, ep, v);
+#pragma unroll
+      for (int u = 0; u < kLB; u++)
+        if (i0 + u * kCT < a.H) om = fmaxf(om, __uint_as_float(v[u]));
+    }
+    for (int e0 = t; e0 < Nq; e0 += kLB * kCT) {
+      uint32_t v[kLB];
+      ll_get_n<kLB>(a.ao, e0, kCT, Nq, ep, v);
+#pragma unroll
+      for (int u = 0; u < kLB; u++)
+        if (e0 + u * kCT < Nq) xs[e0 + u * kCT] = __uint_as_float(v[u]);
+    }
+    om = c_max(om, red);
+    const float sa = glue::qscale(om);
+    for (int e = t; e < Nq; e += kCT) a8p[e] = q8(xs[e], sa);
+    if (t == 0) {
+      plan.n = ranges(a, 1, blockIdx.x, G, plan.r);
+      plan.C[0] = a.o;
+    }
+    cbar();
+    kc = consume<FMT>(a, plan, 1, kc, ring, full0, empty0, a8, tb, ep);
+    arrive(a.sync + 1);
+
+    // ---- D: x1 = x + Co / sa, RMSNorm + quant; gate and up; SwiGLU ----
+    await_count(a.sync + 1, (unsigned int)((l + 1) * G));
+    ss = 0.0f;
+    for (int i0 = t; i0 < D; i0 += kLB * kCT) {
+      float v[kLB], g[kLB];
+      uint32_t c[kLB];
+      if (first) {
+#pragma unroll
+        for (int u = 0; u < kLB; u++) v[u] = i0 + u * kCT < D ? a.x[i0 + u * kCT] : 0.0f;
+      } else {
+        uint32_t w[kLB];
+        ll_get_n<kLB>(a.xl, i0, kCT, D, ep - 1u, w);
+#pragma unroll
+        for (int u = 0; u < kLB; u++) v[u] = __uint_as_float(w[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kLB; u++) g[u] = i0 + u * kCT < D ? lw.ffn_norm[i0 + u * kCT] : 0.0f;
+      ll_get_n<kLB>(a.o, i0, kCT, D, ep, c);
+#pragma unroll
+      for (int u = 0; u < kLB; u++) {
+        const int i = i0 + u * kCT;
+        if (i < D) {
+          const float x1 = v[u] + (int32_t)c[u] / sa;
+          xs[i] = x1;
+          ys[i] = g[u];
+          ss += x1 * x1;
+        }
+      }
+    }
+    ss = c_sum(ss, red);
+    r = glue::rms_recip(ss, D);
+    mx = 1e-6f;
+    for (int i = t; i < D; i += kCT) mx = fmaxf(mx, fabsf(xs[i] * r * ys[i]));
+    mx = c_max(mx, red);
+    const float sf = glue::qscale(mx);
+    for (int i = t; i < D; i += kCT) a8p[i] = q8(xs[i] * r * ys[i], sf);
+    if (t == 0) {
+      plan.n = ranges(a, 2, blockIdx.x, G, plan.r);
+      plan.loc = loc, plan.f0 = f0, plan.nf = nf;
+    }
+    cbar();
+    kc = consume<FMT>(a, plan, 2, kc, ring, full0, empty0, a8, tb, ep);
+    cbar();
+    float hm = 0.0f;
+    for (int i = t; i < nf; i += kCT) {
+      const float hv = glue::silu_mul(loc[i] / sf, loc[nf + i] / sf);
+      ll_putf(a.h + f0 + i, hv, ep);
+      hm = fmaxf(hm, fabsf(hv));
+    }
+    hm = c_max(hm, red);
+    if (t == 0) ll_putf(a.hmax + blockIdx.x, hm, ep);
+    arrive(a.sync + 2);
+
+    // ---- E: quantization of h; down with the residual -> the next layer's x (or x_out) ----
+    await_count(a.sync + 2, (unsigned int)((l + 1) * G));
+    hm = 0.0f;
+    for (int i0 = t; i0 < G; i0 += kLB * kCT) {
+      uint32_t v[kLB];
+      ll_get_n<kLB>(a.hmax, i0, kCT, G, ep, v);
+#pragma unroll
+      for (int u = 0; u < kLB; u++)
+        if (i0 + u * kCT < G) hm = fmaxf(hm, __uint_as_float(v[u]));
+    }
+    for (int i0 = t; i0 < F; i0 += kLB * kCT) {
+      uint32_t v[kLB];
+      ll_get_n<kLB>(a.h, i0, kCT, F, ep, v);
+#pragma unroll
+      for (int u = 0; u < kLB; u++)
+        if (i0 + u * kCT < F) ys[i0 + u * kCT] = __uint_as_float(v[u]);
+    }
+    hm = c_max(hm, red);
+    const float sc = glue::qscale(hm);
+    for (int i = t; i < F; i += kCT) a8p[i] = q8(ys[i], sc);
+    if (t == 0) {
+      plan.n = ranges(a, 3, blockIdx.x, G, plan.r);
+      plan.out = last ? a.x_out : nullptr, plan.xl = last ? nullptr : a.xl, plan.x1 = xs, plan.s = sc;
+    }
+    cbar();
+    kc = consume<FMT>(a, plan, 3, kc, ring, full0, empty0, a8, tb, ep);
+    if (!last) arrive(a.sync + 4);
+  }
+
+  // the last CTA to finish clears the counts and records the last layer's tag for the next launch
   cbar();
   if (t == 0 && atomicAdd(a.sync + 3, 1u) == (unsigned int)G - 1) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) a.sync[i] = 0u;
-    *(volatile unsigned int *)a.epoch = ep;
+    for (int i = 0; i < 5; i++) a.sync[i] = 0u;
+    *(volatile unsigned int *)a.epoch = ep0 + (uint32_t)a.nl - 1u;
   }
 }
 

@@ -42,6 +42,7 @@ cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launche
 inline bool gemv_supports(int fmt, int K) { return K > 0 && fmt >= FMT_F16 && fmt <= FMT_NF4; }
 unsigned int gemv_error_flag(bool reset);
 unsigned int layer_error_flag(bool reset);  // layer.cu: a position outside the caches
+unsigned int peer_error_flag(bool reset);   // peers.cu: a peer wait expired
 
 // Grouped (per-K-group scaled) matmul, ork-driver src/npu/core/buf.c:501-520: C[m][n] fp32 = sum over
 // groups g, ascending, of ((float)P_g[m][n] * aScale[m*Sk+g]) * bScale[g*N+n], P_g the exact int32 dot
@@ -63,10 +64,20 @@ cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, 
 // Output stage of an int8-compute matmul (the reference's fused requant outputs, include/ork/run.h:48-108):
 // OUT_I32 the raw int32 sums; OUT_I8 / OUT_I16 clamp(rne(acc * mult / 2^shift)) to int8 / int16;
 // OUT_EWMUL clamp_i8(rne(acc * G * mult / 2^shift)) with G int8 laid out like C. rne = round half to even.
-enum { OUT_I32 = 0, OUT_I8 = 1, OUT_I16 = 2, OUT_EWMUL = 3 };
+// OUT_PEERS: the int32 sums stored into every rank's C over peer memory (a column shard's share of the
+// gather; peers.cu), each CTA then signalling every rank once.
+enum { OUT_I32 = 0, OUT_I8 = 1, OUT_I16 = 2, OUT_EWMUL = 3, OUT_PEERS = 4 };
+constexpr int kMaxPeers = 8;
+struct PeerTable {                 // device memory, written once when the table is created
+  int n, rank, ldc, col0, ctas;    // ranks, this rank, C row stride, first column, signals per run
+  int32_t *C[kMaxPeers];           // every rank's C [M][ldc], mapped in this process
+  unsigned int *flag[kMaxPeers];   // every rank's signal counts [kMaxPeers] (index: signalling rank)
+  unsigned int *waited;            // this rank's count of completed waits (private)
+};
 struct OutStage {
   int mode, mult, shift;
   const int8_t *G;
+  const PeerTable *pt;  // OUT_PEERS
 };
 struct ChainTask {
   const void *W;
@@ -81,6 +92,14 @@ bool batched_supports(int fmt, int M, int K);
 cudaError_t launch_requant(const int32_t *C, size_t n, const OutStage &os, void *out, cudaStream_t s);
 cudaError_t launch_ewmul_i8(const int8_t *a, const int8_t *b, size_t n, int mult, int shift, int8_t *out,
                             cudaStream_t s);
+// Signal from thread 0 of a CTA whose stores into the peers' C are done (after a block barrier): one
+// release increment of this rank's count on every rank (peers.cu).
+#ifdef __CUDACC__
+__device__ __forceinline__ void peers_signal(const PeerTable *pt) {
+  for (int r = 0; r < pt->n; r++)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pt->flag[r] + pt->rank) : "memory");
+}
+#endif
 cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool pdl, int *launches);
 bool grouped_supports(int fmt, int K, int G);
 
@@ -91,27 +110,35 @@ bool gemm_tc_supports(int fmt, int M, int K, int N);
 // then exits without a result). Read after a synchronisation; reset clears it.
 unsigned int tc_error_flag(bool reset);
 
-// Persistent decode layer (layer_fused.cu): one cooperative launch of one CTA per SM runs a whole
-// ork_i8_mm_layer. The caller fills everything above `slot`; launch_layer_fused plans the shared memory
-// (fused_plan: false when the layer's rows or activations do not fit it) and launches.
-struct FusedArgs {
+// Persistent decode layers (layer_fused.cu): one cooperative launch of one CTA per SM runs nl consecutive
+// ork_i8_mm_layer steps (the residual stream passing from layer to layer on the device). The caller
+// fills everything above `slot`; launch_layer_fused plans the shared memory (fused_plan: false when the
+// layer's rows or activations do not fit it) and launches.
+struct FusedLayerW {  // one layer's pointers (a table in device memory)
   const uint8_t *W[7];  // q, k, v, o, gate, up, down: resident rows of one int8-compute format
-  const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *x;
-  const float *Kc, *Vc;
-  float *Kw, *Vw;  // the caches when the token's k / v are appended, else null
-  float *x_out;
+  const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
+  float *Kc, *Vc;       // caches [Hkv][hstride][dk]
+};
+struct FusedArgs {
+  const FusedLayerW *lw;  // [nl] in device memory, or null for one layer described by lw0
+  FusedLayerW lw0;
+  int nl;
+  int ext;                // append the token's k / v into the caches at slot nkv
+  const float *x;         // the first layer's input
+  float *x_out;           // the last layer's output
   int D, H, Hkv, dk, F, nkv, pos, hstride;
   const int *dpos;
   float scale, base;
-  // values exchanged between CTAs: 64-bit words, the value's bits in the low half and the launch's epoch
-  // in the high half, so a reader polls the data itself (no barrier, no fence)
+  // values exchanged between CTAs: 64-bit words, the value's bits in the low half and the layer's tag
+  // in the high half, so a reader can tell fresh from stale words without a fence
   uint64_t *q, *k, *v, *o;   // projections [H*dk], [Hkv*dk], [Hkv*dk], [D] (int32)
   uint64_t *pm, *pz, *po;    // attention chunk partials [H][Sg], [H][Sg], [H][Sg][dk] (float)
   uint64_t *ao, *amax;       // merged attention output [H][dk] and max |.| per head (float)
   uint64_t *h, *hmax;        // SwiGLU row [F] and max |h| per CTA [grid] (float)
-  unsigned int *epoch;       // launch epoch (advanced by the last CTA to finish)
-  unsigned int *sync;        // arrivals: [0] heads merged, [1] CTAs past o, [2] CTAs past SwiGLU,
-                             // [3] CTAs finished (all zeroed by the last CTA to finish)
+  uint64_t *xl;              // the residual stream between layers [D] (float)
+  unsigned int *epoch;       // tag of the last layer run (advanced by the last CTA to finish)
+  unsigned int *sync;        // arrival counts [5]: heads merged, CTAs past o, past SwiGLU, finished,
+                             // past the residual (all zeroed by the last CTA to finish)
   int Sg, kpc;               // attention chunks per head, most keys per chunk
   uint32_t slot;             // -- planned: ring slot bytes, slots, shared-memory layout
   int nslots;

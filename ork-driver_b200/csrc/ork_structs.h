@@ -22,6 +22,9 @@ struct ork_npu {
   void *ring = nullptr;  // in-flight slots of ork_mm_submit / ork_mm_collect (chain.cpp)
   void *dL = nullptr;    // workspace of the decode layer (layer.cu)
   size_t capL = 0;
+  void *dX = nullptr;    // the residual stream between multi-launch layers (layer.cu)
+  size_t capX = 0;
+  void *ltabs = nullptr; // device tables of persistent-layer pointer lists (layer.cu)
   bool pdl = true;
   int force_route = -1;
   uint64_t launches = 0;
@@ -64,6 +67,8 @@ int layer_enqueue(ork_npu *c, const struct ork_layer_dims *d, ork_w *const *W, c
                   float *x_out, const struct ork_b200_layer_kv *kv);
 // Releases the ork_mm_submit ring of a context (chain.cpp).
 void ring_free(ork_npu *c);
+// Releases the persistent-layer tables of a context (layer.cu).
+void layer_tabs_free(ork_npu *c);
 // Launch one matmul on device buffers of the context's GPU (the route of route_for); 0 or -1.
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC);
 // A new resident weight: device memory of `bytes`, filled from host memory in the resident format.

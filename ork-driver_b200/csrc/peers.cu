@@ -1,0 +1,247 @@
+// peers.cu -- column-sharded matmuls whose output gather is fused into the matmul, over NVLink peer
+// memory (one process per GPU).
+//
+// A weight split by output channels over R ranks (each channel has its own scale and codes, ork-driver
+// src/npu/i4/pack.c:63-80; the reference splits the same way over its NPU cores, src/npu.c:1356-1398)
+// leaves rank g with C[:, g's columns]; every rank needs all of C. Instead of a matmul followed by an
+// all-gather, each rank writes its columns straight into every rank's C buffer from the kernel that
+// computes them, then signals each rank once per CTA with a release add on that rank's count of its
+// signals. A rank that needs C waits (on its stream, bounded) until every rank's count reaches the number
+// of CTAs each run signals times the runs it has consumed.
+//   * M <= 8: the staged decode kernel stores its sums into the peers' C itself (gemv.cu store_out
+//     OUT_PEERS) and signals at its end -- one kernel does the matmul and the gather.
+//   * larger M: the ordinary route to a local scratch, then one scatter kernel with the same number of
+//     CTAs, which copies the rows' shard to every rank and signals the same way.
+// Buffers: symmetric allocations of this library (ork_b200_sym_alloc) exchanged as CUDA IPC handles by
+// the caller (64 bytes each, any transport) and mapped with ork_b200_sym_open. No TMA and no multicast:
+// plain stores and atomics over NVLink.
+//
+// Reuse rule: a rank rewrites a peer's C only after passing a wait that needed a later signal from that
+// peer, so as long as each rank reads C before starting its next peer run, no buffer is overwritten
+// while it is read.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "ork_b200.h"
+#include "ork_internal.h"
+#include "ork_npu.h"
+#include "ork_structs.h"
+
+struct ork_b200_peers {
+  ork_npu *ctx = nullptr;
+  orkb::PeerTable host{};             // the table's contents (host copy)
+  orkb::PeerTable *dev = nullptr;     // the table in device memory (read by the kernels)
+  unsigned int *waited = nullptr;     // private device counter
+};
+
+namespace orkb {
+
+namespace {
+
+__device__ unsigned int g_peer_error = 0;
+constexpr uint64_t kPeerSpin = 4000000000ull;  // ~2 s of SM clock
+
+// CTA b copies columns [8b, 8b + 8) of every row of the local C (row stride n) into every rank's C.
+__global__ void __launch_bounds__(256) scatter_kernel(const int32_t *__restrict__ C, int M, int n,
+                                                       const PeerTable *__restrict__ pt) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int c0 = blockIdx.x * 8;
+  for (int e = threadIdx.x; e < M * 8; e += blockDim.x) {
+    const int m = e / 8, c = c0 + e % 8;
+    if (c < n) {
+      const int32_t v = C[(size_t)m * n + c];
+      const size_t o = (size_t)m * pt->ldc + pt->col0 + c;
+      for (int r = 0; r < pt->n; r++) pt->C[r][o] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) peers_signal(pt);
+}
+
+// One warp: lane r waits until rank r's count of signals here covers one more run than this rank has
+// consumed; bounded (an expired wait sets the error flag and lets the stream go on).
+__global__ void __launch_bounds__(32) wait_kernel(const PeerTable *__restrict__ pt) {
+  const int r = threadIdx.x;
+  const unsigned int target = (*pt->waited + 1u) * (unsigned int)pt->ctas;
+  if (r < pt->n) {
+    const unsigned int *f = pt->flag[pt->rank] + r;
+    const uint64_t t0 = clock64();
+    while (true) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if ((int)(v - target) >= 0) break;
+      if (clock64() - t0 > kPeerSpin) {
+        atomicOr(&g_peer_error, 1u);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+  if (r == 0) *pt->waited += 1u;
+}
+
+}  // namespace
+
+unsigned int peer_error_flag(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_peer_error, sizeof v);
+  if (reset && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_peer_error, &z, sizeof z);
+  }
+  return v;
+}
+
+}  // namespace orkb
+
+using namespace orkb;
+
+namespace {
+
+int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, int dtype, const char *name) {
+  if (!c || !w || !dA || !p || p->ctx != c || M < 1 || w->dtype != dtype || w->fmt == FMT_F16) return -1;
+  const PeerTable &t = p->host;
+  if (w->N + t.col0 > t.ldc || (w->N + 7) / 8 != t.ctas) return -1;  // the table's shard width
+  DeviceGuard dg(c->device);
+  OutStage os{OUT_PEERS, 0, 0, nullptr, p->dev};
+  if (M <= 8 && batched_supports(w->fmt, M, w->K)) {
+    ChainTask task{w->d, dA, nullptr, M, w->K, w->N, t.ldc, w->fmt, os};
+    int nl = 0;
+    const cudaError_t e = launch_gemv_batched(&task, 1, c->stream, c->pdl, &nl);
+    c->launches += (uint64_t)nl;
+    if (e != cudaSuccess) {
+      log_err(name, e);
+      return -1;
+    }
+    return 0;
+  }
+  if (!grow(&c->dC, &c->capC, (size_t)M * w->N * 4)) return -1;
+  if (launch(c, w, M, dA, c->dC)) return -1;
+  scatter_kernel<<<t.ctas, 256, 0, c->stream>>>((const int32_t *)c->dC, M, w->N, p->dev);
+  c->launches += 1;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    log_err(name, e);
+    return -1;
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+void *ork_b200_sym_alloc(ork_npu *c, size_t bytes, void *handle) {
+  if (!c || !bytes || !handle) return nullptr;
+  DeviceGuard dg(c->device);
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return nullptr;
+  }
+  static_assert(sizeof h == ORK_B200_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof h);
+  return p;
+}
+
+int ork_b200_sym_free(ork_npu *c, void *p) {
+  if (!c || !p) return -1;
+  DeviceGuard dg(c->device);
+  return cudaFree(p) == cudaSuccess ? 0 : -1;
+}
+
+void *ork_b200_sym_open(ork_npu *c, const void *handle) {
+  if (!c || !handle) return nullptr;
+  DeviceGuard dg(c->device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  void *p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return p;
+}
+
+int ork_b200_sym_close(ork_npu *c, void *peer) {
+  if (!c || !peer) return -1;
+  DeviceGuard dg(c->device);
+  return cudaIpcCloseMemHandle(peer) == cudaSuccess ? 0 : -1;
+}
+
+ork_b200_peers *ork_b200_peers_create(ork_npu *c, int nranks, int rank, void *const *C, void *const *flags, int ldc,
+                                      int col0, int ncols) {
+  if (!c || nranks < 1 || nranks > kMaxPeers || rank < 0 || rank >= nranks || !C || !flags || ldc < 1 || col0 < 0 ||
+      ncols < 1 || col0 + ncols > ldc)
+    return nullptr;
+  for (int r = 0; r < nranks; r++)
+    if (!C[r] || !flags[r] || (uintptr_t)C[r] % 4 || (uintptr_t)flags[r] % 4) return nullptr;
+  DeviceGuard dg(c->device);
+  ork_b200_peers *p = new (std::nothrow) ork_b200_peers;
+  if (!p) return nullptr;
+  p->ctx = c;
+  PeerTable &t = p->host;
+  t.n = nranks, t.rank = rank, t.ldc = ldc, t.col0 = col0, t.ctas = (ncols + 7) / 8;
+  for (int r = 0; r < nranks; r++) {
+    t.C[r] = (int32_t *)C[r];
+    t.flag[r] = (unsigned int *)flags[r];
+  }
+  if (cudaMalloc(&p->dev, sizeof(PeerTable) + 256) != cudaSuccess) {
+    delete p;
+    return nullptr;
+  }
+  p->waited = (unsigned int *)((uint8_t *)p->dev + ((sizeof(PeerTable) + 255) & ~(size_t)255));
+  t.waited = p->waited;
+  if (cudaMemset(p->waited, 0, 4) != cudaSuccess ||
+      cudaMemcpy(p->dev, &t, sizeof t, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(p->dev);
+    delete p;
+    return nullptr;
+  }
+  return p;
+}
+
+void ork_b200_peers_destroy(ork_b200_peers *p) {
+  if (!p) return;
+  DeviceGuard dg(p->ctx->device);
+  cudaStreamSynchronize(p->ctx->stream);
+  cudaFree(p->dev);
+  delete p;
+}
+
+int ork_i8_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
+  return peers_run(c, w, M, dA, p, DT_I8, "ork_i8_mm_run_peers_async");
+}
+
+int ork_i4_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
+  return peers_run(c, w, M, dA, p, DT_I4, "ork_i4_mm_run_peers_async");
+}
+
+int ork_b200_copy(ork_npu *c, void *dst, const void *src, size_t bytes) {
+  if (!c || !dst || !src) return -1;
+  if (!bytes) return 0;
+  DeviceGuard dg(c->device);
+  if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, c->stream) != cudaSuccess) return -1;
+  return cudaStreamSynchronize(c->stream) == cudaSuccess ? 0 : -1;
+}
+
+int ork_b200_peers_wait_async(ork_npu *c, ork_b200_peers *p) {
+  if (!c || !p || p->ctx != c) return -1;
+  DeviceGuard dg(c->device);
+  wait_kernel<<<1, 32, 0, c->stream>>>(p->dev);
+  c->launches += 1;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    log_err("ork_b200_peers_wait_async", e);
+    return -1;
+  }
+  return 0;
+}
+
+}  // extern "C"

@@ -53,6 +53,16 @@ SIGNATURES = [
     ("ork_i8_mm_run_out16_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
     ("ork_i8_mm_run_ewmul_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
     ("ork_i8_npu_ewmul", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, C.POINTER(C.c_double)]),
+    ("ork_b200_sym_alloc", _vp, [_vp, _sz, _vp]),
+    ("ork_b200_sym_free", _i, [_vp, _vp]),
+    ("ork_b200_sym_open", _vp, [_vp, _vp]),
+    ("ork_b200_sym_close", _i, [_vp, _vp]),
+    ("ork_b200_peers_create", _vp, [_vp, _i, _i, C.POINTER(_vp), C.POINTER(_vp), _i, _i, _i]),
+    ("ork_b200_peers_destroy", None, [_vp]),
+    ("ork_i8_mm_run_peers_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_i4_mm_run_peers_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_peers_wait_async", _i, [_vp, _vp]),
+    ("ork_b200_copy", _i, [_vp, _vp, _vp, _sz]),
     ("ork_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_noalloc", _i, [_vp, _vp, _i, _vp, _vp]),
@@ -80,6 +90,7 @@ SIGNATURES = [
     ("ork_mm_collect", _i, [_vp, _i, _vp]),
     ("ork_i8_mm_layer", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7),
     ("ork_i8_mm_layer_async", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7 + [_vp]),
+    ("ork_i8_mm_layers_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     ("ork_b200_pack_check", _i, [_vp, _sz, _i, _i, _i]),
     ("ork_b200_pack_capid", C.c_uint32, []),
     ("ork_b200_sync", _i, [_vp]),
@@ -245,6 +256,12 @@ class LayerDims(C.Structure):
 class LayerKV(C.Structure):
     """ork_b200_layer_kv (include/ork_b200.h)."""
     _fields_ = [("k_norm", C.c_void_p), ("append", C.c_int), ("hstride", C.c_int), ("dpos", C.c_void_p)]
+
+
+class LayerW(C.Structure):
+    """ork_b200_layer_w (include/ork_b200.h): one layer of ork_i8_mm_layers_async."""
+    _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "attn_norm", "q_norm",
+                                          "ffn_norm", "k_norm", "Kc", "Vc")]
 
 
 class Weight:

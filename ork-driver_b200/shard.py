@@ -79,3 +79,74 @@ class ShardedLinear:
         if fn(self.ctx.ctx, self.w.h, M, A_dev.data_ptr(), C_local.data_ptr()) != 0:
             raise RuntimeError("sharded matmul launch failed")
         return gather_columns(C_local, dist, out=C_full)
+
+
+class PeerGroup:
+    """Fused-gather runs over NVLink peer memory (ork_b200_peers_*, include/ork_b200.h): symmetric buffers
+    allocated by the library on every rank, their CUDA IPC handles exchanged with `dist`
+    (all_gather_object, any backend), each peer's buffer mapped here. `table(M, N, ncols)` returns a peer
+    table for a weight whose N output channels are split into equal shards of `ncols` (this rank's
+    first column = rank * ncols) and the device address of this rank's full C [M][N] int32."""
+
+    HANDLE = 64
+
+    def __init__(self, ctx, dist, group=None):
+        self.ctx, self.dist, self.group = ctx, dist, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.own, self.opened, self.tables = [], [], []
+
+    def _symmetric(self, nbytes):
+        import ctypes as C
+
+        L = self.ctx.L
+        h = (C.c_uint8 * self.HANDLE)()
+        p = L.ork_b200_sym_alloc(self.ctx.ctx, nbytes, h)
+        if not p:
+            raise RuntimeError("ork_b200_sym_alloc failed")
+        self.own.append(p)
+        handles = [bytes(h)]
+        if self.world > 1:
+            handles = [None] * self.world
+            self.dist.all_gather_object(handles, bytes(h), group=self.group)
+        ptrs = []
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs.append(p)
+                continue
+            q = L.ork_b200_sym_open(self.ctx.ctx, (C.c_uint8 * self.HANDLE).from_buffer_copy(handles[r]))
+            if not q:
+                raise RuntimeError(f"ork_b200_sym_open failed for rank {r}")
+            self.opened.append(q)
+            ptrs.append(q)
+        return ptrs
+
+    def table(self, M, N, ncols):
+        import ctypes as C
+
+        if ncols * self.world != N:
+            raise ValueError("shards must tile N exactly")
+        cps = self._symmetric(M * N * 4)
+        fps = self._symmetric(4 * 8)
+        arr = C.c_void_p * self.world
+        t = self.ctx.L.ork_b200_peers_create(self.ctx.ctx, self.world, self.rank, arr(*cps), arr(*fps), N,
+                                             self.rank * ncols, ncols)
+        if not t:
+            raise RuntimeError("ork_b200_peers_create failed")
+        self.tables.append(t)
+        return t, cps[self.rank]
+
+    def close(self):
+        L = self.ctx.L
+        L.ork_b200_sync(self.ctx.ctx)
+        if self.world > 1:
+            self.dist.barrier(group=self.group)  # no rank unmaps while a peer may still store into it
+        for t in self.tables:
+            L.ork_b200_peers_destroy(t)
+        for q in self.opened:
+            L.ork_b200_sym_close(self.ctx.ctx, q)
+        if self.world > 1:
+            self.dist.barrier(group=self.group)
+        for p in self.own:
+            L.ork_b200_sym_free(self.ctx.ctx, p)
+        self.own, self.opened, self.tables = [], [], []

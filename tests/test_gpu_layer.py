@@ -17,7 +17,7 @@ import pytest
 
 import oracle_ffi as of
 import ork_b200
-from ork_b200 import LayerDims, LayerKV
+from ork_b200 import LayerDims, LayerKV, LayerW
 
 pytestmark = pytest.mark.gpu
 _p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
@@ -224,3 +224,64 @@ def test_layer_refusals(ctx, path):
     assert call(d) == 0
     for w in ws:
         w.free()
+
+
+@pytest.mark.parametrize("p0,cap", [(5, 16), (70, 96)])
+def test_layers_stack_graph_replay(ctx, path, p0, cap):
+    """ork_i8_mm_layers_async: three layers with their own weights and caches in one call (one persistent
+    launch, or nine launches per layer), the token's k/v appended at the device position, captured once
+    and replayed for two tokens; each token compared with the oracle layers applied in turn."""
+    import torch
+
+    L = ork_b200.lib()
+    D, H, Hkv, dk, F, NL = 256, 4, 2, 64, 512, 3
+    d = dict(D=D, H=H, Hkv=Hkv, dk=dk, dv=dk, Nff=F, nkv=p0, pos=p0)
+    scale, base = 0.125, 1e4
+    dev = torch.device("cuda", L.ork_b200_device(ctx.ctx))
+    layers, ws, keep = [], [], []
+    for l in range(NL):
+        Bs, norms, x0, Kc, Vc = of.layer_inputs(60 + l, D, H, Hkv, dk, F, p0, p0, hstride=cap)
+        wl = _pack(ctx, Bs)
+        t = {k: torch.from_numpy(v).to(dev) for k, v in dict(an=norms[0], qn=norms[1], fn=norms[2], kn=norms[3],
+                                                             K=Kc, V=Vc).items()}
+        layers.append((Bs, norms, Kc.copy(), Vc.copy()))
+        ws.append(wl)
+        keep.append(t)
+    x = torch.from_numpy(of.layer_inputs(99, D, H, Hkv, dk, F, 1, 1)[2]).to(dev)
+    xo = torch.zeros(D, dtype=torch.float32, device=dev)
+    arr = (LayerW * NL)(*[LayerW(*[w.h for w in ws[l]], keep[l]["an"].data_ptr(), keep[l]["qn"].data_ptr(),
+                                 keep[l]["fn"].data_ptr(), keep[l]["kn"].data_ptr(), keep[l]["K"].data_ptr(),
+                                 keep[l]["V"].data_ptr()) for l in range(NL)])
+    dims = _dims(d, scale, base)
+    stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+    # one eager call with the same list of layers before capture (sizes the workspace, uploads the layer
+    # table); append off, so the caches are only read
+    sp = torch.tensor([p0], dtype=torch.int32, device=dev)
+    kv0 = LayerKV(None, 0, cap, sp.data_ptr())
+    assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NL, arr, x.data_ptr(), xo.data_ptr(), C.byref(kv0)) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    pos = torch.tensor([p0], dtype=torch.int32, device=dev)
+    kv = LayerKV(None, 1, cap, pos.data_ptr())
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NL, arr, x.data_ptr(), xo.data_ptr(),
+                                        C.byref(kv)) == 0
+        x.copy_(xo)
+        pos.add_(1)
+    xr = x.cpu().numpy().copy()
+    for s in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        ds = dict(d, nkv=p0 + s, pos=p0 + s)
+        for l in range(NL):
+            Bs, norms, Kc, Vc = layers[l]
+            xr, Kc, Vc = of.layer(ds, scale, base, Bs, norms, xr, Kc, Vc, kv_ext=True, hstride=cap)
+            layers[l] = (Bs, norms, Kc, Vc)
+        ok, err = _close(xo.cpu().numpy(), xr)
+        assert ok, (s, err)
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    del g
+    for wl in ws:
+        for w in wl:
+            w.free()

@@ -1,0 +1,150 @@
+"""Column-sharded runs with the output gather fused into the matmul over peer memory (ork_b200_peers_*,
+ork_i8_mm_run_peers_async / ork_i4_mm_run_peers_async, include/ork_b200.h).
+
+Output channels are independent (ork-driver src/npu/i4/pack.c:63-80), so rank g packs channels
+[g*N/R, (g+1)*N/R) and its run writes them into every rank's C; after ork_b200_peers_wait_async each
+rank's C must equal the unsharded oracle product exactly. One-rank tables run on any GPU; the two-rank
+test needs two GPUs (one process each) and is skipped otherwise. The bounded wait is tested on one rank
+with a flag that nothing sets (no GPU fault: the wait gives up and the next sync reports it).
+"""
+import ctypes as C
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle_ffi as of
+import ork_b200
+
+pytestmark = pytest.mark.gpu
+_p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+
+
+class _NoDist:
+    @staticmethod
+    def is_initialized():
+        return False
+
+
+def _read(ctx, ptr, shape):
+    out = np.empty(shape, np.int32)
+    assert ctx.L.ork_b200_copy(ctx.ctx, _p(out), ptr, out.nbytes) == 0
+    return out
+
+
+def test_one_rank_table(ctx):
+    import torch
+
+    import shard
+
+    L = ctx.L
+    dev = torch.device("cuda", L.ork_b200_device(ctx.ctx))
+    rng = np.random.default_rng(41)
+    K, N, Mmax = 1024, 256, 40
+    B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+    w = ctx.i8_pack(B)
+    g = shard.PeerGroup(ctx, _NoDist)
+    t, cptr = g.table(Mmax, N, N)
+    for M in (1, 5, 8, 40):  # decode kernel with fused stores; then the scatter path
+        A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+        tA = torch.from_numpy(A).to(dev)
+        torch.cuda.synchronize()
+        assert L.ork_i8_mm_run_peers_async(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+        assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), M
+    w.free()
+    g.close()
+
+
+def test_wait_without_signal_gives_up(ctx):
+    import shard
+
+    L = ctx.L
+    g = shard.PeerGroup(ctx, _NoDist)
+    t, _ = g.table(1, 64, 64)
+    assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0  # nothing will signal: bounded (~2 s)
+    assert L.ork_b200_sync(ctx.ctx) == -1
+    assert L.ork_b200_sync(ctx.ctx) == 0  # the flag was cleared; the context keeps working
+    g.close()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _two_rank_worker(rank, world, port, kind):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import shard
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    ctx = ork_b200.Context()
+    L = ctx.L
+    dev = torch.device("cuda", rank)
+    rng = np.random.default_rng(77)  # the same full weight and activations on every rank
+    K, N, Mmax = 2048, 512, 24
+    ncols = N // world
+    n0 = rank * ncols
+    if kind == "i8":
+        B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+        w = ctx.i8_pack(np.ascontiguousarray(B[:, n0:n0 + ncols]))
+        run = L.ork_i8_mm_run_peers_async
+    else:
+        B = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+        w = ctx.i4_pack(np.ascontiguousarray(B[:, n0:n0 + ncols]))
+        run = L.ork_i4_mm_run_peers_async
+    g = shard.PeerGroup(ctx, dist)
+    t, cptr = g.table(Mmax, N, ncols)
+    try:
+        for M in (1, 8, 3, 24):
+            A = rng.integers(-128 if kind == "i8" else -8, 128 if kind == "i8" else 8, size=(M, K), dtype=np.int8)
+            tA = torch.from_numpy(A).to(dev)
+            torch.cuda.synchronize()
+            assert run(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+            assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), (rank, M)
+            dist.barrier()  # every rank has read C before anyone runs again (the buffers' reuse rule)
+        # the run + wait pair captured once and replayed: the counts advance on the device
+        M = 4
+        A = rng.integers(-8, 8, size=(M, K), dtype=np.int8)
+        tA = torch.from_numpy(A).to(dev)
+        s = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            assert run(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+            assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B))
+            dist.barrier()
+        del graph
+    finally:
+        g.close()
+        w.free()
+        ctx.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind", ["i8", "i4"])
+def test_two_ranks_fused_gather(kind):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_two_rank_worker, args=(2, _free_port(), kind), nprocs=2, join=True)
