@@ -90,13 +90,14 @@ int ork_i8_mm_layers_async(ork_npu *ctx, const struct ork_layer_dims *d, int nla
 
 /* Column-sharded runs with the gather fused into the matmul (one process per GPU, NVLink peer memory).
  * Rank g of R holds output channels [col0, col0 + ncols) of a weight; its run writes those columns of C
- * into EVERY rank's C buffer ([M][ldc] int32) and signals every rank once per CTA; a rank that needs C
+ * into EVERY rank's C buffer ([M][ldc] int32) and signals every rank once per run; a rank that needs C
  * waits with ork_b200_peers_wait_async (bounded: an expired wait reports an error at the next sync).
  * Buffers come from ork_b200_sym_alloc (device memory + its CUDA IPC handle, ORK_B200_IPC_HANDLE_BYTES
  * bytes, exchanged by the caller over any transport) and ork_b200_sym_open (a peer's buffer mapped here).
  * flags[r] is rank r's signal block (at least 4 * R bytes of a symmetric buffer, zero at allocation).
- * M <= 8 runs are one kernel (matmul + peer stores + signal); larger M add one scatter kernel. Rule: read
- * C before starting the next peer run on this rank (a peer rewrites C only after a later signal of ours).
+ * A run is the local matmul plus one push kernel (its programmatic dependent) that stores the shard into
+ * every rank's C and signals. Rule: read C before starting the next peer run on this rank (a peer
+ * rewrites C only after a later signal of ours).
  * Returns 0 / NULL-free on success, -1 (NULL) on bad arguments or CUDA errors. No counterpart in
  * ork-driver, which gathers its cores' column slices on the host (src/npu.c:1356-1398). */
 #define ORK_B200_IPC_HANDLE_BYTES 64

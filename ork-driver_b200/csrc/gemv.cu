@@ -178,11 +178,6 @@ __device__ __forceinline__ void store_out(void *C, const OutStage &os, size_t id
       reinterpret_cast<int32_t *>(C)[idx] = v;
       return;
     }
-    if (os.mode == OUT_PEERS) {  // C = this rank's columns: every rank's copy at the shard's offset
-      const PeerTable *pt = os.pt;
-      for (int r = 0; r < pt->n; r++) pt->C[r][idx + pt->col0] = v;
-      return;
-    }
     int64_t p = (int64_t)v * os.mult;
     if (os.mode == OUT_EWMUL) p *= os.G[idx];
     const int64_t q = requant_rne(p, os.shift);
@@ -340,10 +335,6 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_batched_kernel(const __grid_
   }
   const BatchTask &t = bt.t[lo];
   gemv_block<FMT, MT, TR>(t.W, t.A, t.C, t.M, t.K, t.N, (b - t.block0) * TR, t.cstride, tb, t.os);
-  if (t.os.mode == OUT_PEERS) {  // this CTA's columns are in every rank's C: tell them
-    __syncthreads();
-    if (threadIdx.x == 0) peers_signal(t.os.pt);
-  }
 }
 
 // Grouped variant (per-K-group scales): same staging and arithmetic as gemv_kernel, but each warp walks

@@ -64,20 +64,19 @@ cudaError_t launch_gemv_grouped(const GroupedArgs &a, cudaStream_t s, bool pdl, 
 // Output stage of an int8-compute matmul (the reference's fused requant outputs, include/ork/run.h:48-108):
 // OUT_I32 the raw int32 sums; OUT_I8 / OUT_I16 clamp(rne(acc * mult / 2^shift)) to int8 / int16;
 // OUT_EWMUL clamp_i8(rne(acc * G * mult / 2^shift)) with G int8 laid out like C. rne = round half to even.
-// OUT_PEERS: the int32 sums stored into every rank's C over peer memory (a column shard's share of the
-// gather; peers.cu), each CTA then signalling every rank once.
-enum { OUT_I32 = 0, OUT_I8 = 1, OUT_I16 = 2, OUT_EWMUL = 3, OUT_PEERS = 4 };
+enum { OUT_I32 = 0, OUT_I8 = 1, OUT_I16 = 2, OUT_EWMUL = 3 };
+// Column-sharded runs with the gather over peer memory (peers.cu).
 constexpr int kMaxPeers = 8;
 struct PeerTable {                 // device memory, written once when the table is created
-  int n, rank, ldc, col0, ctas;    // ranks, this rank, C row stride, first column, signals per run
+  int n, rank, ldc, col0, ctas;    // ranks, this rank, C row stride, first column, push CTAs of a run
   int32_t *C[kMaxPeers];           // every rank's C [M][ldc], mapped in this process
   unsigned int *flag[kMaxPeers];   // every rank's signal counts [kMaxPeers] (index: signalling rank)
   unsigned int *waited;            // this rank's count of completed waits (private)
+  unsigned int *done;              // CTAs of the current run finished (private, left at zero)
 };
 struct OutStage {
   int mode, mult, shift;
   const int8_t *G;
-  const PeerTable *pt;  // OUT_PEERS
 };
 struct ChainTask {
   const void *W;
@@ -92,14 +91,7 @@ bool batched_supports(int fmt, int M, int K);
 cudaError_t launch_requant(const int32_t *C, size_t n, const OutStage &os, void *out, cudaStream_t s);
 cudaError_t launch_ewmul_i8(const int8_t *a, const int8_t *b, size_t n, int mult, int shift, int8_t *out,
                             cudaStream_t s);
-// Signal from thread 0 of a CTA whose stores into the peers' C are done (after a block barrier): one
-// release increment of this rank's count on every rank (peers.cu).
-#ifdef __CUDACC__
-__device__ __forceinline__ void peers_signal(const PeerTable *pt) {
-  for (int r = 0; r < pt->n; r++)
-    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pt->flag[r] + pt->rank) : "memory");
-}
-#endif
+
 cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool pdl, int *launches);
 bool grouped_supports(int fmt, int K, int G);
 

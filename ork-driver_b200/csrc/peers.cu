@@ -1,17 +1,18 @@
-// peers.cu -- column-sharded matmuls whose output gather is fused into the matmul, over NVLink peer
-// memory (one process per GPU).
+// peers.cu -- column-sharded matmuls with the output gather over NVLink peer memory (one process per
+// GPU), no collective library on the data path.
 //
 // A weight split by output channels over R ranks (each channel has its own scale and codes, ork-driver
 // src/npu/i4/pack.c:63-80; the reference splits the same way over its NPU cores, src/npu.c:1356-1398)
-// leaves rank g with C[:, g's columns]; every rank needs all of C. Instead of a matmul followed by an
-// all-gather, each rank writes its columns straight into every rank's C buffer from the kernel that
-// computes them, then signals each rank once per CTA with a release add on that rank's count of its
-// signals. A rank that needs C waits (on its stream, bounded) until every rank's count reaches the number
-// of CTAs each run signals times the runs it has consumed.
-//   * M <= 8: the staged decode kernel stores its sums into the peers' C itself (gemv.cu store_out
-//     OUT_PEERS) and signals at its end -- one kernel does the matmul and the gather.
-//   * larger M: the ordinary route to a local scratch, then one scatter kernel with the same number of
-//     CTAs, which copies the rows' shard to every rank and signals the same way.
+// leaves rank g with C[:, g's columns]; every rank needs all of C. A run is the local matmul into a
+// scratch C at full speed, then a push kernel, launched as its programmatic dependent (it is resident
+// while the matmul drains), that copies the shard's rows into every rank's C with 16-byte stores; each
+// push CTA counts itself done on this GPU (acq_rel) and the last one signals every rank once with a
+// system-scope release add (release.gpu -> acquire.gpu -> release.sys orders every CTA's peer stores
+// before the signal). A rank that needs C waits (on its stream, bounded) until every rank's count of
+// signals reaches the runs it has consumed plus one.
+// (Storing into the peers from the matmul's own epilogue was measured 1.6x slower at M = 1: each of the
+// thousands of short matmul CTAs then waits for its NVLink stores to be acknowledged before it can
+// release; a few large push CTAs pay that latency once, in parallel.)
 // Buffers: symmetric allocations of this library (ork_b200_sym_alloc) exchanged as CUDA IPC handles by
 // the caller (64 bytes each, any transport) and mapped with ork_b200_sym_open. No TMA and no multicast:
 // plain stores and atomics over NVLink.
@@ -44,28 +45,56 @@ namespace {
 __device__ unsigned int g_peer_error = 0;
 constexpr uint64_t kPeerSpin = 4000000000ull;  // ~2 s of SM clock
 
-// CTA b copies columns [8b, 8b + 8) of every row of the local C (row stride n) into every rank's C.
-__global__ void __launch_bounds__(256) scatter_kernel(const int32_t *__restrict__ C, int M, int n,
-                                                       const PeerTable *__restrict__ pt) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int c0 = blockIdx.x * 8;
-  for (int e = threadIdx.x; e < M * 8; e += blockDim.x) {
-    const int m = e / 8, c = c0 + e % 8;
-    if (c < n) {
+constexpr int kPushCols = 512;  // shard columns one push CTA copies
+
+// CTA b copies columns [b * kPushCols, +kPushCols) of every row of the local C (row stride n) into every
+// rank's C at the shard's offset (16-byte vectors when the row layout allows), then counts itself done;
+// the run's last push CTA signals every rank.
+__global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C, int M, int n,
+                                                    const PeerTable *__restrict__ pt) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the matmul is complete
+  const int c0 = blockIdx.x * kPushCols, nc = min(kPushCols, n - c0);
+  const bool vec = (n % 4 == 0) && (pt->ldc % 4 == 0) && (pt->col0 % 4 == 0);
+  if (vec) {
+    const int nv = nc / 4;
+    for (int e = threadIdx.x; e < M * nv; e += blockDim.x) {
+      const int m = e / nv, c = c0 + (e % nv) * 4;
+      const int4 v = *reinterpret_cast<const int4 *>(C + (size_t)m * n + c);
+      const size_t o = (size_t)m * pt->ldc + pt->col0 + c;
+      for (int r = 0; r < pt->n; r++) *reinterpret_cast<int4 *>(pt->C[r] + o) = v;
+    }
+  } else {
+    for (int e = threadIdx.x; e < M * nc; e += blockDim.x) {
+      const int m = e / nc, c = c0 + e % nc;
       const int32_t v = C[(size_t)m * n + c];
       const size_t o = (size_t)m * pt->ldc + pt->col0 + c;
       for (int r = 0; r < pt->n; r++) pt->C[r][o] = v;
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) peers_signal(pt);
+  if (threadIdx.x == 0) {
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(pt->done) : "memory");
+    if (old == (unsigned int)pt->ctas - 1u) {
+      *pt->done = 0u;
+      for (int r = 0; r < pt->n; r++)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pt->flag[r] + pt->rank) : "memory");
+    }
+  }
 }
 
 // One warp: lane r waits until rank r's count of signals here covers one more run than this rank has
-// consumed; bounded (an expired wait sets the error flag and lets the stream go on).
+// consumed (each run signals each rank once); bounded (an expired wait sets the error flag and lets the
+// stream go on).
+// Launched as a programmatic dependent of the run and releasing its own dependent at once: the next
+// matmul streams its weights while this waits, and reads its activations only after this completes.
+// The count of consumed runs is read only after the run before it on the stream is complete (so after
+// the previous wait on the same table has counted itself).
 __global__ void __launch_bounds__(32) wait_kernel(const PeerTable *__restrict__ pt) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = threadIdx.x;
-  const unsigned int target = (*pt->waited + 1u) * (unsigned int)pt->ctas;
+  const unsigned int target = *pt->waited + 1u;  // one signal per rank per run
   if (r < pt->n) {
     const unsigned int *f = pt->flag[pt->rank] + r;
     const uint64_t t0 = clock64();
@@ -105,25 +134,23 @@ namespace {
 int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, int dtype, const char *name) {
   if (!c || !w || !dA || !p || p->ctx != c || M < 1 || w->dtype != dtype || w->fmt == FMT_F16) return -1;
   const PeerTable &t = p->host;
-  if (w->N + t.col0 > t.ldc || (w->N + 7) / 8 != t.ctas) return -1;  // the table's shard width
+  if (w->N + t.col0 > t.ldc || (w->N + kPushCols - 1) / kPushCols != t.ctas) return -1;  // the table's shard
   DeviceGuard dg(c->device);
-  OutStage os{OUT_PEERS, 0, 0, nullptr, p->dev};
-  if (M <= 8 && batched_supports(w->fmt, M, w->K)) {
-    ChainTask task{w->d, dA, nullptr, M, w->K, w->N, t.ldc, w->fmt, os};
-    int nl = 0;
-    const cudaError_t e = launch_gemv_batched(&task, 1, c->stream, c->pdl, &nl);
-    c->launches += (uint64_t)nl;
-    if (e != cudaSuccess) {
-      log_err(name, e);
-      return -1;
-    }
-    return 0;
-  }
   if (!grow(&c->dC, &c->capC, (size_t)M * w->N * 4)) return -1;
   if (launch(c, w, M, dA, c->dC)) return -1;
-  scatter_kernel<<<t.ctas, 256, 0, c->stream>>>((const int32_t *)c->dC, M, w->N, p->dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(t.ctas);
+  cfg.blockDim = dim3(256);
+  cfg.stream = c->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = c->pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const int32_t *lc = (const int32_t *)c->dC;
+  const PeerTable *dev = p->dev;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, push_kernel, lc, M, w->N, dev);
   c->launches += 1;
-  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     log_err(name, e);
     return -1;
@@ -187,7 +214,7 @@ ork_b200_peers *ork_b200_peers_create(ork_npu *c, int nranks, int rank, void *co
   if (!p) return nullptr;
   p->ctx = c;
   PeerTable &t = p->host;
-  t.n = nranks, t.rank = rank, t.ldc = ldc, t.col0 = col0, t.ctas = (ncols + 7) / 8;
+  t.n = nranks, t.rank = rank, t.ldc = ldc, t.col0 = col0, t.ctas = (ncols + kPushCols - 1) / kPushCols;
   for (int r = 0; r < nranks; r++) {
     t.C[r] = (int32_t *)C[r];
     t.flag[r] = (unsigned int *)flags[r];
@@ -198,7 +225,8 @@ ork_b200_peers *ork_b200_peers_create(ork_npu *c, int nranks, int rank, void *co
   }
   p->waited = (unsigned int *)((uint8_t *)p->dev + ((sizeof(PeerTable) + 255) & ~(size_t)255));
   t.waited = p->waited;
-  if (cudaMemset(p->waited, 0, 4) != cudaSuccess ||
+  t.done = p->waited + 1;
+  if (cudaMemset(p->waited, 0, 8) != cudaSuccess ||
       cudaMemcpy(p->dev, &t, sizeof t, cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaFree(p->dev);
     delete p;
@@ -234,9 +262,18 @@ int ork_b200_copy(ork_npu *c, void *dst, const void *src, size_t bytes) {
 int ork_b200_peers_wait_async(ork_npu *c, ork_b200_peers *p) {
   if (!c || !p || p->ctx != c) return -1;
   DeviceGuard dg(c->device);
-  wait_kernel<<<1, 32, 0, c->stream>>>(p->dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = c->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = c->pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const PeerTable *dev = p->dev;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, wait_kernel, dev);
   c->launches += 1;
-  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     log_err("ork_b200_peers_wait_async", e);
     return -1;
