@@ -38,11 +38,45 @@ int route_for(const ork_npu *c, const ork_w *w, int M) {
   return tc ? 1 : 0;
 }
 
-// Sticky device-side error flags (a bounded wait that expired); cleared when read.
+// One error word per device in mapped, pinned host memory, set by any kernel that records an error
+// (errword.cuh); the per-module device flags say which and are read (and cleared) only when it is set.
+constexpr int kMaxDevices = 64;
+static unsigned int *g_err_host = nullptr;
+static bool g_err_ready[kMaxDevices];
+static std::mutex g_err_mu;
+
+bool err_word_init(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return false;
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (g_err_ready[dev]) return true;
+  if (!g_err_host) {
+    void *p = nullptr;
+    if (cudaHostAlloc(&p, kMaxDevices * sizeof(unsigned int), cudaHostAllocPortable | cudaHostAllocMapped) !=
+        cudaSuccess)
+      return false;
+    memset(p, 0, kMaxDevices * sizeof(unsigned int));
+    g_err_host = (unsigned int *)p;
+  }
+  unsigned int *d = nullptr;
+  if (cudaHostGetDevicePointer((void **)&d, g_err_host + dev, 0) != cudaSuccess) return false;
+  cudaError_t (*set[])(unsigned int *) = {gemv_set_err_word, tc_set_err_word, layer_set_err_word,
+                                          fused_set_err_word, peer_set_err_word};
+  for (auto f : set)
+    if (f(d) != cudaSuccess) return false;
+  g_err_ready[dev] = true;
+  return true;
+}
+
+// Sticky device-side errors of the current device (a bounded wait that expired, a decode position outside
+// the caches): one read of the host-mapped word after a synchronisation; cleared when read.
 bool device_error() {
-  const unsigned int t = tc_error_flag(true), g = gemv_error_flag(true), l = layer_error_flag(true),
-                     f = fused_error_flag(true), p = peer_error_flag(true);
-  return (t | g | l | f | p) != 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || !g_err_host) return false;
+  volatile unsigned int *w = g_err_host + dev;
+  if (!*w) return false;
+  *w = 0u;
+  tc_error_flag(true), gemv_error_flag(true), layer_error_flag(true), fused_error_flag(true), peer_error_flag(true);
+  return true;
 }
 
 void log_err(const char *what, cudaError_t e) {
@@ -205,6 +239,10 @@ ork_npu *ork_npu_init(void) {
   if (p.major != 10) {
     fprintf(stderr, "[ork] ERROR ork_npu_init: device %d is sm_%d%d; this build targets sm_100a (B200)\n", dev,
             p.major, p.minor);
+    return nullptr;
+  }
+  if (!err_word_init(dev)) {
+    fprintf(stderr, "[ork] ERROR ork_npu_init: cannot map the device error word\n");
     return nullptr;
   }
   ork_npu *c = new (std::nothrow) ork_npu;

@@ -28,6 +28,7 @@
 #include <mutex>
 
 #include "nibble.cuh"
+#include "errword.cuh"
 #include "ork_internal.h"
 
 namespace orkb {
@@ -66,7 +67,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     if (done) return true;
     if (clock64() - t0 > kWaitCycles) {
-      atomicOr(&g_tc_error, 1u);
+      { atomicOr(&g_tc_error, 1u); err_word_set(); }
       return false;
     }
   }
@@ -512,7 +513,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity)
         : "memory");
     if (done) return true;
     if (clock64() - t0 > kWaitCycles) {
-      atomicOr(&g_tc_error, 1u);
+      { atomicOr(&g_tc_error, 1u); err_word_set(); }
       return false;
     }
   }
@@ -967,5 +968,7 @@ unsigned int tc_error_flag(bool reset) {
   }
   return v;
 }
+
+ORKB_ERR_WORD_SETTER(tc_set_err_word)
 
 }  // namespace orkb

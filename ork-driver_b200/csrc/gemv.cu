@@ -35,6 +35,7 @@
 #include <type_traits>
 
 #include "nibble.cuh"
+#include "errword.cuh"
 #include "ork_internal.h"
 #include "requant.cuh"
 
@@ -72,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait0(uint32_t bar) {
         : "memory");
     if (done) return true;
     if (clock64() - t0 > kWaitCycles) {
-      atomicOr(&g_gemv_error, 1u);
+      { atomicOr(&g_gemv_error, 1u); err_word_set(); }
       return false;
     }
   }
@@ -872,6 +873,8 @@ unsigned int gemv_error_flag(bool reset) {
   }
   return v;
 }
+
+ORKB_ERR_WORD_SETTER(gemv_set_err_word)
 
 }  // namespace orkb
 

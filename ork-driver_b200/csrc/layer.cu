@@ -34,6 +34,7 @@
 
 #include "glue.cuh"
 #include "ork_b200.h"
+#include "errword.cuh"
 #include "ork_internal.h"
 #include "ork_npu.h"
 #include "ork_structs.h"
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   const int nk = ext ? nkv + 1 : nkv;
   const int kpc = max(32, (nk + 32 * Sg - 1) / (32 * Sg) * 32);  // <= a.kpc, the shared-memory size
   if (nk < 1 || kpc > a.kpc || nkv > a.hstride || (ext && nkv >= a.hstride)) {
-    if (h == 0 && sp == 0 && t == 0) atomicOr(&g_layer_error, 1u);
+    if (h == 0 && sp == 0 && t == 0) { atomicOr(&g_layer_error, 1u); err_word_set(); }
     return;
   }
   const int S = (nk + kpc - 1) / kpc;
@@ -735,6 +736,8 @@ unsigned int layer_error_flag(bool reset) {
   }
   return v;
 }
+
+ORKB_ERR_WORD_SETTER(layer_set_err_word)
 
 }  // namespace orkb
 

@@ -38,6 +38,7 @@
 
 #include "glue.cuh"
 #include "nibble.cuh"
+#include "errword.cuh"
 #include "ork_internal.h"
 
 namespace orkb {
@@ -117,7 +118,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     if (done) return true;
     if (clock64() - t0 > kSpin || gave_up()) {
-      atomicOr(&g_fused_error, 1u);
+      { atomicOr(&g_fused_error, 1u); err_word_set(); }
       return false;
     }
   }
@@ -153,7 +154,7 @@ __device__ void await_count(const unsigned int *c, unsigned int n) {
       asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
       if (v >= n) break;
       if (clock64() - t0 > kSpin || gave_up()) {
-        atomicOr(&g_fused_error, 2u);
+        { atomicOr(&g_fused_error, 2u); err_word_set(); }
         break;
       }
     }
@@ -166,7 +167,7 @@ __device__ __noinline__ uint32_t ll_wait(const uint64_t *p, uint64_t w, uint32_t
   const uint64_t t0 = clock64();
   while ((uint32_t)(w >> 32) != ep) {
     if (clock64() - t0 > kSpin || gave_up()) {
-      atomicOr(&g_fused_error, 2u);
+      { atomicOr(&g_fused_error, 2u); err_word_set(); }
       break;
     }
     w = ll_load(p);
@@ -595,7 +596,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   const int kpc = max(32, (nk + 32 * Sg - 1) / (32 * Sg) * 32);
   const bool bad = nk < 1 || kpc > a.kpc || nkv > a.hstride || (ext && nkv >= a.hstride);
   const int S = bad ? 1 : (nk + kpc - 1) / kpc;
-  if (bad && blockIdx.x == 0 && t == 0) atomicOr(&g_fused_error, 4u);
+  if (bad && blockIdx.x == 0 && t == 0) { atomicOr(&g_fused_error, 4u); err_word_set(); }
   int f0, f1;
   share(F, blockIdx.x, G, f0, f1);
   const int nf = f1 - f0;
@@ -877,5 +878,7 @@ unsigned int fused_error_flag(bool reset) {
   }
   return v;
 }
+
+ORKB_ERR_WORD_SETTER(fused_set_err_word)
 
 }  // namespace orkb

@@ -43,6 +43,12 @@ inline bool gemv_supports(int fmt, int K) { return K > 0 && fmt >= FMT_F16 && fm
 unsigned int gemv_error_flag(bool reset);
 unsigned int layer_error_flag(bool reset);  // layer.cu: a position outside the caches
 unsigned int peer_error_flag(bool reset);   // peers.cu: a peer wait expired
+// Point each module's kernels at the device's error word (errword.cuh); called once per device.
+cudaError_t gemv_set_err_word(unsigned int *p);
+cudaError_t tc_set_err_word(unsigned int *p);
+cudaError_t layer_set_err_word(unsigned int *p);
+cudaError_t fused_set_err_word(unsigned int *p);
+cudaError_t peer_set_err_word(unsigned int *p);
 
 // Grouped (per-K-group scaled) matmul, ork-driver src/npu/core/buf.c:501-520: C[m][n] fp32 = sum over
 // groups g, ascending, of ((float)P_g[m][n] * aScale[m*Sk+g]) * bScale[g*N+n], P_g the exact int32 dot

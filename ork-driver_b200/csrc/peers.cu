@@ -27,6 +27,7 @@
 #include <new>
 
 #include "ork_b200.h"
+#include "errword.cuh"
 #include "ork_internal.h"
 #include "ork_npu.h"
 #include "ork_structs.h"
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(32) wait_kernel(const PeerTable *__restrict__ 
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
       if ((int)(v - target) >= 0) break;
       if (clock64() - t0 > kPeerSpin) {
-        atomicOr(&g_peer_error, 1u);
+        { atomicOr(&g_peer_error, 1u); err_word_set(); }
         break;
       }
       __nanosleep(64);
@@ -124,6 +125,8 @@ unsigned int peer_error_flag(bool reset) {
   }
   return v;
 }
+
+ORKB_ERR_WORD_SETTER(peer_set_err_word)
 
 }  // namespace orkb
 
