@@ -38,6 +38,20 @@ int route_for(const ork_npu *c, const ork_w *w, int M) {
   return tc ? 1 : 0;
 }
 
+cudaError_t smem_attr(const void *kernel, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void *, int>> done;  // (kernel, device) pairs already raised
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto &d : done)
+    if (d.first == kernel && d.second == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.emplace_back(kernel, dev);
+  return e;
+}
+
 // One error word per device in mapped, pinned host memory, set by any kernel that records an error
 // (errword.cuh); the per-module device flags say which and are read (and cleared) only when it is set.
 constexpr int kMaxDevices = 64;

@@ -756,11 +756,9 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   constexpr size_t smem = 1024 + ring + (3 * STAGES + 1) * 8 + 16;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_tc_kernel<FMT, SWAP, TN, STAGES, NA>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = smem_attr((const void *)kern, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   const Nf4Tables tb = nf4_tables();
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
@@ -802,11 +800,9 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   constexpr size_t smem = 1024 + ring + (4 * STAGES + 1) * 8 + 16;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_tc_pair_kernel<FMT, SWAP, TN, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = smem_attr((const void *)kern, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   const Nf4Tables tb = nf4_tables();
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;

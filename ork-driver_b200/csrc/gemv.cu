@@ -685,11 +685,9 @@ cudaError_t launch_one(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cud
                        const Tables &tb) {
   const size_t smem = (size_t)TR * fmt_row_bytes(FMT, a.K) + (size_t)m * (FMT == FMT_F16 ? 2 : 1) * a.K;
   auto kern = gemv_kernel<FMT, MT, TR>;
-  static bool attr_set = false;  // opt in once to the full dynamic budget (the static part adds ~1 KB)
-  if (!attr_set) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  {  // the full dynamic budget (the static part adds ~1 KB), once per device
+    const cudaError_t e = smem_attr((const void *)kern, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + TR - 1) / TR);
@@ -724,11 +722,9 @@ cudaError_t launch_grouped_one(const GroupedArgs &a, const uint8_t *Ab, const fl
   const size_t rowB = fmt_row_bytes(FMT, a.K);
   const size_t smem = (size_t)TR * rowB + (((size_t)m * a.K + 15) & ~(size_t)15) + (size_t)(a.K / a.G) * TR * MT * 4;
   auto kern = gemv_grouped_kernel<FMT, MT, TR>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  {  // the full dynamic budget (the static part adds ~1 KB), once per device
+    const cudaError_t e = smem_attr((const void *)kern, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + TR - 1) / TR);
@@ -796,11 +792,9 @@ template <int FMT, int MT>
 cudaError_t launch_batched_one(const BatchTable &bt, int blocks, size_t smem, cudaStream_t s, bool pdl,
                                const Tables &tb) {
   auto kern = gemv_batched_kernel<FMT, MT, 8>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  {  // the full dynamic budget (the static part adds ~1 KB), once per device
+    const cudaError_t e = smem_attr((const void *)kern, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks);

@@ -605,13 +605,11 @@ int layer_enqueue(ork_npu *c, const ork_layer_dims *d, ork_w *const *W, const fl
   const int Sg = attn_splits(H, maxk), kpc = attn_kpc(maxk, Sg);
   LayerWs ws;
   if (!layer_ws(c, D, H, Nq, Nk, F, dk, Sg, &ws)) return -1;
-  static bool attrs = false;  // the glue kernels may use up to 200 KB of dynamic shared memory
-  if (!attrs) {
+  {  // the glue kernels may use up to 200 KB of dynamic shared memory
     const void *k[] = {(const void *)norm_quant_kernel, (const void *)swiglu_quant_kernel,
                        (const void *)attention_kernel};
     for (const void *f : k)
-      if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) return -1;
-    attrs = true;
+      if (smem_attr(f, 200 * 1024) != cudaSuccess) return -1;
   }
   const bool pdl = c->pdl;
   cudaStream_t s = c->stream;

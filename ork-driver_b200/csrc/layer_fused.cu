@@ -781,11 +781,9 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
 template <int FMT, int PER>
 cudaError_t launch_one(const FusedArgs &a, int G, cudaStream_t s) {
   auto kern = layer_fused_kernel<FMT, PER>;
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  {
+    const cudaError_t e = smem_attr((const void *)kern, kSmemMax);
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);

@@ -43,6 +43,9 @@ inline bool gemv_supports(int fmt, int K) { return K > 0 && fmt >= FMT_F16 && fm
 unsigned int gemv_error_flag(bool reset);
 unsigned int layer_error_flag(bool reset);  // layer.cu: a position outside the caches
 unsigned int peer_error_flag(bool reset);   // peers.cu: a peer wait expired
+// Raise a kernel's dynamic shared-memory limit on the current device, once per (kernel, device): the
+// attribute belongs to the device's context, so a process driving several GPUs needs it on each.
+cudaError_t smem_attr(const void *kernel, int bytes);
 // Point each module's kernels at the device's error word (errword.cuh); called once per device.
 cudaError_t gemv_set_err_word(unsigned int *p);
 cudaError_t tc_set_err_word(unsigned int *p);

@@ -148,3 +148,34 @@ def test_two_ranks_fused_gather(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.spawn(_two_rank_worker, args=(2, _free_port(), kind), nprocs=2, join=True)
+
+
+def test_two_devices_one_process():
+    """Contexts on two GPUs of one process: every kernel's shared-memory opt-in and the error word are set
+    per device, so the tensor-core, decode and fused-output paths all run exactly on the second GPU too."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    rng = np.random.default_rng(91)
+    K, N = 2048, 512
+    B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+    ctxs = []
+    try:
+        for dev in (0, 1):
+            torch.cuda.set_device(dev)
+            ctxs.append(ork_b200.Context())
+        for ctx in ctxs:
+            w = ctx.i8_pack(B)
+            for M in (1, 8, 300):
+                A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+                rc, Cm = ctx.run(w, A)
+                assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B)), M
+                c8 = np.zeros((M, N), np.int8)
+                assert ctx.L.ork_i8_mm_run_out8(ctx.ctx, w.h, M, _p(A), _p(c8), 0x1000, 15) == 0
+                assert np.array_equal(c8, of.requant(of.gemm_i32(A, B), 0x1000, 15)), M
+            w.free()
+    finally:
+        for ctx in ctxs:
+            ctx.close()
+        torch.cuda.set_device(0)
