@@ -390,8 +390,9 @@ def run_qwen3(args):
     device-side position), o, residual + RMSNorm + quantization, gate/up in one launch, SwiGLU +
     quantization, down, residual -- then the final norm and the LM head (ork_i8_mm_run_async) and a greedy
     argmax; a whole token is one CUDA graph. Prefill of the 128-token prompt runs the same model with
-    PyTorch glue around ork_i8_mm_run (per-row activation quantization). Four distinct layer weight sets
-    (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s; prefill tokens/s beside it."""
+    PyTorch glue around ork_i8_mm_run (per-row activation quantization), captured as one CUDA graph.
+    Four distinct layer weight sets (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s;
+    prefill tokens/s beside it."""
     import ctypes as C
 
     import torch
@@ -501,13 +502,26 @@ def run_qwen3(args):
             prefill(prompt)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        l0 = ctx.launches()
         e0.record(stream)
-        logits = prefill(prompt)
+        prefill(prompt)  # eager: PyTorch's host-side launch rate bounds this one
+        e1.record(stream)
+        torch.cuda.synchronize()
+        prefill_eager_ms = e0.elapsed_time(e1)
+        # the prompt as one CUDA graph (glue + library matmuls), replayed: the device time of prefill
+        pgraph = torch.cuda.CUDAGraph()
+        l0 = ctx.launches()
+        with torch.cuda.graph(pgraph, stream=stream):
+            logits_g = prefill(prompt)
+        prefill_launches = ctx.launches() - l0
+        pgraph.replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        pgraph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         prefill_ms = e0.elapsed_time(e1)
-        prefill_launches = ctx.launches() - l0
+        logits = logits_g.clone()
+        del pgraph
         tok.copy_(logits.argmax(-1))
         pos.fill_(PRE)
         decode_step()  # eager warm-up of the decode shapes (sizes the layer workspace before capture)
@@ -541,13 +555,15 @@ def run_qwen3(args):
                                    "then 256 greedy decode steps, batch 1",
                        "linears": "decode: the 28 layers as one ork_i8_mm_layers_async call (the library's decode "
                                   "layer, one persistent launch), LM head through ork_i8_mm_run_async; "
-                                  "prefill: PyTorch glue around ork_i8_mm_run_async",
+                                  "prefill: PyTorch glue around ork_i8_mm_run_async, captured as one CUDA graph "
+                                  "(prefill_eager_ms: the same prompt launched eagerly)",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
                        "parallelism": "replicas" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": tps * weight_bytes / 1e9, "peak": hbm, "unit": "GB/s",
                          "frac": tps / roof_tps, "traffic": None, "kernel": "decode token (weights once)",
                          "peak_source": src},
             "prefill_tok_s": PRE / (prefill_ms / 1e3) * world, "prefill_ms": prefill_ms,
+            "prefill_eager_ms": prefill_eager_ms,
             "decode_ms_per_token": decode_ms / DEC, "int8_weight_bytes_per_token": weight_bytes,
             "linear_weight_GBs_decode": weight_bytes / (decode_ms / DEC / 1e3) / 1e9,
             "gpu_launches": int(launches_per_token * DEC), "library_launches_per_token": launches_per_token,

@@ -52,8 +52,9 @@ constexpr int kMaxSlots = 32;
 constexpr int kFMaxSplit = 256;
 constexpr int kRowsPass = 8;  // rows a warp reduces together
 constexpr int kLB = 4;        // row elements a thread loads at once in the glue
+constexpr int kHB = 12;       // SwiGLU elements a thread loads at once (F <= 6144 in one round)
 constexpr uint64_t kSpin = 4000000000ull;
-constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic part; the static barriers and scratch use < 1 KB
+constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic part; the static barriers, tables and scratch use <= 1 KB
 
 __device__ unsigned int g_fused_error = 0;
 
@@ -175,20 +176,42 @@ __device__ __noinline__ uint32_t ll_wait(const uint64_t *p, uint64_t w, uint32_t
   return (uint32_t)w;
 }
 
-__device__ __forceinline__ uint32_t ll_get(const uint64_t *p, uint32_t ep) {
-  const uint64_t w = ll_load(p);
-  return (uint32_t)(w >> 32) == ep ? (uint32_t)w : ll_wait(p, w, ep);
-}
-
-// N words at p[i0 + u * stride] (those below n): all loads in flight, then any not yet written re-polled
+// N words at p[i0 + u * stride] (those below n; the others read as written): ll_issue puts the loads in
+// flight, ll_finish re-polls any not yet written. Several vectors issued before the first finish cost one
+// round trip together.
 template <int N>
-__device__ __forceinline__ void ll_get_n(const uint64_t *p, int i0, int stride, int n, uint32_t ep, uint32_t (&v)[N]) {
-  uint64_t w[N];
+__device__ __forceinline__ void ll_issue(const uint64_t *p, int i0, int stride, int n, uint32_t ep, uint64_t (&w)[N]) {
 #pragma unroll
   for (int u = 0; u < N; u++) w[u] = i0 + u * stride < n ? ll_load(p + i0 + u * stride) : ((uint64_t)ep << 32);
+}
+template <int N>
+__device__ __forceinline__ void ll_finish(const uint64_t *p, int i0, int stride, uint32_t ep, const uint64_t (&w)[N],
+                                          uint32_t (&v)[N]) {
 #pragma unroll
   for (int u = 0; u < N; u++)
     v[u] = (uint32_t)(w[u] >> 32) == ep ? (uint32_t)w[u] : ll_wait(p + i0 + u * stride, w[u], ep);
+}
+template <int N>
+__device__ __forceinline__ void ll_get_n(const uint64_t *p, int i0, int stride, int n, uint32_t ep, uint32_t (&v)[N]) {
+  uint64_t w[N];
+  ll_issue<N>(p, i0, stride, n, ep, w);
+  ll_finish<N>(p, i0, stride, ep, w, v);
+}
+
+// The layer's pointer table, 8-byte words copied into shared memory by asynchronous copies (the next
+// layer's while this one runs), so no phase starts with a dependent global load of a pointer.
+constexpr int kLwWords = (int)(sizeof(FusedLayerW) / 8);
+static_assert(sizeof(FusedLayerW) % 8 == 0, "the layer table copies in 8-byte words");
+__device__ __forceinline__ void lw_fetch(FusedLayerW *dst, const FusedLayerW *src, int t) {
+  if (t < kLwWords) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(su32(dst) + 8u * t),
+                 "l"(reinterpret_cast<const uint64_t *>(src) + t)
+                 : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+}
+__device__ __forceinline__ void lw_landed(int t) {
+  if (t < kLwWords) asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ---- the CTA's rows of each phase ---------------------------------------------------------------
@@ -405,18 +428,18 @@ __device__ __noinline__ uint32_t consume(const FusedArgs &a, const Plan &pl, int
 // dequantized, RMS-normed with gain g (if any), rotated at pos. The NeoX pair (d, d + dk / 2) is
 // (i, i + PER / 2) in the same lane.
 template <int PER>
-__device__ __forceinline__ void head_vec(const uint32_t (&c)[PER], float sx, const float *g, int pos, float base,
-                                         int lane, float (&v)[PER]) {
+__device__ __forceinline__ void head_vec(const uint32_t (&c)[PER], float sx, bool has_g, const float (&g)[PER], int pos,
+                                         float base, int lane, float (&v)[PER]) {
   constexpr int dk = 32 * PER;
 #pragma unroll
   for (int i = 0; i < PER; i++) v[i] = (int32_t)c[i] / sx;
-  if (g) {
+  if (has_g) {
     float sq = 0.0f;
 #pragma unroll
     for (int i = 0; i < PER; i++) sq += v[i] * v[i];
     const float rr = glue::rms_recip(warp_sum(sq), dk);
 #pragma unroll
-    for (int i = 0; i < PER; i++) v[i] = v[i] * rr * g[lane + 32 * i];
+    for (int i = 0; i < PER; i++) v[i] = v[i] * rr * g[i];
   }
 #pragma unroll
   for (int i = 0; i < PER / 2; i++) {
@@ -427,9 +450,31 @@ __device__ __forceinline__ void head_vec(const uint32_t (&c)[PER], float sx, con
   }
 }
 
+// Keys jb and jb + kCW of the cache (zeros at or past j1): a warp's step of two keys, lane holding
+// elements lane + 32 i of each row.
+template <int PER>
+__device__ __forceinline__ void load_keys(const float *Kh, const float *Vh, int jb, int j1, int lane,
+                                          float (&kr)[2][PER], float (&vr)[2][PER]) {
+  constexpr int dk = 32 * PER;
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    const int j = jb + u * kCW;
+    const bool in = j < j1;
+    const float *kp = Kh + (size_t)j * dk + lane, *vp = Vh + (size_t)j * dk + lane;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      kr[u][i] = in ? kp[32 * i] : 0.0f;
+      vr[u][i] = in ? vp[32 * i] : 0.0f;
+    }
+  }
+}
+
 // Item (h, sp) of S: keys [sp * kpc, min(nk, sp * kpc + kpc)) of query head h. Warp w takes keys
 // j0 + w + 16 u with an online softmax (running max, rescaled sums); the CTA then combines its warps'
 // maxima, sums and V rows into the item's partials. y: scratch, [kCW][dk] rows then 2 * kCW floats.
+// The first step's cached rows and the norm gains do not depend on this launch's data, so their loads
+// are issued before the polls of q (the token's own key, not yet in the cache, replaces its row when it
+// is used).
 template <int PER>
 __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp, int kpc, int nkv, int nk, int pos,
                        float sx, float *y, uint32_t ep) {
@@ -440,17 +485,31 @@ __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp,
   const int j0 = sp * kpc, j1 = min(nk, j0 + kpc);
   const bool own = ext && j0 <= nkv && nkv < j1;
   const float *Kh = lw.Kc + (size_t)hk * a.hstride * dk, *Vh = lw.Vc + (size_t)hk * a.hstride * dk;
+  float kr[2][PER], vr[2][PER];
+  int jb = j0 + wp;
+  load_keys<PER>(Kh, Vh, jb, j1, lane, kr, vr);
+  const bool hq = lw.q_norm != nullptr, hk_ = lw.k_norm != nullptr;
+  float gq[PER], gk[PER];
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    gq[i] = hq ? lw.q_norm[lane + 32 * i] : 1.0f;
+    gk[i] = hk_ && own ? lw.k_norm[lane + 32 * i] : 1.0f;
+  }
   // the raw q (and the token's own k, v): one round of polls
   uint32_t cq[PER], ck[PER], cv[PER];
-  ll_get_n<PER>(a.q + h * dk, lane, 32, dk, ep, cq);
-  if (own) {
-    ll_get_n<PER>(a.k + hk * dk, lane, 32, dk, ep, ck);
-    ll_get_n<PER>(a.v + hk * dk, lane, 32, dk, ep, cv);
+  {
+    uint64_t wq[PER], wk[PER], wv[PER];
+    ll_issue<PER>(a.q + h * dk, lane, 32, dk, ep, wq);
+    ll_issue<PER>(a.k + hk * dk, lane, 32, own ? dk : 0, ep, wk);
+    ll_issue<PER>(a.v + hk * dk, lane, 32, own ? dk : 0, ep, wv);
+    ll_finish<PER>(a.q + h * dk, lane, 32, ep, wq, cq);
+    ll_finish<PER>(a.k + hk * dk, lane, 32, ep, wk, ck);
+    ll_finish<PER>(a.v + hk * dk, lane, 32, ep, wv, cv);
   }
   float q[PER], kn[PER], vn[PER];
-  head_vec<PER>(cq, sx, lw.q_norm, pos, a.base, lane, q);
+  head_vec<PER>(cq, sx, hq, gq, pos, a.base, lane, q);
   if (own) {
-    head_vec<PER>(ck, sx, lw.k_norm, pos, a.base, lane, kn);
+    head_vec<PER>(ck, sx, hk_, gk, pos, a.base, lane, kn);
 #pragma unroll
     for (int i = 0; i < PER; i++) vn[i] = (int32_t)cv[i] / sx;
     if (h % grp == 0 && wp == 0)  // the group's first query head stores the token's k and v
@@ -463,19 +522,12 @@ __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp,
   float m = -3.0e38f, z = 0.0f, acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; i++) acc[i] = 0.0f;
-  for (int jb = j0 + wp; jb < j1; jb += 2 * kCW) {  // two keys of this warp per step, loads first
-    float kr[2][PER], vr[2][PER];
+  while (jb < j1) {  // two keys of this warp per step, loaded before the step
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int j = jb + u * kCW;
-      const bool mine = own && j == nkv, in = j < j1;
-      const float *kp = Kh + (size_t)j * dk + lane, *vp = Vh + (size_t)j * dk + lane;
+    for (int u = 0; u < 2; u++)
+      if (own && jb + u * kCW == nkv)
 #pragma unroll
-      for (int i = 0; i < PER; i++) {
-        kr[u][i] = mine ? kn[i] : in ? kp[32 * i] : 0.0f;
-        vr[u][i] = mine ? vn[i] : in ? vp[32 * i] : 0.0f;
-      }
-    }
+        for (int i = 0; i < PER; i++) kr[u][i] = kn[i], vr[u][i] = vn[i];
 #pragma unroll
     for (int u = 0; u < 2; u++) {
       if (jb + u * kCW >= j1) break;
@@ -489,6 +541,8 @@ __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp,
       for (int i = 0; i < PER; i++) acc[i] = acc[i] * c + e * vr[u][i];
       m = mn;
     }
+    jb += 2 * kCW;
+    if (jb < j1) load_keys<PER>(Kh, Vh, jb, j1, lane, kr, vr);
   }
   float *rows = y, *wm = y + kCW * dk, *wz = wm + kCW;
 #pragma unroll
@@ -564,6 +618,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   __shared__ __align__(8) uint64_t full[kMaxSlots], empty[kMaxSlots];
   __shared__ float red[32];
   __shared__ Plan plan;
+  __shared__ __align__(16) FusedLayerW slw[2];
   const int G = gridDim.x;
   const uint32_t ring = su32(sm), full0 = su32(full), empty0 = su32(empty);
   if (threadIdx.x == 0) {
@@ -580,6 +635,14 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int t = threadIdx.x;
+  if (a.lw) {
+    lw_fetch(&slw[0], a.lw, t);
+    if (a.nl > 1) lw_fetch(&slw[1], a.lw + 1, t);
+    lw_landed(t);
+  } else if (t < kLwWords) {
+    reinterpret_cast<uint64_t *>(&slw[0])[t] = reinterpret_cast<const uint64_t *>(&a.lw0)[t];
+  }
+  cbar();
   const int D = a.D, F = a.F, Nq = a.H * dk;
   const uint32_t ep0 = *(volatile unsigned int *)a.epoch + 1u;  // the first layer's tag; layer l: ep0 + l
   const uint32_t a8 = ring + a.off_a8;
@@ -602,9 +665,11 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   const int nf = f1 - f0;
 
   for (int l = 0; l < a.nl; l++) {
-    const FusedLayerW &lw = a.lw ? a.lw[l] : a.lw0;
+    const FusedLayerW &lw = slw[l & 1];
     const uint32_t ep = ep0 + (uint32_t)l;
     const bool first = l == 0, last = l == a.nl - 1;
+    // the next layer's table into the other copy (layer l - 1, its last user, is done in every thread)
+    if (!first && l + 1 < a.nl) lw_fetch(&slw[(l + 1) & 1], a.lw + l + 1, t);
     if (t == 0) {  // phase A's plan
       plan.n = ranges(a, 0, blockIdx.x, G, plan.r);
       plan.C[0] = a.q, plan.C[1] = a.k, plan.C[2] = a.v;
@@ -662,19 +727,18 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     // ---- C: ao and the head maxima, quantization; o ----
     await_count(a.sync + 0, (unsigned int)((l + 1) * a.H));
     float om = 0.0f;
-    for (int i0 = t; i0 < a.H; i0 += kLB * kCT) {
-      uint32_t v[kLB];
-      ll_get_n<kLB>(a.amax, i0, kCT, a.H, ep, v);
+    for (int e0 = t; e0 < Nq || e0 < a.H; e0 += kLB * kCT) {  // the head maxima and ao: one round
+      uint64_t wm[kLB], wo[kLB];
+      uint32_t vm[kLB], vo[kLB];
+      ll_issue<kLB>(a.amax, e0, kCT, a.H, ep, wm);
+      ll_issue<kLB>(a.ao, e0, kCT, Nq, ep, wo);
+      ll_finish<kLB>(a.amax, e0, kCT, ep, wm, vm);
+      ll_finish<kLB>(a.ao, e0, kCT, ep, wo, vo);
 #pragma unroll
-      for (int u = 0; u < kLB; u++)
-        if (i0 + u * kCT < a.H) om = fmaxf(om, __uint_as_float(v[u]));
-    }
-    for (int e0 = t; e0 < Nq; e0 += kLB * kCT) {
-      uint32_t v[kLB];
-      ll_get_n<kLB>(a.ao, e0, kCT, Nq, ep, v);
-#pragma unroll
-      for (int u = 0; u < kLB; u++)
-        if (e0 + u * kCT < Nq) xs[e0 + u * kCT] = __uint_as_float(v[u]);
+      for (int u = 0; u < kLB; u++) {
+        if (e0 + u * kCT < a.H) om = fmaxf(om, __uint_as_float(vm[u]));
+        if (e0 + u * kCT < Nq) xs[e0 + u * kCT] = __uint_as_float(vo[u]);
+      }
     }
     om = c_max(om, red);
     const float sa = glue::qscale(om);
@@ -743,19 +807,19 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     // ---- E: quantization of h; down with the residual -> the next layer's x (or x_out) ----
     await_count(a.sync + 2, (unsigned int)((l + 1) * G));
     hm = 0.0f;
-    for (int i0 = t; i0 < G; i0 += kLB * kCT) {
-      uint32_t v[kLB];
-      ll_get_n<kLB>(a.hmax, i0, kCT, G, ep, v);
+    for (int i0 = t; i0 < F || i0 < G; i0 += kHB * kCT) {  // the CTA maxima and h: one round
+      uint64_t wm[2], wh[kHB];
+      uint32_t vm[2], vh[kHB];
+      ll_issue<2>(a.hmax, i0, kCT, G, ep, wm);
+      ll_issue<kHB>(a.h, i0, kCT, F, ep, wh);
+      ll_finish<2>(a.hmax, i0, kCT, ep, wm, vm);
+      ll_finish<kHB>(a.h, i0, kCT, ep, wh, vh);
 #pragma unroll
-      for (int u = 0; u < kLB; u++)
-        if (i0 + u * kCT < G) hm = fmaxf(hm, __uint_as_float(v[u]));
-    }
-    for (int i0 = t; i0 < F; i0 += kLB * kCT) {
-      uint32_t v[kLB];
-      ll_get_n<kLB>(a.h, i0, kCT, F, ep, v);
+      for (int u = 0; u < 2; u++)
+        if (i0 + u * kCT < G) hm = fmaxf(hm, __uint_as_float(vm[u]));
 #pragma unroll
-      for (int u = 0; u < kLB; u++)
-        if (i0 + u * kCT < F) ys[i0 + u * kCT] = __uint_as_float(v[u]);
+      for (int u = 0; u < kHB; u++)
+        if (i0 + u * kCT < F) ys[i0 + u * kCT] = __uint_as_float(vh[u]);
     }
     hm = c_max(hm, red);
     const float sc = glue::qscale(hm);
@@ -766,6 +830,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     }
     cbar();
     kc = consume<FMT>(a, plan, 3, kc, ring, full0, empty0, a8, tb, ep);
+    lw_landed(t);  // the next layer's table (long landed); the arrival's barrier publishes it
     if (!last) arrive(a.sync + 4);
   }
 

@@ -77,7 +77,7 @@ enum { OUT_I32 = 0, OUT_I8 = 1, OUT_I16 = 2, OUT_EWMUL = 3 };
 // Column-sharded runs with the gather over peer memory (peers.cu).
 constexpr int kMaxPeers = 8;
 struct PeerTable {                 // device memory, written once when the table is created
-  int n, rank, ldc, col0, ctas;    // ranks, this rank, C row stride, first column, push CTAs of a run
+  int n, rank, ldc, col0, ctas;    // ranks, this rank, C row stride, first column, shard columns
   int32_t *C[kMaxPeers];           // every rank's C [M][ldc], mapped in this process
   unsigned int *flag[kMaxPeers];   // every rank's signal counts [kMaxPeers] (index: signalling rank)
   unsigned int *waited;            // this rank's count of completed waits (private)

@@ -5,8 +5,9 @@
 // src/npu/i4/pack.c:63-80; the reference splits the same way over its NPU cores, src/npu.c:1356-1398)
 // leaves rank g with C[:, g's columns]; every rank needs all of C. A run is the local matmul into a
 // scratch C at full speed, then a push kernel, launched as its programmatic dependent (it is resident
-// while the matmul drains), that copies the shard's rows into every rank's C with 16-byte stores; each
-// push CTA counts itself done on this GPU (acq_rel) and the last one signals every rank once with a
+// while the matmul drains) with a grid sized from the shard's bytes, that copies the shard's rows into
+// every rank's C with 16-byte stores; each push CTA counts itself done on this GPU (acq_rel) and the
+// last one signals every rank once with a
 // system-scope release add (release.gpu -> acquire.gpu -> release.sys orders every CTA's peer stores
 // before the signal). A rank that needs C waits (on its stream, bounded) until every rank's count of
 // signals reaches the runs it has consumed plus one.
@@ -23,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <new>
 
@@ -46,27 +48,30 @@ namespace {
 __device__ unsigned int g_peer_error = 0;
 constexpr uint64_t kPeerSpin = 4000000000ull;  // ~2 s of SM clock
 
-constexpr int kPushCols = 512;  // shard columns one push CTA copies
+constexpr int kPushVecs = 256;      // 16-byte vectors (or elements) per push CTA when sizing the grid
+constexpr size_t kPushMax = 148 * 8;  // at most eight resident 256-thread CTAs per SM; larger shards grid-stride
 
-// CTA b copies columns [b * kPushCols, +kPushCols) of every row of the local C (row stride n) into every
-// rank's C at the shard's offset (16-byte vectors when the row layout allows), then counts itself done;
-// the run's last push CTA signals every rank.
+// Copies the local C [M][n] (row stride n) into every rank's C at the shard's offset, grid-striding over
+// 16-byte vectors when the row layout allows, then counts the CTA done on this GPU; the run's last push
+// CTA (of gridDim.x) signals every rank. The grid is sized per run from M * n.
 __global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C, int M, int n,
                                                     const PeerTable *__restrict__ pt) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the matmul is complete
-  const int c0 = blockIdx.x * kPushCols, nc = min(kPushCols, n - c0);
   const bool vec = (n % 4 == 0) && (pt->ldc % 4 == 0) && (pt->col0 % 4 == 0);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
   if (vec) {
-    const int nv = nc / 4;
-    for (int e = threadIdx.x; e < M * nv; e += blockDim.x) {
-      const int m = e / nv, c = c0 + (e % nv) * 4;
+    const int nv = n / 4;
+    const size_t total = (size_t)M * nv;
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+      const int m = (int)(e / nv), c = (int)(e % nv) * 4;
       const int4 v = *reinterpret_cast<const int4 *>(C + (size_t)m * n + c);
       const size_t o = (size_t)m * pt->ldc + pt->col0 + c;
       for (int r = 0; r < pt->n; r++) *reinterpret_cast<int4 *>(pt->C[r] + o) = v;
     }
   } else {
-    for (int e = threadIdx.x; e < M * nc; e += blockDim.x) {
-      const int m = e / nc, c = c0 + e % nc;
+    const size_t total = (size_t)M * n;
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+      const int m = (int)(e / n), c = (int)(e % n);
       const int32_t v = C[(size_t)m * n + c];
       const size_t o = (size_t)m * pt->ldc + pt->col0 + c;
       for (int r = 0; r < pt->n; r++) pt->C[r][o] = v;
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C
   if (threadIdx.x == 0) {
     unsigned int old;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(pt->done) : "memory");
-    if (old == (unsigned int)pt->ctas - 1u) {
+    if (old == gridDim.x - 1u) {
       *pt->done = 0u;
       for (int r = 0; r < pt->n; r++)
         asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pt->flag[r] + pt->rank) : "memory");
@@ -137,12 +142,13 @@ namespace {
 int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, int dtype, const char *name) {
   if (!c || !w || !dA || !p || p->ctx != c || M < 1 || w->dtype != dtype || w->fmt == FMT_F16) return -1;
   const PeerTable &t = p->host;
-  if (w->N + t.col0 > t.ldc || (w->N + kPushCols - 1) / kPushCols != t.ctas) return -1;  // the table's shard
+  if (w->N + t.col0 > t.ldc || w->N != t.ctas) return -1;  // the table's shard width
   DeviceGuard dg(c->device);
   if (!grow(&c->dC, &c->capC, (size_t)M * w->N * 4)) return -1;
   if (launch(c, w, M, dA, c->dC)) return -1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(t.ctas);
+  const size_t units = (size_t)M * (w->N % 4 == 0 ? w->N / 4 : w->N);
+  cfg.gridDim = dim3((unsigned int)std::min<size_t>(kPushMax, std::max<size_t>(1, (units + kPushVecs - 1) / kPushVecs)));
   cfg.blockDim = dim3(256);
   cfg.stream = c->stream;
   cudaLaunchAttribute at[1];
@@ -217,7 +223,7 @@ ork_b200_peers *ork_b200_peers_create(ork_npu *c, int nranks, int rank, void *co
   if (!p) return nullptr;
   p->ctx = c;
   PeerTable &t = p->host;
-  t.n = nranks, t.rank = rank, t.ldc = ldc, t.col0 = col0, t.ctas = (ncols + kPushCols - 1) / kPushCols;
+  t.n = nranks, t.rank = rank, t.ldc = ldc, t.col0 = col0, t.ctas = ncols;
   for (int r = 0; r < nranks; r++) {
     t.C[r] = (int32_t *)C[r];
     t.flag[r] = (unsigned int *)flags[r];
