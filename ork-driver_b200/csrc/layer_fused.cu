@@ -378,7 +378,11 @@ struct Plan {
 // Consume the planned phase's slots (the sequence the producer issued, from slot kc). Ring slot s belongs
 // to warp s % kCW for all its uses, so one warp consumes each slot's uses in order: a warp never waits on
 // a slot's next use before that slot's previous use landed (a parity wait two phases ahead would pass at
-// once and let the producer re-arm a barrier whose copy is still in flight). Returns the running count.
+// once and let the producer re-arm a barrier whose copy is still in flight). A warp visits only its own
+// slots' indices, in increasing order (its ring slots w and w + kCW interleaved), found with one division
+// per range: walking every index with a runtime modulo cost the slowest warp ~5,000 cycles a phase.
+// Returns the running count.
+static_assert(kMaxSlots <= 2 * kCW, "a warp owns at most two ring slots");
 template <int FMT>
 __device__ __noinline__ uint32_t consume(const FusedArgs &a, const Plan &pl, int p, uint32_t kc, uint32_t ring,
                                          uint32_t full0, uint32_t empty0, uint32_t a8, const Nf4Tables tb,
@@ -395,11 +399,25 @@ __device__ __noinline__ uint32_t consume(const FusedArgs &a, const Plan &pl, int
     const int rps = (int)(a.slot / rowB);
     const int nslot = (re - rb + rps - 1) / rps;
     uint64_t *C = p == 0 ? pl.C[w] : pl.C[0];
-    for (int q = 0; q < nslot; q++) {
-      const uint32_t k = kc + (uint32_t)q, s = k % ns;
-      if ((int)(s % kCW) != warp) continue;
+    // index kc + q sits in ring slot (kc + q) % ns with parity ((kc + q) / ns) & 1
+    const uint32_t base = kc / ns, rem = kc % ns;
+    uint32_t nq[2], wr[2];  // next index of each of the warp's ring slots, and its use count
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const uint32_t sj = (uint32_t)(warp + j * kCW);
+      nq[j] = sj >= ns ? 0xffffffffu : sj >= rem ? sj - rem : sj + ns - rem;
+      wr[j] = base + (sj >= rem ? 0u : 1u);
+    }
+    while (true) {
+      const int j = nq[1] < nq[0] ? 1 : 0;
+      const uint32_t q32 = nq[j];
+      if (q32 >= (uint32_t)nslot) break;
+      const int q = (int)q32;
+      const uint32_t s = (uint32_t)(warp + j * kCW), par = wr[j] & 1u;
+      nq[j] += ns;
+      wr[j] += 1u;
       const int r0 = rb + q * rps, nr = min(rps, re - r0);
-      const bool ok = mbar_wait(full0 + 8 * s, (k / ns) & 1);
+      const bool ok = mbar_wait(full0 + 8 * s, par);
       for (int j0 = 0; j0 < nr; j0 += kRowsPass) {
         const int m = min(kRowsPass, nr - j0);
         const int v = ok ? rows_dot<FMT>(ring + s * a.slot + (uint32_t)j0 * rowB, a8, rowB, m, lane, tb) : 0;
