@@ -54,7 +54,7 @@ constexpr int kRowsPass = 8;  // rows a warp reduces together
 constexpr int kLB = 4;        // row elements a thread loads at once in the glue
 constexpr int kHB = 12;       // SwiGLU elements a thread loads at once (F <= 6144 in one round)
 constexpr uint64_t kSpin = 4000000000ull;
-constexpr int kSmemMax = 227 * 1024 - 1024;  // dynamic part; the static barriers, tables and scratch use <= 1 KB
+constexpr int kSmemMax = 227 * 1024 - 2048;  // dynamic part; the static barriers, tables and scratch use <= 2 KB
 
 __device__ unsigned int g_fused_error = 0;
 
@@ -363,9 +363,32 @@ __device__ __forceinline__ int rows_dot(uint32_t w, uint32_t a8, uint32_t rowB, 
 
 // One phase of the CTA: its row ranges and where the row results go. Thread 0 writes it to shared memory
 // before the phase; the compute warps read it there (uniform loads, no per-thread copies).
-struct Plan {
-  int n;
+// A CTA's rows of one phase and how they fill the ring: the same for every layer, so computed once per
+// launch (the divisions stay out of the phases).
+struct PhaseGeo {
+  int n;                    // row ranges
   Range r[3];
+  int rps[3], nslot[3];     // rows per slot, slots
+  uint32_t rowB[3];         // bytes per row
+  uint32_t nsq[3], nsr[3];  // slots / ring size, slots % ring size
+};
+// The running slot index kc of the consumers as kc / ns and kc % ns.
+struct Cursor {
+  uint32_t base, rem;
+};
+template <int FMT>
+__device__ void phase_geo(const FusedArgs &a, int p, int G, PhaseGeo &g) {
+  g.n = ranges(a, p, blockIdx.x, G, g.r);
+  const uint32_t ns = (uint32_t)a.nslots;
+  for (int i = 0; i < g.n; i++) {
+    const uint32_t rowB = row_bytes<FMT>(wK(a, g.r[i].w));
+    const int rps = (int)(a.slot / rowB), nslot = (g.r[i].r1 - g.r[i].r0 + rps - 1) / rps;
+    g.rowB[i] = rowB, g.rps[i] = rps, g.nslot[i] = nslot;
+    g.nsq[i] = (uint32_t)nslot / ns, g.nsr[i] = (uint32_t)nslot % ns;
+  }
+}
+
+struct Plan {
   uint64_t *C[3];  // phase 0: q, k, v (by weight); phase 1: o
   int *loc;       // phase 2: this CTA's gate results, then its up results (nf each)
   int f0, nf;
@@ -379,28 +402,27 @@ struct Plan {
 // to warp s % kCW for all its uses, so one warp consumes each slot's uses in order: a warp never waits on
 // a slot's next use before that slot's previous use landed (a parity wait two phases ahead would pass at
 // once and let the producer re-arm a barrier whose copy is still in flight). A warp visits only its own
-// slots' indices, in increasing order (its ring slots w and w + kCW interleaved), found with one division
-// per range: walking every index with a runtime modulo cost the slowest warp ~5,000 cycles a phase.
-// Returns the running count.
+// slots' indices, in increasing order (its ring slots w and w + kCW interleaved), from the cursor and the
+// precomputed geometry, with no division: walking every index with a runtime modulo cost the slowest warp
+// ~5,000 cycles a phase. Returns the advanced cursor.
 static_assert(kMaxSlots <= 2 * kCW, "a warp owns at most two ring slots");
 template <int FMT>
-__device__ __noinline__ uint32_t consume(const FusedArgs &a, const Plan &pl, int p, uint32_t kc, uint32_t ring,
+__device__ __noinline__ Cursor consume(const FusedArgs &a, const PhaseGeo &g, const Plan &pl, int p, Cursor cur, uint32_t ring,
                                          uint32_t full0, uint32_t empty0, uint32_t a8, const Nf4Tables tb,
                                          uint32_t ep) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ns = (uint32_t)a.nslots;
   const int lr = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);  // row of reduce8's lane
-  const int n = pl.n;
+  const int n = g.n;
 #pragma unroll
   for (int i = 0; i < 3; i++) {
     if (i >= n) break;
-    const int w = pl.r[i].w, rb = pl.r[i].r0, re = pl.r[i].r1;
-    const uint32_t rowB = row_bytes<FMT>(wK(a, w));
-    const int rps = (int)(a.slot / rowB);
-    const int nslot = (re - rb + rps - 1) / rps;
+    const int w = g.r[i].w, rb = g.r[i].r0, re = g.r[i].r1;
+    const uint32_t rowB = g.rowB[i];
+    const int rps = g.rps[i], nslot = g.nslot[i];
     uint64_t *C = p == 0 ? pl.C[w] : pl.C[0];
     // index kc + q sits in ring slot (kc + q) % ns with parity ((kc + q) / ns) & 1
-    const uint32_t base = kc / ns, rem = kc % ns;
+    const uint32_t base = cur.base, rem = cur.rem;
     uint32_t nq[2], wr[2];  // next index of each of the warp's ring slots, and its use count
 #pragma unroll
     for (int j = 0; j < 2; j++) {
@@ -436,9 +458,14 @@ __device__ __noinline__ uint32_t consume(const FusedArgs &a, const Plan &pl, int
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty0 + 8 * s) : "memory");
     }
-    kc += (uint32_t)nslot;
+    cur.base += g.nsq[i];
+    cur.rem += g.nsr[i];
+    if (cur.rem >= ns) {
+      cur.rem -= ns;
+      cur.base++;
+    }
   }
-  return kc;
+  return cur;
 }
 
 // ---- phase B: one split-KV attention item, warp-centric -------------------------------------------
@@ -636,6 +663,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   __shared__ __align__(8) uint64_t full[kMaxSlots], empty[kMaxSlots];
   __shared__ float red[32];
   __shared__ Plan plan;
+  __shared__ PhaseGeo geo[4];
   __shared__ __align__(16) FusedLayerW slw[2];
   const int G = gridDim.x;
   const uint32_t ring = su32(sm), full0 = su32(full), empty0 = su32(empty);
@@ -645,6 +673,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(empty0 + 8 * s));
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int p = 0; p < 4; p++) phase_geo<FMT>(a, p, G, geo[p]);
   }
   __syncthreads();
   if (threadIdx.x >= kCT) {  // the producer warp: one lane streams, the others are done
@@ -668,7 +697,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
   float *xs = reinterpret_cast<float *>(sm + a.off_x);  // x, ao, then x1 (kept to the end of the layer)
   float *ys = reinterpret_cast<float *>(sm + a.off_y);  // norm gains / attention scratch / h
   int *loc = reinterpret_cast<int *>(sm + a.off_loc);   // this CTA's gate and up results
-  uint32_t kc = 0;
+  Cursor kc = {0u, 0u};
   const bool ext = a.ext != 0;
   const int pos = a.dpos ? *a.dpos : a.pos;
   const int nkv = a.dpos ? *a.dpos : a.nkv;
@@ -689,7 +718,6 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     // the next layer's table into the other copy (layer l - 1, its last user, is done in every thread)
     if (!first && l + 1 < a.nl) lw_fetch(&slw[(l + 1) & 1], a.lw + l + 1, t);
     if (t == 0) {  // phase A's plan
-      plan.n = ranges(a, 0, blockIdx.x, G, plan.r);
       plan.C[0] = a.q, plan.C[1] = a.k, plan.C[2] = a.v;
     }
 
@@ -727,7 +755,7 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     const float sx = glue::qscale(mx);
     for (int i = t; i < D; i += kCT) a8p[i] = q8(xs[i] * r * ys[i], sx);
     cbar();
-    kc = consume<FMT>(a, plan, 0, kc, ring, full0, empty0, a8, tb, ep);
+    kc = consume<FMT>(a, geo[0], plan, 0, kc, ring, full0, empty0, a8, tb, ep);
 
     // ---- B: attention items, then the merge of head h by CTA h ----
     if (bad) {  // no attention: ao is zero (the error is reported), so the phases after still complete
@@ -762,11 +790,10 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     const float sa = glue::qscale(om);
     for (int e = t; e < Nq; e += kCT) a8p[e] = q8(xs[e], sa);
     if (t == 0) {
-      plan.n = ranges(a, 1, blockIdx.x, G, plan.r);
       plan.C[0] = a.o;
     }
     cbar();
-    kc = consume<FMT>(a, plan, 1, kc, ring, full0, empty0, a8, tb, ep);
+    kc = consume<FMT>(a, geo[1], plan, 1, kc, ring, full0, empty0, a8, tb, ep);
     arrive(a.sync + 1);
 
     // ---- D: x1 = x + Co / sa, RMSNorm + quant; gate and up; SwiGLU ----
@@ -806,11 +833,10 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     const float sf = glue::qscale(mx);
     for (int i = t; i < D; i += kCT) a8p[i] = q8(xs[i] * r * ys[i], sf);
     if (t == 0) {
-      plan.n = ranges(a, 2, blockIdx.x, G, plan.r);
       plan.loc = loc, plan.f0 = f0, plan.nf = nf;
     }
     cbar();
-    kc = consume<FMT>(a, plan, 2, kc, ring, full0, empty0, a8, tb, ep);
+    kc = consume<FMT>(a, geo[2], plan, 2, kc, ring, full0, empty0, a8, tb, ep);
     cbar();
     float hm = 0.0f;
     for (int i = t; i < nf; i += kCT) {
@@ -843,11 +869,10 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     const float sc = glue::qscale(hm);
     for (int i = t; i < F; i += kCT) a8p[i] = q8(ys[i], sc);
     if (t == 0) {
-      plan.n = ranges(a, 3, blockIdx.x, G, plan.r);
       plan.out = last ? a.x_out : nullptr, plan.xl = last ? nullptr : a.xl, plan.x1 = xs, plan.s = sc;
     }
     cbar();
-    kc = consume<FMT>(a, plan, 3, kc, ring, full0, empty0, a8, tb, ep);
+    kc = consume<FMT>(a, geo[3], plan, 3, kc, ring, full0, empty0, a8, tb, ep);
     lw_landed(t);  // the next layer's table (long landed); the arrival's barrier publishes it
     if (!last) arrive(a.sync + 4);
   }
