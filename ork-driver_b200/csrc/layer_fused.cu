@@ -542,12 +542,12 @@ __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp,
   }
   // the raw q (and the token's own k, v): one round of polls
   uint32_t cq[PER], ck[PER], cv[PER];
+  // q first (what is awaited); the token's k and v, written in the same phase, in one round after
+  ll_get_n<PER>(a.q + h * dk, lane, 32, dk, ep, cq);
   {
-    uint64_t wq[PER], wk[PER], wv[PER];
-    ll_issue<PER>(a.q + h * dk, lane, 32, dk, ep, wq);
+    uint64_t wk[PER], wv[PER];
     ll_issue<PER>(a.k + hk * dk, lane, 32, own ? dk : 0, ep, wk);
     ll_issue<PER>(a.v + hk * dk, lane, 32, own ? dk : 0, ep, wv);
-    ll_finish<PER>(a.q + h * dk, lane, 32, ep, wq, cq);
     ll_finish<PER>(a.k + hk * dk, lane, 32, ep, wk, ck);
     ll_finish<PER>(a.v + hk * dk, lane, 32, ep, wv, cv);
   }
@@ -626,10 +626,15 @@ __device__ void merge_head(const FusedArgs &a, int h, int S, float *red, uint32_
   if (t < dk) {
     float Mh = -3.0e38f, Z = 0.0f, o = 0.0f;
     for (int i0 = 0; i0 < S; i0 += 8) {
+      // the chunk maxima first (they are what is awaited); the sums and V rows, written with them, in one
+      // round after (polled together before the maxima land, every word would be re-polled in turn)
       uint32_t vm[8], vz[8], vo[8];
       ll_get_n<8>(a.pm + h * Sg, i0, 1, S, ep, vm);
-      ll_get_n<8>(a.pz + h * Sg, i0, 1, S, ep, vz);
-      ll_get_n<8>(a.po + (size_t)h * Sg * dk + t, i0 * dk, dk, S * dk, ep, vo);
+      uint64_t wz[8], wo[8];
+      ll_issue<8>(a.pz + h * Sg, i0, 1, S, ep, wz);
+      ll_issue<8>(a.po + (size_t)h * Sg * dk + t, i0 * dk, dk, S * dk, ep, wo);
+      ll_finish<8>(a.pz + h * Sg, i0, 1, ep, wz, vz);
+      ll_finish<8>(a.po + (size_t)h * Sg * dk + t, i0 * dk, dk, ep, wo, vo);
       float mb = Mh;
 #pragma unroll
       for (int u = 0; u < 8; u++)
@@ -799,21 +804,24 @@ __global__ void __launch_bounds__(kFThreads, 1) layer_fused_kernel(const __grid_
     // ---- D: x1 = x + Co / sa, RMSNorm + quant; gate and up; SwiGLU ----
     await_count(a.sync + 1, (unsigned int)((l + 1) * G));
     ss = 0.0f;
-    for (int i0 = t; i0 < D; i0 += kLB * kCT) {
+    for (int i0 = t; i0 < D; i0 += kLB * kCT) {  // gains, x and Co: one round
       float v[kLB], g[kLB];
       uint32_t c[kLB];
+#pragma unroll
+      for (int u = 0; u < kLB; u++) g[u] = i0 + u * kCT < D ? lw.ffn_norm[i0 + u * kCT] : 0.0f;
+      uint64_t wx[kLB], wo[kLB];
+      if (!first) ll_issue<kLB>(a.xl, i0, kCT, D, ep - 1u, wx);
+      ll_issue<kLB>(a.o, i0, kCT, D, ep, wo);
       if (first) {
 #pragma unroll
         for (int u = 0; u < kLB; u++) v[u] = i0 + u * kCT < D ? a.x[i0 + u * kCT] : 0.0f;
       } else {
         uint32_t w[kLB];
-        ll_get_n<kLB>(a.xl, i0, kCT, D, ep - 1u, w);
+        ll_finish<kLB>(a.xl, i0, kCT, ep - 1u, wx, w);
 #pragma unroll
         for (int u = 0; u < kLB; u++) v[u] = __uint_as_float(w[u]);
       }
-#pragma unroll
-      for (int u = 0; u < kLB; u++) g[u] = i0 + u * kCT < D ? lw.ffn_norm[i0 + u * kCT] : 0.0f;
-      ll_get_n<kLB>(a.o, i0, kCT, D, ep, c);
+      ll_finish<kLB>(a.o, i0, kCT, ep, wo, c);
 #pragma unroll
       for (int u = 0; u < kLB; u++) {
         const int i = i0 + u * kCT;
