@@ -928,6 +928,80 @@ def run_profile(spec):
     ctx.close()
 
 
+def run_tc_peak(args):
+    """The tensor pipe's ceiling: the library's tcgen05 GEMM (ork_i8_mm_run_async, ork_f16_mm_run_async) at
+    M = K = N = 8192, where the work is compute-bound (1.1 T ops against ~0.4 GB), timed beside the GPU's
+    measured dense peak on the same shapes (torch._int_mm and torch.mm, i.e. cuBLASLt). Not a BASELINE
+    config: it measures the denominator the prefill fractions need and how close the kernel comes to it.
+    The int8 result is checked equal to torch._int_mm's (exact int32)."""
+    import torch
+
+    import ork_b200
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    L = ork_b200.lib()
+    ctx = ork_b200.Context()
+    stream = torch.cuda.Stream()
+    L.ork_b200_set_stream(ctx.ctx, stream.cuda_stream)
+    S = 8192
+    ops = 2.0 * S * S * S
+    g = torch.Generator(device="cuda").manual_seed(7)
+
+    def timed(fn, reps=10):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = {}
+    with Clocks(local) as clk:
+        A8 = torch.randint(-127, 128, (S, S), dtype=torch.int8, device="cuda", generator=g)
+        B8 = torch.randint(-127, 128, (S, S), dtype=torch.int8, device="cuda", generator=g)
+        w8 = ctx.i8_pack(B8.cpu().numpy())
+        C32 = torch.empty((S, S), dtype=torch.int32, device="cuda")
+        ms = timed(lambda: L.ork_i8_mm_run_async(ctx.ctx, w8.h, S, A8.data_ptr(), C32.data_ptr()))
+        out["int8_ours_tops"] = ops / (ms * 1e-3) / 1e12
+        try:
+            ms_lib = timed(lambda: torch._int_mm(A8, B8))
+            out["int8_torch_int_mm_tops"] = ops / (ms_lib * 1e-3) / 1e12
+            with torch.cuda.stream(stream):
+                same = bool(torch.equal(C32, torch._int_mm(A8, B8)))
+            torch.cuda.synchronize()
+            out["int8_equal_to_torch"] = same
+        except RuntimeError as e:
+            out["int8_torch_int_mm"] = f"unavailable: {str(e).splitlines()[0][:120]}"
+        w8.free()
+        del A8, B8, C32
+        A16 = (torch.randn((S, S), device="cuda", generator=g) * 0.5).to(torch.float16)
+        B16 = (torch.randn((S, S), device="cuda", generator=g) * 0.02).to(torch.float16)
+        w16 = ctx.f16_pack(B16.cpu().numpy())
+        C = torch.empty((S, S), dtype=torch.float32, device="cuda")
+        ms = timed(lambda: L.ork_f16_mm_run_async(ctx.ctx, w16.h, S, A16.data_ptr(), C.data_ptr()))
+        out["f16_ours_tflops"] = ops / (ms * 1e-3) / 1e12
+        ms_lib = timed(lambda: torch.mm(A16, B16))
+        out["f16_torch_mm_tflops"] = ops / (ms_lib * 1e-3) / 1e12
+        w16.free()
+    line = {"metric": "tcgen05 GEMM throughput at 8192^3 (ours vs the cuBLASLt peak on this GPU)",
+            "value": out["int8_ours_tops"], "unit": "TOPS", "n_gpus": 1, "steps": 10, "warmup": 3,
+            "higher_is_better": True, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "M = K = N = 8192, int8 (A, B ~ U[-127, 127]) and fp16; C int32 / fp32"},
+            **{k: (round(v, 1) if isinstance(v, float) else v) for k, v in out.items()},
+            "clocks": clk.summary()}
+    if "int8_torch_int_mm_tops" in out:
+        line["int8_frac_of_measured_peak"] = out["int8_ours_tops"] / out["int8_torch_int_mm_tops"]
+    line["f16_frac_of_measured_peak"] = out["f16_ours_tflops"] / out["f16_torch_mm_tflops"]
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -939,10 +1013,11 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
-    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped", "moe"],
+    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped", "moe", "tc_peak"],
                     help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack; "
                          "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack; grouped: grouped-scale W4A8 decode; "
-                         "moe: a batch of 64 NF4 expert matmuls through ork_i8_mm_run_chain")
+                         "moe: a batch of 64 NF4 expert matmuls through ork_i8_mm_run_chain; tc_peak: the GEMM "
+                         "at 8192^3 beside torch._int_mm / torch.mm")
     ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="70b workload at N > 1: the C gather fused into the matmul over peer memory, or NCCL")
@@ -962,6 +1037,8 @@ def main():
         return run_grouped(args)
     if args.workload == "moe":
         return run_moe(args)
+    if args.workload == "tc_peak":
+        return run_tc_peak(args)
 
     import torch
 
