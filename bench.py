@@ -388,8 +388,9 @@ def run_qwen3(args):
     ork_i8_mm_layers_async call (one persistent launch) -- the library's decode layer: RMSNorm + int8 quantization, q/k/v in one
     batched launch, q/k RMSNorm + RoPE + attention over the fp32 KV cache (the token's k/v appended at the
     device-side position), o, residual + RMSNorm + quantization, gate/up in one launch, SwiGLU +
-    quantization, down, residual -- then the final norm and the LM head (ork_i8_mm_run_async) and a greedy
-    argmax; a whole token is one CUDA graph. Prefill of the 128-token prompt runs the same model with
+    quantization, down, residual -- then the final norm + quantization (ork_b200_rmsnorm_q8_async), the LM
+    head (ork_i8_mm_run_async) and the greedy pick (ork_b200_argmax_scaled_async); a whole token is one
+    CUDA graph. Prefill of the 128-token prompt runs the same model with
     PyTorch glue around ork_i8_mm_run (per-row activation quantization), captured as one CUDA graph.
     Four distinct layer weight sets (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s;
     prefill tokens/s beside it."""
@@ -489,12 +490,17 @@ def run_qwen3(args):
                                     ones_h.data_ptr(), ones_d.data_ptr(), kc[li].data_ptr(), vc[li].data_ptr())
                              for li in range(NLY)])
 
+    q8h = torch.empty(H, dtype=torch.int8, device=dev)
+    c_lm = torch.empty(V, dtype=torch.int32, device=dev)
+
     def decode_step():
         xa.copy_(emb.index_select(0, tok).float().view(-1))
         assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NLY, stack, xa.data_ptr(), xb.data_ptr(),
                                         C.byref(kv)) == 0
-        logits = linear(rmsnorm(xb.view(1, -1), ones_h), lm)
-        tok.copy_(logits.argmax(-1))
+        # the final norm + quantization, the LM head and the greedy pick: three library launches
+        assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, xb.data_ptr(), ones_h.data_ptr(), H, q8h.data_ptr(), None) == 0
+        assert L.ork_i8_mm_run_async(ctx.ctx, lm[0].h, 1, q8h.data_ptr(), c_lm.data_ptr()) == 0
+        assert L.ork_b200_argmax_scaled_async(ctx.ctx, c_lm.data_ptr(), lm[1].data_ptr(), V, tok.data_ptr()) == 0
         pos.add_(1)
 
     with torch.cuda.stream(stream):
@@ -554,7 +560,8 @@ def run_qwen3(args):
                                    "16/8 heads x 128, SwiGLU 6144, vocab 151936, q/k norms, RoPE 1e6; prefill 128 "
                                    "then 256 greedy decode steps, batch 1",
                        "linears": "decode: the 28 layers as one ork_i8_mm_layers_async call (the library's decode "
-                                  "layer, one persistent launch), LM head through ork_i8_mm_run_async; "
+                                  "layer, one persistent launch), final norm + quantization, LM head "
+                                  "(ork_i8_mm_run_async) and greedy pick as three library launches; "
                                   "prefill: PyTorch glue around ork_i8_mm_run_async, captured as one CUDA graph "
                                   "(prefill_eager_ms: the same prompt launched eagerly)",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",

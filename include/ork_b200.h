@@ -88,6 +88,16 @@ typedef struct ork_b200_layer_w {
 int ork_i8_mm_layers_async(ork_npu *ctx, const struct ork_layer_dims *d, int nlayers, const ork_b200_layer_w *layers,
                            const float *x, float *x_out, const ork_b200_layer_kv *kv);
 
+/* Decode glue around the LM head (device pointers, on the context stream; 0, or -1 on bad arguments).
+ * ork_b200_rmsnorm_q8_async: RMSNorm of the row x[n] with gain g (NULL: none; eps 1e-6) and its per-tensor
+ *   int8 quantization, the decode layer's formulas (ork-driver src/spine_kernels.h spine_rmsnorm +
+ *   spine_quant): y = (x / sqrt(mean(x^2) + 1e-6)) * g, s = 127 / max(1e-6, max|y|), q8 = clamp(rint(y*s),
+ *   +-127); *scale = s when scale is not NULL. n <= 8192.
+ * ork_b200_argmax_scaled_async: the first j with the largest C[j] * bs[j] over an int32 matmul row C[n]
+ *   (bs: the weight's per-channel scales), written as int64 to *idx: the greedy pick over the LM head. */
+int ork_b200_rmsnorm_q8_async(ork_npu *ctx, const float *x, const float *g, int n, int8_t *q8, float *scale);
+int ork_b200_argmax_scaled_async(ork_npu *ctx, const int32_t *C, const float *bs, int n, long long *idx);
+
 /* Column-sharded runs with the gather fused into the matmul (one process per GPU, NVLink peer memory).
  * Rank g of R holds output channels [col0, col0 + ncols) of a weight; its run writes those columns of C
  * into EVERY rank's C buffer ([M][ldc] int32) and signals every rank once per run; a rank that needs C

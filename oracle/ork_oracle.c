@@ -441,6 +441,22 @@ static float orc_q8(const float *x, int n, int8_t *q)
     return s;
 }
 
+/* The decode glue in front of the LM head: RMSNorm of one row (gain g, NULL = none) and its per-tensor int8
+ * quantization, as orc_rms + orc_q8 (src/spine_kernels.h spine_rmsnorm + spine_quant); returns s. */
+ORC_API float orc_rms_q8(const float *x, const float *g, int n, int8_t *q)
+{
+    float *y = malloc((size_t)n * sizeof *y), *one = NULL;
+    if (!g) {
+        one = malloc((size_t)n * sizeof *one);
+        for (int i = 0; i < n; i++) one[i] = 1.0f;
+    }
+    orc_rms(x, g ? g : one, n, y);
+    const float s = orc_q8(y, n, q);
+    free(y);
+    free(one);
+    return s;
+}
+
 static void orc_rope(float *x, int n, int pos, float base)
 {
     const int h = n / 2;

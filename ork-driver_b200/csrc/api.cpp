@@ -267,6 +267,12 @@ ork_npu *ork_npu_init(void) {
     return nullptr;
   }
   c->stream = c->own_stream;
+  if (cudaMalloc(&c->dG, 16) != cudaSuccess || cudaMemset(c->dG, 0, 16) != cudaSuccess) {
+    if (c->dG) cudaFree(c->dG);
+    cudaStreamDestroy(c->own_stream);
+    delete c;
+    return nullptr;
+  }
   return c;
 }
 
@@ -282,6 +288,7 @@ void ork_npu_free(ork_npu *c) {
     layer_tabs_free(c);
     if (c->dL) cudaFree(c->dL);
     if (c->dX) cudaFree(c->dX);
+    if (c->dG) cudaFree(c->dG);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;

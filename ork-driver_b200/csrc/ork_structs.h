@@ -25,6 +25,7 @@ struct ork_npu {
   void *dX = nullptr;    // the residual stream between multi-launch layers (layer.cu)
   size_t capX = 0;
   void *ltabs = nullptr; // device tables of persistent-layer pointer lists (layer.cu)
+  void *dG = nullptr;    // 16 bytes, zero between calls: the argmax's running key and CTA count (decode_glue.cu)
   bool pdl = true;
   int force_route = -1;
   uint64_t launches = 0;

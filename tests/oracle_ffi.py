@@ -45,6 +45,8 @@ def restated():
         lib.orc_gen_rnd_f16.argtypes = [C.POINTER(C.c_uint32), C.c_void_p, C.c_size_t]
         lib.orc_nf4_lut.argtypes = [C.c_void_p]
         lib.orc_threads.restype = C.c_int
+        lib.orc_rms_q8.restype = C.c_float
+        lib.orc_rms_q8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
         lib.orc_layer_i8.restype = C.c_int
         lib.orc_layer_i8.argtypes = [C.c_void_p, C.c_double, C.c_double] + [C.c_void_p] * 7 + [C.c_void_p] * 7 + \
             [C.c_int, C.c_void_p, C.c_int]
@@ -201,6 +203,15 @@ def layer(dims, attn_scale, rope_base, Bs, norms, x, Kc, Vc, kv_ext=False, hstri
                                  None if kn is None else _p(kn), hstride)
     assert rc == 0
     return out, Kc, Vc
+
+
+def rms_q8(x, g=None):
+    """RMSNorm + per-tensor int8 quantization of one row (src/spine_kernels.h spine_rmsnorm + spine_quant):
+    (codes int8 [n], scale s)."""
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.empty(x.size, np.int8)
+    s = restated().orc_rms_q8(_p(x), None if g is None else _p(np.ascontiguousarray(g, np.float32)), x.size, _p(q))
+    return q, s
 
 
 def i8_quant_f32(f32_nk):

@@ -1,0 +1,122 @@
+"""The decode glue around the LM head on the B200 (ork_b200_rmsnorm_q8_async, ork_b200_argmax_scaled_async,
+include/ork_b200.h): RMSNorm + per-tensor int8 quantization against the oracle's restatement of the
+reference's CPU glue (src/spine_kernels.h spine_rmsnorm + spine_quant; the sum of squares is reduced in a
+different order on the GPU, so a code may differ by one at a rounding boundary and the scale by an ulp),
+and the greedy pick against numpy's first-maximum argmax, including ties, repeated calls (the scratch is
+cleared for the next call) and CUDA-graph replay. Refusals as documented."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle_ffi as of
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(ctx):
+    import torch
+
+    return torch.device("cuda", ctx.L.ork_b200_device(ctx.ctx))
+
+
+@pytest.mark.parametrize("n,gain", [(2048, True), (5000, True), (8192, False), (1, True), (37, False)])
+def test_rmsnorm_q8_matches_oracle(ctx, n, gain):
+    import torch
+
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) * 3.0).astype(np.float32)
+    g = (0.5 + rng.random(n)).astype(np.float32) if gain else None
+    want_q, want_s = of.rms_q8(x, g)
+    dev = _dev(ctx)
+    tx = torch.from_numpy(x).to(dev)
+    tg = torch.from_numpy(g).to(dev) if gain else None
+    q = torch.zeros(n, dtype=torch.int8, device=dev)
+    s = torch.zeros(1, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    assert ctx.L.ork_b200_rmsnorm_q8_async(ctx.ctx, tx.data_ptr(), tg.data_ptr() if gain else None, n, q.data_ptr(),
+                                          s.data_ptr()) == 0
+    assert ctx.L.ork_b200_sync(ctx.ctx) == 0
+    got_q, got_s = q.cpu().numpy(), float(s.item())
+    assert abs(got_s - want_s) <= 2e-6 * abs(want_s)
+    d = np.abs(got_q.astype(np.int32) - want_q.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() <= 0.01, (d.max(), (d > 0).mean())
+
+
+def test_rmsnorm_q8_refusals(ctx):
+    import torch
+
+    dev = _dev(ctx)
+    x = torch.ones(9000, device=dev)
+    q = torch.zeros(9000, dtype=torch.int8, device=dev)
+    L = ctx.L
+    assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, x.data_ptr(), None, 0, q.data_ptr(), None) == -1
+    assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, x.data_ptr(), None, 8193, q.data_ptr(), None) == -1
+    assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, None, None, 16, q.data_ptr(), None) == -1
+    assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, x.data_ptr(), None, 16, None, None) == -1
+    assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, x.data_ptr(), None, 16, q.data_ptr(), None) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    assert np.all(q[:16].cpu().numpy() == 127)
+
+
+def _pick(ctx, C_, bs, n):
+    import torch
+
+    idx = torch.full((1,), -7, dtype=torch.int64, device=C_.device)
+    assert ctx.L.ork_b200_argmax_scaled_async(ctx.ctx, C_.data_ptr(), bs.data_ptr(), n, idx.data_ptr()) == 0
+    assert ctx.L.ork_b200_sync(ctx.ctx) == 0
+    return int(idx.item())
+
+
+def test_argmax_scaled(ctx):
+    import torch
+
+    dev = _dev(ctx)
+    rng = np.random.default_rng(11)
+    for n in (151936, 1, 513, 100000):
+        c = rng.integers(-(1 << 22), 1 << 22, size=n, dtype=np.int32)
+        bs = (rng.random(n) * 0.02 + 1e-4).astype(np.float32)
+        want = int(np.argmax(c.astype(np.float32) * bs))
+        got = _pick(ctx, torch.from_numpy(c).to(dev), torch.from_numpy(bs).to(dev), n)
+        assert got == want, (n, got, want)
+    # ties: the first index wins; all-negative rows; twice in a row (the scratch is cleared)
+    c = np.full(4096, -5, np.int32)
+    c[[100, 7, 3000]] = 9
+    bs = np.ones(4096, np.float32)
+    for _ in range(2):
+        assert _pick(ctx, torch.from_numpy(c).to(dev), torch.from_numpy(bs).to(dev), 4096) == 7
+    c = -np.arange(1, 1001, dtype=np.int32)
+    assert _pick(ctx, torch.from_numpy(c).to(dev), torch.ones(1000, device=dev), 1000) == 0
+
+
+def test_argmax_scaled_graph_replay(ctx):
+    import torch
+
+    dev = _dev(ctx)
+    L = ctx.L
+    n = 65536
+    Cd = torch.zeros(n, dtype=torch.int32, device=dev)
+    bs = torch.ones(n, dtype=torch.float32, device=dev)
+    idx = torch.zeros(1, dtype=torch.int64, device=dev)
+    s = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
+    assert L.ork_b200_argmax_scaled_async(ctx.ctx, Cd.data_ptr(), bs.data_ptr(), n, idx.data_ptr()) == 0
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        assert L.ork_b200_argmax_scaled_async(ctx.ctx, Cd.data_ptr(), bs.data_ptr(), n, idx.data_ptr()) == 0
+    for j in (12345, 77, n - 1):
+        Cd.zero_()
+        Cd[j] = 1
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert int(idx.item()) == j
+    del graph
+
+
+def test_argmax_scaled_refusals(ctx):
+    L = ctx.L
+    buf = (C.c_int32 * 4)()
+    assert L.ork_b200_argmax_scaled_async(ctx.ctx, None, None, 4, None) == -1
+    assert L.ork_b200_argmax_scaled_async(None, C.addressof(buf), C.addressof(buf), 4, C.addressof(buf)) == -1
+    assert L.ork_b200_argmax_scaled_async(ctx.ctx, C.addressof(buf), C.addressof(buf), 0, C.addressof(buf)) == -1
