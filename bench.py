@@ -390,8 +390,9 @@ def run_qwen3(args):
     device-side position), o, residual + RMSNorm + quantization, gate/up in one launch, SwiGLU +
     quantization, down, residual -- then the final norm + quantization (ork_b200_rmsnorm_q8_async), the LM
     head (ork_i8_mm_run_async) and the greedy pick (ork_b200_argmax_scaled_async); a whole token is one
-    CUDA graph. Prefill of the 128-token prompt runs the same model with
-    PyTorch glue around ork_i8_mm_run (per-row activation quantization), captured as one CUDA graph.
+    CUDA graph. Prefill of the 128-token prompt runs the same layer arithmetic over the rows (the
+    library's row glue around ork_i8_mm_run_async; PyTorch for q/k norms, RoPE and attention), captured as
+    one CUDA graph.
     Four distinct layer weight sets (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s;
     prefill tokens/s beside it."""
     import ctypes as C
@@ -454,27 +455,59 @@ def run_qwen3(args):
         assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, xq.data_ptr(), c.data_ptr()) == 0
         return c.float() * as_ * bs
 
+    # prefill buffers: the rows' codes and scales, the matmul results, the dequantized projections
+    pq8 = torch.empty((PRE, max(H, NH * D, FF)), dtype=torch.int8, device=dev)
+    psc = torch.empty(PRE, dtype=torch.float32, device=dev)
+    pC = {n: torch.empty((PRE, N), dtype=torch.int32, device=dev)
+          for n, N in (("q", NH * D), ("k", NKV * D), ("v", NKV * D), ("o", H), ("g", FF), ("u", FF), ("d", H))}
+    pf = {n: torch.empty((PRE, N), dtype=torch.float32, device=dev) for n, N in (("q", NH * D), ("k", NKV * D),
+                                                                                   ("v", NKV * D))}
+    px = [torch.empty((PRE, H), dtype=torch.float32, device=dev) for _ in range(2)]
+
+    def mm(w, T, a, c):
+        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, T, a.data_ptr(), c.data_ptr()) == 0
+
     def prefill_layer(x, li, T):  # x [T, H] fp32, positions 0..T-1; fills the fp32 caches
+        # the decode layer's arithmetic over T rows (weights are int8 codes, activations per-row int8):
+        # the library's row glue around the library matmuls, PyTorch for q/k norms, RoPE and attention
         ws = wsets[li % NDIST]
-        xn = rmsnorm(x, ones_h)
-        q = linear(xn, ws["q"]).view(T, NH, D).transpose(0, 1)
-        k = linear(xn, ws["k"]).view(T, NKV, D).transpose(0, 1)
-        v = linear(xn, ws["v"]).view(T, NKV, D).transpose(0, 1)
+        x1, xo = px[0][:T], px[1][:T]
+        a = pq8[:T]
+        assert L.ork_b200_rows_q8_async(ctx.ctx, x.data_ptr(), ones_h.data_ptr(), T, H, 1, a.data_ptr(),
+                                        psc.data_ptr()) == 0
+        for n in ("q", "k", "v"):
+            mm(ws[n][0], T, a, pC[n])
+            assert L.ork_b200_rows_dequant_async(ctx.ctx, pC[n].data_ptr(), T, pC[n].shape[1], psc.data_ptr(), None,
+                                                 None, pf[n].data_ptr()) == 0
+        q = pf["q"][:T].view(T, NH, D).transpose(0, 1)
+        k = pf["k"][:T].view(T, NKV, D).transpose(0, 1)
+        v = pf["v"][:T].view(T, NKV, D).transpose(0, 1)
         q, k = rmsnorm(q, ones_d), rmsnorm(k, ones_d)
         cos, sin = cos_t[:T], sin_t[:T]
         q, k = rope(q, cos, sin), rope(k, cos, sin)
         kc[li][:, :T] = k
         vc[li][:, :T] = v
         o = F.scaled_dot_product_attention(q, kc[li][:, :T], vc[li][:, :T], is_causal=True, enable_gqa=True)
-        x = x + linear(o.transpose(0, 1).reshape(T, NH * D), ws["o"])
-        xn = rmsnorm(x, ones_h)
-        x = x + linear(F.silu(linear(xn, ws["g"])) * linear(xn, ws["u"]), ws["d"])
-        return x
+        o = o.transpose(0, 1).reshape(T, NH * D)
+        assert L.ork_b200_rows_q8_async(ctx.ctx, o.data_ptr(), None, T, NH * D, 0, a.data_ptr(), psc.data_ptr()) == 0
+        mm(ws["o"][0], T, a, pC["o"])
+        assert L.ork_b200_rows_dequant_async(ctx.ctx, pC["o"].data_ptr(), T, H, psc.data_ptr(), None, x.data_ptr(),
+                                             x1.data_ptr()) == 0  # x1 = x + Co / s
+        assert L.ork_b200_rows_q8_async(ctx.ctx, x1.data_ptr(), ones_h.data_ptr(), T, H, 1, a.data_ptr(),
+                                        psc.data_ptr()) == 0
+        mm(ws["g"][0], T, a, pC["g"])
+        mm(ws["u"][0], T, a, pC["u"])
+        assert L.ork_b200_rows_swiglu_q8_async(ctx.ctx, pC["g"].data_ptr(), pC["u"].data_ptr(), T, FF,
+                                               psc.data_ptr(), a.data_ptr(), psc.data_ptr()) == 0
+        mm(ws["d"][0], T, a, pC["d"])
+        assert L.ork_b200_rows_dequant_async(ctx.ctx, pC["d"].data_ptr(), T, H, psc.data_ptr(), None, x1.data_ptr(),
+                                             xo.data_ptr()) == 0  # x_out = x1 + Cd / s
+        return xo
 
     def prefill(tokens):
         x = emb.index_select(0, tokens).float()
         for li in range(NLY):
-            x = prefill_layer(x, li, x.shape[0])
+            x = prefill_layer(x, li, x.shape[0])  # layer outputs alternate between two buffers
         return linear(rmsnorm(x[-1:], ones_h), lm)
 
     prompt = torch.randint(0, V, (PRE,), device=dev, generator=g)
@@ -562,8 +595,10 @@ def run_qwen3(args):
                        "linears": "decode: the 28 layers as one ork_i8_mm_layers_async call (the library's decode "
                                   "layer, one persistent launch), final norm + quantization, LM head "
                                   "(ork_i8_mm_run_async) and greedy pick as three library launches; "
-                                  "prefill: PyTorch glue around ork_i8_mm_run_async, captured as one CUDA graph "
-                                  "(prefill_eager_ms: the same prompt launched eagerly)",
+                                  "prefill: the same layer arithmetic over 128 rows -- the library's row glue "
+                                  "(norm + quantization, dequantization + residual, SwiGLU + quantization) around "
+                                  "ork_i8_mm_run_async, PyTorch for q/k norms, RoPE and attention -- captured as "
+                                  "one CUDA graph (prefill_eager_ms: the same prompt launched eagerly)",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
                        "parallelism": "replicas" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": tps * weight_bytes / 1e9, "peak": hbm, "unit": "GB/s",

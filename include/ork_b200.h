@@ -96,6 +96,20 @@ int ork_i8_mm_layers_async(ork_npu *ctx, const struct ork_layer_dims *d, int nla
  * ork_b200_argmax_scaled_async: the first j with the largest C[j] * bs[j] over an int32 matmul row C[n]
  *   (bs: the weight's per-channel scales), written as int64 to *idx: the greedy pick over the LM head. */
 int ork_b200_rmsnorm_q8_async(ork_npu *ctx, const float *x, const float *g, int n, int8_t *q8, float *scale);
+/* The same glue over a block of rows (a prefill), one launch each, device pointers, 0 or -1:
+ * ork_b200_rows_q8_async: each row of x [rows][n] (n <= 8192) RMSNorm-ed with gain g when norm != 0 (g NULL:
+ *   none), then quantized with its own scale: q8 [rows][n], scales[rows] (may be NULL).
+ * ork_b200_rows_swiglu_q8_async: h = silu(Cg / s) * (Cu / s) per element of the gate / up results
+ *   [rows][n] (int32; s = scales_in[row], the scales their input rows were quantized with), each row of h
+ *   quantized: q8 [rows][n], scales[rows]. n <= 8192.
+ * ork_b200_rows_dequant_async: out[m][j] = res[m][j] + C[m][j] / scales[m] * bs[j] (bs, res may be NULL;
+ *   out may be res). */
+int ork_b200_rows_q8_async(ork_npu *ctx, const float *x, const float *g, int rows, int n, int norm, int8_t *q8,
+                           float *scales);
+int ork_b200_rows_swiglu_q8_async(ork_npu *ctx, const int32_t *Cg, const int32_t *Cu, int rows, int n,
+                                  const float *scales_in, int8_t *q8, float *scales);
+int ork_b200_rows_dequant_async(ork_npu *ctx, const int32_t *C, int rows, int n, const float *scales, const float *bs,
+                                const float *res, float *out);
 int ork_b200_argmax_scaled_async(ork_npu *ctx, const int32_t *C, const float *bs, int n, long long *idx);
 
 /* Column-sharded runs with the gather fused into the matmul (one process per GPU, NVLink peer memory).

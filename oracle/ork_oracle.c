@@ -457,6 +457,21 @@ ORC_API float orc_rms_q8(const float *x, const float *g, int n, int8_t *q)
     return s;
 }
 
+/* The FFN epilogue of the decode layer over one row: SwiGLU of the dequantized gate / up results
+ * (g = cg / s, u = cu / s, h = g / (1 + expf(-g)) * u; src/spine_kernels.h spine_silu_glu) and the
+ * per-tensor int8 quantization of h (spine_quant); returns the new scale. */
+ORC_API float orc_swiglu_q8(const int32_t *cg, const int32_t *cu, int n, float s, int8_t *q)
+{
+    float *h = malloc((size_t)n * sizeof *h);
+    for (int i = 0; i < n; i++) {
+        const float gi = cg[i] / s, ui = cu[i] / s;
+        h[i] = (gi / (1.0f + expf(-gi))) * ui;
+    }
+    const float sh = orc_q8(h, n, q);
+    free(h);
+    return sh;
+}
+
 static void orc_rope(float *x, int n, int pos, float base)
 {
     const int h = n / 2;

@@ -1,9 +1,14 @@
-// decode_glue.cu -- the decode step's glue around the LM head, as one launch each:
+// decode_glue.cu -- the glue around int8 matmuls outside the decode layer (the LM head of a decode step, and
+// the rows of a prefill), one launch each:
 //   ork_b200_rmsnorm_q8_async   RMSNorm (gain g) of one row and its per-tensor int8 quantization: the
 //                               formulas of glue.cuh, i.e. the decode layer's own (ork-driver's CPU glue,
 //                               src/spine_kernels.h spine_rmsnorm / spine_quant), in the same order:
 //                               r = 1 / sqrt(sum(x^2) / n + 1e-6), y = (x * r) * g, s = 127 / max(1e-6,
 //                               max|y|), q = clamp(rint(y * s), +-127);
+//   ork_b200_rows_q8_async      the same for each row of a block (per-row scales), RMSNorm optional;
+//   ork_b200_rows_swiglu_q8_async  SwiGLU of dequantized gate / up rows, then per-row quantization (the
+//                               decode layer's FFN epilogue: h = silu(g / s) * (u / s));
+//   ork_b200_rows_dequant_async out = res + C / s[row] * bs[col] (the decode layer's x1 = x + Co / sa);
 //   ork_b200_argmax_scaled_async the greedy pick over an int32 matmul row C[n] whose weight has per-channel
 //                               scales bs[n]: the first j with the largest C[j] * bs[j] (the row's positive
 //                               activation factor does not move it), as int64.
@@ -36,42 +41,98 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_q8_kernel(const float *__restrict__ x,
-                                                                  const float *__restrict__ g, int n,
-                                                                  int8_t *__restrict__ q8, float *__restrict__ scale) {
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();  // red may still be read by a previous reduction
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  return warp_sum(lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f);
+}
+__device__ __forceinline__ float block_max(float v, float *red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  return warp_max(lane < (int)(blockDim.x >> 5) ? red[lane] : -3.0e38f);
+}
+
+// The per-tensor quantization of one row held in registers (y[u] = element t + u * blockDim.x): s =
+// 127 / max(1e-6, max|y|) (the block's maximum), q = clamp(rint(y * s), +-127).
+__device__ __forceinline__ void row_q8(const float (&y)[kNormPer], int n, int8_t *q8, float *scale, float *red) {
+  const int t = threadIdx.x;
+  float mx = 1e-6f;
+#pragma unroll
+  for (int u = 0; u < kNormPer; u++)
+    if (t + u * (int)blockDim.x < n) mx = fmaxf(mx, fabsf(y[u]));
+  mx = block_max(mx, red);
+  const float s = glue::qscale(mx);
+#pragma unroll
+  for (int u = 0; u < kNormPer; u++) {
+    const int i = t + u * (int)blockDim.x;
+    if (i < n) q8[i] = glue::q8(y[u], s);
+  }
+  if (t == 0 && scale) *scale = s;
+}
+
+// Row blockIdx.x of x [rows][n]: optionally RMSNorm-ed (gain g, may be NULL), then quantized.
+__global__ void __launch_bounds__(kNormThreads) rows_q8_kernel(const float *__restrict__ x,
+                                                               const float *__restrict__ g, int n, int norm,
+                                                               int8_t *__restrict__ q8, float *__restrict__ scale) {
   __shared__ float red[32];
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  float v[kNormPer], gg[kNormPer];
+  const int t = threadIdx.x;
+  const float *xr = x + (size_t)blockIdx.x * n;
+  float v[kNormPer];
   float ss = 0.0f;
 #pragma unroll
   for (int u = 0; u < kNormPer; u++) {
     const int i = t + u * kNormThreads;
-    v[u] = i < n ? x[i] : 0.0f;
-    gg[u] = i < n ? (g ? g[i] : 1.0f) : 0.0f;
+    v[u] = i < n ? xr[i] : 0.0f;
+    ss += v[u] * v[u];
   }
+  if (norm) {
+    const float r = glue::rms_recip(block_sum(ss, red), n);
 #pragma unroll
-  for (int u = 0; u < kNormPer; u++) ss += v[u] * v[u];
-  ss = warp_sum(ss);
-  if (lane == 0) red[w] = ss;
-  __syncthreads();
-  ss = warp_sum(lane < kNormThreads / 32 ? red[lane] : 0.0f);
-  const float r = glue::rms_recip(ss, n);
-  float mx = 1e-6f;
-#pragma unroll
-  for (int u = 0; u < kNormPer; u++)
-    if (t + u * kNormThreads < n) mx = fmaxf(mx, fabsf(v[u] * r * gg[u]));
-  mx = warp_max(mx);
-  __syncthreads();  // red is reused
-  if (lane == 0) red[w] = mx;
-  __syncthreads();
-  mx = warp_max(lane < kNormThreads / 32 ? red[lane] : -3.0e38f);
-  const float s = glue::qscale(mx);
+    for (int u = 0; u < kNormPer; u++) {
+      const int i = t + u * kNormThreads;
+      v[u] = i < n ? v[u] * r * (g ? g[i] : 1.0f) : 0.0f;
+    }
+  }
+  row_q8(v, n, q8 + (size_t)blockIdx.x * n, scale ? scale + blockIdx.x : nullptr, red);
+}
+
+// Row blockIdx.x of the gate / up matmul results [rows][n] (int32, activation scale s[row]): SwiGLU of
+// the dequantized pair, then quantized -- the decode layer's FFN epilogue.
+__global__ void __launch_bounds__(kNormThreads) rows_swiglu_q8_kernel(const int32_t *__restrict__ Cg,
+                                                                      const int32_t *__restrict__ Cu, int n,
+                                                                      const float *__restrict__ s_in,
+                                                                      int8_t *__restrict__ q8, float *__restrict__ scale) {
+  __shared__ float red[32];
+  const int t = threadIdx.x;
+  const size_t o = (size_t)blockIdx.x * n;
+  const float sa = s_in[blockIdx.x];
+  float h[kNormPer];
 #pragma unroll
   for (int u = 0; u < kNormPer; u++) {
     const int i = t + u * kNormThreads;
-    if (i < n) q8[i] = glue::q8(v[u] * r * gg[u], s);
+    h[u] = i < n ? glue::silu_mul(Cg[o + i] / sa, Cu[o + i] / sa) : 0.0f;
   }
-  if (t == 0 && scale) *scale = s;
+  row_q8(h, n, q8 + o, scale ? scale + blockIdx.x : nullptr, red);
+}
+
+// out[m][j] = res[m][j] + C[m][j] / s[m] * bs[j] (res, bs optional): the dequantization (and residual)
+// after a matmul of quantized rows.
+__global__ void rows_dequant_kernel(const int32_t *__restrict__ C, int rows, int n, const float *__restrict__ s,
+                                    const float *__restrict__ bs, const float *__restrict__ res,
+                                    float *__restrict__ out) {
+  const size_t total = (size_t)rows * n;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(e / n), j = (int)(e % n);
+    float v = C[e] / s[m];
+    if (bs) v = v * bs[j];
+    out[e] = res ? res[e] + v : v;
+  }
 }
 
 // float -> unsigned key with the same order (larger float, larger key)
@@ -119,17 +180,44 @@ using namespace orkb;
 
 extern "C" {
 
-int ork_b200_rmsnorm_q8_async(ork_npu *c, const float *x, const float *g, int n, int8_t *q8, float *scale) {
-  if (!c || !x || !q8 || n < 1 || n > kNormThreads * kNormPer) return -1;
-  DeviceGuard dg(c->device);
-  rmsnorm_q8_kernel<<<1, kNormThreads, 0, c->stream>>>(x, g, n, q8, scale);
+static int glue_launched(ork_npu *c, const char *name) {
   c->launches += 1;
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
-    log_err("ork_b200_rmsnorm_q8_async", e);
+    log_err(name, e);
     return -1;
   }
   return 0;
+}
+
+int ork_b200_rmsnorm_q8_async(ork_npu *c, const float *x, const float *g, int n, int8_t *q8, float *scale) {
+  return ork_b200_rows_q8_async(c, x, g, 1, n, 1, q8, scale);
+}
+
+int ork_b200_rows_q8_async(ork_npu *c, const float *x, const float *g, int rows, int n, int norm, int8_t *q8,
+                           float *scales) {
+  if (!c || !x || !q8 || rows < 1 || n < 1 || n > kNormThreads * kNormPer) return -1;
+  DeviceGuard dg(c->device);
+  rows_q8_kernel<<<rows, kNormThreads, 0, c->stream>>>(x, g, n, norm, q8, scales);
+  return glue_launched(c, "ork_b200_rows_q8_async");
+}
+
+int ork_b200_rows_swiglu_q8_async(ork_npu *c, const int32_t *Cg, const int32_t *Cu, int rows, int n,
+                                  const float *scales_in, int8_t *q8, float *scales) {
+  if (!c || !Cg || !Cu || !scales_in || !q8 || rows < 1 || n < 1 || n > kNormThreads * kNormPer) return -1;
+  DeviceGuard dg(c->device);
+  rows_swiglu_q8_kernel<<<rows, kNormThreads, 0, c->stream>>>(Cg, Cu, n, scales_in, q8, scales);
+  return glue_launched(c, "ork_b200_rows_swiglu_q8_async");
+}
+
+int ork_b200_rows_dequant_async(ork_npu *c, const int32_t *C, int rows, int n, const float *scales, const float *bs,
+                                const float *res, float *out) {
+  if (!c || !C || !scales || !out || rows < 1 || n < 1) return -1;
+  DeviceGuard dg(c->device);
+  const size_t total = (size_t)rows * n;
+  const int blocks = (int)std::min<size_t>(148 * 8, (total + 255) / 256);
+  rows_dequant_kernel<<<blocks, 256, 0, c->stream>>>(C, rows, n, scales, bs, res, out);
+  return glue_launched(c, "ork_b200_rows_dequant_async");
 }
 
 int ork_b200_argmax_scaled_async(ork_npu *c, const int32_t *C, const float *bs, int n, long long *idx) {
@@ -139,13 +227,7 @@ int ork_b200_argmax_scaled_async(ork_npu *c, const int32_t *C, const float *bs, 
   unsigned int *count = reinterpret_cast<unsigned int *>(best + 1);
   const int blocks = (int)std::min<long long>(296, ((long long)n + kPickThreads - 1) / kPickThreads);
   argmax_scaled_kernel<<<blocks, kPickThreads, 0, c->stream>>>(C, bs, n, best, count, idx);
-  c->launches += 1;
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    log_err("ork_b200_argmax_scaled_async", e);
-    return -1;
-  }
-  return 0;
+  return glue_launched(c, "ork_b200_argmax_scaled_async");
 }
 
 }  // extern "C"

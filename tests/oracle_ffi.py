@@ -45,6 +45,8 @@ def restated():
         lib.orc_gen_rnd_f16.argtypes = [C.POINTER(C.c_uint32), C.c_void_p, C.c_size_t]
         lib.orc_nf4_lut.argtypes = [C.c_void_p]
         lib.orc_threads.restype = C.c_int
+        lib.orc_swiglu_q8.restype = C.c_float
+        lib.orc_swiglu_q8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p]
         lib.orc_rms_q8.restype = C.c_float
         lib.orc_rms_q8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
         lib.orc_layer_i8.restype = C.c_int
@@ -212,6 +214,15 @@ def rms_q8(x, g=None):
     q = np.empty(x.size, np.int8)
     s = restated().orc_rms_q8(_p(x), None if g is None else _p(np.ascontiguousarray(g, np.float32)), x.size, _p(q))
     return q, s
+
+
+def swiglu_q8(cg, cu, s):
+    """The decode layer's FFN epilogue over one row (spine_silu_glu + spine_quant): (codes int8 [n], scale)."""
+    cg = np.ascontiguousarray(cg, np.int32)
+    cu = np.ascontiguousarray(cu, np.int32)
+    q = np.empty(cg.size, np.int8)
+    sh = restated().orc_swiglu_q8(_p(cg), _p(cu), cg.size, float(s), _p(q))
+    return q, sh
 
 
 def i8_quant_f32(f32_nk):

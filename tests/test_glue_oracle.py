@@ -32,3 +32,20 @@ def test_rms_q8_against_restatement():
     q1, _ = of.rms_q8(x, None)
     q2, _ = of.rms_q8(x, np.ones(x.size, np.float32))
     assert np.array_equal(q1, q2)
+
+
+def test_swiglu_q8_against_restatement():
+    rng = np.random.default_rng(9)
+    f = np.float32
+    cg = rng.integers(-50000, 50000, size=700).astype(np.int32)
+    cu = rng.integers(-50000, 50000, size=700).astype(np.int32)
+    s = f(9000.0)
+    q, sh = of.swiglu_q8(cg, cu, s)
+    g = (cg.astype(f) / s).astype(f)
+    u = (cu.astype(f) / s).astype(f)
+    h = ((g / (f(1.0) + np.exp(-g).astype(f))).astype(f) * u).astype(f)
+    mx = max(f(1e-6), f(np.abs(h).max()))
+    ws = f(f(127.0) / mx)
+    assert abs(f(sh) - ws) <= 1e-6 * ws  # expf of two libms may differ in the last place
+    wq = np.clip(np.rint((h * ws).astype(f)), -127, 127).astype(np.int8)
+    assert np.abs(q.astype(int) - wq.astype(int)).max() <= 1

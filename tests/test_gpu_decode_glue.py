@@ -1,5 +1,6 @@
-"""The decode glue around the LM head on the B200 (ork_b200_rmsnorm_q8_async, ork_b200_argmax_scaled_async,
-include/ork_b200.h): RMSNorm + per-tensor int8 quantization against the oracle's restatement of the
+"""The glue around int8 matmuls on the B200 (include/ork_b200.h: ork_b200_rmsnorm_q8_async,
+ork_b200_argmax_scaled_async, and the row forms ork_b200_rows_q8_async / _rows_swiglu_q8_async /
+_rows_dequant_async): RMSNorm + per-tensor int8 quantization and SwiGLU + quantization against the oracle's restatement of the
 reference's CPU glue (src/spine_kernels.h spine_rmsnorm + spine_quant; the sum of squares is reduced in a
 different order on the GPU, so a code may differ by one at a rounding boundary and the scale by an ulp),
 and the greedy pick against numpy's first-maximum argmax, including ties, repeated calls (the scratch is
@@ -120,3 +121,73 @@ def test_argmax_scaled_refusals(ctx):
     assert L.ork_b200_argmax_scaled_async(ctx.ctx, None, None, 4, None) == -1
     assert L.ork_b200_argmax_scaled_async(None, C.addressof(buf), C.addressof(buf), 4, C.addressof(buf)) == -1
     assert L.ork_b200_argmax_scaled_async(ctx.ctx, C.addressof(buf), C.addressof(buf), 0, C.addressof(buf)) == -1
+
+
+def test_rows_q8_norm_and_plain(ctx):
+    import torch
+
+    dev = _dev(ctx)
+    rng = np.random.default_rng(21)
+    rows, n = 128, 2048
+    x = (rng.standard_normal((rows, n)) * 2.0).astype(np.float32)
+    g = (0.5 + rng.random(n)).astype(np.float32)
+    tx, tg = torch.from_numpy(x).to(dev), torch.from_numpy(g).to(dev)
+    q = torch.zeros((rows, n), dtype=torch.int8, device=dev)
+    s = torch.zeros(rows, dtype=torch.float32, device=dev)
+    L = ctx.L
+    # RMSNorm + quantization against the oracle, row by row
+    assert L.ork_b200_rows_q8_async(ctx.ctx, tx.data_ptr(), tg.data_ptr(), rows, n, 1, q.data_ptr(), s.data_ptr()) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    gq, gs = q.cpu().numpy(), s.cpu().numpy()
+    for m in range(0, rows, 17):
+        wq, ws = of.rms_q8(x[m], g)
+        assert abs(gs[m] - ws) <= 2e-6 * ws
+        assert np.abs(gq[m].astype(int) - wq.astype(int)).max() <= 1
+    # plain quantization: no reduction order involved, so exact
+    assert L.ork_b200_rows_q8_async(ctx.ctx, tx.data_ptr(), None, rows, n, 0, q.data_ptr(), s.data_ptr()) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    f = np.float32
+    ws = (f(127.0) / np.maximum(f(1e-6), np.abs(x).max(axis=1))).astype(f)
+    wq = np.clip(np.rint((x * ws[:, None]).astype(f)), -127, 127).astype(np.int8)
+    assert np.array_equal(s.cpu().numpy(), ws) and np.array_equal(q.cpu().numpy(), wq)
+
+
+def test_rows_swiglu_q8_and_dequant(ctx):
+    import torch
+
+    dev = _dev(ctx)
+    rng = np.random.default_rng(22)
+    rows, n = 64, 6144
+    cg = rng.integers(-60000, 60000, size=(rows, n)).astype(np.int32)
+    cu = rng.integers(-60000, 60000, size=(rows, n)).astype(np.int32)
+    sin = (5000.0 + 5000.0 * rng.random(rows)).astype(np.float32)
+    tg, tu, ts = (torch.from_numpy(a).to(dev) for a in (cg, cu, sin))
+    q = torch.zeros((rows, n), dtype=torch.int8, device=dev)
+    s = torch.zeros(rows, dtype=torch.float32, device=dev)
+    L = ctx.L
+    assert L.ork_b200_rows_swiglu_q8_async(ctx.ctx, tg.data_ptr(), tu.data_ptr(), rows, n, ts.data_ptr(), q.data_ptr(),
+                                          s.data_ptr()) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    gq, gs = q.cpu().numpy(), s.cpu().numpy()
+    for m in range(0, rows, 9):
+        wq, ws = of.swiglu_q8(cg[m], cu[m], sin[m])
+        assert abs(gs[m] - ws) <= 1e-6 * ws
+        assert np.abs(gq[m].astype(int) - wq.astype(int)).max() <= 1
+    # dequantization with per-channel scales and a residual: one IEEE op at a time, so exact
+    f = np.float32
+    bs = (rng.random(n) * 0.01).astype(f)
+    res = rng.standard_normal((rows, n)).astype(f)
+    tb, tr = torch.from_numpy(bs).to(dev), torch.from_numpy(res).to(dev)
+    out = torch.zeros((rows, n), dtype=torch.float32, device=dev)
+    assert L.ork_b200_rows_dequant_async(ctx.ctx, tg.data_ptr(), rows, n, ts.data_ptr(), tb.data_ptr(), tr.data_ptr(),
+                                        out.data_ptr()) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    want = (res + ((cg.astype(f) / sin[:, None]).astype(f) * bs).astype(f)).astype(f)
+    assert np.array_equal(out.cpu().numpy(), want)
+    plain = torch.zeros((rows, n), dtype=torch.float32, device=dev)
+    assert L.ork_b200_rows_dequant_async(ctx.ctx, tu.data_ptr(), rows, n, ts.data_ptr(), None, None,
+                                        plain.data_ptr()) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+    assert np.array_equal(plain.cpu().numpy(), (cu.astype(f) / sin[:, None]).astype(f))
+    assert L.ork_b200_rows_q8_async(ctx.ctx, tr.data_ptr(), None, rows, 8193, 0, q.data_ptr(), None) == -1
+    assert L.ork_b200_rows_dequant_async(ctx.ctx, tg.data_ptr(), 0, n, ts.data_ptr(), None, None, out.data_ptr()) == -1
