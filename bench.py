@@ -106,6 +106,18 @@ class Clocks:
                 "samples": len(sm), "source": "nvml"}
 
 
+def cpu_model():
+    """The host CPU's model name (the CPU baseline runs on it)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_reference_sweep(min_seconds, max_reps=3):
     """The reference's CPU int8 GEMM over the sweep: oracle/_ref (its own code) if built, else the
     restatement. Returns (GB/s, cores, kind, sample description)."""
@@ -153,7 +165,7 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "parallelism": "host CPU, OpenMP over M"},
-            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind, "cpu": cpu_model(),
                              "sample": f"each step = one full sweep of the 12 calls on the host ({sample})"},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -391,8 +403,7 @@ def run_qwen3(args):
     quantization, down, residual -- then the final norm + quantization (ork_b200_rmsnorm_q8_async), the LM
     head (ork_i8_mm_run_async) and the greedy pick (ork_b200_argmax_scaled_async); a whole token is one
     CUDA graph. Prefill of the 128-token prompt runs the same layer arithmetic over the rows (the
-    library's row glue around ork_i8_mm_run_async; PyTorch for q/k norms, RoPE and attention), captured as
-    one CUDA graph.
+    library's row glue around ork_i8_mm_run_async; PyTorch's attention), captured as one CUDA graph.
     Four distinct layer weight sets (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s;
     prefill tokens/s beside it."""
     import ctypes as C
@@ -432,28 +443,16 @@ def run_qwen3(args):
     emb = (torch.randn((V, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
     ones_h = torch.ones(H, device=dev)
     ones_d = torch.ones(D, device=dev)
-    inv = 1.0 / (Q3["theta"] ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
-    ang = torch.outer(torch.arange(MAXT, device=dev, dtype=torch.float32), inv)
-    cos_t, sin_t = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
     kc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.float32) for _ in range(NLY)]
     vc = [torch.zeros((NKV, MAXT, D), device=dev, dtype=torch.float32) for _ in range(NLY)]
+    tok = torch.zeros(1, dtype=torch.long, device=dev)
+    q8h = torch.empty(H, dtype=torch.int8, device=dev)
+    c_lm = torch.empty(V, dtype=torch.int32, device=dev)
 
-    def rmsnorm(x, w):
-        x = x.float()
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + Q3["eps"]) * w
-
-    def rope(x, cos, sin):  # x [..., T, D]
-        x1, x2 = x[..., : D // 2], x[..., D // 2:]
-        return x * cos + torch.cat([-x2, x1], -1) * sin
-
-    def linear(x, wb):  # x [M, K] float -> [M, N] float through the int8 library matmul
-        w, bs = wb
-        M = x.shape[0]
-        as_ = x.abs().amax(dim=1, keepdim=True).clamp_min(1e-9) / 127.0
-        xq = torch.clamp(torch.round(x / as_), -127, 127).to(torch.int8)
-        c = torch.empty((M, w.N), device=dev, dtype=torch.int32)
-        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, xq.data_ptr(), c.data_ptr()) == 0
-        return c.float() * as_ * bs
+    def head(x_row):  # final norm + quantization, the LM head and the greedy pick into tok
+        assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, x_row.data_ptr(), ones_h.data_ptr(), H, q8h.data_ptr(), None) == 0
+        assert L.ork_i8_mm_run_async(ctx.ctx, lm[0].h, 1, q8h.data_ptr(), c_lm.data_ptr()) == 0
+        assert L.ork_b200_argmax_scaled_async(ctx.ctx, c_lm.data_ptr(), lm[1].data_ptr(), V, tok.data_ptr()) == 0
 
     # prefill buffers: the rows' codes and scales, the matmul results, the dequantized projections
     pq8 = torch.empty((PRE, max(H, NH * D, FF)), dtype=torch.int8, device=dev)
@@ -463,13 +462,14 @@ def run_qwen3(args):
     pf = {n: torch.empty((PRE, N), dtype=torch.float32, device=dev) for n, N in (("q", NH * D), ("k", NKV * D),
                                                                                    ("v", NKV * D))}
     px = [torch.empty((PRE, H), dtype=torch.float32, device=dev) for _ in range(2)]
+    pqh = torch.empty((NH, PRE, D), dtype=torch.float32, device=dev)
 
     def mm(w, T, a, c):
         assert L.ork_i8_mm_run_async(ctx.ctx, w.h, T, a.data_ptr(), c.data_ptr()) == 0
 
     def prefill_layer(x, li, T):  # x [T, H] fp32, positions 0..T-1; fills the fp32 caches
         # the decode layer's arithmetic over T rows (weights are int8 codes, activations per-row int8):
-        # the library's row glue around the library matmuls, PyTorch for q/k norms, RoPE and attention
+        # the library's row glue around the library matmuls, PyTorch's attention over the caches
         ws = wsets[li % NDIST]
         x1, xo = px[0][:T], px[1][:T]
         a = pq8[:T]
@@ -479,14 +479,11 @@ def run_qwen3(args):
             mm(ws[n][0], T, a, pC[n])
             assert L.ork_b200_rows_dequant_async(ctx.ctx, pC[n].data_ptr(), T, pC[n].shape[1], psc.data_ptr(), None,
                                                  None, pf[n].data_ptr()) == 0
-        q = pf["q"][:T].view(T, NH, D).transpose(0, 1)
-        k = pf["k"][:T].view(T, NKV, D).transpose(0, 1)
-        v = pf["v"][:T].view(T, NKV, D).transpose(0, 1)
-        q, k = rmsnorm(q, ones_d), rmsnorm(k, ones_d)
-        cos, sin = cos_t[:T], sin_t[:T]
-        q, k = rope(q, cos, sin), rope(k, cos, sin)
-        kc[li][:, :T] = k
-        vc[li][:, :T] = v
+        # q / k norms + RoPE, k and v into the caches at rows 0..T-1, q head-major: one library launch
+        assert L.ork_b200_rows_qk_rope_async(ctx.ctx, pf["q"].data_ptr(), pf["k"].data_ptr(), pf["v"].data_ptr(), T,
+                                             NH, NKV, D, ones_d.data_ptr(), ones_d.data_ptr(), 0, Q3["theta"],
+                                             pqh.data_ptr(), kc[li].data_ptr(), vc[li].data_ptr(), MAXT) == 0
+        q = pqh.view(-1)[:NH * T * D].view(NH, T, D)
         o = F.scaled_dot_product_attention(q, kc[li][:, :T], vc[li][:, :T], is_causal=True, enable_gqa=True)
         o = o.transpose(0, 1).reshape(T, NH * D)
         assert L.ork_b200_rows_q8_async(ctx.ctx, o.data_ptr(), None, T, NH * D, 0, a.data_ptr(), psc.data_ptr()) == 0
@@ -504,14 +501,13 @@ def run_qwen3(args):
                                              xo.data_ptr()) == 0  # x_out = x1 + Cd / s
         return xo
 
-    def prefill(tokens):
+    def prefill(tokens):  # the prompt's rows through the layers, then the first generated token into tok
         x = emb.index_select(0, tokens).float()
         for li in range(NLY):
             x = prefill_layer(x, li, x.shape[0])  # layer outputs alternate between two buffers
-        return linear(rmsnorm(x[-1:], ones_h), lm)
+        head(x[-1])
 
     prompt = torch.randint(0, V, (PRE,), device=dev, generator=g)
-    tok = torch.zeros(1, dtype=torch.long, device=dev)
     pos = torch.zeros(1, dtype=torch.int32, device=dev)
     xa = torch.zeros(H, dtype=torch.float32, device=dev)
     xb = torch.zeros(H, dtype=torch.float32, device=dev)
@@ -523,17 +519,11 @@ def run_qwen3(args):
                                     ones_h.data_ptr(), ones_d.data_ptr(), kc[li].data_ptr(), vc[li].data_ptr())
                              for li in range(NLY)])
 
-    q8h = torch.empty(H, dtype=torch.int8, device=dev)
-    c_lm = torch.empty(V, dtype=torch.int32, device=dev)
-
     def decode_step():
         xa.copy_(emb.index_select(0, tok).float().view(-1))
         assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NLY, stack, xa.data_ptr(), xb.data_ptr(),
                                         C.byref(kv)) == 0
-        # the final norm + quantization, the LM head and the greedy pick: three library launches
-        assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, xb.data_ptr(), ones_h.data_ptr(), H, q8h.data_ptr(), None) == 0
-        assert L.ork_i8_mm_run_async(ctx.ctx, lm[0].h, 1, q8h.data_ptr(), c_lm.data_ptr()) == 0
-        assert L.ork_b200_argmax_scaled_async(ctx.ctx, c_lm.data_ptr(), lm[1].data_ptr(), V, tok.data_ptr()) == 0
+        head(xb)  # the final norm + quantization, the LM head and the greedy pick: three library launches
         pos.add_(1)
 
     with torch.cuda.stream(stream):
@@ -550,18 +540,16 @@ def run_qwen3(args):
         pgraph = torch.cuda.CUDAGraph()
         l0 = ctx.launches()
         with torch.cuda.graph(pgraph, stream=stream):
-            logits_g = prefill(prompt)
+            prefill(prompt)
         prefill_launches = ctx.launches() - l0
         pgraph.replay()
         torch.cuda.synchronize()
         e0.record(stream)
-        pgraph.replay()
+        pgraph.replay()  # leaves the first generated token in tok
         e1.record(stream)
         torch.cuda.synchronize()
         prefill_ms = e0.elapsed_time(e1)
-        logits = logits_g.clone()
         del pgraph
-        tok.copy_(logits.argmax(-1))
         pos.fill_(PRE)
         decode_step()  # eager warm-up of the decode shapes (sizes the layer workspace before capture)
         pos.fill_(PRE)
@@ -596,9 +584,10 @@ def run_qwen3(args):
                                   "layer, one persistent launch), final norm + quantization, LM head "
                                   "(ork_i8_mm_run_async) and greedy pick as three library launches; "
                                   "prefill: the same layer arithmetic over 128 rows -- the library's row glue "
-                                  "(norm + quantization, dequantization + residual, SwiGLU + quantization) around "
-                                  "ork_i8_mm_run_async, PyTorch for q/k norms, RoPE and attention -- captured as "
-                                  "one CUDA graph (prefill_eager_ms: the same prompt launched eagerly)",
+                                  "(norm + quantization, dequantization + residual, q/k norms + RoPE + cache "
+                                  "writes, SwiGLU + quantization) around ork_i8_mm_run_async, PyTorch's "
+                                  "scaled_dot_product_attention -- captured as one CUDA graph (prefill_eager_ms: "
+                                  "the same prompt launched eagerly)",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
                        "parallelism": "replicas" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": tps * weight_bytes / 1e9, "peak": hbm, "unit": "GB/s",
@@ -1270,7 +1259,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, cores, kind, sample, _ = cpu_reference_sweep(10.0)
-        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": kind, "cpu": cpu_model(), "sample": sample}
 
     dec = [k for k in breakdown if k.endswith("M1") or k.endswith("M8")]
     pre = [k for k in breakdown if k not in dec]

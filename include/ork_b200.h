@@ -110,6 +110,14 @@ int ork_b200_rows_swiglu_q8_async(ork_npu *ctx, const int32_t *Cg, const int32_t
                                   const float *scales_in, int8_t *q8, float *scales);
 int ork_b200_rows_dequant_async(ork_npu *ctx, const int32_t *C, int rows, int n, const float *scales, const float *bs,
                                 const float *res, float *out);
+/* ork_b200_rows_qk_rope_async: rows t = 0..T-1 of the q [T][H*dk], k and v [T][Hkv*dk] projections at positions
+ *   pos0 + t: each q and k head RMSNorm-ed (gains q_norm / k_norm [dk], may be NULL; eps 1e-6) and rotated
+ *   (RoPE NeoX at angle pos * base^(-2i/dk), ork-driver src/spine_kernels.h spine_rope_neox); q_out
+ *   [H][T][dk]; k and v written into the caches Kc / Vc [Hkv][hstride][dk] at row pos0 + t
+ *   (pos0 + T <= hstride). dk 64, 128 or 256. */
+int ork_b200_rows_qk_rope_async(ork_npu *ctx, const float *q, const float *k, const float *v, int T, int H, int Hkv,
+                                int dk, const float *q_norm, const float *k_norm, int pos0, float base, float *q_out,
+                                float *Kc, float *Vc, int hstride);
 int ork_b200_argmax_scaled_async(ork_npu *ctx, const int32_t *C, const float *bs, int n, long long *idx);
 
 /* Column-sharded runs with the gather fused into the matmul (one process per GPU, NVLink peer memory).

@@ -9,6 +9,8 @@
 //   ork_b200_rows_swiglu_q8_async  SwiGLU of dequantized gate / up rows, then per-row quantization (the
 //                               decode layer's FFN epilogue: h = silu(g / s) * (u / s));
 //   ork_b200_rows_dequant_async out = res + C / s[row] * bs[col] (the decode layer's x1 = x + Co / sa);
+//   ork_b200_rows_qk_rope_async per row and head: q / k RMSNorm + RoPE NeoX (the decode layer's head_vec),
+//                               q out head-major, k and v into the caches at the row's position;
 //   ork_b200_argmax_scaled_async the greedy pick over an int32 matmul row C[n] whose weight has per-channel
 //                               scales bs[n]: the first j with the largest C[j] * bs[j] (the row's positive
 //                               activation factor does not move it), as int64.
@@ -121,6 +123,59 @@ __global__ void __launch_bounds__(kNormThreads) rows_swiglu_q8_kernel(const int3
   row_q8(h, n, q8 + o, scale ? scale + blockIdx.x : nullptr, red);
 }
 
+// Row t (position pos0 + t) of the q / k / v projections [T][heads * dk]: each q and k head RMSNorm-ed
+// (gains qg / kg, may be NULL) and rotated (RoPE NeoX, pair (i, i + dk/2) at angle pos * base^(-2i/dk)),
+// the decode layer's head_vec arithmetic; q written head-major [H][T][dk], k and v into the caches at
+// [Hkv][hstride][dk] row pos0 + t. One warp per (row, head); lane l holds elements l + 32 u.
+template <int PER>
+__global__ void __launch_bounds__(128) rows_qk_rope_kernel(const float *__restrict__ q, const float *__restrict__ k,
+                                                           const float *__restrict__ v, int T, int H, int Hkv,
+                                                           const float *__restrict__ qg, const float *__restrict__ kg,
+                                                           int pos0, float base, float *__restrict__ qo,
+                                                           float *__restrict__ Kc, float *__restrict__ Vc,
+                                                           int hstride) {
+  constexpr int dk = 32 * PER;
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // (t, head) of H + Hkv heads
+  if (item >= T * (H + Hkv)) return;  // whole warps
+  const int t = item / (H + Hkv), hh = item % (H + Hkv);
+  const bool isq = hh < H;
+  const int h = isq ? hh : hh - H;
+  const float *src = isq ? q + ((size_t)t * H + h) * dk : k + ((size_t)t * Hkv + h) * dk;
+  const float *g = isq ? qg : kg;
+  float x[PER];
+#pragma unroll
+  for (int u = 0; u < PER; u++) x[u] = src[lane + 32 * u];
+  if (g) {
+    float sq = 0.0f;
+#pragma unroll
+    for (int u = 0; u < PER; u++) sq += x[u] * x[u];
+    const float rr = glue::rms_recip(warp_sum(sq), dk);
+#pragma unroll
+    for (int u = 0; u < PER; u++) x[u] = x[u] * rr * g[lane + 32 * u];
+  }
+  const int pos = pos0 + t;
+#pragma unroll
+  for (int u = 0; u < PER / 2; u++) {
+    const float th = glue::rope_angle(pos, base, lane + 32 * u, dk);
+    const float c = cosf(th), s = sinf(th), x0 = x[u], x1 = x[u + PER / 2];
+    x[u] = x0 * c - x1 * s;
+    x[u + PER / 2] = x0 * s + x1 * c;
+  }
+  if (isq) {
+#pragma unroll
+    for (int u = 0; u < PER; u++) qo[((size_t)h * T + t) * dk + lane + 32 * u] = x[u];
+  } else {
+    const size_t o = ((size_t)h * hstride + pos) * dk;
+    const float *vs = v + ((size_t)t * Hkv + h) * dk;
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+      Kc[o + lane + 32 * u] = x[u];
+      Vc[o + lane + 32 * u] = vs[lane + 32 * u];
+    }
+  }
+}
+
 // out[m][j] = res[m][j] + C[m][j] / s[m] * bs[j] (res, bs optional): the dequantization (and residual)
 // after a matmul of quantized rows.
 __global__ void rows_dequant_kernel(const int32_t *__restrict__ C, int rows, int n, const float *__restrict__ s,
@@ -218,6 +273,28 @@ int ork_b200_rows_dequant_async(ork_npu *c, const int32_t *C, int rows, int n, c
   const int blocks = (int)std::min<size_t>(148 * 8, (total + 255) / 256);
   rows_dequant_kernel<<<blocks, 256, 0, c->stream>>>(C, rows, n, scales, bs, res, out);
   return glue_launched(c, "ork_b200_rows_dequant_async");
+}
+
+int ork_b200_rows_qk_rope_async(ork_npu *c, const float *q, const float *k, const float *v, int T, int H, int Hkv,
+                                int dk, const float *q_norm, const float *k_norm, int pos0, float base, float *q_out,
+                                float *Kc, float *Vc, int hstride) {
+  if (!c || !q || !k || !v || !q_out || !Kc || !Vc || T < 1 || H < 1 || Hkv < 1 || pos0 < 0 ||
+      pos0 + T > hstride)
+    return -1;
+  DeviceGuard dg(c->device);
+  const int blocks = (T * (H + Hkv) + 3) / 4;
+  if (dk == 64)
+    rows_qk_rope_kernel<2><<<blocks, 128, 0, c->stream>>>(q, k, v, T, H, Hkv, q_norm, k_norm, pos0, base, q_out, Kc,
+                                                          Vc, hstride);
+  else if (dk == 128)
+    rows_qk_rope_kernel<4><<<blocks, 128, 0, c->stream>>>(q, k, v, T, H, Hkv, q_norm, k_norm, pos0, base, q_out, Kc,
+                                                          Vc, hstride);
+  else if (dk == 256)
+    rows_qk_rope_kernel<8><<<blocks, 128, 0, c->stream>>>(q, k, v, T, H, Hkv, q_norm, k_norm, pos0, base, q_out, Kc,
+                                                          Vc, hstride);
+  else
+    return -1;
+  return glue_launched(c, "ork_b200_rows_qk_rope_async");
 }
 
 int ork_b200_argmax_scaled_async(ork_npu *c, const int32_t *C, const float *bs, int n, long long *idx) {

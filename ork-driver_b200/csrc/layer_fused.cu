@@ -518,8 +518,8 @@ __device__ __forceinline__ void load_keys(const float *Kh, const float *Vh, int 
 // j0 + w + 16 u with an online softmax (running max, rescaled sums); the CTA then combines its warps'
 // maxima, sums and V rows into the item's partials. y: scratch, [kCW][dk] rows then 2 * kCW floats.
 // The first step's cached rows and the norm gains do not depend on this launch's data, so their loads
-// are issued before the polls of q (the token's own key, not yet in the cache, replaces its row when it
-// is used).
+// are issued before q is checked (the token's own key, not yet in the cache, replaces its row when it is
+// used).
 template <int PER>
 __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp, int kpc, int nkv, int nk, int pos,
                        float sx, float *y, uint32_t ep) {
@@ -530,6 +530,10 @@ __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp,
   const int j0 = sp * kpc, j1 = min(nk, j0 + kpc);
   const bool own = ext && j0 <= nkv && nkv < j1;
   const float *Kh = lw.Kc + (size_t)hk * a.hstride * dk, *Vh = lw.Vc + (size_t)hk * a.hstride * dk;
+  // the first poll of q goes out ahead of the key rows' loads (a poll queued behind them would return
+  // later); q is checked after they are issued
+  uint64_t wq[PER];
+  ll_issue<PER>(a.q + h * dk, lane, 32, dk, ep, wq);
   float kr[2][PER], vr[2][PER];
   int jb = j0 + wp;
   load_keys<PER>(Kh, Vh, jb, j1, lane, kr, vr);
@@ -540,10 +544,10 @@ __device__ void attend(const FusedArgs &a, const FusedLayerW &lw, int h, int sp,
     gq[i] = hq ? lw.q_norm[lane + 32 * i] : 1.0f;
     gk[i] = hk_ && own ? lw.k_norm[lane + 32 * i] : 1.0f;
   }
-  // the raw q (and the token's own k, v): one round of polls
+  // the raw q (and the token's own k, v): q first (what is awaited); the token's k and v, written in the
+  // same phase, in one round after
   uint32_t cq[PER], ck[PER], cv[PER];
-  // q first (what is awaited); the token's k and v, written in the same phase, in one round after
-  ll_get_n<PER>(a.q + h * dk, lane, 32, dk, ep, cq);
+  ll_finish<PER>(a.q + h * dk, lane, 32, ep, wq, cq);
   {
     uint64_t wk[PER], wv[PER];
     ll_issue<PER>(a.k + hk * dk, lane, 32, own ? dk : 0, ep, wk);

@@ -96,6 +96,7 @@ SIGNATURES = [
     ("ork_b200_rows_q8_async", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     ("ork_b200_rows_swiglu_q8_async", _i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
     ("ork_b200_rows_dequant_async", _i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
+    ("ork_b200_rows_qk_rope_async", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _f, _vp, _vp, _vp, _i]),
     ("ork_b200_pack_check", _i, [_vp, _sz, _i, _i, _i]),
     ("ork_b200_pack_capid", C.c_uint32, []),
     ("ork_b200_sync", _i, [_vp]),

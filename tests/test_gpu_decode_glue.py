@@ -1,6 +1,6 @@
 """The glue around int8 matmuls on the B200 (include/ork_b200.h: ork_b200_rmsnorm_q8_async,
 ork_b200_argmax_scaled_async, and the row forms ork_b200_rows_q8_async / _rows_swiglu_q8_async /
-_rows_dequant_async): RMSNorm + per-tensor int8 quantization and SwiGLU + quantization against the oracle's restatement of the
+_rows_dequant_async / _rows_qk_rope_async): RMSNorm + per-tensor int8 quantization and SwiGLU + quantization against the oracle's restatement of the
 reference's CPU glue (src/spine_kernels.h spine_rmsnorm + spine_quant; the sum of squares is reduced in a
 different order on the GPU, so a code may differ by one at a rounding boundary and the scale by an ulp),
 and the greedy pick against numpy's first-maximum argmax, including ties, repeated calls (the scratch is
@@ -191,3 +191,56 @@ def test_rows_swiglu_q8_and_dequant(ctx):
     assert np.array_equal(plain.cpu().numpy(), (cu.astype(f) / sin[:, None]).astype(f))
     assert L.ork_b200_rows_q8_async(ctx.ctx, tr.data_ptr(), None, rows, 8193, 0, q.data_ptr(), None) == -1
     assert L.ork_b200_rows_dequant_async(ctx.ctx, tg.data_ptr(), 0, n, ts.data_ptr(), None, None, out.data_ptr()) == -1
+
+
+@pytest.mark.parametrize("dk,gains", [(128, True), (64, False), (256, True)])
+def test_rows_qk_rope(ctx, dk, gains):
+    """q / k head RMSNorm + RoPE NeoX over rows at positions pos0 + t (the decode layer's head_vec), q
+    written head-major, k and v into the caches at those rows, other cache rows untouched; against a
+    float64 restatement (float32 angles of a few hundred radians are off by ~2e-5 rad: tolerance 2e-4 of
+    the head's magnitude)."""
+    import torch
+
+    dev = _dev(ctx)
+    rng = np.random.default_rng(dk)
+    T, H, Hkv, pos0, hstride, base = 37, 4, 2, 300, 400, 1e6
+    q = rng.standard_normal((T, H * dk)).astype(np.float32)
+    k = rng.standard_normal((T, Hkv * dk)).astype(np.float32)
+    v = rng.standard_normal((T, Hkv * dk)).astype(np.float32)
+    qg = (0.5 + rng.random(dk)).astype(np.float32) if gains else None
+    kg = (0.5 + rng.random(dk)).astype(np.float32) if gains else None
+    tq, tk, tv = (torch.from_numpy(a).to(dev) for a in (q, k, v))
+    tqg = torch.from_numpy(qg).to(dev) if gains else None
+    tkg = torch.from_numpy(kg).to(dev) if gains else None
+    qo = torch.zeros((H, T, dk), device=dev)
+    Kc = torch.full((Hkv, hstride, dk), 7.0, device=dev)
+    Vc = torch.full((Hkv, hstride, dk), 7.0, device=dev)
+    L = ctx.L
+    assert L.ork_b200_rows_qk_rope_async(ctx.ctx, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), T, H, Hkv, dk,
+                                         tqg.data_ptr() if gains else None, tkg.data_ptr() if gains else None, pos0,
+                                         base, qo.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), hstride) == 0
+    assert L.ork_b200_sync(ctx.ctx) == 0
+
+    def head(x, g, pos):
+        x = x.astype(np.float64)
+        if g is not None:
+            x = x / np.sqrt((x * x).sum() / dk + 1e-6) * g
+        th = pos * np.power(base, -2.0 * np.arange(dk // 2) / dk)
+        a, b = x[: dk // 2].copy(), x[dk // 2:].copy()
+        return np.concatenate([a * np.cos(th) - b * np.sin(th), a * np.sin(th) + b * np.cos(th)])
+
+    gq, gK, gV = qo.cpu().numpy(), Kc.cpu().numpy(), Vc.cpu().numpy()
+    for t in range(0, T, 6):
+        for h in range(H):
+            w = head(q[t, h * dk:(h + 1) * dk], qg, pos0 + t)
+            assert np.abs(gq[h, t] - w).max() <= 2e-4 * np.abs(w).max(), (t, h)
+        for h in range(Hkv):
+            w = head(k[t, h * dk:(h + 1) * dk], kg, pos0 + t)
+            assert np.abs(gK[h, pos0 + t] - w).max() <= 2e-4 * np.abs(w).max(), (t, h)
+            assert np.array_equal(gV[h, pos0 + t], v[t, h * dk:(h + 1) * dk])
+    assert np.all(gK[:, :pos0] == 7.0) and np.all(gK[:, pos0 + T:] == 7.0)
+    assert L.ork_b200_rows_qk_rope_async(ctx.ctx, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), T, H, Hkv, 96, None,
+                                         None, 0, base, qo.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), hstride) == -1
+    assert L.ork_b200_rows_qk_rope_async(ctx.ctx, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), T, H, Hkv, dk, None,
+                                         None, hstride - T + 1, base, qo.data_ptr(), Kc.data_ptr(), Vc.data_ptr(),
+                                         hstride) == -1
