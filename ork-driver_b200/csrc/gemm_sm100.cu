@@ -238,6 +238,34 @@ __device__ __forceinline__ uint4 add4(uint4 a, uint4 b) {
   }
 }
 
+// Expands one stage's nibble tile (WROWS rows x 64 bytes) into the 128-byte-swizzled int8 MMA tile
+// (row r, 16-byte k chunk c at chunk position c ^ (r & 7)): WROWS * 8 chunks over the 128 converter
+// threads. Every nibble word of the thread's chunks is loaded before the first expansion, so the
+// chunks' integer chains overlap: the four converter warps of a CTA have little else to hide their
+// latency with, and with a 2-chunk unroll the expansion, not the weight stream, set the pace of
+// decode-sized nibble runs (ncu: 41 % issue-active, stalls on fixed-latency dependencies).
+template <int FMT, int WROWS>
+__device__ __forceinline__ void expand_stage(const uint8_t *src, uint8_t *dst, int ct, const Nf4Tables &tb) {
+  static_assert((WROWS * 8) % 128 == 0, "whole chunks per converter thread");
+  constexpr int ITEMS = WROWS * 8 / 128;
+  const int r0 = ct >> 3, c = ct & 7;  // chunk q of this thread: row r0 + 16 q, same k chunk c
+  const uint32_t s_src = smem_u32(src) + (uint32_t)(r0 * 64 + c * 8);
+  const uint32_t s_dst = smem_u32(dst) + (uint32_t)(r0 * 128 + ((c ^ (r0 & 7)) << 4));
+  uint32_t nb[ITEMS][2];
+#pragma unroll
+  for (int q = 0; q < ITEMS; q++)
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                 : "=r"(nb[q][0]), "=r"(nb[q][1])
+                 : "r"(s_src + (uint32_t)(q * 16 * 64)));
+#pragma unroll
+  for (int q = 0; q < ITEMS; q++) {
+    const uint2 lo = expand8<FMT>(nb[q][0], tb), hi = expand8<FMT>(nb[q][1], tb);
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_dst + (uint32_t)(q * 16 * 128)), "r"(lo.x),
+                 "r"(lo.y), "r"(hi.x), "r"(hi.y)
+                 : "memory");
+  }
+}
+
 constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 128 ? 128 : 256; }
 
 // Nibble weights (FMT_U4 / FMT_NF4): the W tile arrives as nibbles ([rows][64 bytes] per 128-k block)
@@ -371,13 +399,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         if (!cok) break;
         const uint8_t *src = sN + s * NIB_BYTES;
         uint8_t *dst = sW + s * (SWAP ? R_BYTES : S_BYTES);
-#pragma unroll 2
-        for (int t = ct; t < WROWS * 8; t += 128) {
-          const int r = t >> 3, c = t & 7;
-          const uint2 nb = *reinterpret_cast<const uint2 *>(src + r * 64 + c * 8);
-          const uint2 lo = expand8<FMT>(nb.x, tb), hi = expand8<FMT>(nb.y, tb);
-          *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
-        }
+        expand_stage<FMT, WROWS>(src, dst, ct, tb);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(conv0 + 8 * s) : "memory");
@@ -655,13 +677,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
         if (!cok) break;
         const uint8_t *src = sN + s * NIB_BYTES;
         uint8_t *dst = sW + s * (SWAP ? R_BYTES : S_BYTES);
-#pragma unroll 2
-        for (int t = ct; t < WROWS * 8; t += 128) {
-          const int r = t >> 3, c = t & 7;
-          const uint2 nb = *reinterpret_cast<const uint2 *>(src + r * 64 + c * 8);
-          const uint2 lo = expand8<FMT>(nb.x, tb), hi = expand8<FMT>(nb.y, tb);
-          *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
-        }
+        expand_stage<FMT, WROWS>(src, dst, ct, tb);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(mapa_u32(conv0 + 8 * s, leader_rank));

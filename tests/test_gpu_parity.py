@@ -363,6 +363,32 @@ def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
         w4.free()
 
 
+@pytest.mark.parametrize("nf4", [False, True])
+@pytest.mark.parametrize("sk", [1, 3])
+def test_tensor_core_nibble_long_k_exact(ctx, env_clean, nf4, sk):
+    """Decode-sized M on nibble weights through the tensor-core kernel with a long K per CTA (split
+    forced to 1 or 3), so the stage ring wraps many times and every stage is expanded from nibbles; a
+    K tail (K % 128 != 0) ends the last block."""
+    env_clean.setenv("ORKB_TC_SK", str(sk))
+    if nf4:
+        env_clean.setenv("ORK_NF4", "1")
+    L = ork_b200.lib()
+    rng = np.random.default_rng(700 + 10 * sk + nf4)
+    K, N = 4128, 384
+    f32 = rng.standard_normal((N, K), dtype=np.float32)
+    w, _ = ctx.i4a8_pack(f32)
+    codes, _, _ = of.i4a8_blob_codes(w.dump(), K, N)
+    try:
+        assert L.ork_b200_force_route(ctx.ctx, 1) == 0
+        for M in (1, 8, 16, 17, 32, 33, 64):
+            A = rand_i8(rng, (M, K))
+            rc, Cm = ctx.run(w, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), M
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w.free()
+
+
 @pytest.mark.parametrize("pair,tn,sk", [(2, 256, 1), (2, 256, 2), (2, 128, 1), (2, 128, 4), (2, 64, 1),
                                         (2, 64, 2), (2, 192, 1), (2, 192, 4), (3, 0, 1), (3, 0, 2), (3, 0, 4)])
 def test_tensor_core_pair_tiles_exact(ctx, env_clean, pair, tn, sk):
