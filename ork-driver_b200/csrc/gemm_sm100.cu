@@ -869,6 +869,13 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
     // long int8 rows (K >= 6144): a 6-deep ring streams faster (6144x2048, M 8 / 16: 6.2 -> 5.6 us); for
     // shorter rows the default ring, with more CTAs resident for the next launch, is as fast or faster
     if (!nib && fmt != FMT_F16 && c.tn <= 32 && KB >= 48) c.stages = 6;
+    // nibble weights whose unsplit grid already exceeds two CTAs per SM (wide N, M <= 16): the 2-stage
+    // ring (up to four CTAs, so twice the converter warps, per SM) with a 2-way split measured fastest
+    // (NF4 8192x57344xM8 80.6 -> 70.5 us, 8192x42752xM8 67.5 -> 56.5 us); on smaller grids it is slower
+    if (nib && c.tn == 16 && tiles > 2 * 148 && KB >= 2) {
+      c.stages = 2;
+      c.sk = 2;
+    }
   } else {
     const int mt = (M + BM - 1) / BM;
     auto tiles = [&](int tn) { return mt * ((N + tn - 1) / tn); };
@@ -947,6 +954,12 @@ cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl)
         if (c.tn == 16) return launch_tc<FMT, true, 16, 6>(a, c.sk, s, pdl);
         if (c.tn == 32) return launch_tc<FMT, true, 32, 6>(a, c.sk, s, pdl);
         return launch_tc<FMT, true, 64, 5>(a, c.sk, s, pdl);
+      }
+    }
+    if constexpr (NIB) {  // tuning override ORKB_TC_STAGES = 2: a 53-56 KB ring, up to four CTAs per SM
+      if (c.stages == 2) {
+        if (c.tn == 16) return launch_tc<FMT, true, 16, 2>(a, c.sk, s, pdl);
+        if (c.tn == 32) return launch_tc<FMT, true, 32, 2>(a, c.sk, s, pdl);
       }
     }
     if (c.tn == 16) return launch_tc<FMT, true, 16, NIB ? 3 : 4>(a, c.sk, s, pdl);

@@ -365,11 +365,14 @@ def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
 
 @pytest.mark.parametrize("nf4", [False, True])
 @pytest.mark.parametrize("sk", [1, 3])
-def test_tensor_core_nibble_long_k_exact(ctx, env_clean, nf4, sk):
+@pytest.mark.parametrize("stages", [0, 2])
+def test_tensor_core_nibble_long_k_exact(ctx, env_clean, nf4, sk, stages):
     """Decode-sized M on nibble weights through the tensor-core kernel with a long K per CTA (split
-    forced to 1 or 3), so the stage ring wraps many times and every stage is expanded from nibbles; a
-    K tail (K % 128 != 0) ends the last block."""
+    forced to 1 or 3), so the stage ring (default depth, or the 2-stage ring) wraps many times and every
+    stage is expanded from nibbles; a K tail (K % 128 != 0) ends the last block."""
     env_clean.setenv("ORKB_TC_SK", str(sk))
+    if stages:
+        env_clean.setenv("ORKB_TC_STAGES", str(stages))
     if nf4:
         env_clean.setenv("ORK_NF4", "1")
     L = ork_b200.lib()
@@ -381,6 +384,29 @@ def test_tensor_core_nibble_long_k_exact(ctx, env_clean, nf4, sk):
     try:
         assert L.ork_b200_force_route(ctx.ctx, 1) == 0
         for M in (1, 8, 16, 17, 32, 33, 64):
+            A = rand_i8(rng, (M, K))
+            rc, Cm = ctx.run(w, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), M
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w.free()
+
+
+@pytest.mark.parametrize("nf4", [False, True])
+def test_tensor_core_nibble_wide_grid_exact(ctx, env_clean, nf4):
+    """Nibble weights wide enough (N > 296 * 128) that the router picks the 2-stage ring with a 2-way
+    split for M <= 16, through the default choice (no tuning variables), with a K tail."""
+    if nf4:
+        env_clean.setenv("ORK_NF4", "1")
+    L = ork_b200.lib()
+    rng = np.random.default_rng(800 + nf4)
+    K, N = 1056, 297 * 128
+    f32 = rng.standard_normal((N, K), dtype=np.float32)
+    w, _ = ctx.i4a8_pack(f32)
+    codes, _, _ = of.i4a8_blob_codes(w.dump(), K, N)
+    try:
+        assert L.ork_b200_force_route(ctx.ctx, 1) == 0
+        for M in (1, 8, 16):
             A = rand_i8(rng, (M, K))
             rc, Cm = ctx.run(w, A)
             assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), M
