@@ -178,6 +178,13 @@ size_t ork_b200_weight_read(const ork_w *w, void *out, size_t cap);
 int ork_b200_route(const ork_w *w, int M);
 /* Force a route for subsequent runs on this context: -1 automatic (default), 0 GEMV, 1 tensor core. */
 int ork_b200_force_route(ork_npu *ctx, int route);
+/* The tensor-core kernel's tile choice for a run of M rows on a K x N weight of format fmt (0 fp16,
+ * 1 int8, 2 uniform int4 -- w4a8 uniform and W4A4 --, 3 NF4), as the router makes it (tuning variables
+ * ORKB_TC_* in the environment included): out[0] operands swapped (the weight on the 128-row MMA side),
+ * out[1] tile width on the other side, out[2] K split (CTAs per cluster), out[3] stage ring depth
+ * (0 = the variant's default), out[4] CTA-pair tile. Host-only: needs no device. Returns 0, or -1 on a
+ * bad argument. For tests and tooling. */
+int ork_b200_tc_choice(int fmt, int M, int K, int N, int *out);
 
 #ifdef __cplusplus
 }

@@ -1012,3 +1012,14 @@ unsigned int tc_error_flag(bool reset) {
 ORKB_ERR_WORD_SETTER(tc_set_err_word)
 
 }  // namespace orkb
+
+extern "C" int ork_b200_tc_choice(int fmt, int M, int K, int N, int *out) {
+  if (!out || fmt < orkb::FMT_F16 || fmt > orkb::FMT_NF4 || M < 1 || K < 1 || N < 1) return -1;
+  const orkb::TcCfg c = orkb::choose_tc(fmt, M, K, N);
+  out[0] = c.swap ? 1 : 0;
+  out[1] = c.tn;
+  out[2] = c.sk;
+  out[3] = c.stages;
+  out[4] = c.pair ? 1 : 0;
+  return 0;
+}

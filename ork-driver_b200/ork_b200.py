@@ -109,6 +109,7 @@ SIGNATURES = [
     ("ork_b200_weight_read", _sz, [_vp, _vp, _sz]),
     ("ork_b200_route", _i, [_vp, _i]),
     ("ork_b200_force_route", _i, [_vp, _i]),
+    ("ork_b200_tc_choice", _i, [_i, _i, _i, _i, _vp]),
 ]
 
 
