@@ -185,6 +185,12 @@ int ork_b200_force_route(ork_npu *ctx, int route);
  * (0 = the variant's default), out[4] CTA-pair tile. Host-only: needs no device. Returns 0, or -1 on a
  * bad argument. For tests and tooling. */
 int ork_b200_tc_choice(int fmt, int M, int K, int N, int *out);
+/* The decode GEMV's kernel choice for a block of M <= 8 rows (format codes as above; tuning variables
+ * ORKB_GEMV_* included): out[0] 1 = direct-load kernel (a warp per channel group, any K), 0 = staged
+ * kernel (a CTA stages whole rows in shared memory); out[1] channels per warp of the direct kernel
+ * (0 for staged); out[2] channels per CTA of the staged kernel (0 for direct); out[3] activation rows
+ * per pass (1, 2, 4 or 8). Host-only; returns 0, or -1 on a bad argument. For tests and tooling. */
+int ork_b200_gemv_choice(int fmt, int M, int K, int N, int *out);
 
 #ifdef __cplusplus
 }

@@ -960,3 +960,13 @@ cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool 
 }
 
 }  // namespace orkb
+
+extern "C" int ork_b200_gemv_choice(int fmt, int M, int K, int N, int *out) {
+  if (!out || fmt < orkb::FMT_F16 || fmt > orkb::FMT_NF4 || M < 1 || M > 8 || K < 1 || N < 1) return -1;
+  const orkb::Cfg c = orkb::choose(fmt, M, K, N);
+  out[0] = c.direct ? 1 : 0;
+  out[1] = c.direct ? c.cpw : 0;
+  out[2] = c.direct ? 0 : c.tr;
+  out[3] = c.mt;
+  return 0;
+}

@@ -110,6 +110,7 @@ SIGNATURES = [
     ("ork_b200_route", _i, [_vp, _i]),
     ("ork_b200_force_route", _i, [_vp, _i]),
     ("ork_b200_tc_choice", _i, [_i, _i, _i, _i, _vp]),
+    ("ork_b200_gemv_choice", _i, [_i, _i, _i, _i, _vp]),
 ]
 
 

@@ -1,11 +1,17 @@
-"""The tensor-core kernel's tile and split choice (host logic, no GPU), pinned on the BASELINE shapes.
+"""The kernel choices of the router (host logic, no GPU), pinned on the BASELINE shapes.
 
+Tensor-core tiles:
 Each expectation restates a rule of the router in the library's tile choice: swapped operands with
 the narrowest tile covering M for M <= 64, split-K doubling while the grid stays within ~320 CTAs;
 for larger M, 128-wide weight tiles widened to 192 / 256 only while the grid would exceed one wave of
 148 CTAs, CTA-pair tiles for nibble weights past one wave, split-K for grids of at most 32 / 64
 tiles; nibble weights at M <= 16 whose unsplit grid exceeds 296 tiles take the 2-stage ring with a
 2-way split; long int8 rows (K >= 6144) at M <= 32 take a 6-deep ring.
+
+Decode GEMV (M <= 8 per pass): the staged kernel (8 channels per CTA, whole rows in shared memory)
+unless its rows and 8 activation rows exceed 196 KB, or M > 4 with K >= 8192, or nibble weights with
+short rows (K <= 2048, N <= 8192); the direct kernel then takes 4 channels per warp (2 for NF4 at
+M > 4, and for the short nibble rows).
 """
 import ctypes
 
@@ -24,7 +30,8 @@ def choice(fmt, M, K, N):
 
 @pytest.fixture(autouse=True)
 def no_tuning_variables(monkeypatch):
-    for v in ("ORKB_TC_TN", "ORKB_TC_NA", "ORKB_TC_STAGES", "ORKB_TC_PAIR", "ORKB_TC_SK"):
+    for v in ("ORKB_TC_TN", "ORKB_TC_NA", "ORKB_TC_STAGES", "ORKB_TC_PAIR", "ORKB_TC_SK", "ORKB_GEMV_KIND",
+              "ORKB_GEMV_CPW", "ORKB_GEMV_TR"):
         monkeypatch.delenv(v, raising=False)
 
 
@@ -64,3 +71,35 @@ def test_bad_arguments_refused():
     assert L.ork_b200_tc_choice(4, 8, 2048, 2048, out) == -1
     assert L.ork_b200_tc_choice(I8, 0, 2048, 2048, out) == -1
     assert L.ork_b200_tc_choice(I8, 8, 2048, 2048, None) == -1
+
+
+def gemv_choice(fmt, M, K, N):
+    out = (ctypes.c_int * 4)()
+    assert ork_b200.lib().ork_b200_gemv_choice(fmt, M, K, N, out) == 0
+    return list(out)
+
+
+@pytest.mark.parametrize("fmt,M,K,N,want", [
+    # [direct, channels per warp (direct), channels per CTA (staged), activation rows per pass]
+    (NF4, 1, 28672, 8192, [1, 4, 0, 1]),    # 70B down projection: rows too long to stage
+    (NF4, 1, 8192, 57344, [0, 0, 8, 1]),    # 70B gate+up at M = 1: staged
+    (NF4, 8, 8192, 10240, [1, 2, 0, 8]),    # M = 8, K >= 8192: direct, 2 NF4 channels per warp
+    (I8, 8, 8192, 8192, [1, 4, 0, 8]),
+    (I8, 1, 6144, 2048, [0, 0, 8, 1]),      # configs[1] decode shapes: staged
+    (I8, 3, 2048, 2048, [0, 0, 8, 4]),
+    (I8, 2, 2048, 6144, [0, 0, 8, 2]),
+    (U4, 1, 2048, 6144, [1, 2, 0, 1]),      # short nibble rows
+    (U4, 1, 2048, 12288, [0, 0, 8, 1]),     # ... unless N > 8192
+    (F16, 1, 2048, 6144, [0, 0, 8, 1]),     # configs[0] M = 1
+    (F16, 4, 16384, 2048, [1, 4, 0, 4]),    # fp16 rows of 32 KB: too long to stage
+])
+def test_gemv_choice(fmt, M, K, N, want):
+    assert gemv_choice(fmt, M, K, N) == want
+
+
+def test_gemv_choice_refuses_bad_arguments():
+    L = ork_b200.lib()
+    out = (ctypes.c_int * 4)()
+    assert L.ork_b200_gemv_choice(I8, 9, 2048, 2048, out) == -1  # more than one decode pass
+    assert L.ork_b200_gemv_choice(5, 1, 2048, 2048, out) == -1
+    assert L.ork_b200_gemv_choice(I8, 1, 2048, 2048, None) == -1
