@@ -1033,6 +1033,71 @@ def run_tc_peak(args):
     ctx.close()
 
 
+def run_pack(args):
+    """Pack-time quantization, timed on the host beside the reference's own CPU code (the measurement
+    plan times the pack-time quantizers apart from the runs). BASELINE configs[2] inputs: B f32[N][K] ~
+    N(0, 0.02), imatrix ~ U(0.5, 2), (K, N) in {(6144, 2048), (2048, 12288)}; uniform and NF4, with and
+    without an imatrix. Ours: ork_i4a8_pack_cpu_blob, the library's host-only O4N1 writer -- the same
+    quantizer ork_i4a8_mm_pack(_im) runs before its upload. Reference: ork-driver's
+    ork_i4a8_pack_cpu_blob_qerr (src/npu/i4/pack.c:787-795, byte-identical to its pack_im + w_dump)
+    from oracle/_ref, compiled from its sources. Every blob is compared byte for byte. No GPU needed."""
+    import ork_b200
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_ffi as of
+
+    L = ork_b200.lib()
+    R = of.reference()
+    reps = max(1, min(args.steps, 3))
+    rng = np.random.default_rng(2)
+    table, t_ours, t_ref, weights, identical = {}, 0.0, 0.0, 0, True
+
+    def best(fn):
+        fn()  # warm-up (page faults of the output buffer)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    for K, N in ((6144, 2048), (2048, 12288)):
+        f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        im = (rng.random(K, dtype=np.float32) * np.float32(1.5) + np.float32(0.5)).astype(np.float32)
+        for nf4 in (False, True):
+            for imx in (None, im):
+                imp = None if imx is None else imx.ctypes.data
+                need = L.ork_i4a8_pack_cpu_blob(None, K, N, f32.ctypes.data, imp, int(nf4), None, 0)
+                ours = np.zeros(need, np.uint8)
+                to = best(lambda: L.ork_i4a8_pack_cpu_blob(None, K, N, f32.ctypes.data, imp, int(nf4),
+                                                           ours.ctypes.data, need))
+                row = {"ours_ms": to * 1e3}
+                if R is not None:
+                    ref = np.zeros(need, np.uint8)
+                    tr = best(lambda: R.ork_i4a8_pack_cpu_blob_qerr(None, K, N, f32.ctypes.data, imp, int(nf4),
+                                                                    ref.ctypes.data, need, None))
+                    same = bool(np.array_equal(ours, ref))
+                    identical &= same
+                    row.update({"reference_ms": tr * 1e3, "speedup": tr / to, "identical": same})
+                    t_ref += tr
+                name = f"{'nf4' if nf4 else 'uniform'}{'+imatrix' if imx is not None else ''} {K}x{N}"
+                table[name] = row
+                t_ours += to
+                weights += K * N
+    out = {"metric": "w4a8 pack-time quantization (ork_i4a8_mm_pack(_im) host quantizer), configs[2] inputs",
+           "value": weights / t_ours / 1e6, "unit": "Mweights/s", "n_gpus": 0, "steps": reps, "warmup": 1,
+           "ms_per_step": t_ours * 1e3, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "pack: 2 shapes x {uniform, NF4} x {no imatrix, imatrix}; best of steps",
+                      "threads": os.cpu_count()},
+           "table": table}
+    if R is not None:
+        out["cpu_baseline"] = {"value": weights / t_ref / 1e6, "unit": "Mweights/s", "cores": os.cpu_count(),
+                               "kind": "reference", "cpu": cpu_model(),
+                               "sample": "the same 8 packs, best of steps, by ork-driver's own pack code"}
+        out["bytes_identical"] = identical
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1044,11 +1109,12 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="after warm-up, replay one cycle of step graphs between cudaProfilerStart/Stop and exit "
                          "(for `ncu --profile-from-start off` launch lists of exactly the timed work)")
-    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped", "moe", "tc_peak"],
+    ap.add_argument("--workload", default="w8a8", choices=["w8a8", "70b", "qwen3", "grouped", "moe", "tc_peak", "pack"],
                     help="w8a8: BASELINE configs[1] sweep (default); 70b: configs[4] column-sharded NF4 stack; "
                          "qwen3: configs[3] Qwen3-1.7B-shape w8a8 stack; grouped: grouped-scale W4A8 decode; "
                          "moe: a batch of 64 NF4 expert matmuls through ork_i8_mm_run_chain; tc_peak: the GEMM "
-                         "at 8192^3 beside torch._int_mm / torch.mm")
+                         "at 8192^3 beside torch._int_mm / torch.mm; pack: the pack-time quantizers on the host beside "
+                         "the reference's (no GPU)")
     ap.add_argument("--tokens", type=int, default=1, help="70b workload: tokens per pass M (1, 8 or 256)")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="70b workload at N > 1: the C gather fused into the matmul over peer memory, or NCCL")
@@ -1070,6 +1136,8 @@ def main():
         return run_moe(args)
     if args.workload == "tc_peak":
         return run_tc_peak(args)
+    if args.workload == "pack":
+        return run_pack(args)
 
     import torch
 
