@@ -78,12 +78,24 @@ static uint32_t xs32(uint32_t *s) {  // src/npu/internal.h:589
   return x;
 }
 
+// The levels with a 16th entry that no value is below (+inf), for the branchless search in nf4_index.
+static const float kNf4Search[16] = {
+    kNf4Levels[0], kNf4Levels[1], kNf4Levels[2],  kNf4Levels[3],  kNf4Levels[4],  kNf4Levels[5],
+    kNf4Levels[6], kNf4Levels[7], kNf4Levels[8],  kNf4Levels[9],  kNf4Levels[10], kNf4Levels[11],
+    kNf4Levels[12], kNf4Levels[13], kNf4Levels[14], HUGE_VALF};
+
 // src/npu/i4/quant.c:73-86: hi = first level >= wn (capped at 15), lo = hi-1; nearest with ties to hi,
-// or stochastic (hi when t > u). The levels are increasing, so the first-level search is a lower_bound.
+// or stochastic (hi when t > u). The levels are increasing, so the first level >= wn is the number of
+// levels below wn: a four-step binary search whose steps add 8 / 4 / 2 / 1 by comparison results instead
+// of branching (random weights made the branches of a lower_bound mispredict about half the time). A NaN
+// compares below nothing and lands on 0, as in the reference's scan.
 static inline int nf4_index(float wn, int sr, uint32_t *seed) {
   if (wn > 1.0f) wn = 1.0f;
   else if (wn < -1.0f) wn = -1.0f;
-  int hi = (int)(std::lower_bound(kNf4Levels, kNf4Levels + 15, wn) - kNf4Levels);
+  int hi = (kNf4Search[7] < wn) * 8;
+  hi += (kNf4Search[hi + 3] < wn) * 4;
+  hi += (kNf4Search[hi + 1] < wn) * 2;
+  hi += (kNf4Search[hi] < wn) * 1;
   const int lo = hi > 0 ? hi - 1 : 0;
   if (lo == hi) return hi;
   const float t = (wn - kNf4Levels[lo]) / (kNf4Levels[hi] - kNf4Levels[lo]);
