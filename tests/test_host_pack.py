@@ -75,3 +75,49 @@ def test_oracle_refuses_malformed_blobs():
         bad[off:off + 4] = np.frombuffer(np.uint32(val).tobytes(), np.uint8)
         assert of.i4a8_blob_codes(bad, K, N) is None, off
     assert of.i4a8_blob_codes(blob, K, N + 32) is None
+
+
+def _nf4_boundary_rows(N=32, K=128, seed=9):
+    """Rows of max |w| = 1 (so the normalised value is the weight itself) holding every NF4 level, its two
+    float neighbours, every midpoint between adjacent levels and the midpoints' neighbours: the values on
+    which a level search or the tie rule (t >= 0.5 goes up) could decide differently."""
+    lv = np.array([-1.0, -0.6961928009986877, -0.5250730514526367, -0.39491748809814453,
+                   -0.28444138169288635, -0.18477343022823334, -0.09105003625154495, 0.0,
+                   0.07958029955625534, 0.16093020141124725, 0.24611230194568634, 0.33791524171829224,
+                   0.44070982933044434, 0.5626170039176941, 0.7229568362236023, 1.0], np.float32)
+    mids = ((lv[:-1] + lv[1:]) / np.float32(2)).astype(np.float32)
+    vals = []
+    for x in np.concatenate([lv, mids]):
+        vals += [x, np.nextafter(x, np.float32(-2)), np.nextafter(x, np.float32(2))]
+    vals = np.clip(np.array(vals, np.float32), -1, 1)
+    vals = np.concatenate([vals, np.array([-0.0], np.float32)])
+    assert vals.size < K
+    rng = np.random.default_rng(seed)
+    w = np.zeros((N, K), np.float32)
+    for n in range(N):
+        row = np.concatenate([vals, np.zeros(K - vals.size, np.float32)])
+        rng.shuffle(row)
+        row[np.argmax(np.abs(row))] = np.float32(1.0 if n % 2 else -1.0)  # absmax exactly 1
+        w[n] = row
+    return w
+
+
+def test_nf4_level_boundaries_quantize_like_oracle(env_clean):
+    w = _nf4_boundary_rows()
+    K = w.shape[1]
+    for im in (None, np.ones(K, np.float32), seeded_imatrix(11, K)):
+        assert np.array_equal(ork_b200.cpu_blob(w, im, nf4=True), of.i4a8_blob(w, im, nf4=True))
+
+
+@pytest.mark.skipif(of.reference() is None, reason="oracle/_ref not built")
+def test_nf4_level_boundaries_equal_reference(env_clean):
+    """The same rows, and one with a NaN weight (its normalised value compares below no level: index 0),
+    against ork-driver's own compiled quantizer, byte for byte."""
+    from make_fixtures import ref_blob
+
+    w = _nf4_boundary_rows()
+    w[5, 7] = np.float32("nan")
+    K = w.shape[1]
+    for im in (None, seeded_imatrix(12, K)):
+        rblob, _ = ref_blob(of.reference(), w, im, 1, False)
+        assert np.array_equal(ork_b200.cpu_blob(w, im, nf4=True), rblob)
