@@ -8,7 +8,7 @@ bytes = K*N (weight) + M*K (A) + 4*M*N (int32 C) per call, summed over the step 
 time; every config is HBM-bound by that formula on B200 (int32 C is heavy), so GB/s is the common unit.
 
 - value: device-resident inputs, the twelve calls queued back to back on the library's stream
-  (ork_i8_mm_run_async, with programmatic dependent launch) and replayed as one CUDA graph per step,
+  (ork_b200_i8_mm_run_async, with programmatic dependent launch) and replayed as one CUDA graph per step,
   timed with CUDA events on that stream, max over ranks.
 - e2e: the same sweep through the synchronous public call ork_i8_mm_run with pinned host buffers: each
   call copies A in, runs, copies C out and synchronises.
@@ -118,11 +118,22 @@ def cpu_model():
     return None
 
 
+def host_cores():
+    """Host CPU threads this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_reference_sweep(min_seconds, max_reps=3):
     """The reference's CPU int8 GEMM over the sweep: oracle/_ref (its own code) if built, else the
-    restatement. Returns (GB/s, cores, kind, sample description)."""
+    restatement, with an OpenMP team of every host core (set explicitly: torchrun exports
+    OMP_NUM_THREADS=1). Returns (GB/s, cores, kind, sample description, seconds per sweep)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_ffi as of
+
+    of.restated().orc_set_threads(host_cores())
 
     ref = of.reference()
     kind = "reference" if ref is not None else "port"
@@ -182,7 +193,19 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
     rng = np.random.default_rng(99)
     out = {}
 
-    def timed(kind, w_list, K, N, M):
+    def check(kind, fmt, w, A, Cm, K, N):
+        """C of one call against an exact int32 GEMM of the weight's codes (integer formats), or an fp32
+        matmul of the same fp16 values within 1e-3 * sqrt(K) * max|A| * max|B| (fp16)."""
+        if kind == "f16":
+            raw = np.zeros(K * N * 2, np.uint8)
+            assert L.ork_b200_weight_read(w.h, raw.ctypes.data, raw.nbytes) == raw.nbytes
+            Wt = torch.from_numpy(raw.view(np.float16).reshape(N, K)).cuda().float()
+            ref = A.float() @ Wt.t()
+            tol = 1e-3 * np.sqrt(K) * float(A.float().abs().max()) * float(Wt.abs().max())
+            return float((Cm - ref).abs().max()) <= tol
+        return bool(torch.equal(Cm, exact_i32(A, resident_codes(ctx, w, fmt))))
+
+    def timed(kind, w_list, K, N, M, fmt):
         dtype_in = torch.float16 if kind == "f16" else torch.int8
         dtype_out = torch.float32 if kind == "f16" else torch.int32
         if kind == "f16":
@@ -191,10 +214,14 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
             lo, hi = (-7, 8) if kind == "i4" else (-127, 128)
             A = [torch.randint(lo, hi, (M, K), dtype=dtype_in, device="cuda") for _ in range(ncopies)]
         C = [torch.empty((M, N), dtype=dtype_out, device="cuda") for _ in range(ncopies)]
-        fn = {"f16": L.ork_f16_mm_run_async, "i8": L.ork_i8_mm_run_async, "i4": L.ork_i4_mm_run_async}[kind]
+        fn = {"f16": L.ork_b200_f16_mm_run_async, "i8": L.ork_b200_i8_mm_run_async, "i4": L.ork_b200_i4_mm_run_async}[kind]
         for i in range(ncopies):
             assert fn(ctx.ctx, w_list[i].h, M, A[i].data_ptr(), C[i].data_ptr()) == 0
         torch.cuda.synchronize()
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        if not check(kind, fmt, w_list[0], A[0], C[0], K, N):
+            print(json.dumps({"error": f"{fmt} {K}x{N} M{M}: C differs from the checker"}), flush=True)
+            raise SystemExit(3)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for i in range(ncopies):
@@ -210,19 +237,20 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / (reps * ncopies), L.ork_b200_route(w_list[0].h, M)
 
-    def record(name, kind, ws, K, N, Ms, wbytes):
+    def record(name, kind, ws, K, N, Ms, wbytes, fmt):
         for M in Ms:
-            ms, route = timed(kind, ws, K, N, M)
+            ms, route = timed(kind, ws, K, N, M, fmt)
             abytes = M * K * (2 if kind == "f16" else 1)
             by = wbytes + abytes + 4 * M * N
             out[f"{name} {K}x{N} M{M}"] = {"us": ms * 1e3, "GB/s": by / (ms / 1e3) / 1e9,
-                                           "TOPS": 2 * M * K * N / (ms / 1e3) / 1e12, "route": route}
+                                           "TOPS": 2 * M * K * N / (ms / 1e3) / 1e12, "route": route,
+                                           "parity": "within tolerance" if kind == "f16" else "exact"}
 
     # fp16 K=2048 N=6144, M in {1, 64}; B ~ N(0, 0.02)
     K, N = 2048, 6144
     B = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
     ws = [ctx.f16_pack(B) for _ in range(ncopies)]
-    record("fp16", "f16", ws, K, N, (1, 64), 2 * K * N)
+    record("fp16", "f16", ws, K, N, (1, 64), 2 * K * N, "f16")
     for w in ws:
         w.free()
     # w4a8 uniform / NF4 with imatrix ~ U(0.5, 2), and W4A4 with A ~ U[-7, 7]
@@ -232,12 +260,13 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
         for nf4 in (False, True):
             blob = ork_b200.cpu_blob(f32, im, nf4=nf4)
             ws = [ctx.i4a8_load(blob, K, N) for _ in range(ncopies)]
-            record("w4a8-" + ("nf4" if nf4 else "uniform"), "i8", ws, K, N, (1, 32, 256), K * N // 2)
+            record("w4a8-" + ("nf4" if nf4 else "uniform"), "i8", ws, K, N, (1, 32, 256), K * N // 2,
+                   "nf4" if nf4 else "u4")
             for w in ws:
                 w.free()
         B4 = rng.integers(-7, 8, size=(K, N), dtype=np.int8)
         ws = [ctx.i4_pack(B4) for _ in range(ncopies)]
-        record("w4a4", "i4", ws, K, N, (1, 32, 256), K * N // 2)
+        record("w4a4", "i4", ws, K, N, (1, 32, 256), K * N // 2, "u4")
         for w in ws:
             w.free()
     return out
@@ -248,41 +277,74 @@ def other_configs(ctx, L, stream, ncopies=10, reps=10):
 # weight. (K, N) per linear; the LM head runs once per pass.
 L70 = {"layers": 80, "linears": [("qkv", 8192, 10240), ("o", 8192, 8192), ("gate_up", 8192, 57344),
                                  ("down", 28672, 8192)], "lm_head": (8192, 128256)}
+# NF4 codebook as int8 codes, lut[i] = rint(level[i] * 127) (ork-driver src/npu/i4/pack.c:128-131 over the
+# levels of src/npu.c:888-892): the format's decoding table, used to rebuild a weight's int8 codes from
+# its resident nibbles for the benchmark's own result checks
+NF4_LUT = [-127, -88, -67, -50, -36, -23, -12, 0, 10, 20, 31, 43, 56, 71, 92, 127]
 
 
-def run_70b(args):
-    """every weight NF4 (w4a8, B ~ N(0, 0.02)), column-sharded over the ranks; each matmul
-    runs on the local shard and its int32 C is all-gathered over NCCL. One step = one pass of M tokens
-    through the 80 layers' four linears and the LM head, captured as one CUDA graph (kernels and
-    collectives). Each rank quantizes its own channel slice once on the host and loads enough distinct
-    copies of a layer that its per-pass working set exceeds L2. value = tokens/s of the whole job."""
-    import datetime
-
+def resident_codes(ctx, w, fmt):
+    """The int8 codes [N][K] of a packed weight as a device tensor, rebuilt from its resident bytes (int8
+    as stored; uniform int4 nibbles sign-extended; NF4 nibbles through the codebook), low nibble = even k."""
     import torch
-    import torch.distributed as dist
+
+    raw = np.zeros(ctx.L.ork_b200_weight_read(w.h, None, 0), np.uint8)
+    assert ctx.L.ork_b200_weight_read(w.h, raw.ctypes.data, raw.nbytes) == raw.nbytes
+    t = torch.from_numpy(raw).cuda()
+    if fmt == "i8":
+        return t.view(torch.int8).view(w.N, w.K)
+    lo, hi = (t & 15).to(torch.int16), (t >> 4).to(torch.int16)
+    if fmt == "nf4":
+        lut = torch.tensor(NF4_LUT, dtype=torch.int16, device="cuda")
+        lo, hi = lut[lo.long()], lut[hi.long()]
+    else:
+        lo, hi = (lo ^ 8) - 8, (hi ^ 8) - 8
+    return torch.stack((lo, hi), dim=-1).view(w.N, w.K).to(torch.int8)
+
+
+def exact_i32(A, codes_nk):
+    """C = A . codes^T in exact int32 on the device through torch._int_mm (cuBLASLt): an independent exact
+    GEMM that checks the benchmark's own calls outside the timed regions (integer sums have one right
+    answer, so any exact int32 GEMM is a valid checker). A [M][K] int8, codes [N][K] int8."""
+    import torch
+
+    M, K = A.shape
+    Mp = max(32, (M + 7) // 8 * 8)
+    Ap = torch.zeros((Mp, K), dtype=torch.int8, device=A.device)
+    Ap[:M] = A
+    return torch._int_mm(Ap, codes_nk.t().contiguous())[:M]
+
+
+def sharded_70b(args, Ms, dist=None):
+    """every weight NF4 (w4a8, B ~ N(0, 0.02)), column-sharded over the ranks of the job; each
+    matmul runs on the local shard and its int32 C reaches every rank -- over NVLink peer memory (the
+    library's fused gather: the shard's columns stored into every rank's C, a bounded signal wait) or,
+    with --gather nccl, by an NCCL all-gather. One step = one pass of M tokens through the 80 layers' four
+    linears and the LM head, captured as one CUDA graph. Each rank quantizes its own channel slice once on
+    the host and loads enough distinct copies of a layer that its per-pass working set exceeds L2. Before
+    timing, every linear's C is checked: this rank's columns against an exact int32 GEMM of its own
+    resident codes, and the whole gathered C by a checksum that must agree on every rank.
+    Returns ({"M<m>": result}, description)."""
+    import torch
 
     import ork_b200
     import shard
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
+    world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
+    rank = dist.get_rank() if world > 1 else 0
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
     L = ork_b200.lib()
     ctx = ork_b200.Context()
     stream = torch.cuda.Stream()
     L.ork_b200_set_stream(ctx.ctx, stream.cuda_stream)
-    M = args.tokens
     layer_bytes = sum(K * N // 2 for _, K, N in L70["linears"]) // world
     ncopies = max(2, -(-400 * 2 ** 20 // layer_bytes))
-    rng = np.random.default_rng(4242 + rank)
+    gen = torch.Generator(device="cuda").manual_seed(4242 + rank)
 
     def packed(K, N, copies):
         n0, n1 = shard.shard_range(N, rank, world)
-        f32 = (rng.standard_normal((n1 - n0, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        # N(0, 0.02) weights drawn on the device (fast), quantized to NF4 on the host by the library's packer
+        f32 = (torch.randn((n1 - n0, K), device="cuda", generator=gen) * 0.02).cpu().numpy()
         blob = ork_b200.cpu_blob(f32, None, nf4=True)
         del f32
         return [ctx.i4a8_load(blob, K, n1 - n0) for _ in range(copies)]
@@ -293,99 +355,138 @@ def run_70b(args):
     # blocks keep every rank's slice a multiple of 32 channels for 1, 2, 4 and 8 ranks
     head_chunks = 3
     head = [(Kh, Nv // head_chunks, packed(Kh, Nv // head_chunks, 1)[0]) for _ in range(head_chunks)]
-    A = {8192: torch.randint(-127, 128, (M, 8192), dtype=torch.int8, device="cuda"),
-         28672: torch.randint(-127, 128, (M, 28672), dtype=torch.int8, device="cuda")}
+    # (the LM head's C holds its last chunk's result after a pass)
+    shapes = [(name, K, N, ws[0]) for name, (K, N, ws) in lin.items()] + [("lm_head", Kh, Nv // head_chunks, head[-1][2])]
     p2p = world > 1 and args.gather == "p2p"
-    if p2p:
-        # the gather fused into the matmul: each rank's decode kernel stores its columns into every rank's C
-        # over NVLink and signals; a bounded wait on the stream makes C complete before the next matmul
-        peers = shard.PeerGroup(ctx, dist)
-        tab = {name: peers.table(M, N, N // world)[0] for name, K, N in L70["linears"]}
-        tab_head = peers.table(M, Nv // head_chunks, Nv // head_chunks // world)[0]
-    else:
-        Cl = {name: torch.empty((M, N // world), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
-        Cf = {name: torch.empty((M, N), dtype=torch.int32, device="cuda") for name, K, N in L70["linears"]}
-        Chl = torch.empty((M, Nv // head_chunks // world), dtype=torch.int32, device="cuda")
-        Chf = torch.empty((M, Nv // head_chunks), dtype=torch.int32, device="cuda")
+    peers = shard.PeerGroup(ctx, dist) if p2p else None
+    results = {}
+    for M in Ms:
+        A = {8192: torch.randint(-127, 128, (M, 8192), dtype=torch.int8, device="cuda", generator=gen),
+             28672: torch.randint(-127, 128, (M, 28672), dtype=torch.int8, device="cuda", generator=gen)}
+        Cfull = {}
+        if p2p:
+            tab = {}
+            for name, K, N, _ in shapes:
+                tab[name], Cfull[name] = peers.table(M, N, N // world)
+        else:
+            Cl = {name: torch.empty((M, N // world), dtype=torch.int32, device="cuda") for name, K, N, _ in shapes}
+            Cf = {name: torch.empty((M, N), dtype=torch.int32, device="cuda") for name, K, N, _ in shapes}
+            Cfull = {name: (Cf[name] if world > 1 else Cl[name]).data_ptr() for name, K, N, _ in shapes}
 
-    def run(w, a, cl, cf):
-        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), cl.data_ptr()) == 0
-        if world > 1:
-            shard.gather_columns(cl, dist, out=cf)
-
-    def run_p2p(w, a, t):
-        assert L.ork_i8_mm_run_peers_async(ctx.ctx, w.h, M, a.data_ptr(), t) == 0
-        assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
-
-    def one_pass():
-        for layer in range(L70["layers"]):
-            for name, K, N in L70["linears"]:
-                if p2p:
-                    run_p2p(lin[name][2][layer % ncopies], A[K], tab[name])
-                else:
-                    run(lin[name][2][layer % ncopies], A[K], Cl[name], Cf[name])
-        for K, N, w in head:
+        def run(name, w, a):
             if p2p:
-                run_p2p(w, A[K], tab_head)
+                assert L.ork_b200_i8_mm_run_peers_async(ctx.ctx, w.h, M, a.data_ptr(), tab[name]) == 0
+                assert L.ork_b200_peers_wait_async(ctx.ctx, tab[name]) == 0
             else:
-                run(w, A[K], Chl, Chf)
+                assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), Cl[name].data_ptr()) == 0
+                if world > 1:
+                    shard.gather_columns(Cl[name], dist, out=Cf[name])
 
-    with torch.cuda.stream(stream):
-        one_pass()  # eager warm-up: kernel attributes, tensor maps, NCCL communicator
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        l0 = ctx.launches()
-        with torch.cuda.graph(g, stream=stream):
-            one_pass()
-        launches_per_pass = ctx.launches() - l0
-        for _ in range(args.warmup):
-            g.replay()
-        torch.cuda.synchronize()
-        if dist.is_initialized():
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with Clocks(local) as clk:
-            e0.record(stream)
-            for _ in range(args.steps):
-                g.replay()
-            e1.record(stream)
+        def one_pass():
+            for layer in range(L70["layers"]):
+                for name, K, N in L70["linears"]:
+                    run(name, lin[name][2][layer % ncopies], A[K])
+            for K, N, w in head:
+                run("lm_head", w, A[K])
+
+        with torch.cuda.stream(stream):
+            one_pass()  # eager warm-up: kernel attributes, tensor maps, NCCL communicator
             torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    del g
-    per_pass = ms / args.steps
-    rank_bytes = L70["layers"] * layer_bytes + Kh * Nv // 2 // world
-    line = {"metric": "70B-shape NF4 linear stack tok/s (configs[4])", "value": M / (per_pass / 1e3),
-            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": per_pass, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "Llama-70B-shaped linears, NF4 weights ~N(0,0.02), 80 layers x (QKV 8192x10240, "
-                                   "O 8192x8192, gate+up 8192x57344, down 28672x8192) + LM head 8192x128256, "
-                                   f"column-sharded over {world} GPU(s), "
-                                   + ("gather fused into each matmul over NVLink peer memory (P2P stores + "
-                                      "bounded signal wait)" if p2p else "NCCL all-gather of each int32 C"),
-                       "M": M, "parallelism": f"column shard x{world}",
-                       "l2": f"inputs larger than L2: {ncopies} distinct copies of the per-rank layer weights "
-                             f"({ncopies * layer_bytes / 2**20:.0f} MiB) cycled over the 80 layers"},
-            "per_gpu_weight_GBs": rank_bytes / (per_pass / 1e3) / 1e9,
-            "weight_bytes_per_rank_per_pass": rank_bytes, "gpu_launches": int(launches_per_pass * args.steps),
-            "clocks": clk.summary()}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+            assert L.ork_b200_sync(ctx.ctx) == 0
+        # every linear's C after the pass (all copies of a weight are identical): own columns exact,
+        # the gathered whole identical on every rank
+        sums = []
+        for name, K, N, w in shapes:
+            full = np.zeros((M, N), np.int32)
+            assert L.ork_b200_copy(ctx.ctx, full.ctypes.data, Cfull[name], full.nbytes) == 0
+            n0, n1 = shard.shard_range(N, rank, world)
+            want = exact_i32(A[K], resident_codes(ctx, w, "nf4")).cpu().numpy()
+            if not np.array_equal(full[:, n0:n1], want):
+                raise SystemExit(f"70B {name} M={M}: C differs from the exact int32 GEMM of the shard")
+            sums.append(int(full.astype(np.int64).sum()) ^ int((full.astype(np.int64) * np.arange(N)).sum()))
+        if world > 1:
+            every = [None] * world
+            dist.all_gather_object(every, sums)
+            if any(e != sums for e in every):
+                raise SystemExit(f"70B M={M}: gathered C differs between ranks")
+        with torch.cuda.stream(stream):
+            g = torch.cuda.CUDAGraph()
+            l0 = ctx.launches()
+            with torch.cuda.graph(g, stream=stream):
+                one_pass()
+            launches_per_pass = ctx.launches() - l0
+            for _ in range(args.warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with Clocks(local) as clk:
+                e0.record(stream)
+                for _ in range(args.steps):
+                    g.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        del g
+        per_pass = ms / args.steps
+        rank_bytes = L70["layers"] * layer_bytes + Kh * Nv // 2 // world
+        results[f"M{M}"] = {"tok_s": M / (per_pass / 1e3), "ms_per_pass": per_pass,
+                            "per_gpu_weight_GBs": rank_bytes / (per_pass / 1e3) / 1e9,
+                            "weight_bytes_per_rank_per_pass": rank_bytes,
+                            "gpu_launches": int(launches_per_pass * args.steps), "steps": args.steps,
+                            "parity": "exact", "clocks": clk.summary()}
+    desc = {"workload": "Llama-70B-shaped linears, NF4 weights ~N(0,0.02), 80 layers x (QKV 8192x10240, "
+                        "O 8192x8192, gate+up 8192x57344, down 28672x8192) + LM head 8192x128256, "
+                        f"column-sharded over {world} GPU(s), "
+                        + ("gather fused into each matmul over NVLink peer memory (P2P stores + bounded "
+                           "signal wait)" if p2p else "NCCL all-gather of each int32 C" if world > 1
+                           else "one GPU, no gather"),
+            "parallelism": f"column shard x{world}",
+            "l2": f"inputs larger than L2: {ncopies} distinct copies of the per-rank layer weights "
+                  f"({ncopies * layer_bytes / 2**20:.0f} MiB) cycled over the 80 layers",
+            "parity": "before timing, every linear's C: this rank's columns equal an exact int32 GEMM "
+                      "(torch._int_mm) of its resident codes; the gathered C's checksum equal on every rank"}
     for _, _, ws in lin.values():
         for w in ws:
             w.free()
     for _, _, w in head:
         w.free()
-    if p2p:
+    if peers is not None:
         peers.close()
     ctx.close()
-    if dist.is_initialized():
+    return results, desc
+
+
+def run_70b(args):
+    """--workload 70b: configs[4] at M = --tokens alone, as its own JSON line (see sharded_70b)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    res, desc = sharded_70b(args, [args.tokens], dist if world > 1 else None)
+    r = res[f"M{args.tokens}"]
+    line = {"metric": "70B-shape NF4 linear stack tok/s (configs[4])", "value": r["tok_s"], "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_pass"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": {**desc, "M": args.tokens},
+            **{k: v for k, v in r.items() if k not in ("tok_s", "ms_per_pass")}}
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
 
 
@@ -395,15 +496,22 @@ Q3 = {"H": 2048, "NH": 16, "NKV": 8, "D": 128, "FF": 6144, "layers": 28, "V": 15
 
 
 def run_qwen3(args):
+    """--workload qwen3: the Qwen3 decode / prefill measurement of qwen3() as its own JSON line."""
+    line = qwen3(args)
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(line), flush=True)
+
+
+def qwen3(args):
     """random-init (~N(0,0.02)) Qwen3-1.7B-shaped w8a8 stack; every projection's weight is
     packed per output channel by ork_i8_mm_pack_f32. Decode (the headline): the 28 layers are one
-    ork_i8_mm_layers_async call (one persistent launch) -- the library's decode layer: RMSNorm + int8 quantization, q/k/v in one
+    ork_b200_i8_mm_layers_async call (one persistent launch) -- the library's decode layer: RMSNorm + int8 quantization, q/k/v in one
     batched launch, q/k RMSNorm + RoPE + attention over the fp32 KV cache (the token's k/v appended at the
     device-side position), o, residual + RMSNorm + quantization, gate/up in one launch, SwiGLU +
     quantization, down, residual -- then the final norm + quantization (ork_b200_rmsnorm_q8_async), the LM
-    head (ork_i8_mm_run_async) and the greedy pick (ork_b200_argmax_scaled_async); a whole token is one
+    head (ork_b200_i8_mm_run_async) and the greedy pick (ork_b200_argmax_scaled_async); a whole token is one
     CUDA graph. Prefill of the 128-token prompt runs the same layer arithmetic over the rows (the
-    library's row glue around ork_i8_mm_run_async; PyTorch's attention), captured as one CUDA graph.
+    library's row glue around ork_b200_i8_mm_run_async; PyTorch's attention), captured as one CUDA graph.
     Four distinct layer weight sets (200 MB, > L2) cycle over the 28 layers. value = decode tokens/s;
     prefill tokens/s beside it."""
     import ctypes as C
@@ -429,8 +537,10 @@ def run_qwen3(args):
     rng = np.random.default_rng(1234 + rank)
     dev = "cuda"
 
-    def pack(N, K):
-        f32 = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    wgen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def pack(N, K):  # N(0, 0.02) drawn on the device (fast), quantized per channel by ork_i8_mm_pack_f32
+        f32 = (torch.randn((N, K), device=dev, generator=wgen) * 0.02).cpu().numpy()
         w, bs = ctx.i8_pack_f32(f32)
         assert w
         return w, torch.from_numpy(bs).to(dev)
@@ -451,7 +561,7 @@ def run_qwen3(args):
 
     def head(x_row):  # final norm + quantization, the LM head and the greedy pick into tok
         assert L.ork_b200_rmsnorm_q8_async(ctx.ctx, x_row.data_ptr(), ones_h.data_ptr(), H, q8h.data_ptr(), None) == 0
-        assert L.ork_i8_mm_run_async(ctx.ctx, lm[0].h, 1, q8h.data_ptr(), c_lm.data_ptr()) == 0
+        assert L.ork_b200_i8_mm_run_async(ctx.ctx, lm[0].h, 1, q8h.data_ptr(), c_lm.data_ptr()) == 0
         assert L.ork_b200_argmax_scaled_async(ctx.ctx, c_lm.data_ptr(), lm[1].data_ptr(), V, tok.data_ptr()) == 0
 
     # prefill buffers: the rows' codes and scales, the matmul results, the dequantized projections
@@ -465,7 +575,7 @@ def run_qwen3(args):
     pqh = torch.empty((NH, PRE, D), dtype=torch.float32, device=dev)
 
     def mm(w, T, a, c):
-        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, T, a.data_ptr(), c.data_ptr()) == 0
+        assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, T, a.data_ptr(), c.data_ptr()) == 0
 
     def prefill_layer(x, li, T):  # x [T, H] fp32, positions 0..T-1; fills the fp32 caches
         # the decode layer's arithmetic over T rows (weights are int8 codes, activations per-row int8):
@@ -514,14 +624,14 @@ def run_qwen3(args):
     dims = LayerDims(H, NH, NKV, D, D, FF, PRE, PRE, 1.0 / float(np.sqrt(D)), Q3["theta"])
     kv = LayerKV(ones_d.data_ptr(), 1, MAXT, pos.data_ptr())
 
-    # the 28 layers as one ork_i8_mm_layers_async call (one persistent launch per token)
+    # the 28 layers as one ork_b200_i8_mm_layers_async call (one persistent launch per token)
     stack = (LayerW * NLY)(*[LayerW(*[wsets[li % NDIST][n][0].h for n in names], ones_h.data_ptr(), ones_d.data_ptr(),
                                     ones_h.data_ptr(), ones_d.data_ptr(), kc[li].data_ptr(), vc[li].data_ptr())
                              for li in range(NLY)])
 
     def decode_step():
         xa.copy_(emb.index_select(0, tok).float().view(-1))
-        assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NLY, stack, xa.data_ptr(), xb.data_ptr(),
+        assert L.ork_b200_i8_mm_layers_async(ctx.ctx, C.byref(dims), NLY, stack, xa.data_ptr(), xb.data_ptr(),
                                         C.byref(kv)) == 0
         head(xb)  # the final norm + quantization, the LM head and the greedy pick: three library launches
         pos.add_(1)
@@ -580,12 +690,12 @@ def run_qwen3(args):
             "config": {"workload": "Qwen3-1.7B-shaped w8a8 stack, random weights ~N(0,0.02): 28 layers, hidden 2048, "
                                    "16/8 heads x 128, SwiGLU 6144, vocab 151936, q/k norms, RoPE 1e6; prefill 128 "
                                    "then 256 greedy decode steps, batch 1",
-                       "linears": "decode: the 28 layers as one ork_i8_mm_layers_async call (the library's decode "
+                       "linears": "decode: the 28 layers as one ork_b200_i8_mm_layers_async call (the library's decode "
                                   "layer, one persistent launch), final norm + quantization, LM head "
-                                  "(ork_i8_mm_run_async) and greedy pick as three library launches; "
+                                  "(ork_b200_i8_mm_run_async) and greedy pick as three library launches; "
                                   "prefill: the same layer arithmetic over 128 rows -- the library's row glue "
                                   "(norm + quantization, dequantization + residual, q/k norms + RoPE + cache "
-                                  "writes, SwiGLU + quantization) around ork_i8_mm_run_async, PyTorch's "
+                                  "writes, SwiGLU + quantization) around ork_b200_i8_mm_run_async, PyTorch's "
                                   "scaled_dot_product_attention -- captured as one CUDA graph (prefill_eager_ms: "
                                   "the same prompt launched eagerly)",
                        "l2": f"{NDIST} distinct layer weight sets cycled (~{NDIST * 50} MB) + 311 MB LM head",
@@ -599,13 +709,12 @@ def run_qwen3(args):
             "linear_weight_GBs_decode": weight_bytes / (decode_ms / DEC / 1e3) / 1e9,
             "gpu_launches": int(launches_per_token * DEC), "library_launches_per_token": launches_per_token,
             "library_launches_prefill": prefill_launches, "clocks": clk.summary()}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     for ws in wsets:
         for w, _ in ws.values():
             w.free()
     lm[0].free()
     ctx.close()
+    return line
 
 
 # grouped scales (per-K-group aScale/bScale, fp32 C): the reference's own grouped W4A8 test shapes
@@ -662,7 +771,7 @@ def run_grouped(args):
 
     def enqueue(sel):
         for _, _, w, (dA, daS, dbS), dC in sel:
-            assert L.ork_i8_mm_run_grouped_async(ctx.ctx, w.h, dA.shape[0], dA.data_ptr(), daS.data_ptr(),
+            assert L.ork_b200_i8_mm_run_grouped_async(ctx.ctx, w.h, dA.shape[0], dA.data_ptr(), daS.data_ptr(),
                                                  dbS.data_ptr(), dC.data_ptr()) == 0
 
     def graph_of(sel):
@@ -747,6 +856,7 @@ def run_grouped(args):
             "clocks": clk.summary(), "gpu_launches": int(len(calls) * reps),
             "breakdown": breakdown}
     if rank == 0 and not args.no_cpu:
+        of.restated().orc_set_threads(host_cores())
         ref = of.reference()
         fn = ref.orki_cpu_gemm_grouped if ref is not None else of.restated().orc_gemm_grouped
         sample = [h for h in host if h[3] == 1]
@@ -770,11 +880,11 @@ def run_grouped(args):
 
 
 def run_moe(args):
-    """Batches of independent matmuls (ork_i8_mm_run_chain_async): an MoE decode layer of 64 experts, each a
+    """Batches of independent matmuls (ork_b200_i8_mm_run_chain_async): an MoE decode layer of 64 experts, each a
     2048 x 1408 w4a8 NF4 weight (ork_i4a8_mm_pack with ORK_NF4) seeing 1-4 tokens, as one batch; 4 distinct
     expert sets (>= 180 MB of nibbles) cycle so no batch finds its weights in L2. value = algorithmic GB/s of
     the batch (device-resident inputs, one CUDA graph per step, events); breakdown: the same 64 matmuls
-    issued as 64 separate ork_i8_mm_run_async launches; e2e: the synchronous ork_i8_mm_run_chain over host
+    issued as 64 separate ork_b200_i8_mm_run_async launches; e2e: the synchronous ork_i8_mm_run_chain over host
     buffers; cpu_baseline: the reference's own chain semantics (orki_cpu_gemm_i32 per task, oracle/_ref)."""
     import torch
 
@@ -814,7 +924,7 @@ def run_moe(args):
     step_bytes = sum(K * N // 2 + t.M * K + 4 * t.M * N for t in sets[0][1])
 
     # correctness of the batched launch against the oracle, before timing
-    assert L.ork_i8_mm_run_chain_async(ctx.ctx, E, sets[0][1]) == 0
+    assert L.ork_b200_i8_mm_run_chain_async(ctx.ctx, E, sets[0][1]) == 0
     assert L.ork_b200_sync(ctx.ctx) == 0
     for w, M, A, codes, Cd in host:
         assert np.array_equal(Cd.cpu().numpy(), of.gemm_i32(A, codes))
@@ -829,12 +939,12 @@ def run_moe(args):
 
     def batched():
         for ws, arr, _ in sets:
-            assert L.ork_i8_mm_run_chain_async(ctx.ctx, E, arr) == 0
+            assert L.ork_b200_i8_mm_run_chain_async(ctx.ctx, E, arr) == 0
 
     def separate():
         for ws, arr, _ in sets:
             for t in arr:
-                assert L.ork_i8_mm_run_async(ctx.ctx, t.w, t.M, t.A, t.C) == 0
+                assert L.ork_b200_i8_mm_run_async(ctx.ctx, t.w, t.M, t.A, t.C) == 0
 
     def timed(g, reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -879,6 +989,7 @@ def run_moe(args):
                           "separate_GBs": step_bytes / t_s / 1e9},
             "clocks": clk.summary(), "gpu_launches": int(reps * NSET)}
     if rank == 0 and not args.no_cpu:
+        of.restated().orc_set_threads(host_cores())
         ref = of.reference()
         fn = ref.ork_i8_mm_run_cpu if ref is not None else of.restated().orc_gemm_i32
         Cm = [np.zeros((M, N), np.int32) for _, M, _, _, _ in host]
@@ -918,7 +1029,7 @@ def run_profile(spec):
                 a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
                 c = torch.empty((M, N), dtype=torch.int32, device="cuda")
                 torch.cuda.synchronize()
-                assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
+                assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
                 assert L.ork_b200_sync(ctx.ctx) == 0
             w.free()
         print(json.dumps({"profile": "all", "configs": [f"{K}x{N}xM{M}" for K, N, M in CONFIGS]}))
@@ -942,14 +1053,14 @@ def run_profile(spec):
     c = torch.empty((M, N), dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
     for _ in range(5):
-        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
+        assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
         assert L.ork_b200_sync(ctx.ctx) == 0
     # back-to-back timing of the same call (weight L2-warm after the first): a tuning aid only
     stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(50):
-        assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
+        assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr()) == 0
     e1.record(stream)
     assert L.ork_b200_sync(ctx.ctx) == 0
     us = e0.elapsed_time(e1) * 1e3 / 50
@@ -960,7 +1071,7 @@ def run_profile(spec):
 
 
 def run_tc_peak(args):
-    """The tensor pipe's ceiling: the library's tcgen05 GEMM (ork_i8_mm_run_async, ork_f16_mm_run_async) at
+    """The tensor pipe's ceiling: the library's tcgen05 GEMM (ork_b200_i8_mm_run_async, ork_b200_f16_mm_run_async) at
     M = K = N = 8192, where the work is compute-bound (1.1 T ops against ~0.4 GB), timed beside the GPU's
     measured dense peak on the same shapes (torch._int_mm and torch.mm, i.e. cuBLASLt). Not a BASELINE
     config: it measures the denominator the prefill fractions need and how close the kernel comes to it.
@@ -998,7 +1109,7 @@ def run_tc_peak(args):
         B8 = torch.randint(-127, 128, (S, S), dtype=torch.int8, device="cuda", generator=g)
         w8 = ctx.i8_pack(B8.cpu().numpy())
         C32 = torch.empty((S, S), dtype=torch.int32, device="cuda")
-        ms = timed(lambda: L.ork_i8_mm_run_async(ctx.ctx, w8.h, S, A8.data_ptr(), C32.data_ptr()))
+        ms = timed(lambda: L.ork_b200_i8_mm_run_async(ctx.ctx, w8.h, S, A8.data_ptr(), C32.data_ptr()))
         out["int8_ours_tops"] = ops / (ms * 1e-3) / 1e12
         try:
             ms_lib = timed(lambda: torch._int_mm(A8, B8))
@@ -1015,7 +1126,7 @@ def run_tc_peak(args):
         B16 = (torch.randn((S, S), device="cuda", generator=g) * 0.02).to(torch.float16)
         w16 = ctx.f16_pack(B16.cpu().numpy())
         C = torch.empty((S, S), dtype=torch.float32, device="cuda")
-        ms = timed(lambda: L.ork_f16_mm_run_async(ctx.ctx, w16.h, S, A16.data_ptr(), C.data_ptr()))
+        ms = timed(lambda: L.ork_b200_f16_mm_run_async(ctx.ctx, w16.h, S, A16.data_ptr(), C.data_ptr()))
         out["f16_ours_tflops"] = ops / (ms * 1e-3) / 1e12
         ms_lib = timed(lambda: torch.mm(A16, B16))
         out["f16_torch_mm_tflops"] = ops / (ms_lib * 1e-3) / 1e12
@@ -1179,7 +1290,7 @@ def main():
     def call(K, N, M, i):
         w = weights[(K, N)][i % NCOPIES]
         a, c = bufs[(K, N, M)][i % NCOPIES]
-        rc = L.ork_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr())
+        rc = L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), c.data_ptr())
         assert rc == 0
 
     # Step s issues the 12 calls; call i of a shape (i = 0..3 over the M values) uses packed copy
@@ -1200,6 +1311,23 @@ def main():
     for s in range(NCOPIES):  # eager warm-up of every call (kernel attributes, tensor maps)
         step_calls(s)
     torch.cuda.synchronize()
+    codes = {(K, N): resident_codes(ctx, weights[(K, N)][0], "i8") for K, N in SHAPES}
+
+    def check_sweep(when):
+        """Every config's C (all NCOPIES buffers, each last written by a call with identical weights)
+        equal to an exact int32 GEMM of its A and the packed codes; a mismatch ends the run."""
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        out = {}
+        for K, N, M in CONFIGS:
+            ok = all(torch.equal(c, exact_i32(a, codes[(K, N)])) for a, c in bufs[(K, N, M)])
+            out[f"{K}x{N}xM{M}"] = "exact" if ok else "MISMATCH"
+            if not ok:
+                print(json.dumps({"error": f"{K}x{N}xM{M}: C differs from the exact int32 GEMM {when}"}),
+                      flush=True)
+                raise SystemExit(3)
+        return out
+
+    parity = check_sweep("before timing")
     graphs = []
     launches_per_step = []
     for s in range(NCOPIES):
@@ -1232,6 +1360,7 @@ def main():
         barrier()
     launches = sum(launches_per_step[(args.warmup + s) % NCOPIES] for s in range(args.steps))
     ms = ev0.elapsed_time(ev1)
+    check_sweep("after the timed graph replays")
     if dist is not None:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1276,18 +1405,29 @@ def main():
     dom = max(breakdown, key=lambda k: breakdown[k]["ms"])
     K, N, M = (int(x) for x in dom.replace("M", "").split("x"))
     hbm, bf16, src = peaks()
+    int8_peak = 2.0 * bf16  # dense int8 = 2x the measured dense bf16 burst (no int8 figure measured here)
     db = breakdown[dom]
-    per_launch_ms = db["ms"] / max(db["launches"], 1)
-    achieved = alg_bytes(K, N, M) / max(db["launches"], 1) / (per_launch_ms / 1e3) / 1e9
+    nl = max(db["launches"], 1)
+    per_launch_s = db["ms"] / nl / 1e3
+    bytes_l, ops_l = alg_bytes(K, N, M) / nl, 2.0 * M * K * N / nl
+    t_hbm, t_tc = bytes_l / (hbm * 1e9), ops_l / (int8_peak * 1e12)
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
             traffic = json.load(f).get(dom)
     except Exception:
         pass
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": traffic, "kernel": dom, "share": db["ms"] / tot, "peak_source": src,
-                "algorithmic_bytes_per_launch": alg_bytes(K, N, M) / max(db["launches"], 1)}
+    roofs = {"hbm": {"achieved": bytes_l / per_launch_s / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": t_hbm / per_launch_s, "peak_source": f"{src} (copy)"},
+             "tensor": {"achieved": ops_l / per_launch_s / 1e12, "peak": int8_peak, "unit": "TOPS",
+                        "frac": t_tc / per_launch_s,
+                        "peak_source": f"2 x {src} dense bf16 burst ({bf16:.0f} TFLOP/s): int8 dense"}}
+    bound = "tensor" if t_tc > t_hbm else "hbm"
+    roofline = {"bound": bound, **{k: roofs[bound][k] for k in ("achieved", "peak", "unit", "frac")},
+                "traffic": traffic, "kernel": dom, "share": db["ms"] / tot, "peak_source": roofs[bound]["peak_source"],
+                "algorithmic_bytes_per_launch": bytes_l, "algorithmic_ops_per_launch": ops_l,
+                "us_per_launch": per_launch_s * 1e6, "roofs": roofs,
+                "bound_rule": "the larger of algorithmic bytes / HBM peak and ops / int8 tensor peak"}
     del graphs
 
     # ---- e2e through the synchronous public call with pinned host buffers ---------------------
@@ -1321,8 +1461,30 @@ def main():
         e2e_ms = float(t.item())
     e2e = {"value": world * STEP_BYTES * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps}
+    for K, N, M in CONFIGS:  # the last e2e step's host results
+        a, c = host[(K, N, M)]
+        if not torch.equal(c.cuda(), exact_i32(a.cuda(), codes[(K, N)])):
+            print(json.dumps({"error": f"{K}x{N}xM{M}: e2e C differs from the exact int32 GEMM"}), flush=True)
+            raise SystemExit(3)
+    for ws in weights.values():
+        for w in ws:
+            w.free()
+    del bufs, codes
+
+    # configs[4] column-sharded over the job's ranks, at every N (one GPU included): decode-sized passes
+    s70, d70 = sharded_70b(args, [1, 8], dist)
+    sharded = {"workload": d70["workload"], "parallelism": d70["parallelism"], "l2": d70["l2"],
+               "parity": d70["parity"], "scaling": "strong (the same 70B-shape stack at every N)",
+               **{m: {k: v for k, v in r.items() if k != "steps"} for m, r in s70.items()}}
 
     others = other_configs(ctx, L, stream) if (rank == 0 and not args.no_others) else None
+
+    q3 = None
+    if rank == 0 and world == 1 and not args.no_others:
+        q = qwen3(args)
+        q3 = {"decode_tok_s": q["value"], "prefill_tok_s": q["prefill_tok_s"], "decode_ms_per_token": q["ms_per_step"],
+              "prefill_ms": q["prefill_ms"], "roofline": q["roofline"], "config": q["config"]["workload"],
+              "gpu_launches_per_token": q["library_launches_per_token"], "clocks": q["clocks"]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1341,16 +1503,19 @@ def main():
                        "step_bytes": STEP_BYTES, "step_ops": STEP_OPS},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": int(launches),
+            "parity": parity,
+            "parity_check": "every config's C, before and after the timed replays and after the e2e steps, equal "
+                            "to an exact int32 GEMM (torch._int_mm) of the same A and the packed codes",
             "decode_gbs": sum(alg_bytes(*map(int, k.replace("M", "").split("x"))) for k in dec)
             / (sum(breakdown[k]["ms"] for k in dec) / 1e3) / 1e9,
             "prefill_tops": sum(2 * np.prod([int(x) for x in k.replace("M", "").split("x")]) for k in pre)
             / (sum(breakdown[k]["ms"] for k in pre) / 1e3) / 1e12,
+            "sharded_70b": sharded, "qwen3": q3,
+            "qwen3_decode_tok_s": q3["decode_tok_s"] if q3 else None,
+            "qwen3_prefill_tok_s": q3["prefill_tok_s"] if q3 else None,
             "breakdown": breakdown, "other_configs": others}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    for ws in weights.values():
-        for w in ws:
-            w.free()
     ctx.close()
     if dist is not None:
         dist.destroy_process_group()

@@ -1,9 +1,19 @@
-/* ork_b200.h -- B200-specific additions to the ork_npu.h API (no counterpart in ork-driver).
+/* ork_b200.h -- B200-specific additions to the ork_npu.h API.
+ *
+ * Every name here starts with ork_b200_ (except ork_i8_mm_run_noalloc, which the reference does not
+ * have either) so that none collides with a name of ork-driver's own API: where the reference has a
+ * function of the same purpose, ork_npu.h declares it with the reference's name and prototype, and the
+ * B200 form here carries the prefix (the reference's ork_i8_mm_run_async, for instance, takes host
+ * buffers and returns an ork_async handle; ork_b200_i8_mm_run_async takes device buffers and is
+ * stream-ordered).
  *
  * The reference's run calls are synchronous over host buffers; on a GPU the same matmuls are most
  * useful stream-ordered over device buffers, so they can be queued back to back (or captured in a CUDA
  * graph) without a host round trip per call. These entry points expose that, plus the little a caller
- * needs to integrate the context with its own CUDA stream. Include after ork_npu.h.
+ * needs to integrate the context with its own CUDA stream. Entry points documented as taking device
+ * pointers check, before anything is queued, that each one is memory of the context's GPU (or managed
+ * memory), and return -1 (-3 for the layer calls) with a message when one is not. Include after
+ * ork_npu.h.
  */
 #ifndef ORK_B200_H
 #define ORK_B200_H
@@ -15,10 +25,11 @@ extern "C" {
 
 /* Asynchronous device-pointer runs: A and C must be device memory of the context's GPU; the matmul is
  * enqueued on the context's stream and the call returns without waiting. Same argument rules and return
- * codes as the synchronous runs; launch errors are reported here, execution errors by ork_b200_sync. */
-int ork_i8_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
-int ork_i4_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
-int ork_f16_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *dA, float *dC);
+ * codes as the synchronous runs; launch errors are reported here, execution errors by ork_b200_sync. The
+ * host-buffer forms with an ork_async handle are ork_npu.h's ork_*_mm_run_async. */
+int ork_b200_i8_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
+int ork_b200_i4_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int32_t *dC);
+int ork_b200_f16_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *dA, float *dC);
 
 /* No counterpart in ork-driver. ork_i8_mm_run for callers that cannot let a library allocate device
  * memory at run time (an engine that reserved nearly all HBM for its own pool at start-up, a process
@@ -33,22 +44,22 @@ int ork_i8_mm_run_noalloc(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_
 
 /* Grouped runs over device pointers (A, aScale, bScale, C on the context's GPU), enqueued like the
  * async runs above; same arguments and checks as ork_i4_mm_run_grouped / ork_i8_mm_run_grouped. */
-int ork_i4_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
+int ork_b200_i4_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
                                 const float *dbScale, float *dC);
-int ork_i8_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
+int ork_b200_i8_mm_run_grouped_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const float *daScale,
                                 const float *dbScale, float *dC);
 
 /* ork_i8_mm_run_chain over device pointers (every A and C on the context's GPU), enqueued without waiting:
  * the batch's decode-sized tasks go into one launch, as in the synchronous form. A task with a C row
  * stride other than N must be decode-sized (M <= 8). Capturable in a CUDA graph. */
-int ork_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
+int ork_b200_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
 
 /* The fused output stages (ork_i8_mm_run_out8 / _out16 / _ewmul) over device pointers, enqueued without
  * waiting. Decode-sized runs (M <= 8) requantize inside the matmul kernel; larger M use a context scratch
  * for the int32 sums (allocated on first use: make one call before capturing a CUDA graph). */
-int ork_i8_mm_run_out8_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int8_t *dC, int mult, int shift);
-int ork_i8_mm_run_out16_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, short *dC, int mult, int shift);
-int ork_i8_mm_run_ewmul_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const int8_t *dG, int8_t *dC,
+int ork_b200_i8_mm_run_out8_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, int8_t *dC, int mult, int shift);
+int ork_b200_i8_mm_run_out16_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, short *dC, int mult, int shift);
+int ork_b200_i8_mm_run_ewmul_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, const int8_t *dG, int8_t *dC,
                               int mult, int shift);
 
 /* ork_i8_mm_layer over device pointers, enqueued without waiting (the first layer call on a context
@@ -68,7 +79,7 @@ typedef struct ork_b200_layer_kv {
   int hstride;
   const int *dpos;
 } ork_b200_layer_kv;
-int ork_i8_mm_layer_async(ork_npu *ctx, const struct ork_layer_dims *d, ork_w *wq, ork_w *wk, ork_w *wv, ork_w *wo,
+int ork_b200_i8_mm_layer_async(ork_npu *ctx, const struct ork_layer_dims *d, ork_w *wq, ork_w *wk, ork_w *wv, ork_w *wo,
                           ork_w *wg, ork_w *wu, ork_w *wd, const float *attn_norm, const float *q_norm,
                           const float *ffn_norm, const float *x, float *Kc, float *Vc, float *x_out,
                           const ork_b200_layer_kv *kv);
@@ -79,13 +90,13 @@ int ork_i8_mm_layer_async(ork_npu *ctx, const struct ork_layer_dims *d, ork_w *w
  * k_norm is not used). When the layers fit the persistent kernel the whole stack is ONE launch whose
  * weight stream runs across layer boundaries; otherwise the multi-launch form runs layer by layer. The
  * first call with a given list of layers uploads its pointer table (make it before capturing a CUDA graph).
- * Returns as ork_i8_mm_layer_async. */
+ * Returns as ork_b200_i8_mm_layer_async. */
 typedef struct ork_b200_layer_w {
   ork_w *wq, *wk, *wv, *wo, *wg, *wu, *wd;
   const float *attn_norm, *q_norm, *ffn_norm, *k_norm;
   float *Kc, *Vc;
 } ork_b200_layer_w;
-int ork_i8_mm_layers_async(ork_npu *ctx, const struct ork_layer_dims *d, int nlayers, const ork_b200_layer_w *layers,
+int ork_b200_i8_mm_layers_async(ork_npu *ctx, const struct ork_layer_dims *d, int nlayers, const ork_b200_layer_w *layers,
                            const float *x, float *x_out, const ork_b200_layer_kv *kv);
 
 /* Decode glue around the LM head (device pointers, on the context stream; 0, or -1 on bad arguments).
@@ -141,8 +152,8 @@ int ork_b200_sym_close(ork_npu *ctx, void *peer);
 ork_b200_peers *ork_b200_peers_create(ork_npu *ctx, int nranks, int rank, void *const *C, void *const *flags, int ldc,
                                       int col0, int ncols);
 void ork_b200_peers_destroy(ork_b200_peers *p);
-int ork_i8_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
-int ork_i4_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
+int ork_b200_i8_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
+int ork_b200_i4_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
 int ork_b200_peers_wait_async(ork_npu *ctx, ork_b200_peers *p);
 /* Copy `bytes` between any two host / device addresses, ordered after the context's queued work, and wait
  * for it (for callers without a CUDA binding of their own, e.g. to read a symmetric buffer). 0 or -1. */
@@ -178,18 +189,22 @@ size_t ork_b200_weight_read(const ork_w *w, void *out, size_t cap);
 int ork_b200_route(const ork_w *w, int M);
 /* Force a route for subsequent runs on this context: -1 automatic (default), 0 GEMV, 1 tensor core. */
 int ork_b200_force_route(ork_npu *ctx, int route);
+/* The kernel choice's tuning variables (ORKB_TC_TN, _NA, _STAGES, _PAIR, _SK, ORKB_GEMV_KIND, _CPW, _TR,
+ * ORKB_LAYER_FUSED) are read from the environment once per context, when it is created; this re-reads
+ * them into the context (for tuning sweeps and tests that change them). 0, or -1 for a NULL context. */
+int ork_b200_reload_tuning(ork_npu *ctx);
 /* The tensor-core kernel's tile choice for a run of M rows on a K x N weight of format fmt (0 fp16,
  * 1 int8, 2 uniform int4 -- w4a8 uniform and W4A4 --, 3 NF4), as the router makes it (tuning variables
- * ORKB_TC_* in the environment included): out[0] operands swapped (the weight on the 128-row MMA side),
+ * ORKB_TC_* as the environment holds them at this call): out[0] operands swapped (the weight on the 128-row MMA side),
  * out[1] tile width on the other side, out[2] K split (CTAs per cluster), out[3] stage ring depth
  * (0 = the variant's default), out[4] CTA-pair tile. Host-only: needs no device. Returns 0, or -1 on a
  * bad argument. For tests and tooling. */
 int ork_b200_tc_choice(int fmt, int M, int K, int N, int *out);
-/* The decode GEMV's kernel choice for a block of M <= 8 rows (format codes as above; tuning variables
- * ORKB_GEMV_* included): out[0] 1 = direct-load kernel (a warp per channel group, any K), 0 = staged
+/* The decode GEMV's kernel choice for a block of M <= 8 rows (format codes as above): out[0] 1 = direct-load kernel (a warp per channel group, any K), 0 = staged
  * kernel (a CTA stages whole rows in shared memory); out[1] channels per warp of the direct kernel
  * (0 for staged); out[2] channels per CTA of the staged kernel (0 for direct); out[3] activation rows
- * per pass (1, 2, 4 or 8). Host-only; returns 0, or -1 on a bad argument. For tests and tooling. */
+ * per pass (1, 2, 4 or 8). Tuning variables ORKB_GEMV_* as the environment holds them at this call.
+ * Host-only; returns 0, or -1 on a bad argument. For tests and tooling. */
 int ork_b200_gemv_choice(int fmt, int M, int K, int N, int *out);
 
 #ifdef __cplusplus

@@ -200,6 +200,34 @@ int ork_i4_mm_run_experts(ork_npu *ctx, const ork_mm_task_i4 *ex, int ntask, int
  * already collected ticket or a device error. */
 int ork_mm_submit(ork_npu *ctx, ork_w *w, int M, const void *A);
 int ork_mm_collect(ork_npu *ctx, int ticket, void *C);
+/* include/ork/chain.h:123. The int4 (W4A4) batch, twin of ork_i8_mm_run_stream: same meaning and return
+ * codes as ork_i4_mm_run_chain (the reference deals the tasks over its NPU cores; the GPU serves the
+ * whole batch). */
+int ork_i4_mm_run_stream(ork_npu *ctx, int S, const ork_mm_task_i4 *tasks);
+
+/* include/ork/chain.h:124-143. Runs that return at once, joined by ork_async_wait. Same buffers, checks,
+ * numerics and results as the synchronous call of the same name without _async (host or device
+ * buffers). The whole job is queued on the context's stream -- A in (through pinned staging when A is
+ * pageable host memory), the kernels, C out (to pinned staging when C is pageable) -- and the call
+ * returns; ork_async_wait waits for it, copies staged results into C, and returns the job's status
+ * (0 ok, -1 on any error the synchronous call would report) and frees the handle. No thread is
+ * created. A launcher returns NULL for a NULL context or weight, M < 1, an int8 run on a weight of
+ * another kind, an empty or NULL task list (the reference's refusals), or when a job is already in
+ * flight on the context; ork_async_wait(NULL) returns -1. Contract (the reference's, enforced here):
+ * one job in flight per context; until its wait every other run on the context returns -1; A, C and
+ * the task arrays stay valid until the wait. */
+typedef struct ork_async ork_async;
+ork_async *ork_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *A, float *C);
+ork_async *ork_i8_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
+ork_async *ork_i4_mm_run_async(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
+ork_async *ork_i8_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
+ork_async *ork_i4_mm_run_chain_async(ork_npu *ctx, int S, const ork_mm_task_i4 *tasks);
+ork_async *ork_i8_mm_run_stream_async(ork_npu *ctx, int S, const ork_mm_task_i8 *tasks);
+ork_async *ork_i4_mm_run_stream_async(ork_npu *ctx, int S, const ork_mm_task_i4 *tasks);
+int ork_async_wait(ork_async *h);
+/* include/ork/chain.h:146. The CPU (sched_getcpu) of the thread that queued the context's latest
+ * ork_async job, -1 if none (the reference records its worker thread's CPU). */
+int ork_npu_last_async_cpu(ork_npu *ctx);
 
 /* include/ork/chain.h:105-110. One decode token through a Llama/Qwen-style layer: x fp32 [D] ->
  * RMSNorm(attn_norm) -> per-tensor int8 -> q, k, v projections -> per head: RMSNorm(q_norm), RoPE NeoX at
@@ -207,7 +235,7 @@ int ork_mm_collect(ork_npu *ctx, int ticket, void *C);
  * query heads) -> int8 -> o projection -> residual -> RMSNorm(ffn_norm) -> int8 -> gate, up -> SwiGLU ->
  * int8 -> down -> residual = x_out [D]. The arithmetic of src/npu/i8/chain.c:106-122 with the glue of
  * src/spine_kernels.h; the k and v projections are computed as in the reference but the caches are only
- * read (see ork_i8_mm_layer_async in ork_b200.h for the appending form). Weights: int8-compute weights
+ * read (see ork_b200_i8_mm_layer_async in ork_b200.h for the appending form). Weights: int8-compute weights
  * (wq D x H*dk, wk / wv D x Hkv*dk, wo H*dk x D, wg / wu D x Nff, wd Nff x D). dv must equal dk. Host or
  * device pointers; synchronous. 0 ok, -3 on bad arguments or shapes, -1 on a device error. */
 struct ork_layer_dims {

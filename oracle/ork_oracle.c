@@ -408,6 +408,20 @@ ORC_API int orc_threads(void)
 #endif
 }
 
+/* Sets the OpenMP team size of the parallel regions the calling thread starts next, in this library and
+ * in oracle/_ref (one OpenMP runtime per process): the CPU baselines use every host core even where the
+ * launcher exported OMP_NUM_THREADS=1 (torchrun does). Returns the new team size. */
+ORC_API int orc_set_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
+
 /* ---------------------------------------------------------------------------------------------------
  * Whole decode layer. src/npu/i8/chain.c:106-122 (ork_i8_mm_layer, direct path) over the glue kernels of
  * src/spine_kernels.h:19-38, restated: RMSNorm y = x * (1/sqrtf(sum(x^2)/D + eps)) * g (sum sequential);

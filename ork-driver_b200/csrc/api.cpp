@@ -136,6 +136,42 @@ bool is_device_ptr(const void *p, int device) {
   return at.type == cudaMemoryTypeDevice && at.device == device;
 }
 
+bool device_ptrs_ok(const ork_npu *c, const char *name, std::initializer_list<const void *> ps) {
+  for (const void *p : ps)
+    if (p && !is_device_ptr(p, c->device)) {
+      fprintf(stderr, "[ork] ERROR %s: %p is not device memory of GPU %d (this entry point takes device pointers)\n",
+              name, p, c->device);
+      return false;
+    }
+  return true;
+}
+
+bool async_in_flight(const ork_npu *c, const char *name) {
+  if (!c || !c->async_busy) return false;
+  fprintf(stderr, "[ork] ERROR %s: an ork_async job is in flight on this context; ork_async_wait it first\n",
+          name);
+  return true;
+}
+
+static int env_int(const char *name, int unset) {
+  const char *e = getenv(name);
+  return e ? atoi(e) : unset;
+}
+
+Tuning tuning_from_env() {
+  Tuning t;
+  t.tc_tn = env_int("ORKB_TC_TN", 0);
+  t.tc_na = env_int("ORKB_TC_NA", 0);
+  t.tc_stages = env_int("ORKB_TC_STAGES", 0);
+  t.tc_pair = env_int("ORKB_TC_PAIR", 0);
+  t.tc_sk = env_int("ORKB_TC_SK", 0);
+  t.gemv_kind = env_int("ORKB_GEMV_KIND", -1);
+  t.gemv_cpw = env_int("ORKB_GEMV_CPW", 0);
+  t.gemv_tr = env_int("ORKB_GEMV_TR", 0);
+  t.layer_fused = env_int("ORKB_LAYER_FUSED", -1);
+  return t;
+}
+
 ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host_resident, size_t bytes) {
   if (!c) return nullptr;
   DeviceGuard dg(c->device);
@@ -165,7 +201,7 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
 
 // Launch one matmul on device buffers (A, C already on the context's GPU).
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
-  RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt};
+  RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt, &c->tune};
   int n = 0;
   const int route = route_for(c, w, M);
   if (route < 0) {
@@ -188,6 +224,7 @@ namespace {
 // The synchronous run shared by the three public run functions.
 int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype, const char *name) {
   if (!c || !w || !A || !C || M < 1) return -1;
+  if (async_in_flight(c, name)) return -1;
   if (w->dtype != want_dtype) return -1;  // src/npu/i8/run.c:150, src/npu.c:1829
   const size_t esz = want_dtype == DT_F16 ? 2 : 1;
   const size_t abytes = (size_t)M * w->K * esz, cbytes = (size_t)M * w->N * 4;
@@ -224,12 +261,13 @@ int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype
   return 0;
 }
 
-int run_async(ork_npu *c, ork_w *w, int M, const void *dA, void *dC, int want_dtype) {
+int run_async(ork_npu *c, ork_w *w, int M, const void *dA, void *dC, int want_dtype, const char *name) {
   if (!c || !w || !dA || !dC || M < 1 || w->dtype != want_dtype) return -1;
   const size_t esz = want_dtype == DT_F16 ? 2 : 1;
   if (overlaps(dA, (size_t)M * w->K * esz, dC, (size_t)M * w->N * 4)) return -1;
   if ((uintptr_t)dA % 16 || (uintptr_t)dC % 16) return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, name, {dA, dC})) return -1;
   return launch(c, w, M, dA, dC);
 }
 
@@ -262,6 +300,7 @@ ork_npu *ork_npu_init(void) {
   ork_npu *c = new (std::nothrow) ork_npu;
   if (!c) return nullptr;
   c->device = dev;
+  c->tune = tuning_from_env();
   if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
     return nullptr;
@@ -289,6 +328,8 @@ void ork_npu_free(ork_npu *c) {
     if (c->dL) cudaFree(c->dL);
     if (c->dX) cudaFree(c->dX);
     if (c->dG) cudaFree(c->dG);
+    if (c->hP) cudaFreeHost(c->hP);
+    if (c->async_ev) cudaEventDestroy(c->async_ev);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;
@@ -462,14 +503,20 @@ void ork_i8_mm_run_cpu(int M, int K, int N, const int8_t *A, const int8_t *B, in
 
 // ---- ork_b200.h ----------------------------------------------------------------------------------
 
-int ork_i8_mm_run_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int32_t *dC) {
-  return run_async(c, w, M, dA, dC, DT_I8);
+int ork_b200_i8_mm_run_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int32_t *dC) {
+  return run_async(c, w, M, dA, dC, DT_I8, "ork_b200_i8_mm_run_async");
 }
-int ork_i4_mm_run_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int32_t *dC) {
-  return run_async(c, w, M, dA, dC, DT_I4);
+int ork_b200_i4_mm_run_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int32_t *dC) {
+  return run_async(c, w, M, dA, dC, DT_I4, "ork_b200_i4_mm_run_async");
 }
-int ork_f16_mm_run_async(ork_npu *c, ork_w *w, int M, const ork_f16 *dA, float *dC) {
-  return run_async(c, w, M, dA, dC, DT_F16);
+int ork_b200_f16_mm_run_async(ork_npu *c, ork_w *w, int M, const ork_f16 *dA, float *dC) {
+  return run_async(c, w, M, dA, dC, DT_F16, "ork_b200_f16_mm_run_async");
+}
+
+int ork_b200_reload_tuning(ork_npu *c) {
+  if (!c) return -1;
+  c->tune = tuning_from_env();
+  return 0;
 }
 
 int ork_b200_sync(ork_npu *c) {

@@ -253,6 +253,7 @@ int ork_b200_rows_q8_async(ork_npu *c, const float *x, const float *g, int rows,
                            float *scales) {
   if (!c || !x || !q8 || rows < 1 || n < 1 || n > kNormThreads * kNormPer) return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, "ork_b200_rows_q8_async", {x, g, q8, scales})) return -1;
   rows_q8_kernel<<<rows, kNormThreads, 0, c->stream>>>(x, g, n, norm, q8, scales);
   return glue_launched(c, "ork_b200_rows_q8_async");
 }
@@ -261,6 +262,7 @@ int ork_b200_rows_swiglu_q8_async(ork_npu *c, const int32_t *Cg, const int32_t *
                                   const float *scales_in, int8_t *q8, float *scales) {
   if (!c || !Cg || !Cu || !scales_in || !q8 || rows < 1 || n < 1 || n > kNormThreads * kNormPer) return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, "ork_b200_rows_swiglu_q8_async", {Cg, Cu, scales_in, q8, scales})) return -1;
   rows_swiglu_q8_kernel<<<rows, kNormThreads, 0, c->stream>>>(Cg, Cu, n, scales_in, q8, scales);
   return glue_launched(c, "ork_b200_rows_swiglu_q8_async");
 }
@@ -269,6 +271,7 @@ int ork_b200_rows_dequant_async(ork_npu *c, const int32_t *C, int rows, int n, c
                                 const float *res, float *out) {
   if (!c || !C || !scales || !out || rows < 1 || n < 1) return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, "ork_b200_rows_dequant_async", {C, scales, bs, res, out})) return -1;
   const size_t total = (size_t)rows * n;
   const int blocks = (int)std::min<size_t>(148 * 8, (total + 255) / 256);
   rows_dequant_kernel<<<blocks, 256, 0, c->stream>>>(C, rows, n, scales, bs, res, out);
@@ -282,6 +285,7 @@ int ork_b200_rows_qk_rope_async(ork_npu *c, const float *q, const float *k, cons
       pos0 + T > hstride)
     return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, "ork_b200_rows_qk_rope_async", {q, k, v, q_norm, k_norm, q_out, Kc, Vc})) return -1;
   const int blocks = (T * (H + Hkv) + 3) / 4;
   if (dk == 64)
     rows_qk_rope_kernel<2><<<blocks, 128, 0, c->stream>>>(q, k, v, T, H, Hkv, q_norm, k_norm, pos0, base, q_out, Kc,
@@ -300,6 +304,7 @@ int ork_b200_rows_qk_rope_async(ork_npu *c, const float *q, const float *k, cons
 int ork_b200_argmax_scaled_async(ork_npu *c, const int32_t *C, const float *bs, int n, long long *idx) {
   if (!c || !C || !bs || !idx || n < 1 || !c->dG) return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, "ork_b200_argmax_scaled_async", {C, bs, idx})) return -1;
   unsigned long long *best = reinterpret_cast<unsigned long long *>(c->dG);
   unsigned int *count = reinterpret_cast<unsigned int *>(best + 1);
   const int blocks = (int)std::min<long long>(296, ((long long)n + kPickThreads - 1) / kPickThreads);

@@ -856,7 +856,7 @@ struct TcCfg {
 // grid would exceed one wave of 148 CTAs; nibble weights past one wave use CTA-pair tiles of 256 x 192
 // (the converter work per CTA halves). Split-K (a cluster reduction through distributed shared memory)
 // pays for grids of up to 32 tiles, and for up to 64 tiles when K spans at least 32 blocks.
-TcCfg choose_tc(int fmt, int M, int K, int N) {
+TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
   TcCfg c;
   const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
   const int KB = (K * (fmt == FMT_F16 ? 2 : 1) + BK_BYTES - 1) / BK_BYTES;
@@ -893,37 +893,24 @@ TcCfg choose_tc(int fmt, int M, int K, int N) {
     if (t <= 32 && KB >= 8) c.sk = 4;
     else if (t <= 64 && KB >= 32) c.sk = 2;
   }
-  // tuning overrides, read on every launch: ORKB_TC_TN (128/192/256), ORKB_TC_NA (1/2), ORKB_TC_STAGES (3),
-  // ORKB_TC_SK (1..8)
+  // tuning overrides (the context's ORKB_TC_* values): tile width, accumulators, ring depth, split
   if (!c.swap) {
-    if (const char *e = getenv("ORKB_TC_TN")) {
-      const int v = atoi(e);
-      c.tn = (!nib && (v == 256 || v == 192)) ? v : 128;
-    }
-    if (const char *e = getenv("ORKB_TC_NA")) c.na = atoi(e) == 2 ? 2 : 1;
+    if (tu.tc_tn) c.tn = (!nib && (tu.tc_tn == 256 || tu.tc_tn == 192)) ? tu.tc_tn : 128;
+    if (tu.tc_na) c.na = tu.tc_na == 2 ? 2 : 1;
     if (c.na == 2) c.tn = 128;
   }
-  if (const char *e = getenv("ORKB_TC_STAGES")) c.stages = atoi(e);
-  // ORKB_TC_PAIR: 1 = CTA-pair tiles (swapped operands for M <= 256), 2 = pair with A on the 256-row
-  // side, 3 = pair with the weight on the 256-row side (M <= 256)
-  if (const char *e = getenv("ORKB_TC_PAIR")) {
-    const int v = atoi(e);
-    if (v >= 1 && v <= 3 && !(v == 3 && M > 256)) {
-      c.pair = true;
-      c.na = 1;
-      c.swap = v == 3 || (v == 1 && M <= 256);
-      if (c.swap) c.tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
-      else {
-        const int v = getenv("ORKB_TC_TN") ? atoi(getenv("ORKB_TC_TN")) : 256;
-        c.tn = (v == 64 || v == 128 || v == 192) ? v : 256;
-      }
-      if (c.sk > 4) c.sk = 4;
-    }
+  if (tu.tc_stages) c.stages = tu.tc_stages;
+  // tc_pair: 1 = CTA-pair tiles (swapped operands for M <= 256), 2 = pair with A on the 256-row side,
+  // 3 = pair with the weight on the 256-row side (M <= 256)
+  if (tu.tc_pair >= 1 && tu.tc_pair <= 3 && !(tu.tc_pair == 3 && M > 256)) {
+    c.pair = true;
+    c.na = 1;
+    c.swap = tu.tc_pair == 3 || (tu.tc_pair == 1 && M <= 256);
+    if (c.swap) c.tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    else c.tn = (tu.tc_tn == 64 || tu.tc_tn == 128 || tu.tc_tn == 192) ? tu.tc_tn : 256;
+    if (c.sk > 4) c.sk = 4;
   }
-  if (const char *e = getenv("ORKB_TC_SK")) {
-    const int v = atoi(e);
-    if (v >= 1 && v <= (c.pair ? 4 : 8) && v <= KB) c.sk = v;
-  }
+  if (tu.tc_sk >= 1 && tu.tc_sk <= (c.pair ? 4 : 8) && tu.tc_sk <= KB) c.sk = tu.tc_sk;
   return c;
 }
 
@@ -986,7 +973,8 @@ bool gemm_tc_supports(int fmt, int M, int K, int N) {
 
 cudaError_t launch_gemm_tc(const RunArgs &a, cudaStream_t s, bool pdl, int *launches) {
   if ((uintptr_t)a.A % 16 || (uintptr_t)a.W % 16 || (uintptr_t)a.C % 16) return cudaErrorMisalignedAddress;
-  const TcCfg c = choose_tc(a.fmt, a.M, a.K, a.N);
+  static const Tuning none;
+  const TcCfg c = choose_tc(a.fmt, a.M, a.K, a.N, a.tune ? *a.tune : none);
   cudaError_t e;
   switch (a.fmt) {
     case FMT_I8: e = dispatch<FMT_I8>(a, c, s, pdl); break;
@@ -1015,7 +1003,7 @@ ORKB_ERR_WORD_SETTER(tc_set_err_word)
 
 extern "C" int ork_b200_tc_choice(int fmt, int M, int K, int N, int *out) {
   if (!out || fmt < orkb::FMT_F16 || fmt > orkb::FMT_NF4 || M < 1 || K < 1 || N < 1) return -1;
-  const orkb::TcCfg c = orkb::choose_tc(fmt, M, K, N);
+  const orkb::TcCfg c = orkb::choose_tc(fmt, M, K, N, orkb::tuning_from_env());
   out[0] = c.swap ? 1 : 0;
   out[1] = c.tn;
   out[2] = c.sk;

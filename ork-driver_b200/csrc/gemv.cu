@@ -654,7 +654,7 @@ struct Cfg {
 // - the direct-load kernel wins where each staged CTA would carry a large activation block (M = 8 with
 //   K >= 8192: up to 2x), on nibble weights with short rows (K <= 2048, N <= 8192: 5-20%), and is the
 //   only one for rows that do not fit the staged kernel's shared memory (any K).
-Cfg choose(int fmt, int M, int K, int N) {
+Cfg choose(int fmt, int M, int K, int N, const Tuning &tu) {
   Cfg c;
   c.mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
   const size_t rowB = fmt_row_bytes(fmt, K);
@@ -668,15 +668,12 @@ Cfg choose(int fmt, int M, int K, int N) {
     c.direct = true;
     c.cpw = 2;
   }
-  if (const char *e = getenv("ORKB_GEMV_KIND")) c.direct = atoi(e) == 1 || !staged_fits;  // tuning overrides
-  if (const char *e = getenv("ORKB_GEMV_CPW")) {
-    const int v = atoi(e);
-    if (v == 1 || v == 2 || v == 4) c.cpw = v;
-  }
-  if (const char *e = getenv("ORKB_GEMV_TR")) {
-    const int v = atoi(e);
-    if ((v == 8 || v == 16 || v == 32) && (size_t)v * rowB + (size_t)c.mt * K * 2 <= 196 * 1024) c.tr = v;
-  }
+  // tuning overrides (the context's ORKB_GEMV_* values)
+  if (tu.gemv_kind >= 0) c.direct = tu.gemv_kind == 1 || !staged_fits;
+  if (tu.gemv_cpw == 1 || tu.gemv_cpw == 2 || tu.gemv_cpw == 4) c.cpw = tu.gemv_cpw;
+  if ((tu.gemv_tr == 8 || tu.gemv_tr == 16 || tu.gemv_tr == 32) &&
+      (size_t)tu.gemv_tr * rowB + (size_t)c.mt * K * 2 <= 196 * 1024)
+    c.tr = tu.gemv_tr;
   return c;
 }
 
@@ -829,7 +826,8 @@ cudaError_t launch_gemv(const RunArgs &a, cudaStream_t s, bool pdl, int *launche
   const size_t c_row = (size_t)a.N * 4;
   for (int m0 = 0; m0 < a.M; m0 += 8) {
     const int m = a.M - m0 < 8 ? a.M - m0 : 8;
-    const Cfg c = choose(a.fmt, m, a.K, a.N);
+    static const Tuning none;
+    const Cfg c = choose(a.fmt, m, a.K, a.N, a.tune ? *a.tune : none);
     const uint8_t *Ab = (const uint8_t *)a.A + (size_t)m0 * a_row;
     void *Cb = (uint8_t *)a.C + (size_t)m0 * c_row;
     cudaError_t e;
@@ -963,7 +961,7 @@ cudaError_t launch_gemv_batched(const ChainTask *t, int n, cudaStream_t s, bool 
 
 extern "C" int ork_b200_gemv_choice(int fmt, int M, int K, int N, int *out) {
   if (!out || fmt < orkb::FMT_F16 || fmt > orkb::FMT_NF4 || M < 1 || M > 8 || K < 1 || N < 1) return -1;
-  const orkb::Cfg c = orkb::choose(fmt, M, K, N);
+  const orkb::Cfg c = orkb::choose(fmt, M, K, N, orkb::tuning_from_env());
   out[0] = c.direct ? 1 : 0;
   out[1] = c.direct ? c.cpw : 0;
   out[2] = c.direct ? 0 : c.tr;

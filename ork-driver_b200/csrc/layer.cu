@@ -20,7 +20,7 @@
 // The glue uses the same formulas and operation order as the reference element by element; sums and
 // maxima are tree reductions and expf/sinf/cosf/powf are CUDA's, so results agree with the reference to
 // rounding (a quantization code can flip where a value sits on a rounding boundary).
-// Decode extension (ork_i8_mm_layer_async in ork_b200.h): the token's k (dequantized, k-normed, rotated)
+// Decode extension (ork_b200_i8_mm_layer_async in ork_b200.h): the token's k (dequantized, k-normed, rotated)
 // and v are written into the caches at slot nkv and attention covers nkv + 1 keys; the position can be
 // read from device memory so a captured graph replays across tokens.
 #include <cuda_runtime.h>
@@ -498,6 +498,16 @@ void layer_tabs_free(ork_npu *c) {
   c->ltabs = nullptr;
 }
 
+// True when this exact list of layer pointers already has a device table (its pointers were checked
+// when it was first seen).
+static bool layer_tab_seen(const ork_npu *c, const FusedLayerW *lw, int n) {
+  const LayerTabs *t = (const LayerTabs *)c->ltabs;
+  if (!t) return false;
+  for (auto &p : t->e)
+    if ((int)p.first.size() == n && !memcmp(p.first.data(), lw, sizeof(FusedLayerW) * n)) return true;
+  return false;
+}
+
 static const FusedLayerW *layer_tab(ork_npu *c, const FusedLayerW *lw, int n) {
   if (!c->ltabs) c->ltabs = new (std::nothrow) LayerTabs;
   LayerTabs *t = (LayerTabs *)c->ltabs;
@@ -538,8 +548,7 @@ int fused_enqueue(ork_npu *c, const ork_layer_dims *d, const FusedLayerW *lw, in
   if (G < 1 || G > kMaxGrid) return 1;
   for (int i = 0; i < 7; i++)
     if (W[i]->fmt != fmt) return 1;
-  if (const char *e = getenv("ORKB_LAYER_FUSED"))
-    if (atoi(e) == 0) return 1;
+  if (c->tune.layer_fused == 0) return 1;  // the context's ORKB_LAYER_FUSED=0
   FusedArgs fa = {};
   fa.D = D, fa.H = H, fa.Hkv = Hkv, fa.dk = dk, fa.F = F;
   fa.Sg = fused_splits(H, maxk, G);
@@ -774,6 +783,7 @@ int ork_i8_mm_layer(ork_npu *c, const struct ork_layer_dims *d, ork_w *wq, ork_w
                     const float *ffn_norm, const float *x, const float *Kc, const float *Vc, float *x_out) {
   ork_w *W[7] = {wq, wk, wv, wo, wg, wu, wd};
   if (!c || !attn_norm || !q_norm || !ffn_norm || !x || !Kc || !Vc || !x_out || !dims_ok(d, W, nullptr)) return -3;
+  if (async_in_flight(c, "ork_i8_mm_layer")) return -1;
   DeviceGuard dg(c->device);
   const size_t D = d->D, dk = d->dk, cache = (size_t)d->Hkv * d->nkv * dk;
   // host inputs are staged into one device block: x, norms, K and V caches, x_out
@@ -811,17 +821,21 @@ int ork_i8_mm_layer(ork_npu *c, const struct ork_layer_dims *d, ork_w *wq, ork_w
   return 0;
 }
 
-int ork_i8_mm_layer_async(ork_npu *c, const struct ork_layer_dims *d, ork_w *wq, ork_w *wk, ork_w *wv, ork_w *wo,
+int ork_b200_i8_mm_layer_async(ork_npu *c, const struct ork_layer_dims *d, ork_w *wq, ork_w *wk, ork_w *wv, ork_w *wo,
                           ork_w *wg, ork_w *wu, ork_w *wd, const float *attn_norm, const float *q_norm,
                           const float *ffn_norm, const float *x, float *Kc, float *Vc, float *x_out,
                           const ork_b200_layer_kv *kv) {
   ork_w *W[7] = {wq, wk, wv, wo, wg, wu, wd};
   if (!c || !attn_norm || !q_norm || !ffn_norm || !x || !Kc || !Vc || !x_out || !dims_ok(d, W, kv)) return -3;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, "ork_b200_i8_mm_layer_async",
+                      {attn_norm, q_norm, ffn_norm, x, Kc, Vc, x_out, kv ? kv->k_norm : nullptr,
+                       kv ? (const void *)kv->dpos : nullptr}))
+    return -3;
   return layer_enqueue(c, d, W, attn_norm, q_norm, ffn_norm, x, Kc, Vc, x_out, kv);
 }
 
-int ork_i8_mm_layers_async(ork_npu *c, const struct ork_layer_dims *d, int n, const ork_b200_layer_w *L,
+int ork_b200_i8_mm_layers_async(ork_npu *c, const struct ork_layer_dims *d, int n, const ork_b200_layer_w *L,
                            const float *x, float *x_out, const ork_b200_layer_kv *kv) {
   if (!c || !L || !x || !x_out || n < 1 || n > 1024) return -3;
   for (int l = 0; l < n; l++) {
@@ -841,6 +855,14 @@ int ork_i8_mm_layers_async(ork_npu *c, const struct ork_layer_dims *d, int n, co
     tab[l].attn_norm = y.attn_norm, tab[l].q_norm = y.q_norm, tab[l].k_norm = y.k_norm;
     tab[l].ffn_norm = y.ffn_norm, tab[l].Kc = y.Kc, tab[l].Vc = y.Vc;
   }
+  // device pointers only: the per-layer ones are checked once per distinct list of layers
+  if (!device_ptrs_ok(c, "ork_b200_i8_mm_layers_async", {x, x_out, kv ? (const void *)kv->dpos : nullptr}))
+    return -3;
+  if (!layer_tab_seen(c, tab.data(), n))
+    for (int l = 0; l < n; l++)
+      if (!device_ptrs_ok(c, "ork_b200_i8_mm_layers_async",
+                          {L[l].attn_norm, L[l].q_norm, L[l].ffn_norm, L[l].k_norm, L[l].Kc, L[l].Vc}))
+        return -3;
   ork_w *W0[7] = {L[0].wq, L[0].wk, L[0].wv, L[0].wo, L[0].wg, L[0].wu, L[0].wd};
   const int fr = fused_enqueue(c, d, tab.data(), n, W0[0]->fmt, W0, x, x_out, kv);
   if (fr != 1) return fr;

@@ -26,6 +26,19 @@ inline size_t fmt_row_bytes(int fmt, int K) {
 // negneg = -lut[0..7] and pos = lut[8..15].
 extern const int8_t kNf4Lut[16];
 
+// Tuning overrides of the kernel choice, from the ORKB_* environment variables. A context takes them
+// once, when it is created (or again on ork_b200_reload_tuning), never per launch; 0 / -1 leave the
+// router's own choice:
+//   tc_tn ORKB_TC_TN (128/192/256), tc_na ORKB_TC_NA (1/2), tc_stages ORKB_TC_STAGES, tc_pair ORKB_TC_PAIR
+//   (1..3), tc_sk ORKB_TC_SK (1..8); gemv_kind ORKB_GEMV_KIND (0 staged / 1 direct), gemv_cpw
+//   ORKB_GEMV_CPW (1/2/4), gemv_tr ORKB_GEMV_TR (8/16/32); layer_fused ORKB_LAYER_FUSED (0 multi-launch).
+struct Tuning {
+  int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0;
+  int gemv_kind = -1, gemv_cpw = 0, gemv_tr = 0;
+  int layer_fused = -1;
+};
+Tuning tuning_from_env();
+
 // ---- kernel launchers (gemv.cu, gemm_sm100.cu) --------------------------------------------------
 struct RunArgs {
   const void *W;   // resident weight
@@ -33,6 +46,7 @@ struct RunArgs {
   void *C;         // device output [M][N] (int32 or fp32)
   int M, K, N;
   int fmt;
+  const Tuning *tune = nullptr;  // the context's tuning overrides (nullptr: none)
 };
 
 // Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M). Two kernels:

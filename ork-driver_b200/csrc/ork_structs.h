@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <initializer_list>
+
 #include "ork_internal.h"
 #include "ork_b200.h"
 
@@ -26,9 +28,16 @@ struct ork_npu {
   size_t capX = 0;
   void *ltabs = nullptr; // device tables of persistent-layer pointer lists (layer.cu)
   void *dG = nullptr;    // 16 bytes, zero between calls: the argmax's running key and CTA count (decode_glue.cu)
+  void *hP = nullptr;    // pinned host staging of the ork_async runs (A in, C out), chain.cpp
+  size_t capP = 0;
+  cudaEvent_t async_ev = nullptr;  // completion of the ork_async job in flight
+  bool async_busy = false;         // an ork_async job is in flight (one at a time, as in the reference)
+  int last_async_cpu = -1;         // sched_getcpu() of the thread that queued the latest ork_async job
   bool pdl = true;
   int force_route = -1;
   uint64_t launches = 0;
+  // tuning variables of the kernel choice (ORKB_*), read once when the context is created
+  orkb::Tuning tune;
 };
 
 struct ork_w {
@@ -61,6 +70,14 @@ struct DeviceGuard {
 bool grow(void **p, size_t *cap, size_t need);
 // Memory of the context's GPU (or managed memory) that a kernel can use in place.
 bool is_device_ptr(const void *p, int device);
+// The device-pointer entry points (include/ork_b200.h) launch kernels on their pointers directly: every
+// non-NULL pointer in `ps` must be memory of the context's GPU (or managed memory), else a message
+// naming the call and false, before anything is queued.
+bool device_ptrs_ok(const ork_npu *c, const char *name, std::initializer_list<const void *> ps);
+// An ork_async job (chain.cpp) owns the context's staging buffers until ork_async_wait: every other run
+// on the context is refused meanwhile (message + true), the reference's one-job-in-flight contract
+// (include/ork/chain.h:126-133) made a checked error.
+bool async_in_flight(const ork_npu *c, const char *name);
 bool overlaps(const void *a, size_t an, const void *b, size_t bn);
 // Enqueues one decode layer on device pointers (layer.cu); W = {q, k, v, o, gate, up, down}.
 int layer_enqueue(ork_npu *c, const struct ork_layer_dims *d, ork_w *const *W, const float *attn_norm,

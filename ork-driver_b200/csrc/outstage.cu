@@ -138,6 +138,7 @@ int stage_sync(ork_npu *c, ork_w *w, int M, const int8_t *A, const int8_t *G, vo
   if (!c || !w || !A || !C || (mode == OUT_EWMUL && !G)) return -1;
   if (const int r = stage_check(w, mult, shift)) return r;
   if (M <= 0) return 0;
+  if (async_in_flight(c, name)) return -1;
   const size_t K = w->K, N = w->N, esz = mode == OUT_I16 ? 2 : 1;
   const size_t abytes = (size_t)M * K, cbytes = (size_t)M * N * esz, gbytes = mode == OUT_EWMUL ? (size_t)M * N : 0;
   if (overlaps(A, abytes, C, cbytes) || (gbytes && overlaps(G, gbytes, C, cbytes))) {
@@ -184,6 +185,7 @@ int stage_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const int8_t *dG,
   if ((uintptr_t)dA % 16 || (uintptr_t)dC % esz) return -1;
   if (overlaps(dA, (size_t)M * w->K, dC, (size_t)M * w->N * esz)) return -1;
   DeviceGuard dg(c->device);
+  if (!device_ptrs_ok(c, name, {dA, dG, dC})) return -1;
   return stage_enqueue(c, w, M, dA, dG, dC, OutStage{mode, mult, shift, nullptr}, name);
 }
 
@@ -204,17 +206,17 @@ int ork_i8_mm_run_ewmul(ork_npu *c, ork_w *w, int M, const int8_t *A, const int8
   return stage_sync(c, w, M, A, G, C, OUT_EWMUL, mult, shift, "ork_i8_mm_run_ewmul");
 }
 
-int ork_i8_mm_run_out8_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int8_t *dC, int mult, int shift) {
-  return stage_async(c, w, M, dA, nullptr, dC, OUT_I8, mult, shift, "ork_i8_mm_run_out8_async");
+int ork_b200_i8_mm_run_out8_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int8_t *dC, int mult, int shift) {
+  return stage_async(c, w, M, dA, nullptr, dC, OUT_I8, mult, shift, "ork_b200_i8_mm_run_out8_async");
 }
 
-int ork_i8_mm_run_out16_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, short *dC, int mult, int shift) {
-  return stage_async(c, w, M, dA, nullptr, dC, OUT_I16, mult, shift, "ork_i8_mm_run_out16_async");
+int ork_b200_i8_mm_run_out16_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, short *dC, int mult, int shift) {
+  return stage_async(c, w, M, dA, nullptr, dC, OUT_I16, mult, shift, "ork_b200_i8_mm_run_out16_async");
 }
 
-int ork_i8_mm_run_ewmul_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const int8_t *dG, int8_t *dC, int mult,
+int ork_b200_i8_mm_run_ewmul_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const int8_t *dG, int8_t *dC, int mult,
                               int shift) {
-  return stage_async(c, w, M, dA, dG, dC, OUT_EWMUL, mult, shift, "ork_i8_mm_run_ewmul_async");
+  return stage_async(c, w, M, dA, dG, dC, OUT_EWMUL, mult, shift, "ork_b200_i8_mm_run_ewmul_async");
 }
 
 // out[m][n] = clamp_i8(rne(up[m][n] * silu[m][n] * mult / 2^shift)); us = the kernel's device time.
@@ -226,6 +228,7 @@ int ork_i8_npu_ewmul(ork_npu *c, const int8_t *up, const int8_t *silu, int M, in
   if (mult < 0 || mult > 0x7fff || shift < 0 || shift > 31) return -2;  // run.c:519
   const size_t n = (size_t)M * N, pad = (n + 255) & ~(size_t)255;
   if (overlaps(up, n, out, n) || overlaps(silu, n, out, n)) return -1;
+  if (async_in_flight(c, "ork_i8_npu_ewmul")) return -1;
   DeviceGuard dg(c->device);
   const bool dev = is_device_ptr(up, c->device) && is_device_ptr(silu, c->device) && is_device_ptr(out, c->device);
   const int8_t *da = up, *db = silu;

@@ -144,6 +144,7 @@ int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, 
   const PeerTable &t = p->host;
   if (w->N + t.col0 > t.ldc || w->N != t.ctas) return -1;  // the table's shard width
   DeviceGuard dg(c->device);
+  if ((uintptr_t)dA % 16 || !device_ptrs_ok(c, name, {dA})) return -1;
   if (!grow(&c->dC, &c->capC, (size_t)M * w->N * 4)) return -1;
   if (launch(c, w, M, dA, c->dC)) return -1;
   cudaLaunchConfig_t cfg = {};
@@ -252,12 +253,12 @@ void ork_b200_peers_destroy(ork_b200_peers *p) {
   delete p;
 }
 
-int ork_i8_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
-  return peers_run(c, w, M, dA, p, DT_I8, "ork_i8_mm_run_peers_async");
+int ork_b200_i8_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
+  return peers_run(c, w, M, dA, p, DT_I8, "ork_b200_i8_mm_run_peers_async");
 }
 
-int ork_i4_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
-  return peers_run(c, w, M, dA, p, DT_I4, "ork_i4_mm_run_peers_async");
+int ork_b200_i4_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
+  return peers_run(c, w, M, dA, p, DT_I4, "ork_b200_i4_mm_run_peers_async");
 }
 
 int ork_b200_copy(ork_npu *c, void *dst, const void *src, size_t bytes) {

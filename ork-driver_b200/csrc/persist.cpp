@@ -137,12 +137,14 @@ int grouped_run(ork_npu *c, ork_w *w, int M, const int8_t *A, const float *aS, c
             (const void *)A, abytes, (void *)C, cbytes);
     return -1;
   }
+  if (!async && async_in_flight(c, name)) return -1;
   DeviceGuard dg(c->device);
   const void *dA = A;
   const float *daS = aS, *dbS = bS;
   float *dC = C;
   if (async) {
     if ((uintptr_t)A % 16 || (uintptr_t)C % 4 || (uintptr_t)aS % 4 || (uintptr_t)bS % 4) return -1;
+    if (!device_ptrs_ok(c, name, {A, aS, bS, C})) return -1;
   } else {
     if (!(is_device_ptr(A, c->device) && (uintptr_t)A % 16 == 0)) {
       if (!grow(&c->dA, &c->capA, abytes)) return -1;
@@ -299,14 +301,14 @@ int ork_i8_mm_run_grouped(ork_npu *c, ork_w *w, int M, const int8_t *A, const fl
   return grouped_run(c, w, M, A, aScale, bScale, C, DT_I8, false, "ork_i8_mm_run_grouped");
 }
 
-int ork_i4_mm_run_grouped_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const float *daScale,
+int ork_b200_i4_mm_run_grouped_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const float *daScale,
                                 const float *dbScale, float *dC) {
-  return grouped_run(c, w, M, dA, daScale, dbScale, dC, DT_I4, true, "ork_i4_mm_run_grouped_async");
+  return grouped_run(c, w, M, dA, daScale, dbScale, dC, DT_I4, true, "ork_b200_i4_mm_run_grouped_async");
 }
 
-int ork_i8_mm_run_grouped_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const float *daScale,
+int ork_b200_i8_mm_run_grouped_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, const float *daScale,
                                 const float *dbScale, float *dC) {
-  return grouped_run(c, w, M, dA, daScale, dbScale, dC, DT_I8, true, "ork_i8_mm_run_grouped_async");
+  return grouped_run(c, w, M, dA, daScale, dbScale, dC, DT_I8, true, "ork_b200_i8_mm_run_grouped_async");
 }
 
 }  // extern "C"

@@ -45,13 +45,13 @@ SIGNATURES = [
     ("ork_i8_mm_run", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i4_mm_run", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_cpu", None, [_i, _i, _i, _vp, _vp, _vp]),
-    ("ork_i8_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_i8_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_out8", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
     ("ork_i8_mm_run_out16", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
     ("ork_i8_mm_run_ewmul", _i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
-    ("ork_i8_mm_run_out8_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
-    ("ork_i8_mm_run_out16_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
-    ("ork_i8_mm_run_ewmul_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
+    ("ork_b200_i8_mm_run_out8_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+    ("ork_b200_i8_mm_run_out16_async", _i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+    ("ork_b200_i8_mm_run_ewmul_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
     ("ork_i8_npu_ewmul", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, C.POINTER(C.c_double)]),
     ("ork_b200_sym_alloc", _vp, [_vp, _sz, _vp]),
     ("ork_b200_sym_free", _i, [_vp, _vp]),
@@ -59,12 +59,12 @@ SIGNATURES = [
     ("ork_b200_sym_close", _i, [_vp, _vp]),
     ("ork_b200_peers_create", _vp, [_vp, _i, _i, C.POINTER(_vp), C.POINTER(_vp), _i, _i, _i]),
     ("ork_b200_peers_destroy", None, [_vp]),
-    ("ork_i8_mm_run_peers_async", _i, [_vp, _vp, _i, _vp, _vp]),
-    ("ork_i4_mm_run_peers_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_i8_mm_run_peers_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_i4_mm_run_peers_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_b200_peers_wait_async", _i, [_vp, _vp]),
     ("ork_b200_copy", _i, [_vp, _vp, _vp, _sz]),
-    ("ork_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
-    ("ork_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_noalloc", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_pack_hdr_bytes", _sz, []),
     ("ork_w_dump", _sz, [_vp, _vp, _sz]),
@@ -79,18 +79,18 @@ SIGNATURES = [
     ("ork_w_set_group", _i, [_vp, _i]),
     ("ork_i4_mm_run_grouped", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     ("ork_i8_mm_run_grouped", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
-    ("ork_i4_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
-    ("ork_i8_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_b200_i4_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_b200_i8_mm_run_grouped_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     ("ork_i8_mm_run_chain", _i, [_vp, _i, _vp]),
     ("ork_i8_mm_run_stream", _i, [_vp, _i, _vp]),
-    ("ork_i8_mm_run_chain_async", _i, [_vp, _i, _vp]),
+    ("ork_b200_i8_mm_run_chain_async", _i, [_vp, _i, _vp]),
     ("ork_i4_mm_run_chain", _i, [_vp, _i, _vp]),
     ("ork_i4_mm_run_experts", _i, [_vp, _vp, _i, _i]),
     ("ork_mm_submit", _i, [_vp, _vp, _i, _vp]),
     ("ork_mm_collect", _i, [_vp, _i, _vp]),
     ("ork_i8_mm_layer", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7),
-    ("ork_i8_mm_layer_async", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7 + [_vp]),
-    ("ork_i8_mm_layers_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    ("ork_b200_i8_mm_layer_async", _i, [_vp, _vp] + [_vp] * 7 + [_vp] * 7 + [_vp]),
+    ("ork_b200_i8_mm_layers_async", _i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     ("ork_b200_rmsnorm_q8_async", _i, [_vp, _vp, _vp, _i, _vp, _vp]),
     ("ork_b200_argmax_scaled_async", _i, [_vp, _vp, _vp, _i, _vp]),
     ("ork_b200_rows_q8_async", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
@@ -111,6 +111,17 @@ SIGNATURES = [
     ("ork_b200_force_route", _i, [_vp, _i]),
     ("ork_b200_tc_choice", _i, [_i, _i, _i, _i, _vp]),
     ("ork_b200_gemv_choice", _i, [_i, _i, _i, _i, _vp]),
+    ("ork_b200_reload_tuning", _i, [_vp]),
+    ("ork_i4_mm_run_stream", _i, [_vp, _i, _vp]),
+    ("ork_mm_run_async", _vp, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_i8_mm_run_async", _vp, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_i4_mm_run_async", _vp, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_i8_mm_run_chain_async", _vp, [_vp, _i, _vp]),
+    ("ork_i4_mm_run_chain_async", _vp, [_vp, _i, _vp]),
+    ("ork_i8_mm_run_stream_async", _vp, [_vp, _i, _vp]),
+    ("ork_i4_mm_run_stream_async", _vp, [_vp, _i, _vp]),
+    ("ork_async_wait", _i, [_vp]),
+    ("ork_npu_last_async_cpu", _i, [_vp]),
 ]
 
 
@@ -267,7 +278,7 @@ class LayerKV(C.Structure):
 
 
 class LayerW(C.Structure):
-    """ork_b200_layer_w (include/ork_b200.h): one layer of ork_i8_mm_layers_async."""
+    """ork_b200_layer_w (include/ork_b200.h): one layer of ork_b200_i8_mm_layers_async."""
     _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "attn_norm", "q_norm",
                                           "ffn_norm", "k_norm", "Kc", "Vc")]
 

@@ -75,7 +75,7 @@ class ShardedLinear:
     def forward(self, A_dev, C_local, dist, C_full=None):
         L = self.ctx.L
         M = A_dev.shape[0]
-        fn = L.ork_i4_mm_run_async if self.w.kind == "i4" else L.ork_i8_mm_run_async
+        fn = L.ork_b200_i4_mm_run_async if self.w.kind == "i4" else L.ork_b200_i8_mm_run_async
         if fn(self.ctx.ctx, self.w.h, M, A_dev.data_ptr(), C_local.data_ptr()) != 0:
             raise RuntimeError("sharded matmul launch failed")
         return gather_columns(C_local, dist, out=C_full)

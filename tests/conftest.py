@@ -33,3 +33,23 @@ def env_clean(monkeypatch):
     monkeypatch.delenv("ORK_NF4", raising=False)
     monkeypatch.delenv("ORK_SR", raising=False)
     return monkeypatch
+
+
+@pytest.fixture
+def tune(ctx, monkeypatch):
+    """tune(name, value): sets one ORKB_* kernel-choice variable for this test and has the session
+    context take it (the library reads its tuning variables once per context: ork_b200_reload_tuning).
+    Afterwards every ORKB_* variable is cleared and the context re-reads the clean environment."""
+    import ork_b200
+
+    L = ork_b200.lib()
+
+    def set_(name, value):
+        assert name.startswith("ORKB_")
+        monkeypatch.setenv(name, str(value))
+        assert L.ork_b200_reload_tuning(ctx.ctx) == 0
+
+    yield set_
+    for k in [k for k in os.environ if k.startswith("ORKB_")]:
+        monkeypatch.delenv(k)
+    L.ork_b200_reload_tuning(ctx.ctx)

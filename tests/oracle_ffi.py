@@ -45,6 +45,8 @@ def restated():
         lib.orc_gen_rnd_f16.argtypes = [C.POINTER(C.c_uint32), C.c_void_p, C.c_size_t]
         lib.orc_nf4_lut.argtypes = [C.c_void_p]
         lib.orc_threads.restype = C.c_int
+        lib.orc_set_threads.restype = C.c_int
+        lib.orc_set_threads.argtypes = [C.c_int]
         lib.orc_swiglu_q8.restype = C.c_float
         lib.orc_swiglu_q8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p]
         lib.orc_rms_q8.restype = C.c_float

@@ -107,3 +107,52 @@ def test_cpu_matmul_entry_is_exact():
     Cm = np.zeros((5, 64), np.int32)
     ork_b200.lib().ork_i8_mm_run_cpu(5, 96, 64, A.ctypes.data, B.ctypes.data, Cm.ctypes.data)
     assert np.array_equal(Cm, gemm_i32(A, B))
+
+
+def _exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", ork_b200.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    return {ln.split()[-1] for ln in out.splitlines() if " T " in ln and ln.split()[-1].startswith("ork_")}
+
+
+def test_shared_names_have_the_reference_prototypes():
+    """A caller that binds a symbol by its ork-driver name (a ggml-ork backend, an FFI table) must get the
+    reference's function: every exported name that ork-driver's public headers also declare has exactly
+    the reference's return and parameter types (tests/golden/reference_prototypes.json, written from the
+    reference's include/ork_npu.h and include/ork/*.h by tests/golden/make_reference_prototypes.py)."""
+    import json
+
+    from cproto import prototypes
+
+    ref = json.load(open(os.path.join(ROOT, "tests", "golden", "reference_prototypes.json")))["prototypes"]
+    ours = prototypes([open(os.path.join(ROOT, "include", h)).read() for h in ("ork_npu.h", "ork_b200.h")])
+    shared = sorted(_exported() & set(ref))
+    assert len(shared) >= 50, shared
+    bad = {n: (ours.get(n), ref[n]) for n in shared if ours.get(n) != ref[n]}
+    assert not bad, bad
+
+
+def test_b200_additions_are_prefixed():
+    """Names this library adds beyond the reference's API live under ork_b200_ (ork_i8_mm_run_noalloc, an
+    addition the reference has no name for either, is the one exception), so no future or unread part
+    of the reference's API can collide with them."""
+    import json
+
+    ref = json.load(open(os.path.join(ROOT, "tests", "golden", "reference_prototypes.json")))["prototypes"]
+    extra = sorted(n for n in _exported() - set(ref) if not n.startswith("ork_b200_"))
+    assert extra == ["ork_i8_mm_run_noalloc"], extra
+
+
+def test_async_launchers_refuse_like_the_reference():
+    """The ork_async launchers' NULL refusals (src/npu.c:2212-2222, src/npu/i8/run.c:778-784) and
+    ork_async_wait(NULL) == -1, without a device."""
+    L = ork_b200.lib()
+    for fn in (L.ork_mm_run_async, L.ork_i8_mm_run_async, L.ork_i4_mm_run_async):
+        assert not fn(None, None, 1, None, None)
+    for fn in (L.ork_i8_mm_run_chain_async, L.ork_i4_mm_run_chain_async, L.ork_i8_mm_run_stream_async,
+               L.ork_i4_mm_run_stream_async):
+        assert not fn(None, 1, None)
+    assert L.ork_async_wait(None) == -1
+    assert L.ork_npu_last_async_cpu(None) == -1
+    assert L.ork_i4_mm_run_stream(None, 1, None) == -1
+    assert L.ork_b200_reload_tuning(None) == -1

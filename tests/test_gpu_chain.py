@@ -99,7 +99,7 @@ def test_chain_async_device_pointers_and_stream_alias(ctx):
     tC = [torch.zeros((4, s[1] + 8), dtype=torch.int32, device=dev) for s in shapes]
     arr = (TaskI8 * 3)(*[TaskI8(w.h, 4, a.data_ptr(), c.data_ptr(), s[1] + 8) for w, a, c, s in zip(ws, tA, tC, shapes)])
     torch.cuda.synchronize()
-    assert L.ork_i8_mm_run_chain_async(ctx.ctx, 3, arr) == 0
+    assert L.ork_b200_i8_mm_run_chain_async(ctx.ctx, 3, arr) == 0
     assert L.ork_b200_sync(ctx.ctx) == 0
     for B, A, c, s in zip(Bs, As, tC, shapes):
         got = c.cpu().numpy()

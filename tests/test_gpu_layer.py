@@ -35,8 +35,8 @@ DIMS = [dict(D=256, H=4, Hkv=2, dk=64, dv=64, Nff=512, nkv=17, pos=17),
 
 
 @pytest.fixture(params=["fused", "multi"])
-def path(request, monkeypatch):
-    monkeypatch.setenv("ORKB_LAYER_FUSED", "1" if request.param == "fused" else "0")
+def path(request, tune):
+    tune("ORKB_LAYER_FUSED", "1" if request.param == "fused" else "0")
     return request.param
 
 
@@ -131,7 +131,7 @@ def test_layer_decode_extension_graph_replay(ctx, path, p0, cap):
     stream = torch.cuda.ExternalStream(L.ork_b200_stream(ctx.ctx))
 
     def step():
-        assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
+        assert L.ork_b200_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
                                        t["qn"].data_ptr(), t["fn"].data_ptr(), t["x"].data_ptr(),
                                        t["K"].data_ptr(), t["V"].data_ptr(), xo.data_ptr(), C.byref(kv)) == 0
         t["x"].copy_(xo)  # the next step's input is this step's output
@@ -140,7 +140,7 @@ def test_layer_decode_extension_graph_replay(ctx, path, p0, cap):
     # one eager call sizes the layer workspace before capture (its result is discarded: a scratch cache)
     sK, sV, sp = t["K"].clone(), t["V"].clone(), pos.clone()
     kv0 = LayerKV(t["kn"].data_ptr(), 1, cap, sp.data_ptr())
-    assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
+    assert L.ork_b200_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
                                    t["qn"].data_ptr(), t["fn"].data_ptr(), t["x"].data_ptr(), sK.data_ptr(),
                                    sV.data_ptr(), xo.data_ptr(), C.byref(kv0)) == 0
     assert L.ork_b200_sync(ctx.ctx) == 0
@@ -187,7 +187,7 @@ def test_layer_device_position_past_capacity_is_an_error(ctx, path):
         pos = torch.tensor([p], dtype=torch.int32, device=dev)
         kv = LayerKV(t["kn"].data_ptr(), 1, cap, pos.data_ptr())
         torch.cuda.synchronize()
-        assert L.ork_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
+        assert L.ork_b200_i8_mm_layer_async(ctx.ctx, C.byref(dims), *[w.h for w in ws], t["an"].data_ptr(),
                                        t["qn"].data_ptr(), t["fn"].data_ptr(), t["x"].data_ptr(),
                                        t["K"].data_ptr(), t["V"].data_ptr(), xo.data_ptr(), C.byref(kv)) == 0
         return L.ork_b200_sync(ctx.ctx)
@@ -228,7 +228,7 @@ def test_layer_refusals(ctx, path):
 
 @pytest.mark.parametrize("p0,cap", [(5, 16), (70, 96)])
 def test_layers_stack_graph_replay(ctx, path, p0, cap):
-    """ork_i8_mm_layers_async: three layers with their own weights and caches in one call (one persistent
+    """ork_b200_i8_mm_layers_async: three layers with their own weights and caches in one call (one persistent
     launch, or nine launches per layer), the token's k/v appended at the device position, captured once
     and replayed for two tokens; each token compared with the oracle layers applied in turn."""
     import torch
@@ -258,14 +258,14 @@ def test_layers_stack_graph_replay(ctx, path, p0, cap):
     # table); append off, so the caches are only read
     sp = torch.tensor([p0], dtype=torch.int32, device=dev)
     kv0 = LayerKV(None, 0, cap, sp.data_ptr())
-    assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NL, arr, x.data_ptr(), xo.data_ptr(), C.byref(kv0)) == 0
+    assert L.ork_b200_i8_mm_layers_async(ctx.ctx, C.byref(dims), NL, arr, x.data_ptr(), xo.data_ptr(), C.byref(kv0)) == 0
     assert L.ork_b200_sync(ctx.ctx) == 0
     pos = torch.tensor([p0], dtype=torch.int32, device=dev)
     kv = LayerKV(None, 1, cap, pos.data_ptr())
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
-        assert L.ork_i8_mm_layers_async(ctx.ctx, C.byref(dims), NL, arr, x.data_ptr(), xo.data_ptr(),
+        assert L.ork_b200_i8_mm_layers_async(ctx.ctx, C.byref(dims), NL, arr, x.data_ptr(), xo.data_ptr(),
                                         C.byref(kv)) == 0
         x.copy_(xo)
         pos.add_(1)

@@ -69,11 +69,11 @@ def test_async_device_pointers_one_launch_at_decode(ctx):
         te = torch.zeros((M, N), dtype=torch.int8, device=dev)
         torch.cuda.synchronize()
         l0 = ctx.launches()
-        assert L.ork_i8_mm_run_out8_async(ctx.ctx, w.h, M, tA.data_ptr(), t8.data_ptr(), 0x1000, 15) == 0
+        assert L.ork_b200_i8_mm_run_out8_async(ctx.ctx, w.h, M, tA.data_ptr(), t8.data_ptr(), 0x1000, 15) == 0
         if M <= 8:  # the requant runs in the matmul kernel's store
             assert ctx.launches() - l0 == 1
-        assert L.ork_i8_mm_run_out16_async(ctx.ctx, w.h, M, tA.data_ptr(), t16.data_ptr(), 0x1000, 15) == 0
-        assert L.ork_i8_mm_run_ewmul_async(ctx.ctx, w.h, M, tA.data_ptr(), tG.data_ptr(), te.data_ptr(), 0x2AB0,
+        assert L.ork_b200_i8_mm_run_out16_async(ctx.ctx, w.h, M, tA.data_ptr(), t16.data_ptr(), 0x1000, 15) == 0
+        assert L.ork_b200_i8_mm_run_ewmul_async(ctx.ctx, w.h, M, tA.data_ptr(), tG.data_ptr(), te.data_ptr(), 0x2AB0,
                                            15) == 0
         assert L.ork_b200_sync(ctx.ctx) == 0
         acc = of.gemm_i32(A, B)

@@ -251,11 +251,11 @@ def test_device_pointer_runs(ctx):
     assert np.array_equal(dC.cpu().numpy(), ref)
     dC.zero_()
     torch.cuda.synchronize()
-    assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, dA.data_ptr(), dC.data_ptr()) == 0
+    assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, dA.data_ptr(), dC.data_ptr()) == 0
     assert L.ork_b200_sync(ctx.ctx) == 0
     assert np.array_equal(dC.cpu().numpy(), ref)
     # async refuses host pointers' misalignment and overlap like the sync path
-    assert L.ork_i8_mm_run_async(ctx.ctx, w.h, M, dA.data_ptr() + 1, dC.data_ptr()) == -1
+    assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, dA.data_ptr() + 1, dC.data_ptr()) == -1
     w.free()
 
 
@@ -334,12 +334,12 @@ def test_tensor_core_and_gemv_routes_agree_int4(ctx, env_clean, nf4, K, N):
 
 @pytest.mark.parametrize("na,tn,sk", [(1, 128, 1), (1, 128, 4), (2, 128, 1), (2, 128, 2), (2, 128, 4),
                                       (1, 256, 1), (1, 256, 2), (1, 192, 1), (1, 192, 4)])
-def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
+def test_tensor_core_tile_variants_exact(ctx, env_clean, tune, na, tn, sk):
     """Every non-swapped tile shape and split the router may pick (forced through its tuning variables),
     over M / N / K tails, int8 and NF4 weights."""
-    env_clean.setenv("ORKB_TC_NA", str(na))
-    env_clean.setenv("ORKB_TC_TN", str(tn))
-    env_clean.setenv("ORKB_TC_SK", str(sk))
+    tune("ORKB_TC_NA", str(na))
+    tune("ORKB_TC_TN", str(tn))
+    tune("ORKB_TC_SK", str(sk))
     L = ork_b200.lib()
     rng = np.random.default_rng(na * 100 + tn + sk)
     K, N = 1056, 640
@@ -366,13 +366,13 @@ def test_tensor_core_tile_variants_exact(ctx, env_clean, na, tn, sk):
 @pytest.mark.parametrize("nf4", [False, True])
 @pytest.mark.parametrize("sk", [1, 3])
 @pytest.mark.parametrize("stages", [0, 2])
-def test_tensor_core_nibble_long_k_exact(ctx, env_clean, nf4, sk, stages):
+def test_tensor_core_nibble_long_k_exact(ctx, env_clean, tune, nf4, sk, stages):
     """Decode-sized M on nibble weights through the tensor-core kernel with a long K per CTA (split
     forced to 1 or 3), so the stage ring (default depth, or the 2-stage ring) wraps many times and every
     stage is expanded from nibbles; a K tail (K % 128 != 0) ends the last block."""
-    env_clean.setenv("ORKB_TC_SK", str(sk))
+    tune("ORKB_TC_SK", str(sk))
     if stages:
-        env_clean.setenv("ORKB_TC_STAGES", str(stages))
+        tune("ORKB_TC_STAGES", str(stages))
     if nf4:
         env_clean.setenv("ORK_NF4", "1")
     L = ork_b200.lib()
@@ -417,15 +417,15 @@ def test_tensor_core_nibble_wide_grid_exact(ctx, env_clean, nf4):
 
 @pytest.mark.parametrize("pair,tn,sk", [(2, 256, 1), (2, 256, 2), (2, 128, 1), (2, 128, 4), (2, 64, 1),
                                         (2, 64, 2), (2, 192, 1), (2, 192, 4), (3, 0, 1), (3, 0, 2), (3, 0, 4)])
-def test_tensor_core_pair_tiles_exact(ctx, env_clean, pair, tn, sk):
+def test_tensor_core_pair_tiles_exact(ctx, env_clean, tune, pair, tn, sk):
     """CTA-pair (cta_group::2) tiles forced through the tuning variables: pair = 2 puts the activations
     on the 256-row side (M tails leave the second CTA of the last pair entirely out of range at
     M = 300), pair = 3 the weight (N tails, narrow M). int8, NF4 and uniform int4 exact; f16 within
     its tolerance."""
-    env_clean.setenv("ORKB_TC_PAIR", str(pair))
+    tune("ORKB_TC_PAIR", str(pair))
     if tn:
-        env_clean.setenv("ORKB_TC_TN", str(tn))
-    env_clean.setenv("ORKB_TC_SK", str(sk))
+        tune("ORKB_TC_TN", str(tn))
+    tune("ORKB_TC_SK", str(sk))
     L = ork_b200.lib()
     rng = np.random.default_rng(pair * 1000 + tn + sk)
     K, N = 1056, 640
@@ -461,15 +461,15 @@ def test_tensor_core_pair_tiles_exact(ctx, env_clean, pair, tn, sk):
 
 
 @pytest.mark.parametrize("kind,cpw", [("staged", 0), ("direct", 1), ("direct", 2), ("direct", 4)])
-def test_decode_kernels_exact_all_formats(ctx, env_clean, kind, cpw):
+def test_decode_kernels_exact_all_formats(ctx, env_clean, tune, kind, cpw):
     """Both decode kernels, forced through the tuning variables, on every weight format and M = 1..8,
     including a row far beyond the staged kernel's shared memory (K = 24576: always the direct kernel)."""
     L = ork_b200.lib()
     if kind == "direct":
-        env_clean.setenv("ORKB_GEMV_KIND", "1")
-        env_clean.setenv("ORKB_GEMV_CPW", str(cpw))
+        tune("ORKB_GEMV_KIND", "1")
+        tune("ORKB_GEMV_CPW", str(cpw))
     else:
-        env_clean.setenv("ORKB_GEMV_KIND", "0")
+        tune("ORKB_GEMV_KIND", "0")
     rng = np.random.default_rng(cpw + 40)
     try:
         assert L.ork_b200_force_route(ctx.ctx, 0) == 0

@@ -1,5 +1,5 @@
 """Column-sharded runs with the output gather fused into the matmul over peer memory (ork_b200_peers_*,
-ork_i8_mm_run_peers_async / ork_i4_mm_run_peers_async, include/ork_b200.h).
+ork_b200_i8_mm_run_peers_async / ork_b200_i4_mm_run_peers_async, include/ork_b200.h).
 
 Output channels are independent (ork-driver src/npu/i4/pack.c:63-80), so rank g packs channels
 [g*N/R, (g+1)*N/R) and its run writes them into every rank's C; after ork_b200_peers_wait_async each
@@ -50,7 +50,7 @@ def test_one_rank_table(ctx):
         A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
         tA = torch.from_numpy(A).to(dev)
         torch.cuda.synchronize()
-        assert L.ork_i8_mm_run_peers_async(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+        assert L.ork_b200_i8_mm_run_peers_async(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
         assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
         assert L.ork_b200_sync(ctx.ctx) == 0
         assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), M
@@ -99,11 +99,11 @@ def _two_rank_worker(rank, world, port, kind):
     if kind == "i8":
         B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
         w = ctx.i8_pack(np.ascontiguousarray(B[:, n0:n0 + ncols]))
-        run = L.ork_i8_mm_run_peers_async
+        run = L.ork_b200_i8_mm_run_peers_async
     else:
         B = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
         w = ctx.i4_pack(np.ascontiguousarray(B[:, n0:n0 + ncols]))
-        run = L.ork_i4_mm_run_peers_async
+        run = L.ork_b200_i4_mm_run_peers_async
     g = shard.PeerGroup(ctx, dist)
     t, cptr = g.table(Mmax, N, ncols)
     try:

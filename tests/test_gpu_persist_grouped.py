@@ -270,7 +270,7 @@ def test_grouped_async_device_pointers(ctx):
     tA, taS, tbS = (torch.from_numpy(x).to(dev) for x in (A, aS, bS))
     tC = torch.zeros((M, N), dtype=torch.float32, device=dev)
     torch.cuda.synchronize()
-    assert L.ork_i4_mm_run_grouped_async(ctx.ctx, w.h, M, tA.data_ptr(), taS.data_ptr(), tbS.data_ptr(),
+    assert L.ork_b200_i4_mm_run_grouped_async(ctx.ctx, w.h, M, tA.data_ptr(), taS.data_ptr(), tbS.data_ptr(),
                                          tC.data_ptr()) == 0
     assert L.ork_b200_sync(ctx.ctx) == 0
     assert _bits_equal(tC.cpu().numpy(), of.gemm_grouped(A, B, G, aS, bS))
