@@ -139,6 +139,96 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[1
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// ---- TMA epilogue: C leaves the CTA as bulk tensor stores, or -- for split-K integer tiles -- as bulk
+// tensor reduce-adds into C, which the L2 sums exactly in any order ---------------------------------------
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+               "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, int x, int y, uint32_t src) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   map),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every bulk store / reduce this thread issued has read its shared-memory source
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// One warp's 32 accumulator rows (TN columns from TMEM address taddr) through its staging boxes to C:
+// box b holds columns 32b..32b+31 as 32 rows of 128 bytes, row = lane, with the 16-byte chunk q of a row
+// at position q ^ (row & 7) -- the tensor map's 128-byte swizzle, which makes these row-per-lane writes
+// free of bank conflicts. Box b lies at sbox + b * 16 KB (the four epilogue warps' boxes interleave:
+// warp w's box b at (4b + w) * 4 KB of the tile's staging). Boxes go in groups of up to four (128
+// columns: one TMEM wait, one proxy fence, then one TMA store -- or, for split-K integer tiles,
+// reduce-add -- per box at C columns x0 + 32b, rows y), so the TMA drains one group while the next is
+// written.
+template <int TN>
+__device__ __forceinline__ void drain_rows_tma(uint32_t taddr, int lane, uint32_t sbox, const CUtensorMap *mapC,
+                                               int x0, int y, int M, int N, bool reduce) {
+  static_assert(TN % 32 == 0, "row tiles drain in 32-column boxes");
+  constexpr int NB = TN / 32;                                          // boxes
+  constexpr int GB = NB % 4 == 0 ? 4 : NB % 3 == 0 ? 3 : NB % 2 == 0 ? 2 : 1;  // boxes per group
+  const uint32_t rowoff = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
+#pragma unroll 1
+  for (int g = 0; g < NB; g += GB) {
+    uint32_t v[2 * GB][16];
+#pragma unroll
+    for (int j = 0; j < 2 * GB; j++) tmem_ld16_nowait(taddr + (uint32_t)(32 * g + 16 * j), v[j]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int k = 0; k < GB; k++) {
+      const uint32_t box = sbox + (uint32_t)(g + k) * 16384u + rowoff;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        st_shared_v4(box + ((q ^ sw) << 4), v[2 * k][4 * q], v[2 * k][4 * q + 1], v[2 * k][4 * q + 2],
+                     v[2 * k][4 * q + 3]);
+        st_shared_v4(box + (((q + 4) ^ sw) << 4), v[2 * k + 1][4 * q], v[2 * k + 1][4 * q + 1],
+                     v[2 * k + 1][4 * q + 2], v[2 * k + 1][4 * q + 3]);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the TMA (async proxy)
+    __syncwarp();
+    if (lane == 0 && y < M) {
+#pragma unroll
+      for (int k = 0; k < GB; k++)
+        if (x0 + 32 * (g + k) < N) {
+          const uint32_t box = sbox + (uint32_t)(g + k) * 16384u;
+          if (reduce) tma_reduce_add_2d(mapC, x0 + 32 * (g + k), y, box);
+          else tma_store_2d(mapC, x0 + 32 * (g + k), y, box);
+        }
+      bulk_commit();
+    }
+  }
+}
+
+// Swapped tiles hold a column of C per lane (TMEM lane = weight row n, columns = activation rows m): the
+// warp's TN x 32 block goes to staging as [TN rows m][32 words n] (consecutive lanes, consecutive words:
+// no bank conflicts), one TMA box of 32 x TN. Columns go 64 at a time.
+template <int TN>
+__device__ __forceinline__ void drain_cols_tma(uint32_t taddr, int lane, uint32_t sbox) {
+  constexpr int CB = TN < 64 ? TN : 64;
+  constexpr int NJ = CB / 16;
+#pragma unroll 1
+  for (int cb = 0; cb < TN; cb += CB) {
+    uint32_t v[NJ][16];
+#pragma unroll
+    for (int j = 0; j < NJ; j++) tmem_ld16_nowait(taddr + (uint32_t)(cb + 16 * j), v[j]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+#pragma unroll
+      for (int q = 0; q < 16; q++)
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(sbox + (uint32_t)(((cb + 16 * j + q) * 32 + lane) * 4)),
+                     "r"(v[j][q])
+                     : "memory");
+  }
+}
 // Epilogue store of a 32-row x 32-column block held one row per lane: the warp transposes it through
 // its own shared-memory tile (row stride 36 words: both the row-per-lane writes and the row-wise reads
 // are free of bank conflicts) so that every global store instruction writes four whole 128-byte rows
@@ -214,16 +304,74 @@ __device__ __forceinline__ void drain_rows(uint32_t taddr, int lane, bool split,
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// the two halves of a cluster barrier, for threads that can signal long before they need the others
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t local_addr, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t cluster_addr) {
   uint4 v;
   asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(remote)
+               : "r"(cluster_addr)
                : "memory");
   return v;
+}
+
+template <bool F16>
+__device__ __forceinline__ uint4 add4(uint4 a, uint4 b);
+
+// Split-K reduction of this CTA's share of a tile after the cluster barrier: output items t = first,
+// first + stride, ... < items, an item being one 16-byte vector of C (output row t / vpr, vector t % vpr
+// of the tile, C row m0 + row, column n0 + 4 * vector). The SK partial tiles lie at the same offset of
+// the shared memory of cluster ranks rank0 + rstep * q. Items go BATCH at a time and every remote read
+// of a batch is issued before its first add, so a thread waits out one distributed-shared-memory round
+// trip per batch rather than one per item (one per item was several microseconds of every split launch).
+template <bool F16, int SK>
+__device__ __forceinline__ void reduce_split(uint32_t pbase, int pstr, int first, int stride, int items, int vpr,
+                                             uint32_t rank0, uint32_t rstep, uint32_t *C, int N, int m0, int n0) {
+  constexpr int BATCH = SK <= 2 ? 8 : SK <= 4 ? 4 : 2;
+  uint32_t remote[SK];
+#pragma unroll
+  for (int q = 0; q < SK; q++) {
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote[q]) : "r"(pbase), "r"(rank0 + rstep * q));
+  }
+  for (int t0 = first; t0 < items; t0 += BATCH * stride) {
+    uint4 v[BATCH][SK];
+#pragma unroll
+    for (int b = 0; b < BATCH; b++) {
+      const int t = t0 + b * stride;
+      if (t < items) {
+        const uint32_t off = (uint32_t)((t / vpr) * pstr + 4 * (t % vpr)) * 4u;
+#pragma unroll
+        for (int q = 0; q < SK; q++) v[b][q] = ld_cluster_v4(remote[q] + off);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < BATCH; b++) {
+      const int t = t0 + b * stride;
+      if (t < items) {
+        uint4 acc = v[b][0];
+#pragma unroll
+        for (int q = 1; q < SK; q++) acc = add4<F16>(acc, v[b][q]);
+        *reinterpret_cast<uint4 *>(C + (size_t)(m0 + t / vpr) * N + n0 + 4 * (t % vpr)) = acc;
+      }
+    }
+  }
+}
+
+template <bool F16>
+__device__ __forceinline__ void reduce_split_any(int SK, uint32_t pbase, int pstr, int first, int stride, int items,
+                                                 int vpr, uint32_t rank0, uint32_t rstep, uint32_t *C, int N, int m0,
+                                                 int n0) {
+  switch (SK) {
+    case 2: reduce_split<F16, 2>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+    case 3: reduce_split<F16, 3>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+    case 4: reduce_split<F16, 4>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+    case 5: reduce_split<F16, 5>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+    case 6: reduce_split<F16, 6>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+    case 7: reduce_split<F16, 7>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+    default: reduce_split<F16, 8>(pbase, pstr, first, stride, items, vpr, rank0, rstep, C, N, m0, n0); break;
+  }
 }
 
 template <bool F16>
@@ -275,7 +423,8 @@ constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 1
 template <int FMT, bool SWAP, int TN, int STAGES, int NA>
 __global__ void __launch_bounds__(192)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
-               void *__restrict__ Cout, int M, int N, int K, Nf4Tables tb) {
+               const __grid_constant__ CUtensorMap mapC, void *__restrict__ Cout, int M, int N, int K,
+               Nf4Tables tb) {
   // NA accumulators of 128 rows stacked along the R side (TM = 128*NA): each K step issues NA MMAs that
   // share the S tile, so S is fetched once per 128*NA rows (less operand traffic per output)
   constexpr bool F16 = FMT == FMT_F16;
@@ -346,6 +495,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     else tma_load_2d(smem_u32(sR + s * R_BYTES), &mapR, x, r0, full0 + 8 * s);
   };
 
+  bool ep_ok = false;  // the epilogue warps' accumulator is complete (no bounded wait expired)
+  // integer split-K: the splits reduce-add into C after split 0 has zeroed it. A split-phase cluster
+  // barrier orders the two: every thread arrives as early as it can (split 0's epilogue warps once the
+  // zeroes are written) and only the epilogue warps wait, well before they need to
+  const bool tma_reduce = !F16 && SK > 1;
+  if (tma_reduce && (warp < 2 || ks != 0)) cluster_arrive();
   if (warp == 0) {
     if (lane == 0) {
       // the weight tiles do not depend on the previous kernel: the first ring's worth is requested
@@ -388,6 +543,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     }
   } else {
     const int ct = threadIdx.x - 64;  // 0..127 over warps 2..5
+    if (tma_reduce && ks == 0) {
+      // split 0 zeroes the tile of C that every split reduce-adds into, once the previous grid (which may
+      // still read C) has finished
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      const int rows = SWAP ? min(TN, M - c0) : min(TM, M - r0);
+      const int cols = SWAP ? min(TM, N - r0) : min(TN, N - c0);
+      const int m0 = SWAP ? c0 : r0, n0 = SWAP ? r0 : c0, vpr = cols / 4;
+      uint32_t *Cz = (uint32_t *)Cout;
+      for (int t = ct; t < rows * vpr; t += 128)
+        *reinterpret_cast<uint4 *>(Cz + (size_t)(m0 + t / vpr) * N + n0 + 4 * (t % vpr)) = make_uint4(0, 0, 0, 0);
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // the zeroes, before any reduce (async proxy)
+      __syncwarp();
+      cluster_arrive();
+    }
     if constexpr (NIB) {
       // converter: per stage, WROWS x 8 chunks of 16 output bytes (row r, k chunk c), written at the
       // 128-byte-swizzle position (chunk c ^ (r & 7)) of the 1024-byte-aligned tile
@@ -405,51 +574,62 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(conv0 + 8 * s) : "memory");
       }
     }
-    // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = row of an R accumulator
+    if (tma_reduce) {  // split 0's zeroes are visible to this thread's reduces from here on
+      __syncwarp();
+      cluster_wait();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = row of an R accumulator. The
+    // ring is idle once done fired and holds the staging boxes (or, for fp16 split-K, the partial tile)
     const int sub = warp & 3;
-    const bool ok = mbar_wait(done, 0);
+    ep_ok = mbar_wait(done, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
-      uint32_t *stg = (uint32_t *)smem + sub * 32 * kStgStride;  // the ring is idle once done fired
+    if (ep_ok) {
+      if (F16 && SK > 1) {
+        uint32_t *stg = (uint32_t *)smem + sub * 32 * kStgStride;
 #pragma unroll 1
-      for (int a = 0; a < NA; a++)
-        drain_rows<SWAP, TN, PSTR>(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(a * TN), lane, SK > 1, P,
-                                   a * BM + sub * 32 + lane, stg, (uint32_t *)Cout, M, N, r0 + a * BM + sub * 32,
-                                   c0);
+        for (int a = 0; a < NA; a++)
+          drain_rows<SWAP, TN, PSTR>(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(a * TN), lane, true, P,
+                                     a * BM + sub * 32 + lane, stg, (uint32_t *)Cout, M, N, r0 + a * BM + sub * 32,
+                                     c0);
+      } else if constexpr (SWAP) {
+        const uint32_t sbox = smem_u32(smem) + (uint32_t)(sub * TN * 128);
+        drain_cols_tma<TN>(tmem + ((uint32_t)(sub * 32) << 16), lane, sbox);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0 && r0 + sub * 32 < N && c0 < M) {
+          if (tma_reduce) tma_reduce_add_2d(&mapC, r0 + sub * 32, c0, sbox);
+          else tma_store_2d(&mapC, r0 + sub * 32, c0, sbox);
+          bulk_commit();
+        }
+      } else {
+#pragma unroll 1
+        for (int a = 0; a < NA; a++)
+          drain_rows_tma<TN>(tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(a * TN), lane,
+                             smem_u32(smem) + (uint32_t)(((a * (TN / 32)) * 4 + sub) * 4096), &mapC, c0,
+                             r0 + a * BM + sub * 32, M, N, tma_reduce);
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();
-  if (SK > 1) {
+  if (F16 && SK > 1) {
     cluster_sync();  // every CTA's partial tile is in its shared memory
-    // reduce: output items are (output row, 4-column vector) of the tile in C's row-major order
-    const int out_rows = SWAP ? min(TN, M - c0) : min(TM, M - r0);
-    const int out_cols = SWAP ? min(TM, N - r0) : min(TN, N - c0);
-    const int vpr = out_cols / 4;  // N is a multiple of 16, tiles start at multiples of 16
-    const int items = out_rows * vpr;
-    const uint32_t pbase = smem_u32(P);
-    uint32_t *Cp = (uint32_t *)Cout;
-    // every remote read of an item is issued before the first add, so the SK distributed-shared-memory
-    // latencies overlap instead of adding up
-    // every remote read of an item is issued before the first add, so the SK distributed-shared-memory
-    // latencies overlap instead of adding up
-    for (int t = ks * 192 + (int)threadIdx.x; t < items; t += SK * 192) {
-      const int orow = t / vpr, ov = t % vpr;
-      const uint32_t off = (uint32_t)(orow * PSTR + 4 * ov) * 4u;
-      uint4 v[8];
-#pragma unroll
-      for (int q = 0; q < 8; q++)
-        if (q < SK) v[q] = ld_dsmem_v4(pbase + off, (uint32_t)q);
-      uint4 acc = v[0];
-#pragma unroll
-      for (int q = 1; q < 8; q++)
-        if (q < SK) acc = add4<F16>(acc, v[q]);
-      const int m = SWAP ? c0 + orow : r0 + orow;
-      const int n = (SWAP ? r0 : c0) + 4 * ov;
-      *reinterpret_cast<uint4 *>(Cp + (size_t)m * N + n) = acc;
+    {
+      // fp16 (fp32 C): the partials are summed through distributed shared memory in a fixed order, so the
+      // result does not depend on the order the splits finish in
+      const int out_rows = SWAP ? min(TN, M - c0) : min(TM, M - r0);
+      const int out_cols = SWAP ? min(TM, N - r0) : min(TN, N - c0);
+      const int vpr = out_cols / 4;  // N is a multiple of 16, tiles start at multiples of 16
+      const int items = out_rows > 0 && out_cols > 0 ? out_rows * vpr : 0;
+      reduce_split_any<F16>(SK, smem_u32(P), PSTR, ks * 192 + (int)threadIdx.x, SK * 192, items, vpr, 0u, 1u,
+                            (uint32_t *)Cout, N, SWAP ? c0 : r0, SWAP ? r0 : c0);
+      cluster_sync();  // no CTA leaves while its partial tile may still be read
     }
-    cluster_sync();  // no CTA leaves while its partial tile may still be read
   }
+  // the staging boxes have been read by the TMA before the CTA (and its shared memory) goes; the writes
+  // themselves complete with the grid
+  if (warp >= 2 && lane == 0) bulk_wait_read();
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
 }
@@ -549,7 +729,8 @@ __host__ __device__ constexpr uint32_t idesc_pair(int tn) {
 template <int FMT, bool SWAP, int TN, int STAGES>
 __global__ void __launch_bounds__(192)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
-                    void *__restrict__ Cout, int M, int N, int K, Nf4Tables tb) {
+                    const __grid_constant__ CUtensorMap mapC, void *__restrict__ Cout, int M, int N, int K,
+                    Nf4Tables tb) {
   constexpr bool F16 = FMT == FMT_F16;
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
   constexpr int HS = TN / 2;                             // S rows held by each CTA
@@ -608,6 +789,11 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
   cluster_sync();  // both CTAs' barriers and TMEM exist before any peer signal or MMA
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  // integer split-K: every split reduce-adds into C after split 0's pair has zeroed it, ordered by a
+  // split-phase cluster barrier (see gemm_tc_kernel); the warps that arrive early complete that phase
+  // before the final cluster barrier
+  const bool tma_reduce = !F16 && SK > 1;
+  if (tma_reduce && (warp < 2 || ks != 0)) cluster_arrive();
 
   auto load_w = [&](int s, int kb) {
     if constexpr (NIB) {
@@ -668,6 +854,18 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
     }
   } else {
     const int ct = threadIdx.x - 64;
+    if (tma_reduce && ks == 0) {  // this CTA's 128-row half of the tile, zeroed after the previous grid
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      const int rows = SWAP ? min(TN, M - c0) : min(BM, M - rr);
+      const int cols = SWAP ? min(BM, N - rr) : min(TN, N - c0);
+      const int m0 = SWAP ? c0 : rr, n0 = SWAP ? rr : c0, vpr = cols / 4;
+      uint32_t *Cz = (uint32_t *)Cout;
+      for (int t = ct; t < rows * vpr; t += 128)
+        *reinterpret_cast<uint4 *>(Cz + (size_t)(m0 + t / vpr) * N + n0 + 4 * (t % vpr)) = make_uint4(0, 0, 0, 0);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncwarp();
+      cluster_arrive();
+    }
     if constexpr (NIB) {
       bool cok = true;
       for (int kb = kb0; kb < kb1 && cok; kb++) {
@@ -683,16 +881,40 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
         if (lane == 0) mbar_arrive_remote(mapa_u32(conv0 + 8 * s, leader_rank));
       }
     }
+    if (tma_reduce) {
+      __syncwarp();
+      cluster_wait();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
     const int sub = warp & 3;
     const bool ok = mbar_wait(done, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok)
-      drain_rows<SWAP, TN, PSTR>(tmem + ((uint32_t)(sub * 32) << 16), lane, SK > 1, P, sub * 32 + lane,
-                                 (uint32_t *)smem + sub * 32 * kStgStride, (uint32_t *)Cout, M, N, rr + sub * 32, c0);
+    if (ok) {
+      if (F16 && SK > 1) {
+        drain_rows<SWAP, TN, PSTR>(tmem + ((uint32_t)(sub * 32) << 16), lane, true, P, sub * 32 + lane,
+                                   (uint32_t *)smem + sub * 32 * kStgStride, (uint32_t *)Cout, M, N, rr + sub * 32,
+                                   c0);
+      } else if constexpr (SWAP) {
+        const uint32_t sbox = smem_u32(smem) + (uint32_t)(sub * TN * 128);
+        drain_cols_tma<TN>(tmem + ((uint32_t)(sub * 32) << 16), lane, sbox);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0 && rr + sub * 32 < N && c0 < M) {
+          if (tma_reduce) tma_reduce_add_2d(&mapC, rr + sub * 32, c0, sbox);
+          else tma_store_2d(&mapC, rr + sub * 32, c0, sbox);
+          bulk_commit();
+        }
+      } else {
+        drain_rows_tma<TN>(tmem + ((uint32_t)(sub * 32) << 16), lane, smem_u32(smem) + (uint32_t)(sub * 4096), &mapC,
+                           c0, rr + sub * 32, M, N, tma_reduce);
+      }
+    }
+    if (lane == 0) bulk_wait_read();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();
-  if (SK > 1) {
+  if (tma_reduce && warp < 2) cluster_wait();  // the early arrivals' phase, before the final barrier
+  if (F16 && SK > 1) {
     cluster_sync();
     // this CTA's slice of its half-tile: (output row, 4-column vector) items in C's row-major order,
     // summed over the partials of cluster ranks half + 2q
@@ -700,23 +922,8 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
     const int out_cols = SWAP ? min(BM, N - rr) : min(TN, N - c0);
     const int vpr = out_cols / 4;
     const int items = out_rows > 0 && out_cols > 0 ? out_rows * vpr : 0;
-    const uint32_t pbase = smem_u32(P);
-    uint32_t *Cp = (uint32_t *)Cout;
-    for (int t = ks * 192 + (int)threadIdx.x; t < items; t += SK * 192) {
-      const int orow = t / vpr, ov = t % vpr;
-      const uint32_t off = (uint32_t)(orow * PSTR + 4 * ov) * 4u;
-      uint4 v[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++)
-        if (q < SK) v[q] = ld_dsmem_v4(pbase + off, half + 2u * (uint32_t)q);
-      uint4 acc = v[0];
-#pragma unroll
-      for (int q = 1; q < 4; q++)
-        if (q < SK) acc = add4<F16>(acc, v[q]);
-      const int m = SWAP ? c0 + orow : rr + orow;
-      const int n = (SWAP ? rr : c0) + 4 * ov;
-      *reinterpret_cast<uint4 *>(Cp + (size_t)m * N + n) = acc;
-    }
+    reduce_split_any<F16>(SK, smem_u32(P), PSTR, ks * 192 + (int)threadIdx.x, SK * 192, items, vpr, half, 2u,
+                          (uint32_t *)Cout, N, SWAP ? c0 : rr, SWAP ? rr : c0);
   }
   cluster_sync();  // the pair (and every split-K partial) is finished before TMEM and shared memory go
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
@@ -738,18 +945,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 2-D map over a row-major [rows][row_bytes] byte matrix (element = esz bytes) with a box of
 // box_rows x box_bytes; 128-byte swizzle for MMA operand tiles, none for the nibble staging tiles.
 bool make_map(CUtensorMap *map, const void *base, int rows, size_t row_bytes, int esz, int box_rows,
-              int box_bytes, bool swizzle) {
+              int box_bytes, bool swizzle,
+              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8) {
   auto fn = encode_fn();
   if (!fn) return false;
+  if (esz == 2) dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / esz), (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / esz), (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
-                        const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+  const CUresult r = fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// The output map: C [M][N] of 4-byte elements (s32 sums, or f32 for fp16 runs), boxes of 32 columns by
+// 32 rows with the 128-byte swizzle for row tiles, or by TN rows unswizzled for swapped tiles.
+bool make_c_map(CUtensorMap *map, void *C, int M, int N, bool f32, bool swap, int tn) {
+  return make_map(map, C, M, (size_t)N * 4, 4, swap ? tn : 32, 128, !swap,
+                  f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_INT32);
 }
 
 
@@ -765,10 +980,14 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   const bool okW = NIB ? make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, 1, WROWS, 64, false)
                        : make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, ESZ, WROWS, BK_BYTES, true);
   const bool okA = make_map(SWAP ? &mS : &mR, a.A, a.M, a_row, ESZ, SWAP ? TN : TM, BK_BYTES, true);
-  if (!okW || !okA) return cudaErrorInvalidValue;
+  CUtensorMap mC;
+  const bool okC = make_c_map(&mC, a.C, a.M, a.N, FMT == FMT_F16, SWAP, TN);
+  if (!okW || !okA || !okC) return cudaErrorInvalidValue;
   constexpr size_t ring = (size_t)STAGES * ((TM + TN) * BK_BYTES + (NIB ? WROWS * 64 : 0));
   constexpr size_t part = (size_t)(SWAP ? TN * (TM + 4) : TM * (TN + 4)) * 4;
   static_assert(part <= ring, "partial tile must fit in the stage ring");
+  constexpr size_t staging = SWAP ? (size_t)4 * TN * 128 : (size_t)TM * TN * 4;
+  static_assert(staging <= ring, "the output staging boxes must fit in the stage ring");
   constexpr size_t smem = 1024 + ring + (3 * STAGES + 1) * 8 + 16;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_tc_kernel<FMT, SWAP, TN, STAGES, NA>;
@@ -792,7 +1011,7 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].val.clusterDim.z = sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K, tb);
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb);
 }
 
 // CTA-pair launch: grid x = 2 CTAs per 256 R rows, y = S tiles of TN, z = split-K; cluster (2, 1, sk).
@@ -809,10 +1028,14 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   const bool okW = NIB ? make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, 1, WROWS, 64, false)
                        : make_map(SWAP ? &mR : &mS, a.W, a.N, w_row, ESZ, WROWS, BK_BYTES, true);
   const bool okA = make_map(SWAP ? &mS : &mR, a.A, a.M, a_row, ESZ, SWAP ? HS : BM, BK_BYTES, true);
-  if (!okW || !okA) return cudaErrorInvalidValue;
+  CUtensorMap mC;
+  const bool okC = make_c_map(&mC, a.C, a.M, a.N, FMT == FMT_F16, SWAP, TN);
+  if (!okW || !okA || !okC) return cudaErrorInvalidValue;
   constexpr size_t ring = (size_t)STAGES * ((BM + HS) * BK_BYTES + (NIB ? WROWS * 64 : 0));
   constexpr size_t part = (size_t)(SWAP ? TN * (BM + 4) : BM * (TN + 4)) * 4;
   static_assert(part <= ring, "partial tile must fit in the stage ring");
+  constexpr size_t staging = SWAP ? (size_t)4 * TN * 128 : (size_t)BM * TN * 4;
+  static_assert(staging <= ring, "the output staging boxes must fit in the stage ring");
   constexpr size_t smem = 1024 + ring + (4 * STAGES + 1) * 8 + 16;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = gemm_tc_pair_kernel<FMT, SWAP, TN, STAGES>;
@@ -836,7 +1059,7 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].val.clusterDim.z = sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, a.C, a.M, a.N, a.K, tb);
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb);
 }
 
 struct TcCfg {
@@ -850,12 +1073,13 @@ struct TcCfg {
 // Tile and split choice. Swapped operands with the narrowest N-tile covering M for M <= 64 (weight
 // streaming; K split over a cluster up to 8 ways while the grid stays within ~320 CTAs, two per SM).
 // For larger M, measured on B200 over configs of K in {2048, 6144}, N in {2048, 6144, 12288},
-// M in {128, 256, 512}: a CTA's time is set by
-// its own operand bytes in flight and its C tile, so the grid should cover the SMs once with the
-// narrowest tile that fits: 128-wide weight tiles, widened to 192 then 256 (int8 / f16) only while the
-// grid would exceed one wave of 148 CTAs; nibble weights past one wave use CTA-pair tiles of 256 x 192
-// (the converter work per CTA halves). Split-K (a cluster reduction through distributed shared memory)
-// pays for grids of up to 32 tiles, and for up to 64 tiles when K spans at least 32 blocks.
+// M in {128, 256, 512} with a per-phase timeline of the kernel: a CTA streams its operands at ~115 GB/s
+// (the TMA's rate per SM, from L2 or HBM alike) and writes its C tile at ~60 GB/s, and every launch
+// carries ~2-3 us of fixed latency (first data after the dependency wait, the gap to the next launch).
+// So the grid should cover the SMs once: 128-wide weight tiles, widened to 192 then 256 (int8 / f16)
+// only while the grid would exceed one wave of 148 CTAs; nibble weights past one wave use CTA-pair tiles
+// of 256 x 192 (the converter work per CTA halves); then split-K (integer partial tiles reduce-added by
+// the TMA) as far as below.
 TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
   TcCfg c;
   const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
@@ -889,9 +1113,14 @@ TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
       }
     }
     const int t = c.pair ? 2 * ((M + 255) / 256) * ((N + c.tn - 1) / c.tn) : tiles(c.tn);
+    // split K as far as the grid stays one wave with room for cluster placement (132 of 148 SMs: clusters
+    // of 3 or more do not pack every GPC), every split keeps at least 4 k-blocks, and the cluster stays
+    // at most 6 CTAs (8-CTA clusters scheduled in two waves on these grids). Measured over the BASELINE
+    // shapes: 2048x6144xM128 7.6 us at split 2 vs 8.6 unsplit and 12.7 at split 3 (144 CTAs);
+    // 6144x2048xM128 7.4 us at 6 vs 8.0 at 4; 2048x2048xM512 7.7 at 2 vs 8.5 unsplit.
     c.sk = 1;
-    if (t <= 32 && KB >= 8) c.sk = 4;
-    else if (t <= 64 && KB >= 32) c.sk = 2;
+    for (int s : {2, 3, 4, 6})
+      if (t * s <= 132 && KB / s >= 4 && (!c.pair || s <= 2)) c.sk = s;
   }
   // tuning overrides (the context's ORKB_TC_* values): tile width, accumulators, ring depth, split
   if (!c.swap) {

@@ -4,8 +4,8 @@ Tensor-core tiles:
 Each expectation restates a rule of the router in the library's tile choice: swapped operands with
 the narrowest tile covering M for M <= 64, split-K doubling while the grid stays within ~320 CTAs;
 for larger M, 128-wide weight tiles widened to 192 / 256 only while the grid would exceed one wave of
-148 CTAs, CTA-pair tiles for nibble weights past one wave, split-K for grids of at most 32 / 64
-tiles; nibble weights at M <= 16 whose unsplit grid exceeds 296 tiles take the 2-stage ring with a
+148 CTAs, CTA-pair tiles for nibble weights past one wave, then the largest split of {2, 3, 4, 6}
+that keeps tiles x split <= 132 CTAs and at least 4 k-blocks per split (2 at most for CTA pairs); nibble weights at M <= 16 whose unsplit grid exceeds 296 tiles take the 2-stage ring with a
 2-way split; long int8 rows (K >= 6144) at M <= 32 take a 6-deep ring.
 
 Decode GEMV (M <= 8 per pass): the staged kernel (8 channels per CTA, whole rows in shared memory)
@@ -39,10 +39,12 @@ def no_tuning_variables(monkeypatch):
     # [swap, tile width, K split, ring depth (0 = default), CTA pair]
     (I8, 8, 6144, 2048, [1, 16, 8, 6, 0]),        # decode-sized int8, long rows: 6-deep ring
     (I8, 8, 2048, 6144, [1, 16, 4, 0, 0]),        # 48 tiles: split while <= 320 CTAs
-    (I8, 128, 6144, 2048, [0, 128, 4, 0, 0]),     # 16 tiles, long K
+    (I8, 128, 6144, 2048, [0, 128, 6, 0, 0]),     # 16 tiles, K of 48 blocks: 96 CTAs
+    (I8, 128, 2048, 6144, [0, 128, 2, 0, 0]),     # 48 tiles: split 3 would be 144 CTAs (> 132)
+    (I8, 128, 2048, 2048, [0, 128, 4, 0, 0]),     # 16 tiles, K of 16 blocks: 4 blocks per split
     (I8, 512, 6144, 2048, [0, 128, 2, 0, 0]),     # 64 tiles, K of 48 blocks
     (I8, 512, 2048, 6144, [0, 192, 1, 0, 0]),     # 192 tiles of 128 > 148: widened to 192 (128 tiles)
-    (I8, 512, 2048, 2048, [0, 128, 1, 0, 0]),     # 64 tiles, K of 16 blocks: too short to split
+    (I8, 512, 2048, 2048, [0, 128, 2, 0, 0]),     # 64 tiles: split 2 (128 CTAs)
     (F16, 64, 2048, 6144, [1, 64, 4, 0, 0]),      # fp16 decode-sized batch
     (NF4, 8, 8192, 10240, [1, 16, 4, 0, 0]),      # 70B QKV at M = 8: 80 tiles x 4 = 320 CTAs
     (NF4, 8, 8192, 57344, [1, 16, 2, 2, 0]),      # 70B gate+up at M = 8: 448 tiles -> 2-stage ring, split 2
