@@ -34,12 +34,13 @@ int ork_b200_f16_mm_run_async(ork_npu *ctx, ork_w *w, int M, const ork_f16 *dA, 
 /* No counterpart in ork-driver. ork_i8_mm_run for callers that cannot let a library allocate device
  * memory at run time (an engine that reserved nearly all HBM for its own pool at start-up, a process
  * under a hard device-memory cap, or code that must not trigger the device-wide synchronisation
- * cudaMalloc / cudaFree can cause). Same arguments, checks and result as ork_i8_mm_run; A and C are
- * staged through a fixed 4 MiB scratch area built into the library (held on every GPU that loads it)
- * instead of buffers the context allocates, and the call allocates nothing. Limit: M*K rounded up to
- * 256, plus 4*M*N, must fit in 4 MiB, else -1 with a message. The first call on a device looks up the
- * scratch address (make it before any stream capture); calls that overlap on one GPU race on the
- * shared scratch. */
+ * cudaMalloc / cudaFree can cause). Same arguments, checks and result as ork_i8_mm_run: device-resident
+ * A and C are used in place, and host A and C are staged through a fixed 4 MiB scratch area built into
+ * the library (held on every GPU that loads it) instead of buffers the context allocates; the call
+ * allocates nothing. Limit: the host buffers' share -- M*K rounded up to 256 for a host A, 4*M*N for a
+ * host C -- must fit in 4 MiB, else -1 with a message. The first call on a device looks up the scratch
+ * address (make it before any stream capture). One scratch array per GPU serves every call, so calls on
+ * one device must not overlap (they would race on it). */
 int ork_i8_mm_run_noalloc(ork_npu *ctx, ork_w *w, int M, const int8_t *A, int32_t *C);
 
 /* Grouped runs over device pointers (A, aScale, bScale, C on the context's GPU), enqueued like the
@@ -176,6 +177,10 @@ int ork_b200_device(const ork_npu *ctx);
 /* Programmatic dependent launch for the async runs (default on): a queued matmul starts streaming its
  * weights while the previous kernel on the stream drains, and waits for that kernel before reading A. */
 int ork_b200_set_pdl(ork_npu *ctx, int on);
+/* Device bytes of run-time staging the context holds (host-buffer runs, grouped scales, decode-layer
+ * workspace, ork_async pinned staging), all allocated on first use and grown on demand: 0 for a context
+ * that has made no such call. For tests and tooling (e.g. that ork_i8_mm_run_noalloc allocated nothing). */
+size_t ork_b200_staging_bytes(const ork_npu *ctx);
 /* Number of kernels this context has launched (all kernels are this library's own). */
 uint64_t ork_b200_launches(const ork_npu *ctx);
 /* Device address and byte size of a weight's resident storage (read-only for callers). */

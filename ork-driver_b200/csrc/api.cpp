@@ -54,7 +54,6 @@ cudaError_t smem_attr(const void *kernel, int bytes) {
 
 // One error word per device in mapped, pinned host memory, set by any kernel that records an error
 // (errword.cuh); the per-module device flags say which and are read (and cleared) only when it is set.
-constexpr int kMaxDevices = 64;
 static unsigned int *g_err_host = nullptr;
 static bool g_err_ready[kMaxDevices];
 static std::mutex g_err_mu;
@@ -511,6 +510,10 @@ int ork_b200_i4_mm_run_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, int3
 }
 int ork_b200_f16_mm_run_async(ork_npu *c, ork_w *w, int M, const ork_f16 *dA, float *dC) {
   return run_async(c, w, M, dA, dC, DT_F16, "ork_b200_f16_mm_run_async");
+}
+
+size_t ork_b200_staging_bytes(const ork_npu *c) {
+  return c ? c->capA + c->capC + c->capS + c->capL + c->capX + c->capP : 0;
 }
 
 int ork_b200_reload_tuning(ork_npu *c) {

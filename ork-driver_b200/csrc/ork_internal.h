@@ -14,6 +14,9 @@ namespace orkb {
 //   FMT_NF4 : [N][K/2] bytes, NF4 codebook indices 0..15, low nibble = even k (the O4N1 nibble layout)
 enum Fmt { FMT_F16 = 0, FMT_I8 = 1, FMT_U4 = 2, FMT_NF4 = 3 };
 
+// Device ordinals the per-device tables (error words, no-allocation scratch addresses) cover.
+constexpr int kMaxDevices = 64;
+
 // Which public run function a weight belongs to (ork-driver src/npu/internal.h DT_* values).
 enum ApiDtype { DT_F16 = 0, DT_I8 = 1, DT_I4 = 2 };
 

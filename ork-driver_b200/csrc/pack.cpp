@@ -15,7 +15,7 @@
 namespace orkb {
 
 // src/npu.c:888-892 (ORKI_NF4_LEVELS): the 16 normalised NF4 levels.
-static const float kNf4Levels[16] = {
+static constexpr float kNf4Levels[16] = {
     -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
     -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
     0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
@@ -78,8 +78,9 @@ static uint32_t xs32(uint32_t *s) {  // src/npu/internal.h:589
   return x;
 }
 
-// The levels with a 16th entry that no value is below (+inf), for the branchless search in nf4_index.
-static const float kNf4Search[16] = {
+// The levels with a 16th entry that no value is below (+inf), for the branchless search in nf4_index;
+// constant-initialised (constexpr), so a pack made during another unit's static initialisation sees it.
+static constexpr float kNf4Search[16] = {
     kNf4Levels[0], kNf4Levels[1], kNf4Levels[2],  kNf4Levels[3],  kNf4Levels[4],  kNf4Levels[5],
     kNf4Levels[6], kNf4Levels[7], kNf4Levels[8],  kNf4Levels[9],  kNf4Levels[10], kNf4Levels[11],
     kNf4Levels[12], kNf4Levels[13], kNf4Levels[14], HUGE_VALF};

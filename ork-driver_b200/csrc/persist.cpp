@@ -86,8 +86,8 @@ int check(const void *blob, size_t n, int dtype, int K, int N) {
     memcpy(soc, h.soc, 16);
     if (!said_caps++)
       fprintf(stderr,
-              "[ork] refusing a persisted weight built against DIFFERENT caps (pack soc='%s' capid=%08x, this "
-              "build soc='%s' capid=%08x): its tiles use another layout; rebuild the .orkpack on this machine\n",
+              "[ork] persisted weight rejected: it was written for device '%s' (caps id %08x) and this library "
+              "is '%s' (caps id %08x), whose resident layout differs; dump the weight again with this library\n",
               soc, h.capid, kSocId, capid());
     return ORK_PACKERR_CAPS;
   }

@@ -112,6 +112,7 @@ SIGNATURES = [
     ("ork_b200_tc_choice", _i, [_i, _i, _i, _i, _vp]),
     ("ork_b200_gemv_choice", _i, [_i, _i, _i, _i, _vp]),
     ("ork_b200_reload_tuning", _i, [_vp]),
+    ("ork_b200_staging_bytes", _sz, [_vp]),
     ("ork_i4_mm_run_stream", _i, [_vp, _i, _vp]),
     ("ork_mm_run_async", _vp, [_vp, _vp, _i, _vp, _vp]),
     ("ork_i8_mm_run_async", _vp, [_vp, _vp, _i, _vp, _vp]),

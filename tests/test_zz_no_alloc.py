@@ -84,3 +84,47 @@ def test_noalloc_refuses_bad_arguments(ctx):
         w8.free()
     finally:
         w.free()
+
+
+def test_noalloc_allocates_nothing_on_a_fresh_context():
+    """What the entry point exists for: on a context that has never run anything, two calls with host
+    buffers leave the context without any run-time staging (ork_b200_staging_bytes stays 0), while one
+    ork_i8_mm_run on the same context does allocate its staging buffers."""
+    L = ork_b200.lib()
+    K, N, M = 2048, 1024, 8
+    rng = np.random.default_rng(17)
+    B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+    with ork_b200.Context() as fresh:
+        w = fresh.i8_pack(B)
+        try:
+            assert L.ork_b200_staging_bytes(fresh.ctx) == 0
+            for call in range(2):
+                A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+                rc, got = _noalloc(fresh, w, A)
+                assert rc == 0 and np.array_equal(got, of.gemm_i32(A, B)), call
+                assert L.ork_b200_staging_bytes(fresh.ctx) == 0, call
+            rc, _ = fresh.run(w, A)
+            assert rc == 0 and L.ork_b200_staging_bytes(fresh.ctx) > 0
+        finally:
+            w.free()
+
+
+def test_noalloc_device_buffers_in_place_beyond_the_scratch(ctx):
+    """Device-resident A and C are used in place, as by ork_i8_mm_run, so a run whose host buffers would
+    not fit the 4 MiB scratch (1 MiB of A + 4 MiB of C) works when they are device memory."""
+    import torch
+
+    L = ork_b200.lib()
+    K, N, M = 2048, 2048, 512
+    rng = np.random.default_rng(23)
+    B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+    w = ctx.i8_pack(B)
+    try:
+        A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+        dA = torch.from_numpy(A).cuda()
+        dC = torch.zeros((M, N), dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        assert L.ork_i8_mm_run_noalloc(ctx.ctx, w.h, M, dA.data_ptr(), dC.data_ptr()) == 0
+        assert np.array_equal(dC.cpu().numpy(), of.gemm_i32(A, B))
+    finally:
+        w.free()
