@@ -135,6 +135,15 @@ bool is_device_ptr(const void *p, int device) {
   return at.type == cudaMemoryTypeDevice && at.device == device;
 }
 
+bool pinned_host_ptr(const void *p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeHost;
+}
+
 bool device_ptrs_ok(const ork_npu *c, const char *name, std::initializer_list<const void *> ps) {
   for (const void *p : ps)
     if (p && !is_device_ptr(p, c->device)) {
@@ -199,7 +208,9 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
 }
 
 // Launch one matmul on device buffers (A, C already on the context's GPU).
-int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
+int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) { return launch_on(c, w, M, dA, dC, c->pdl); }
+
+int launch_on(ork_npu *c, ork_w *w, int M, const void *dA, void *dC, bool pdl) {
   RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt, &c->tune};
   int n = 0;
   const int route = route_for(c, w, M);
@@ -207,7 +218,7 @@ int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
     fprintf(stderr, "[ork] ERROR: no kernel for this weight format at K=%d\n", w->K);
     return -1;
   }
-  cudaError_t e = route == 1 ? launch_gemm_tc(a, c->stream, c->pdl, &n) : launch_gemv(a, c->stream, c->pdl, &n);
+  cudaError_t e = route == 1 ? launch_gemm_tc(a, c->stream, pdl, &n) : launch_gemv(a, c->stream, pdl, &n);
   c->launches += (uint64_t)n;
   if (e != cudaSuccess) {
     log_err("kernel launch", e);
@@ -219,6 +230,58 @@ int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) {
 }  // namespace orkb
 
 namespace {
+
+int finish_sync(ork_npu *c, cudaStream_t s, const char *name) {
+  const cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    log_err(name, e);
+    return -1;
+  }
+  if (device_error()) {
+    fprintf(stderr, "[ork] ERROR [%s]: a kernel's bounded pipeline wait timed out; result discarded\n", name);
+    return -1;
+  }
+  return 0;
+}
+
+// A host-buffer run large enough to pay for it, with A and C in pinned memory, goes through in row blocks
+// on three streams: block i's activations upload (up), its matmul runs on the context's stream once they
+// have landed, and its results read back (down) once it has finished. PCIe moves data both ways at once,
+// so the upload of block i + 1 and the readback of block i overlap each other and the kernels; the call
+// takes about the larger of the two transfer directions instead of their sum. Blocks hold about 1 MiB of
+// results each (2 to 8 blocks, rows a multiple of 16).
+constexpr size_t kPipeMinBytes = (size_t)1 << 20;
+
+int run_pipelined(ork_npu *c, ork_w *w, int M, const void *A, void *C, size_t esz, const char *name) {
+  const size_t arow = (size_t)w->K * esz, crow = (size_t)w->N * 4;
+  const size_t abytes = (size_t)M * arow, cbytes = (size_t)M * crow;
+  int nb = (int)((cbytes + kPipeMinBytes - 1) / kPipeMinBytes);
+  nb = nb < 2 ? 2 : nb > 8 ? 8 : nb;
+  int R = (M + nb - 1) / nb;
+  R = (R + 15) & ~15;
+  nb = (M + R - 1) / R;
+  if (!grow(&c->dA, &c->capA, abytes) || !grow(&c->dC, &c->capC, cbytes)) return -1;
+  // the staging buffers may still be read or written by work queued earlier on the context's stream
+  if (cudaEventRecord(c->pev[0], c->stream) != cudaSuccess || cudaStreamWaitEvent(c->up, c->pev[0], 0) != cudaSuccess)
+    return -1;
+  for (int b = 0; b < nb; b++) {
+    const int m0 = b * R, rows = M - m0 < R ? M - m0 : R;
+    const uint8_t *ha = (const uint8_t *)A + (size_t)m0 * arow;
+    uint8_t *da = (uint8_t *)c->dA + (size_t)m0 * arow, *dc = (uint8_t *)c->dC + (size_t)m0 * crow;
+    cudaEvent_t landed = c->pev[1 + 2 * b], done = c->pev[2 + 2 * b];
+    if (cudaMemcpyAsync(da, ha, (size_t)rows * arow, cudaMemcpyHostToDevice, c->up) != cudaSuccess ||
+        cudaEventRecord(landed, c->up) != cudaSuccess || cudaStreamWaitEvent(c->stream, landed, 0) != cudaSuccess)
+      return -1;
+    // no programmatic overlap: each block's kernel starts after its upload, not with the previous kernel
+    if (launch_on(c, w, rows, da, dc, false)) return -1;
+    if (cudaEventRecord(done, c->stream) != cudaSuccess || cudaStreamWaitEvent(c->down, done, 0) != cudaSuccess ||
+        cudaMemcpyAsync((uint8_t *)C + (size_t)m0 * crow, dc, (size_t)rows * crow, cudaMemcpyDeviceToHost, c->down) !=
+            cudaSuccess)
+      return -1;
+  }
+  if (finish_sync(c, c->down, name)) return -1;
+  return finish_sync(c, c->stream, name);
+}
 
 // The synchronous run shared by the three public run functions.
 int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype, const char *name) {
@@ -235,6 +298,8 @@ int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype
   DeviceGuard dg(c->device);
   const bool a_dev = is_device_ptr(A, c->device) && ((uintptr_t)A % 16 == 0);
   const bool c_dev = is_device_ptr(C, c->device) && ((uintptr_t)C % 4 == 0);
+  if (!a_dev && !c_dev && cbytes >= kPipeMinBytes && M >= 32 && c->up && pinned_host_ptr(A) && pinned_host_ptr(C))
+    return run_pipelined(c, w, M, A, C, esz, name);
   const void *dA = A;
   void *dC = C;
   if (!a_dev) {
@@ -305,6 +370,17 @@ ork_npu *ork_npu_init(void) {
     return nullptr;
   }
   c->stream = c->own_stream;
+  bool aux = cudaStreamCreateWithFlags(&c->up, cudaStreamNonBlocking) == cudaSuccess &&
+             cudaStreamCreateWithFlags(&c->down, cudaStreamNonBlocking) == cudaSuccess;
+  for (cudaEvent_t &e : c->pev) aux = aux && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+  if (!aux) {  // the pipelined host-buffer path is an optimisation: without it runs go in one piece
+    cudaGetLastError();
+    if (c->up) cudaStreamDestroy(c->up);
+    if (c->down) cudaStreamDestroy(c->down);
+    for (cudaEvent_t &e : c->pev)
+      if (e) cudaEventDestroy(e), e = nullptr;
+    c->up = c->down = nullptr;
+  }
   if (cudaMalloc(&c->dG, 16) != cudaSuccess || cudaMemset(c->dG, 0, 16) != cudaSuccess) {
     if (c->dG) cudaFree(c->dG);
     cudaStreamDestroy(c->own_stream);
@@ -329,6 +405,10 @@ void ork_npu_free(ork_npu *c) {
     if (c->dG) cudaFree(c->dG);
     if (c->hP) cudaFreeHost(c->hP);
     if (c->async_ev) cudaEventDestroy(c->async_ev);
+    if (c->up) cudaStreamDestroy(c->up);
+    if (c->down) cudaStreamDestroy(c->down);
+    for (cudaEvent_t e : c->pev)
+      if (e) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
   }
   delete c;

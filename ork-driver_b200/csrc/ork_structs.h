@@ -31,6 +31,10 @@ struct ork_npu {
   void *hP = nullptr;    // pinned host staging of the ork_async runs (A in, C out), chain.cpp
   size_t capP = 0;
   cudaEvent_t async_ev = nullptr;  // completion of the ork_async job in flight
+  // pipelined host-buffer runs (api.cpp run_sync): upload and readback streams beside the context's
+  // stream, and the events that chain a run's row blocks through the three
+  cudaStream_t up = nullptr, down = nullptr;
+  cudaEvent_t pev[1 + 2 * 8] = {};
   bool async_busy = false;         // an ork_async job is in flight (one at a time, as in the reference)
   int last_async_cpu = -1;         // sched_getcpu() of the thread that queued the latest ork_async job
   bool pdl = true;
@@ -87,8 +91,12 @@ int layer_enqueue(ork_npu *c, const struct ork_layer_dims *d, ork_w *const *W, c
 void ring_free(ork_npu *c);
 // Releases the persistent-layer tables of a context (layer.cu).
 void layer_tabs_free(ork_npu *c);
-// Launch one matmul on device buffers of the context's GPU (the route of route_for); 0 or -1.
+// Launch one matmul on device buffers of the context's GPU (the route of route_for); 0 or -1. launch_on
+// chooses programmatic dependent launch explicitly (launch: the context's setting).
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC);
+int launch_on(ork_npu *c, ork_w *w, int M, const void *dA, void *dC, bool pdl);
+// Pinned (page-locked) host memory, which copies can move asynchronously.
+bool pinned_host_ptr(const void *p);
 // A new resident weight: device memory of `bytes`, filled from host memory in the resident format.
 ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host_resident, size_t bytes);
 }  // namespace orkb

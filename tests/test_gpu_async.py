@@ -196,3 +196,42 @@ def test_device_entry_points_refuse_host_buffers(ctx):
         assert ctx.launches() == n0
     finally:
         w.free()
+
+
+@pytest.mark.parametrize("kind,K,N,M", [("i8", 2048, 2048, 512), ("i8", 6144, 2048, 300), ("i8", 1024, 8192, 40),
+                                        ("i4", 2048, 4096, 200), ("f16", 1024, 4096, 96)])
+def test_pinned_host_runs_in_row_blocks(ctx, kind, K, N, M):
+    """A synchronous run over pinned host buffers with at least 1 MiB of results goes through in row blocks
+    on three streams (upload, matmul, readback overlapping); C must equal the oracle's exactly (fp16:
+    within the tolerance), row tails included, and equal the one-piece result of pageable buffers."""
+    import torch
+
+    L = ork_b200.lib()
+    rng = np.random.default_rng(K + N + M)
+    if kind == "f16":
+        B = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+        w = ctx.f16_pack(B)
+        A = rng.uniform(-1, 1, size=(M, K)).astype(np.float16)
+        tA, tC = torch.from_numpy(A).pin_memory(), torch.zeros((M, N), dtype=torch.float32).pin_memory()
+        fn = L.ork_f16_mm_run
+    else:
+        lo, hi = (-8, 8) if kind == "i4" else (-128, 128)
+        B = rng.integers(lo, hi, size=(K, N), dtype=np.int8)
+        w = ctx.i4_pack(B) if kind == "i4" else ctx.i8_pack(B)
+        A = rng.integers(lo, hi, size=(M, K), dtype=np.int8)
+        tA, tC = torch.from_numpy(A).pin_memory(), torch.zeros((M, N), dtype=torch.int32).pin_memory()
+        fn = L.ork_i4_mm_run if kind == "i4" else L.ork_i8_mm_run
+    try:
+        for _ in range(2):
+            tC.zero_()
+            assert fn(ctx.ctx, w.h, M, tA.data_ptr(), tC.data_ptr()) == 0
+            got = tC.numpy()
+            rc, one_piece = ctx.run(w, A)
+            assert rc == 0
+            if kind == "f16":
+                assert np.abs(got - of.gemm_f16(A, B)).max() <= f16_tol(A, B)
+            else:
+                assert np.array_equal(got, of.gemm_i32(A, B))
+                assert np.array_equal(got, one_piece)
+    finally:
+        w.free()
