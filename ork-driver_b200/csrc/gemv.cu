@@ -189,13 +189,14 @@ __device__ __forceinline__ void store_out(void *C, const OutStage &os, size_t id
   }
 }
 
-template <int FMT, int MT, int TR>
+template <int FMT, int MT, int TR, int NW = kWarps>
 __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A,
                                            void *__restrict__ Cout, int M, int K, int N, int n0, int cstride,
                                            const Tables &tb, const OutStage &os) {
   using T = typename Acc<FMT>::T;
   constexpr int WR = TR / (4 * kR);  // warp-row groups
-  constexpr int WK = kWarps / WR;    // warps splitting K
+  constexpr int WK = NW / WR;        // warps splitting K
+  static_assert(WK >= 1 && NW % WR == 0, "whole warp-row groups");
   constexpr int V = kR * MT;
   constexpr int NGRP = TR / 8;       // 8-channel copy groups (one mbarrier each)
   extern __shared__ __align__(128) uint8_t smem[];
@@ -290,7 +291,7 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
       }
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < TR * MT; t += kWarps * 32) {
+    for (int t = threadIdx.x; t < TR * MT; t += NW * 32) {
       const int m = t / TR, lr = t % TR;
       if (m < M && lr < rows) {
         T s = red[0][lr][m];
@@ -302,11 +303,11 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
   }
 }
 
-template <int FMT, int MT, int TR>
-__global__ void __launch_bounds__(kWarps * 32)
+template <int FMT, int MT, int TR, int NW>
+__global__ void __launch_bounds__(NW * 32)
 gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M, int K,
             int N, Tables tb) {
-  gemv_block<FMT, MT, TR>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb, OutStage{});
+  gemv_block<FMT, MT, TR, NW>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb, OutStage{});
 }
 
 // Batched (chain / MoE) variant: many independent matmuls of one weight format in one launch. Task t
@@ -643,6 +644,7 @@ gemv_direct_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A,
 
 struct Cfg {
   int mt, tr;
+  int nw = kWarps;      // warps per CTA of the staged kernel
   bool direct = false;  // the direct-load kernel (cpw channels per warp) instead of the staged one
   int cpw = 2;
 };
@@ -668,27 +670,34 @@ Cfg choose(int fmt, int M, int K, int N, const Tuning &tu) {
     c.direct = true;
     c.cpw = 2;
   }
+  // 8 warps per 8-channel CTA (K split 8 ways: the post-dependency dot product of a CTA halves) for one
+  // row on weights of 8 Mi elements or more with N <= 8192 (measured: 2048x6144 3.65 -> 3.46 us, 6144x2048
+  // 3.73 -> 3.66, 8192x8192 12.74 -> 12.46; slower on 2048x12288 and no gain on 2048x2048)
+  if (!c.direct && c.mt == 1 && c.tr == 8 && (size_t)K * N >= ((size_t)8 << 20) && N <= 8192) c.nw = 8;
   // tuning overrides (the context's ORKB_GEMV_* values)
   if (tu.gemv_kind >= 0) c.direct = tu.gemv_kind == 1 || !staged_fits;
   if (tu.gemv_cpw == 1 || tu.gemv_cpw == 2 || tu.gemv_cpw == 4) c.cpw = tu.gemv_cpw;
   if ((tu.gemv_tr == 8 || tu.gemv_tr == 16 || tu.gemv_tr == 32) &&
       (size_t)tu.gemv_tr * rowB + (size_t)c.mt * K * 2 <= 196 * 1024)
     c.tr = tu.gemv_tr;
+  if (tu.gemv_nw == 4 || tu.gemv_nw == 8 || tu.gemv_nw == 16) c.nw = tu.gemv_nw;
+  // only the (channels, warps) pairs that are built: fall back to 4 warps
+  if (!((c.nw == 4) || (c.nw == 8 && c.tr <= 16) || (c.nw == 16 && c.tr >= 16))) c.nw = 4;
   return c;
 }
 
-template <int FMT, int MT, int TR>
+template <int FMT, int MT, int TR, int NW>
 cudaError_t launch_one(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cudaStream_t s, bool pdl,
                        const Tables &tb) {
   const size_t smem = (size_t)TR * fmt_row_bytes(FMT, a.K) + (size_t)m * (FMT == FMT_F16 ? 2 : 1) * a.K;
-  auto kern = gemv_kernel<FMT, MT, TR>;
+  auto kern = gemv_kernel<FMT, MT, TR, NW>;
   {  // the full dynamic budget (the static part adds ~1 KB), once per device
     const cudaError_t e = smem_attr((const void *)kern, 200 * 1024);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + TR - 1) / TR);
-  cfg.blockDim = dim3(kWarps * 32);
+  cfg.blockDim = dim3(NW * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
@@ -702,12 +711,15 @@ cudaError_t launch_one(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cud
 template <int FMT>
 cudaError_t dispatch_fmt(const RunArgs &a, const Cfg &c, const uint8_t *Ab, void *Cb, int m, cudaStream_t s,
                          bool pdl, const Tables &tb) {
-#define ORKB_GEMV_CASE(MT_, TR_) \
-  if (c.mt == MT_ && c.tr == TR_) return launch_one<FMT, MT_, TR_>(a, Ab, Cb, m, s, pdl, tb);
-  ORKB_GEMV_CASE(1, 8) ORKB_GEMV_CASE(1, 16) ORKB_GEMV_CASE(1, 32)
-  ORKB_GEMV_CASE(2, 8) ORKB_GEMV_CASE(2, 16) ORKB_GEMV_CASE(2, 32)
-  ORKB_GEMV_CASE(4, 8) ORKB_GEMV_CASE(4, 16) ORKB_GEMV_CASE(4, 32)
-  ORKB_GEMV_CASE(8, 8) ORKB_GEMV_CASE(8, 16) ORKB_GEMV_CASE(8, 32)
+  // (channels per CTA, warps): 4 warps for 8 / 16 / 32 channels, 8 warps for 8 / 16, 16 warps for 16 / 32
+#define ORKB_GEMV_CASE(MT_, TR_, NW_) \
+  if (c.mt == MT_ && c.tr == TR_ && c.nw == NW_) return launch_one<FMT, MT_, TR_, NW_>(a, Ab, Cb, m, s, pdl, tb);
+#define ORKB_GEMV_MT(MT_)                                                                  \
+  ORKB_GEMV_CASE(MT_, 8, 4) ORKB_GEMV_CASE(MT_, 16, 4) ORKB_GEMV_CASE(MT_, 32, 4)           \
+  ORKB_GEMV_CASE(MT_, 8, 8) ORKB_GEMV_CASE(MT_, 16, 8) ORKB_GEMV_CASE(MT_, 16, 16)          \
+  ORKB_GEMV_CASE(MT_, 32, 16)
+  ORKB_GEMV_MT(1) ORKB_GEMV_MT(2) ORKB_GEMV_MT(4) ORKB_GEMV_MT(8)
+#undef ORKB_GEMV_MT
 #undef ORKB_GEMV_CASE
   return cudaErrorInvalidConfiguration;
 }

@@ -34,10 +34,11 @@ extern const int8_t kNf4Lut[16];
 // router's own choice:
 //   tc_tn ORKB_TC_TN (128/192/256), tc_na ORKB_TC_NA (1/2), tc_stages ORKB_TC_STAGES, tc_pair ORKB_TC_PAIR
 //   (1..3), tc_sk ORKB_TC_SK (1..8); gemv_kind ORKB_GEMV_KIND (0 staged / 1 direct), gemv_cpw
-//   ORKB_GEMV_CPW (1/2/4), gemv_tr ORKB_GEMV_TR (8/16/32); layer_fused ORKB_LAYER_FUSED (0 multi-launch).
+//   ORKB_GEMV_CPW (1/2/4), gemv_tr ORKB_GEMV_TR (8/16/32), gemv_nw ORKB_GEMV_NW (4/8/16 warps);
+//   layer_fused ORKB_LAYER_FUSED (0 multi-launch).
 struct Tuning {
   int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0;
-  int gemv_kind = -1, gemv_cpw = 0, gemv_tr = 0;
+  int gemv_kind = -1, gemv_cpw = 0, gemv_tr = 0, gemv_nw = 0;
   int layer_fused = -1;
 };
 Tuning tuning_from_env();
