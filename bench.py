@@ -374,9 +374,8 @@ def sharded_70b(args, Ms, dist=None):
             Cfull = {name: (Cf[name] if world > 1 else Cl[name]).data_ptr() for name, K, N, _ in shapes}
 
         def run(name, w, a):
-            if p2p:
-                assert L.ork_b200_i8_mm_run_peers_async(ctx.ctx, w.h, M, a.data_ptr(), tab[name]) == 0
-                assert L.ork_b200_peers_wait_async(ctx.ctx, tab[name]) == 0
+            if p2p:  # matmul + push of the shard to every rank + bounded wait for every rank's shard
+                assert L.ork_b200_i8_mm_run_gather_async(ctx.ctx, w.h, M, a.data_ptr(), tab[name]) == 0
             else:
                 assert L.ork_b200_i8_mm_run_async(ctx.ctx, w.h, M, a.data_ptr(), Cl[name].data_ptr()) == 0
                 if world > 1:

@@ -140,8 +140,11 @@ int ork_b200_argmax_scaled_async(ork_npu *ctx, const int32_t *C, const float *bs
  * bytes, exchanged by the caller over any transport) and ork_b200_sym_open (a peer's buffer mapped here).
  * flags[r] is rank r's signal block (at least 4 * R bytes of a symmetric buffer, zero at allocation).
  * A run is the local matmul plus one push kernel (its programmatic dependent) that stores the shard into
- * every rank's C and signals. Rule: read C before starting the next peer run on this rank (a peer
- * rewrites C only after a later signal of ours).
+ * every rank's C and signals. ork_b200_{i8,i4}_mm_run_gather_async is a run whose push kernel also
+ * waits (bounded) for every rank's signal of the run: C is complete on this rank once the stream passes
+ * it, with no separate wait (one launch fewer per matmul); each run is consumed by exactly one wait,
+ * its own or an ork_b200_peers_wait_async, in order. Rule: read C before starting the next peer run on
+ * this rank (a peer rewrites C only after a later signal of ours).
  * Returns 0 / NULL-free on success, -1 (NULL) on bad arguments or CUDA errors. No counterpart in
  * ork-driver, which gathers its cores' column slices on the host (src/npu.c:1356-1398). */
 #define ORK_B200_IPC_HANDLE_BYTES 64
@@ -156,6 +159,8 @@ void ork_b200_peers_destroy(ork_b200_peers *p);
 int ork_b200_i8_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
 int ork_b200_i4_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
 int ork_b200_peers_wait_async(ork_npu *ctx, ork_b200_peers *p);
+int ork_b200_i8_mm_run_gather_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
+int ork_b200_i4_mm_run_gather_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
 /* Copy `bytes` between any two host / device addresses, ordered after the context's queued work, and wait
  * for it (for callers without a CUDA binding of their own, e.g. to read a symmetric buffer). 0 or -1. */
 int ork_b200_copy(ork_npu *ctx, void *dst, const void *src, size_t bytes);

@@ -73,6 +73,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// L2 prefetch of one tile of a tensor map (no data returned, no effect on the values later loads read)
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -494,6 +499,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     if (SWAP) tma_load_2d(smem_u32(sS + s * S_BYTES), &mapS, x, c0, full0 + 8 * s);
     else tma_load_2d(smem_u32(sR + s * R_BYTES), &mapR, x, r0, full0 + 8 * s);
   };
+  auto prefetch_a = [&](int kb) {
+    const int x = kb * (BK_BYTES / ESZ);
+    if (SWAP) tma_prefetch_2d(&mapS, x, c0);
+    else tma_prefetch_2d(&mapR, x, r0);
+  };
 
   bool ep_ok = false;  // the epilogue warps' accumulator is complete (no bounded wait expired)
   // integer split-K: the splits reduce-add into C after split 0 has zeroed it. A split-phase cluster
@@ -510,6 +520,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         mbar_expect_tx(full0 + 8 * i, TX_BYTES);
         load_w(i, kb0 + i);
       }
+      // the first ring's activation tiles are prefetched into L2 before the wait (a hint: the loads
+      // after it read the current data through L2 either way), so a cold A costs L2 latency, not HBM's.
+      // Every CTA of a row (column, when swapped) of tiles reads the same A tiles: one CTA in eight of a
+      // swapped grid asks, and for row tiles only the first weight tile's CTAs (each tile once: a
+      // prefetch by all 16-48 CTAs sharing it slowed M = 512 runs by 3-4 %)
+      if (SWAP ? (blockIdx.x & 7) == 0 : blockIdx.y == 0)
+        for (int i = 0; i < pre; i++) prefetch_a(kb0 + i);
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int i = 0; i < pre; i++) load_a(i, kb0 + i);
       for (int kb = kb0 + pre; kb < kb1; kb++) {
@@ -809,6 +826,11 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
     if (SWAP) tma_load_2d_pair(smem_u32(sS + s * S_BYTES), &mapS, x, sr, mapa_u32(full0 + 8 * s, leader_rank));
     else tma_load_2d_pair(smem_u32(sR + s * R_BYTES), &mapR, x, rr, mapa_u32(full0 + 8 * s, leader_rank));
   };
+  auto prefetch_a = [&](int kb) {
+    const int x = kb * (BK_BYTES / ESZ);
+    if (SWAP) tma_prefetch_2d(&mapS, x, sr);
+    else tma_prefetch_2d(&mapR, x, rr);
+  };
   auto expect = [&](int s) {
     if (leader) mbar_expect_tx(full0 + 8 * s, FULL_TX);
     if (NIB) mbar_expect_tx(wfull0 + 8 * s, NIB_BYTES);
@@ -821,6 +843,8 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
         expect(i);
         load_w(i, kb0 + i);
       }
+      if (SWAP ? (blockIdx.x & 15) < 2 : blockIdx.y == 0)  // L2 hint before the wait (see gemm_tc_kernel)
+        for (int i = 0; i < pre; i++) prefetch_a(kb0 + i);
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int i = 0; i < pre; i++) load_a(i, kb0 + i);
       for (int kb = kb0 + pre; kb < kb1; kb++) {

@@ -189,7 +189,7 @@ __device__ __forceinline__ void store_out(void *C, const OutStage &os, size_t id
   }
 }
 
-template <int FMT, int MT, int TR, int NW = kWarps>
+template <int FMT, int MT, int TR, int NW = kWarps, int P = 2>
 __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A,
                                            void *__restrict__ Cout, int M, int K, int N, int n0, int cstride,
                                            const Tables &tb, const OutStage &os) {
@@ -229,6 +229,12 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
                      : "memory");
     }
   }
+  // The activations are read only after the wait (the previous kernel may write them); an L2 prefetch
+  // of them before it has no effect on the values read and saves the HBM latency when they are cold (a
+  // prefetch is a hint: the copy after the wait reads the current data through L2 either way). One CTA
+  // in eight asks.
+  if (threadIdx.x == 0 && (blockIdx.x & 7) == 0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(A), "r"((uint32_t)(M * a_row)) : "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // the activations (written by the previous kernel) come after the wait: one copy of the M x K block
   const uint32_t sA = sW + (uint32_t)(TR * rowB);
@@ -247,13 +253,37 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
 
   // this lane's channels: local rows wr*8 + g + 4r, r < kR (the warp-row group is one copy group)
   const int lrow0 = wr * 8 + g;
-  const bool ok = mbar_wait0(smem_u32(&bars[wr])) && mbar_wait0(smem_u32(&bars[NGRP]));
   const int S = (int)((rowB + 127) / 128);
-  if (ok && wr * 8 < rows) {
-    const uint32_t base0 = sW + (uint32_t)(lrow0 * rowB) + (uint32_t)(j * 16);
-    const uint32_t a_k = (FMT == FMT_U4 || FMT == FMT_NF4) ? 2u : 1u;  // activation bytes per weight byte
+  const uint32_t base0 = sW + (uint32_t)(lrow0 * rowB) + (uint32_t)(j * 16);
+  const uint32_t a_k = (FMT == FMT_U4 || FMT == FMT_NF4) ? 2u : 1u;  // activation bytes per weight byte
+  // The weights land long before the activations (they were requested before the dependency wait), so
+  // the warp's first P chunks per lane move from shared memory into registers while the activations are
+  // still in flight: after they land only the multiply-adds remain (the shared-memory read of a CTA's
+  // weight block is a second pass over every weight byte, which would otherwise start only then). P is
+  // sized to the chunks a warp actually has (its registers bound how many CTAs, this launch's and the
+  // next one's, share an SM).
+  uint4 pre[P][kR];
+  const bool live = wr * 8 < rows;
+  const bool okw = mbar_wait0(smem_u32(&bars[wr]));
+  if (okw && live) {
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+      const int s = wk + p * WK;
+      if ((uint32_t)s * 128u + (uint32_t)j * 16u < rowB) {
+#pragma unroll
+        for (int r = 0; r < kR; r++) pre[p][r] = lds128(base0 + (uint32_t)(4 * r * rowB) + (uint32_t)(s * 128));
+      }
+    }
+  }
+  const bool ok = okw && mbar_wait0(smem_u32(&bars[NGRP]));
+  if (ok && live) {
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+      const uint32_t o = (uint32_t)(wk + p * WK) * 128u + (uint32_t)j * 16u;
+      if (o < rowB) mac_chunk<FMT, MT, T>(pre[p], sA + a_k * o, (uint32_t)a_row, M, acc, tb);
+    }
 #pragma unroll 4
-    for (int s = wk; s < S; s += WK) {
+    for (int s = wk + P * WK; s < S; s += WK) {
       const uint32_t o = (uint32_t)s * 128u + (uint32_t)j * 16u;
       if (o >= rowB) break;
       uint4 wv[kR];
@@ -303,11 +333,11 @@ __device__ __forceinline__ void gemv_block(const uint8_t *__restrict__ W, const 
   }
 }
 
-template <int FMT, int MT, int TR, int NW>
+template <int FMT, int MT, int TR, int NW, int P>
 __global__ void __launch_bounds__(NW * 32)
 gemv_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A, void *__restrict__ Cout, int M, int K,
             int N, Tables tb) {
-  gemv_block<FMT, MT, TR, NW>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb, OutStage{});
+  gemv_block<FMT, MT, TR, NW, P>(W, A, Cout, M, K, N, (int)blockIdx.x * TR, N, tb, OutStage{});
 }
 
 // Batched (chain / MoE) variant: many independent matmuls of one weight format in one launch. Task t
@@ -392,6 +422,8 @@ gemv_grouped_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A
     }
   }
   for (int t = threadIdx.x; t < Sk * TR * MT; t += kWarps * 32) P[t] = 0;
+  if (threadIdx.x == 0 && (blockIdx.x & 7) == 0)  // L2 prefetch of the activations (see gemv_block)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(A), "r"((uint32_t)(M * a_row)) : "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     const uint32_t bar = smem_u32(&bars[NGRP]), bytes = (uint32_t)(M * a_row);
@@ -612,6 +644,9 @@ gemv_direct_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ A,
     for (int r = 0; r < CPW; r++)
       if (active && ch < nch) ring[u][r] = ldg_stream(wrow[r] + (size_t)ch * 16);
   }
+  // L2 prefetch of the activations before the wait (a hint only: they are read through L1 after it)
+  if (threadIdx.x == 0 && (blockIdx.x & 7) == 0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(A), "r"((uint32_t)(M * a_row)) : "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (!active) return;
 
@@ -686,11 +721,27 @@ Cfg choose(int fmt, int M, int K, int N, const Tuning &tu) {
   return c;
 }
 
+// Weight chunks per lane that a warp preloads into registers (gemv_block): one-row launches of at most
+// 8192 channels take as many as the warp has, up to 8 (4 for nibbles, whose chunks expand to twice the
+// registers); wider weights (their grids run several waves, which the larger register footprint
+// lengthens: 2048x12288 5.3 -> 5.9 us) and larger M (whose dot product dwarfs the preload) keep 2.
+// Measured at M = 1: 6144x2048 3.66 -> 3.42 us, 8192x8192 12.5 -> 11.6 us, 2048x2048 / 2048x6144 unchanged.
+template <int FMT, int MT, int TR, int NW>
+int preload_chunks(int K, int N) {
+  if (MT > 1 || N > 8192) return 2;
+  const int S = (int)((fmt_row_bytes(FMT, K) + 127) / 128), WK = NW / (TR / 8);
+  const int c = (S + WK - 1) / WK;
+  return c <= 2 ? 2 : (c <= 4 || FMT == FMT_U4 || FMT == FMT_NF4) ? 4 : 8;
+}
+
 template <int FMT, int MT, int TR, int NW>
 cudaError_t launch_one(const RunArgs &a, const uint8_t *Ab, void *Cb, int m, cudaStream_t s, bool pdl,
                        const Tables &tb) {
   const size_t smem = (size_t)TR * fmt_row_bytes(FMT, a.K) + (size_t)m * (FMT == FMT_F16 ? 2 : 1) * a.K;
-  auto kern = gemv_kernel<FMT, MT, TR, NW>;
+  const int P = preload_chunks<FMT, MT, TR, NW>(a.K, a.N);
+  auto kern = MT > 1 || P == 2 ? gemv_kernel<FMT, MT, TR, NW, 2>
+              : P == 4         ? gemv_kernel<FMT, MT, TR, NW, (MT > 1 ? 2 : 4)>
+                               : gemv_kernel<FMT, MT, TR, NW, (MT > 1 ? 2 : 8)>;
   {  // the full dynamic budget (the static part adds ~1 KB), once per device
     const cudaError_t e = smem_attr((const void *)kern, 200 * 1024);
     if (e != cudaSuccess) return e;

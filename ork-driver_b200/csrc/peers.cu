@@ -7,10 +7,10 @@
 // scratch C at full speed, then a push kernel, launched as its programmatic dependent (it is resident
 // while the matmul drains) with a grid sized from the shard's bytes, that copies the shard's rows into
 // every rank's C with 16-byte stores; each push CTA counts itself done on this GPU (acq_rel) and the
-// last one signals every rank once with a
-// system-scope release add (release.gpu -> acquire.gpu -> release.sys orders every CTA's peer stores
-// before the signal). A rank that needs C waits (on its stream, bounded) until every rank's count of
-// signals reaches the runs it has consumed plus one.
+// last one signals every rank once: one system-scope fence, then a relaxed add per rank (release.gpu ->
+// acquire.gpu -> fence.acq_rel.sys orders every CTA's peer stores before the signals). A rank that needs
+// C waits (on its stream, bounded) until every rank's count of signals reaches the runs it has consumed
+// plus one.
 // (Storing into the peers from the matmul's own epilogue was measured 1.6x slower at M = 1: each of the
 // thousands of short matmul CTAs then waits for its NVLink stores to be acknowledged before it can
 // release; a few large push CTAs pay that latency once, in parallel.)
@@ -51,11 +51,35 @@ constexpr uint64_t kPeerSpin = 4000000000ull;  // ~2 s of SM clock
 constexpr int kPushVecs = 256;      // 16-byte vectors (or elements) per push CTA when sizing the grid
 constexpr size_t kPushMax = 148 * 8;  // at most eight resident 256-thread CTAs per SM; larger shards grid-stride
 
+// Bounded wait until every rank's count of signals to this rank reaches `target` (lane r watches rank
+// r); false when the wait expired (the error flag is then set).
+__device__ __forceinline__ bool wait_signals(const PeerTable *__restrict__ pt, int r, unsigned int target) {
+  if (r >= pt->n) return true;
+  const unsigned int *f = pt->flag[pt->rank] + r;
+  const uint64_t t0 = clock64();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if ((int)(v - target) >= 0) return true;
+    if (clock64() - t0 > kPeerSpin) {
+      { atomicOr(&g_peer_error, 1u); err_word_set(); }
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
 // Copies the local C [M][n] (row stride n) into every rank's C at the shard's offset, grid-striding over
 // 16-byte vectors when the row layout allows, then counts the CTA done on this GPU; the run's last push
-// CTA (of gridDim.x) signals every rank. The grid is sized per run from M * n.
+// CTA (of gridDim.x) signals every rank. The grid is sized per run from M * n. With WAIT, that last CTA
+// then also waits (bounded) for every rank's signal of this run and counts the run consumed, so C is
+// complete on this rank when the kernel is: the gather costs one launch instead of two.
+// The dependent launch (the wait kernel, or the next matmul, which streams its weights before its own
+// dependency wait) is released at once; it still reads nothing of this run before the kernel completes.
+template <bool WAIT>
 __global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C, int M, int n,
                                                     const PeerTable *__restrict__ pt) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the matmul is complete
   const bool vec = (n % 4 == 0) && (pt->ldc % 4 == 0) && (pt->col0 % 4 == 0);
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -83,8 +107,20 @@ __global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(pt->done) : "memory");
     if (old == gridDim.x - 1u) {
       *pt->done = 0u;
+      // one system-scope fence, then relaxed adds (a release pattern for every one of them): a release
+      // add per rank would fence once per rank (measured ~1.7 us each on two GPUs, the largest part of the
+      // gather)
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
       for (int r = 0; r < pt->n; r++)
-        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pt->flag[r] + pt->rank) : "memory");
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(pt->flag[r] + pt->rank) : "memory");
+      if (WAIT) {
+        // the count of consumed runs was last advanced by a wait that completed before this run's
+        // matmul started (stream order)
+        const unsigned int target = *pt->waited + 1u;
+        for (int r = 0; r < pt->n; r++)
+          if (!wait_signals(pt, r, target)) break;
+        *pt->waited = target;
+      }
     }
   }
 }
@@ -99,24 +135,10 @@ __global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C
 __global__ void __launch_bounds__(32) wait_kernel(const PeerTable *__restrict__ pt) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int r = threadIdx.x;
   const unsigned int target = *pt->waited + 1u;  // one signal per rank per run
-  if (r < pt->n) {
-    const unsigned int *f = pt->flag[pt->rank] + r;
-    const uint64_t t0 = clock64();
-    while (true) {
-      unsigned int v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if ((int)(v - target) >= 0) break;
-      if (clock64() - t0 > kPeerSpin) {
-        { atomicOr(&g_peer_error, 1u); err_word_set(); }
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
+  wait_signals(pt, threadIdx.x, target);
   __syncwarp();
-  if (r == 0) *pt->waited += 1u;
+  if (threadIdx.x == 0) *pt->waited = target;
 }
 
 }  // namespace
@@ -139,7 +161,8 @@ using namespace orkb;
 
 namespace {
 
-int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, int dtype, const char *name) {
+int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, int dtype, bool wait,
+              const char *name) {
   if (!c || !w || !dA || !p || p->ctx != c || M < 1 || w->dtype != dtype || w->fmt == FMT_F16) return -1;
   const PeerTable &t = p->host;
   if (w->N + t.col0 > t.ldc || w->N != t.ctas) return -1;  // the table's shard width
@@ -159,7 +182,8 @@ int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, 
   cfg.numAttrs = 1;
   const int32_t *lc = (const int32_t *)c->dC;
   const PeerTable *dev = p->dev;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, push_kernel, lc, M, w->N, dev);
+  const cudaError_t e = wait ? cudaLaunchKernelEx(&cfg, push_kernel<true>, lc, M, w->N, dev)
+                             : cudaLaunchKernelEx(&cfg, push_kernel<false>, lc, M, w->N, dev);
   c->launches += 1;
   if (e != cudaSuccess) {
     log_err(name, e);
@@ -254,11 +278,19 @@ void ork_b200_peers_destroy(ork_b200_peers *p) {
 }
 
 int ork_b200_i8_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
-  return peers_run(c, w, M, dA, p, DT_I8, "ork_b200_i8_mm_run_peers_async");
+  return peers_run(c, w, M, dA, p, DT_I8, false, "ork_b200_i8_mm_run_peers_async");
 }
 
 int ork_b200_i4_mm_run_peers_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
-  return peers_run(c, w, M, dA, p, DT_I4, "ork_b200_i4_mm_run_peers_async");
+  return peers_run(c, w, M, dA, p, DT_I4, false, "ork_b200_i4_mm_run_peers_async");
+}
+
+int ork_b200_i8_mm_run_gather_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
+  return peers_run(c, w, M, dA, p, DT_I8, true, "ork_b200_i8_mm_run_gather_async");
+}
+
+int ork_b200_i4_mm_run_gather_async(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p) {
+  return peers_run(c, w, M, dA, p, DT_I4, true, "ork_b200_i4_mm_run_gather_async");
 }
 
 int ork_b200_copy(ork_npu *c, void *dst, const void *src, size_t bytes) {

@@ -1,5 +1,6 @@
 """Column-sharded runs with the output gather fused into the matmul over peer memory (ork_b200_peers_*,
-ork_b200_i8_mm_run_peers_async / ork_b200_i4_mm_run_peers_async, include/ork_b200.h).
+ork_b200_i8_mm_run_peers_async / ork_b200_i4_mm_run_peers_async, and the one-call run + gather
+ork_b200_i8_mm_run_gather_async / ork_b200_i4_mm_run_gather_async, include/ork_b200.h).
 
 Output channels are independent (ork-driver src/npu/i4/pack.c:63-80), so rank g packs channels
 [g*N/R, (g+1)*N/R) and its run writes them into every rank's C; after ork_b200_peers_wait_async each
@@ -46,7 +47,7 @@ def test_one_rank_table(ctx):
     w = ctx.i8_pack(B)
     g = shard.PeerGroup(ctx, _NoDist)
     t, cptr = g.table(Mmax, N, N)
-    for M in (1, 5, 8, 40):  # decode kernel with fused stores; then the scatter path
+    for M in (1, 5, 8, 40):  # decode and tensor-core matmuls; run + wait, then the one-call run + gather
         A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
         tA = torch.from_numpy(A).to(dev)
         torch.cuda.synchronize()
@@ -54,6 +55,12 @@ def test_one_rank_table(ctx):
         assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
         assert L.ork_b200_sync(ctx.ctx) == 0
         assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), M
+        A2 = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+        tA = torch.from_numpy(A2).to(dev)
+        torch.cuda.synchronize()
+        assert L.ork_b200_i8_mm_run_gather_async(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A2, B)), M
     w.free()
     g.close()
 
@@ -99,11 +106,11 @@ def _two_rank_worker(rank, world, port, kind):
     if kind == "i8":
         B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
         w = ctx.i8_pack(np.ascontiguousarray(B[:, n0:n0 + ncols]))
-        run = L.ork_b200_i8_mm_run_peers_async
+        run, gather = L.ork_b200_i8_mm_run_peers_async, L.ork_b200_i8_mm_run_gather_async
     else:
         B = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
         w = ctx.i4_pack(np.ascontiguousarray(B[:, n0:n0 + ncols]))
-        run = L.ork_b200_i4_mm_run_peers_async
+        run, gather = L.ork_b200_i4_mm_run_peers_async, L.ork_b200_i4_mm_run_gather_async
     g = shard.PeerGroup(ctx, dist)
     t, cptr = g.table(Mmax, N, ncols)
     try:
@@ -116,6 +123,14 @@ def _two_rank_worker(rank, world, port, kind):
             assert L.ork_b200_sync(ctx.ctx) == 0
             assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), (rank, M)
             dist.barrier()  # every rank has read C before anyone runs again (the buffers' reuse rule)
+            # the same through the one-call run + gather (its push kernel waits for every rank's signal)
+            A = rng.integers(-128 if kind == "i8" else -8, 128 if kind == "i8" else 8, size=(M, K), dtype=np.int8)
+            tA = torch.from_numpy(A).to(dev)
+            torch.cuda.synchronize()
+            assert gather(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), (rank, M, "gather")
+            dist.barrier()
         # the run + wait pair captured once and replayed: the counts advance on the device
         M = 4
         A = rng.integers(-8, 8, size=(M, K), dtype=np.int8)
@@ -126,6 +141,21 @@ def _two_rank_worker(rank, world, port, kind):
         with torch.cuda.graph(graph, stream=s):
             assert run(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
             assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B))
+            dist.barrier()
+        del graph
+        # a captured chain of run + gather calls (each consumes its own run), replayed
+        A = rng.integers(-8, 8, size=(M, K), dtype=np.int8)
+        tA = torch.from_numpy(A).to(dev)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(4):
+                assert gather(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
         for _ in range(3):
             graph.replay()
             torch.cuda.synchronize()
