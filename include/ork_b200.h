@@ -143,8 +143,11 @@ int ork_b200_argmax_scaled_async(ork_npu *ctx, const int32_t *C, const float *bs
  * every rank's C and signals. ork_b200_{i8,i4}_mm_run_gather_async is a run whose push kernel also
  * waits (bounded) for every rank's signal of the run: C is complete on this rank once the stream passes
  * it, with no separate wait (one launch fewer per matmul); each run is consumed by exactly one wait,
- * its own or an ork_b200_peers_wait_async, in order. Rule: read C before starting the next peer run on
- * this rank (a peer rewrites C only after a later signal of ours).
+ * its own or an ork_b200_peers_wait_async, in order. Every rank issues the same runs (same M) on a table
+ * in the same order. Reuse rule: a run stores into every rank's C as soon as it starts on any rank, so
+ * every rank must be done reading a table's C before any rank issues the next run on that table: e.g.
+ * read C before issuing the next peer run (on any table) and alternate between at least two tables, or
+ * pass a barrier after reading.
  * Returns 0 / NULL-free on success, -1 (NULL) on bad arguments or CUDA errors. No counterpart in
  * ork-driver, which gathers its cores' column slices on the host (src/npu.c:1356-1398). */
 #define ORK_B200_IPC_HANDLE_BYTES 64

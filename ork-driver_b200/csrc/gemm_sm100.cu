@@ -11,12 +11,14 @@
 //   warp 1      allocates the TMEM accumulator; one thread issues tcgen05.mma (kind::i8 -> s32, or
 //               kind::f16 -> f32) per 32-byte K step; tcgen05.commit frees each stage and finally
 //               signals the epilogue;
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from their TMEM sub-partition.
+//   warps 2..5  epilogue: tcgen05.ld from their TMEM sub-partition into 128-byte-swizzled staging
+//               boxes in the (now idle) ring, written to C by bulk tensor stores (the TMA).
 // Split-K across a thread-block cluster: the SK CTAs of a cluster (gridDim.z = cluster z = SK) take
-// consecutive K ranges of the same tile; each dumps its partial tile to its own shared memory, the
-// cluster synchronises, and every CTA reduces a slice of the tile by reading all SK partials through
-// distributed shared memory, then stores it. No atomics, no workspace, no zeroing of C; the integer
-// sum is exact in any order, so results equal ork-driver's CPU oracle bit for bit.
+// consecutive K ranges of the same tile. Integer tiles: split 0 zeroes the tile, a split-phase cluster
+// barrier orders that before any partial lands, and every split's partial is reduce-added into C by the
+// TMA (cp.reduce.async.bulk.tensor .add: the int32 sum is exact in any order, so results equal
+// ork-driver's CPU oracle bit for bit). fp32 tiles (fp16 weights) are summed in a fixed order through
+// distributed shared memory instead, so their result does not depend on which split finishes first.
 // Out-of-range rows / K columns are zero-filled by the tensor maps, so M, N and K need no padding.
 //
 // Every mbarrier wait is bounded by a clock deadline; on expiry the kernel records an error in a

@@ -66,15 +66,41 @@ def test_one_rank_table(ctx):
 
 
 def test_wait_without_signal_gives_up(ctx):
-    import shard
+    """A two-rank table whose second rank is a buffer of this process that no run ever signals from: the
+    run posts its signals, the wait for the missing rank's gives up (bounded, ~2 s), the next sync reports
+    it once and the context keeps working -- through the separate wait and through the one-call gather."""
+    import torch
 
     L = ctx.L
-    g = shard.PeerGroup(ctx, _NoDist)
-    t, _ = g.table(1, 64, 64)
-    assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0  # nothing will signal: bounded (~2 s)
-    assert L.ork_b200_sync(ctx.ctx) == -1
-    assert L.ork_b200_sync(ctx.ctx) == 0  # the flag was cleared; the context keeps working
-    g.close()
+    dev = torch.device("cuda", L.ork_b200_device(ctx.ctx))
+    K, N = 256, 64
+    rng = np.random.default_rng(5)
+    B = rng.integers(-128, 128, size=(K, N // 2), dtype=np.int8)
+    w = ctx.i8_pack(B)
+    h = (C.c_uint8 * 64)()
+    bufs = [L.ork_b200_sym_alloc(ctx.ctx, N * 4, h) for _ in range(2)]
+    flags = [L.ork_b200_sym_alloc(ctx.ctx, 64, h) for _ in range(2)]
+    assert all(bufs) and all(flags)
+    arr = C.c_void_p * 2
+    t = L.ork_b200_peers_create(ctx.ctx, 2, 0, arr(*bufs), arr(*flags), N, 0, N // 2)
+    assert t
+    tA = torch.from_numpy(rng.integers(-128, 128, size=(1, K), dtype=np.int8)).to(dev)
+    torch.cuda.synchronize()
+    try:
+        assert L.ork_b200_i8_mm_run_peers_async(ctx.ctx, w.h, 1, tA.data_ptr(), t) == 0
+        assert L.ork_b200_peers_wait_async(ctx.ctx, t) == 0  # rank 1 never signals
+        assert L.ork_b200_sync(ctx.ctx) == -1
+        assert L.ork_b200_sync(ctx.ctx) == 0  # the flag was cleared; the context keeps working
+        assert L.ork_b200_i8_mm_run_gather_async(ctx.ctx, w.h, 1, tA.data_ptr(), t) == 0
+        assert L.ork_b200_sync(ctx.ctx) == -1
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        # this rank's own columns did arrive in its C
+        assert np.array_equal(_read(ctx, bufs[0], (1, N))[:, : N // 2], of.gemm_i32(tA.cpu().numpy(), B))
+    finally:
+        L.ork_b200_peers_destroy(t)
+        for p in bufs + flags:
+            L.ork_b200_sym_free(ctx.ctx, p)
+        w.free()
 
 
 def _free_port():
@@ -113,6 +139,7 @@ def _two_rank_worker(rank, world, port, kind):
         run, gather = L.ork_b200_i4_mm_run_peers_async, L.ork_b200_i4_mm_run_gather_async
     g = shard.PeerGroup(ctx, dist)
     t, cptr = g.table(Mmax, N, ncols)
+    t2, cptr2 = g.table(Mmax, N, ncols)
     try:
         for M in (1, 8, 3, 24):
             A = rng.integers(-128 if kind == "i8" else -8, 128 if kind == "i8" else 8, size=(M, K), dtype=np.int8)
@@ -148,19 +175,20 @@ def _two_rank_worker(rank, world, port, kind):
             assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B))
             dist.barrier()
         del graph
-        # a captured chain of run + gather calls (each consumes its own run), replayed
+        # a captured chain of run + gather calls alternating between two tables (the reuse rule), replayed
         A = rng.integers(-8, 8, size=(M, K), dtype=np.int8)
         tA = torch.from_numpy(A).to(dev)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=s):
-            for _ in range(4):
-                assert gather(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
+            for i in range(4):
+                assert gather(ctx.ctx, w.h, M, tA.data_ptr(), t if i % 2 == 0 else t2) == 0
         for _ in range(3):
             graph.replay()
             torch.cuda.synchronize()
             assert L.ork_b200_sync(ctx.ctx) == 0
             assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B))
+            assert np.array_equal(_read(ctx, cptr2, (M, N)), of.gemm_i32(A, B))
             dist.barrier()
         del graph
     finally:
