@@ -174,6 +174,7 @@ Tuning tuning_from_env() {
   t.tc_stages = env_int("ORKB_TC_STAGES", 0);
   t.tc_pair = env_int("ORKB_TC_PAIR", 0);
   t.tc_sk = env_int("ORKB_TC_SK", 0);
+  t.tc_flags = env_int("ORKB_TC_FLAGS", 1);
   t.gemv_kind = env_int("ORKB_GEMV_KIND", -1);
   t.gemv_cpw = env_int("ORKB_GEMV_CPW", 0);
   t.gemv_tr = env_int("ORKB_GEMV_TR", 0);
@@ -213,7 +214,7 @@ ork_w *new_weight(ork_npu *c, int K, int N, int fmt, int dtype, const void *host
 int launch(ork_npu *c, ork_w *w, int M, const void *dA, void *dC) { return launch_on(c, w, M, dA, dC, c->pdl); }
 
 int launch_on(ork_npu *c, ork_w *w, int M, const void *dA, void *dC, bool pdl) {
-  RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt, &c->tune};
+  RunArgs a{w->d, dA, dC, M, w->K, w->N, w->fmt, &c->tune, c->tune.tc_flags ? c->dF : nullptr};
   int n = 0;
   const int route = route_for(c, w, M);
   if (route < 0) {
@@ -389,6 +390,13 @@ ork_npu *ork_npu_init(void) {
     delete c;
     return nullptr;
   }
+  // the split-K tile flags are an optimisation: without them split-K orders its zeroing per cluster
+  const size_t fbytes = (size_t)orkb::kTcFlagTiles * 2 * sizeof(unsigned int);
+  if (cudaMalloc(&c->dF, fbytes) != cudaSuccess || cudaMemset(c->dF, 0, fbytes) != cudaSuccess) {
+    cudaGetLastError();
+    if (c->dF) cudaFree(c->dF);
+    c->dF = nullptr;
+  }
   return c;
 }
 
@@ -405,6 +413,7 @@ void ork_npu_free(ork_npu *c) {
     if (c->dL) cudaFree(c->dL);
     if (c->dX) cudaFree(c->dX);
     if (c->dG) cudaFree(c->dG);
+    if (c->dF) cudaFree(c->dF);
     if (c->hP) cudaFreeHost(c->hP);
     if (c->async_ev) cudaEventDestroy(c->async_ev);
     if (c->up) cudaStreamDestroy(c->up);

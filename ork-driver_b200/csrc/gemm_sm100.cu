@@ -315,6 +315,43 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// Split-K zeroing ordered by a per-tile flag in global memory instead of a cluster barrier (so the
+// splits of a tile need not share a cluster): word 0 = the tile is zeroed, word 1 = splits that have
+// seen it. Split 0 sets word 0 once its zeroes are written; every other split waits for it (bounded)
+// before its first reduce-add; each split counts itself in word 1 once past that point, and the last
+// one clears both words, so the flags are zero again when the launch completes (a later launch reads
+// them only after its dependency wait, i.e. after this grid has finished).
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }  // warps 2..5
+__device__ __forceinline__ void tile_flag_count(unsigned int *tf, int SK) {
+  if (atomicAdd(&tf[1], 1u) == (unsigned int)(SK - 1)) {
+    tf[1] = 0u;
+    tf[0] = 0u;
+  }
+}
+__device__ __forceinline__ void tile_flag_set(unsigned int *tf) {
+  asm volatile("fence.acq_rel.gpu;\n\tst.relaxed.gpu.global.u32 [%0], 1;" ::"l"(tf) : "memory");
+}
+__device__ __forceinline__ bool tile_flag_wait(const unsigned int *tf);
+// a non-zero split's epilogue warps (0..127 = ct): split 0's zeroes of this launch are in C from here on
+__device__ __forceinline__ void tile_flag_pass(const unsigned int *tf, int ct) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // a flag read only once earlier launches are done
+  if (ct == 0) tile_flag_wait(tf);
+  epi_bar_sync();
+}
+__device__ __forceinline__ bool tile_flag_wait(const unsigned int *tf) {
+  const uint64_t t0 = clock64();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(tf) : "memory");
+    if (v) return true;
+    if (clock64() - t0 > kWaitCycles) {
+      { atomicOr(&g_tc_error, 1u); err_word_set(); }
+      return false;
+    }
+    __nanosleep(32);
+  }
+}
+
 __device__ __forceinline__ uint4 ld_cluster_v4(uint32_t cluster_addr) {
   uint4 v;
   asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -399,11 +436,12 @@ __device__ __forceinline__ uint4 add4(uint4 a, uint4 b) {
 // chunks' integer chains overlap: the four converter warps of a CTA have little else to hide their
 // latency with, and with a 2-chunk unroll the expansion, not the weight stream, set the pace of
 // decode-sized nibble runs (ncu: 41 % issue-active, stalls on fixed-latency dependencies).
-template <int FMT, int WROWS>
+template <int FMT, int WROWS, int CT = 128>
 __device__ __forceinline__ void expand_stage(const uint8_t *src, uint8_t *dst, int ct, const Nf4Tables &tb) {
-  static_assert((WROWS * 8) % 128 == 0, "whole chunks per converter thread");
-  constexpr int ITEMS = WROWS * 8 / 128;
-  const int r0 = ct >> 3, c = ct & 7;  // chunk q of this thread: row r0 + 16 q, same k chunk c
+  static_assert((WROWS * 8) % CT == 0 && (CT / 8) % 8 == 0, "whole chunks per converter thread");
+  constexpr int ITEMS = WROWS * 8 / CT;
+  constexpr int RSTEP = CT / 8;        // rows between a thread's chunks (a multiple of 8: same swizzle)
+  const int r0 = ct >> 3, c = ct & 7;  // chunk q of this thread: row r0 + RSTEP q, same k chunk c
   const uint32_t s_src = smem_u32(src) + (uint32_t)(r0 * 64 + c * 8);
   const uint32_t s_dst = smem_u32(dst) + (uint32_t)(r0 * 128 + ((c ^ (r0 & 7)) << 4));
   uint32_t nb[ITEMS][2];
@@ -411,15 +449,25 @@ __device__ __forceinline__ void expand_stage(const uint8_t *src, uint8_t *dst, i
   for (int q = 0; q < ITEMS; q++)
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
                  : "=r"(nb[q][0]), "=r"(nb[q][1])
-                 : "r"(s_src + (uint32_t)(q * 16 * 64)));
+                 : "r"(s_src + (uint32_t)(q * RSTEP * 64)));
 #pragma unroll
   for (int q = 0; q < ITEMS; q++) {
     const uint2 lo = expand8<FMT>(nb[q][0], tb), hi = expand8<FMT>(nb[q][1], tb);
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_dst + (uint32_t)(q * 16 * 128)), "r"(lo.x),
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_dst + (uint32_t)(q * RSTEP * 128)), "r"(lo.x),
                  "r"(lo.y), "r"(hi.x), "r"(hi.y)
                  : "memory");
   }
 }
+
+// Converter warps of the one-CTA kernel: nibble weights in row tiles get four more warps (6..9 beside
+// the epilogue's 2..5), so each SM sub-partition runs two converter warps and one hides the other's
+// dependent-latency stalls (w4a8 6144x2048 M256 10.8 -> 10.4 us, M32 6.4 -> 6.0-6.3). Decode-sized
+// (swapped) grids already put two to four CTAs, each with its four converter warps, on an SM; eight
+// there were slower (70B NF4 M = 8: 686 -> 650 tok/s) and they keep four.
+template <int FMT, bool SWAP>
+constexpr int conv_warps() { return ((FMT == FMT_U4 || FMT == FMT_NF4) && !SWAP) ? 8 : 4; }
+template <int FMT, bool SWAP>
+constexpr int tc_threads() { return 64 + 32 * conv_warps<FMT, SWAP>(); }
 
 constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 128 ? 128 : 256; }
 
@@ -428,10 +476,10 @@ constexpr int tmem_cols(int tn) { return tn <= 32 ? 32 : tn <= 64 ? 64 : tn <= 1
 // (expand8, nibble.cuh) into the 128-byte-swizzled int8 tile the MMA reads, then publish it to the async
 // proxy.
 template <int FMT, bool SWAP, int TN, int STAGES, int NA>
-__global__ void __launch_bounds__(192)
+__global__ void __launch_bounds__(tc_threads<FMT, SWAP>())
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
                const __grid_constant__ CUtensorMap mapC, void *__restrict__ Cout, int M, int N, int K,
-               Nf4Tables tb) {
+               Nf4Tables tb, unsigned int *__restrict__ tflag) {
   // NA accumulators of 128 rows stacked along the R side (TM = 128*NA): each K step issues NA MMAs that
   // share the S tile, so S is fetched once per 128*NA rows (less operand traffic per output)
   constexpr bool F16 = FMT == FMT_F16;
@@ -470,7 +518,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     for (int s = 0; s < STAGES; s++) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
-      mbar_init(conv0 + 8 * s, 4);  // one arrival per converter warp
+      mbar_init(conv0 + 8 * s, conv_warps<FMT, SWAP>());  // one arrival per converter warp
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -510,9 +558,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
   bool ep_ok = false;  // the epilogue warps' accumulator is complete (no bounded wait expired)
   // integer split-K: the splits reduce-add into C after split 0 has zeroed it. A split-phase cluster
   // barrier orders the two: every thread arrives as early as it can (split 0's epilogue warps once the
-  // zeroes are written) and only the epilogue warps wait, well before they need to
+  // zeroes are written) and only the epilogue warps wait, well before they need to -- or, with tile
+  // flags (the splits then are not one cluster), split 0 sets the tile's flag and the others wait on it
   const bool tma_reduce = !F16 && SK > 1;
-  if (tma_reduce && (warp < 2 || ks != 0)) cluster_arrive();
+  const bool flagz = tma_reduce && tflag != nullptr;
+  unsigned int *tf = flagz ? tflag + 2 * (blockIdx.y * gridDim.x + blockIdx.x) : nullptr;
+  // every thread of the cluster arrives once: here warps 0-1 and the converter-only warps 6-9 (and all
+  // warps of the other splits); split 0's epilogue warps after their zeroes
+  if (tma_reduce && !flagz && (warp < 2 || warp >= 6 || ks != 0)) cluster_arrive();
   if (warp == 0) {
     if (lane == 0) {
       // the weight tiles do not depend on the previous kernel: the first ring's worth is requested
@@ -561,8 +614,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
       umma_commit(done);
     }
   } else {
-    const int ct = threadIdx.x - 64;  // 0..127 over warps 2..5
-    if (tma_reduce && ks == 0) {
+    const int ct = threadIdx.x - 64;  // over the converter warps 2.. (0..127: warps 2..5, the epilogue's)
+    const bool epi = warp < 6;        // warps 6..9 (nibble weights only) convert and then leave
+    if (epi && tma_reduce && ks == 0) {
       // split 0 zeroes the tile of C that every split reduce-adds into, once the previous grid (which may
       // still read C) has finished
       asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -574,8 +628,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         *reinterpret_cast<uint4 *>(Cz + (size_t)(m0 + t / vpr) * N + n0 + 4 * (t % vpr)) = make_uint4(0, 0, 0, 0);
       asm volatile("fence.proxy.async.global;" ::: "memory");  // the zeroes, before any reduce (async proxy)
       __syncwarp();
-      cluster_arrive();
+      if (flagz) {
+        epi_bar_sync();  // all four warps' zeroes are written
+        if (ct == 0) tile_flag_set(tf);
+      } else {
+        cluster_arrive();
+      }
     }
+    // the other splits wait for the flag now, while their accumulators fill (nibble weights: after the
+    // conversion, which these warps do meanwhile); they count themselves once their adds are issued
+    if (!NIB && epi && flagz && ks != 0) tile_flag_pass(tf, ct);
     if constexpr (NIB) {
       // converter: per stage, WROWS x 8 chunks of 16 output bytes (row r, k chunk c), written at the
       // 128-byte-swizzle position (chunk c ^ (r & 7)) of the 1024-byte-aligned tile
@@ -587,15 +649,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
         if (!cok) break;
         const uint8_t *src = sN + s * NIB_BYTES;
         uint8_t *dst = sW + s * (SWAP ? R_BYTES : S_BYTES);
-        expand_stage<FMT, WROWS>(src, dst, ct, tb);
+        expand_stage<FMT, WROWS, 32 * conv_warps<FMT, SWAP>()>(src, dst, ct, tb);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(conv0 + 8 * s) : "memory");
       }
     }
+    if (!epi) {
+      // converter-only warps: nothing more to do
+    } else {
     if (tma_reduce) {  // split 0's zeroes are visible to this thread's reduces from here on
-      __syncwarp();
-      cluster_wait();
+      if (flagz) {
+        if (NIB && ks != 0) tile_flag_pass(tf, ct);
+      } else {
+        __syncwarp();
+        cluster_wait();
+      }
       asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     // epilogue warps 2..5 read TMEM sub-partition (warp % 4): TMEM lane = row of an R accumulator. The
@@ -629,6 +698,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
                              r0 + a * BM + sub * 32, M, N, tma_reduce);
       }
     }
+    if (flagz && ct == 0) tile_flag_count(tf, SK);  // past the flag (or its setter): the last one clears it
+    }  // epi
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();
@@ -749,7 +820,7 @@ template <int FMT, bool SWAP, int TN, int STAGES>
 __global__ void __launch_bounds__(192)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
                     const __grid_constant__ CUtensorMap mapC, void *__restrict__ Cout, int M, int N, int K,
-                    Nf4Tables tb) {
+                    Nf4Tables tb, unsigned int *__restrict__ tflag) {
   constexpr bool F16 = FMT == FMT_F16;
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
   constexpr int HS = TN / 2;                             // S rows held by each CTA
@@ -812,7 +883,9 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
   // split-phase cluster barrier (see gemm_tc_kernel); the warps that arrive early complete that phase
   // before the final cluster barrier
   const bool tma_reduce = !F16 && SK > 1;
-  if (tma_reduce && (warp < 2 || ks != 0)) cluster_arrive();
+  const bool flagz = tma_reduce && tflag != nullptr;  // tile flags instead (each CTA's half its own flag)
+  unsigned int *tf = flagz ? tflag + 2 * (blockIdx.y * gridDim.x + blockIdx.x) : nullptr;
+  if (tma_reduce && !flagz && (warp < 2 || ks != 0)) cluster_arrive();
 
   auto load_w = [&](int s, int kb) {
     if constexpr (NIB) {
@@ -890,8 +963,14 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
         *reinterpret_cast<uint4 *>(Cz + (size_t)(m0 + t / vpr) * N + n0 + 4 * (t % vpr)) = make_uint4(0, 0, 0, 0);
       asm volatile("fence.proxy.async.global;" ::: "memory");
       __syncwarp();
-      cluster_arrive();
+      if (flagz) {
+        epi_bar_sync();
+        if (ct == 0) tile_flag_set(tf);
+      } else {
+        cluster_arrive();
+      }
     }
+    if (!NIB && flagz && ks != 0) tile_flag_pass(tf, ct);  // while the accumulator fills (see gemm_tc_kernel)
     if constexpr (NIB) {
       bool cok = true;
       for (int kb = kb0; kb < kb1 && cok; kb++) {
@@ -908,8 +987,12 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
       }
     }
     if (tma_reduce) {
-      __syncwarp();
-      cluster_wait();
+      if (flagz) {
+        if (NIB && ks != 0) tile_flag_pass(tf, ct);
+      } else {
+        __syncwarp();
+        cluster_wait();
+      }
       asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     const int sub = warp & 3;
@@ -935,11 +1018,12 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
                            c0, rr + sub * 32, M, N, tma_reduce);
       }
     }
+    if (flagz && ct == 0) tile_flag_count(tf, SK);
     if (lane == 0) bulk_wait_read();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();
-  if (tma_reduce && warp < 2) cluster_wait();  // the early arrivals' phase, before the final barrier
+  if (tma_reduce && !flagz && warp < 2) cluster_wait();  // the early arrivals' phase, before the final barrier
   if (F16 && SK > 1) {
     cluster_sync();
     // this CTA's slice of its half-tile: (output row, 4-column vector) items in C's row-major order,
@@ -1023,9 +1107,14 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   }
   const Nf4Tables tb = nf4_tables();
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
+  const int gx = (rowsR + TM - 1) / TM, gy = (rowsS + TN - 1) / TN;
+  // integer split-K with the context's tile flags: the splits need not share a cluster. Row tiles only:
+  // decode-sized (swapped) grids split up to 8 ways into short K ranges, where a cluster barrier was
+  // measured faster (int8 M = 8: 2048x2048 2.98 against 3.6 us, 6144x2048 4.65 against 5.2)
+  const bool flagz = !SWAP && FMT != FMT_F16 && sk > 1 && a.tflag && gx * gy <= kTcFlagTiles;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((rowsR + TM - 1) / TM, (rowsS + TN - 1) / TN, sk);
-  cfg.blockDim = dim3(192);
+  cfg.gridDim = dim3(gx, gy, sk);
+  cfg.blockDim = dim3(tc_threads<FMT, SWAP>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[2];
@@ -1034,10 +1123,10 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].id = cudaLaunchAttributeClusterDimension;
   at[1].val.clusterDim.x = 1;
   at[1].val.clusterDim.y = 1;
-  at[1].val.clusterDim.z = sk;
+  at[1].val.clusterDim.z = flagz ? 1 : sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb);
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb, flagz ? a.tflag : (unsigned int *)nullptr);
 }
 
 // CTA-pair launch: grid x = 2 CTAs per 256 R rows, y = S tiles of TN, z = split-K; cluster (2, 1, sk).
@@ -1071,8 +1160,10 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   }
   const Nf4Tables tb = nf4_tables();
   const int rowsR = SWAP ? a.N : a.M, rowsS = SWAP ? a.M : a.N;
+  const int gx = 2 * ((rowsR + 2 * BM - 1) / (2 * BM)), gy = (rowsS + TN - 1) / TN;
+  const bool flagz = !SWAP && FMT != FMT_F16 && sk > 1 && a.tflag && gx * gy <= kTcFlagTiles;  // (as launch_tc)
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * ((rowsR + 2 * BM - 1) / (2 * BM)), (rowsS + TN - 1) / TN, sk);
+  cfg.gridDim = dim3(gx, gy, sk);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -1082,10 +1173,10 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].id = cudaLaunchAttributeClusterDimension;
   at[1].val.clusterDim.x = 2;
   at[1].val.clusterDim.y = 1;
-  at[1].val.clusterDim.z = sk;
+  at[1].val.clusterDim.z = flagz ? 1 : sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb);
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb, flagz ? a.tflag : (unsigned int *)nullptr);
 }
 
 struct TcCfg {
@@ -1147,10 +1238,29 @@ TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
     c.sk = 1;
     for (int s : {2, 3, 4, 6})
       if (t * s <= 132 && KB / s >= 4 && (!c.pair || s <= 2)) c.sk = s;
+    // int8 weights with the split-K tile flags (the splits then share no cluster, so any split and up to
+    // one full wave of 148 CTAs): tile width and split from a cost model fitted to a sweep of the
+    // BASELINE prefill shapes (M 128-512, K and N 2048 / 6144, widths 64-256, splits 1-6; mean error
+    // 0.4 us): us = 4.17 + 0.0088 * operand KB per CTA + 0.0052 * C KB per CTA + 0.166 * MB of C that
+    // all splits write. It trades the per-SM operand stream (narrower tiles re-read more of A and W)
+    // against the int32 tile drain and the split partials the L2 adds up; every split keeps >= 5
+    // k-blocks. Measured against the rule above: 6144x2048xM512 12.6 -> 11.6 us (192 wide, split 3),
+    // 2048x2048xM128 6.6 -> 5.4 us (64 wide), 2048x6144xM128 7.9 -> 7.5 us (split 3, 144 CTAs).
+    if (fmt == FMT_I8 && tu.tc_flags) {
+      double best = 1e30;
+      for (int tn : {64, 128, 192, 256})
+        for (int s : {1, 2, 3, 4, 6}) {
+          const long long ctas = (long long)tiles(tn) * s;
+          if (ctas > 148 || (s > 1 && KB / s < 5)) continue;
+          const double in_kb = (double)K / s * (128 + tn) / 1024.0, out_kb = 128.0 * tn * 4 / 1024.0;
+          const double us = 4.17 + 0.0088 * in_kb + 0.0052 * out_kb + 0.166 * (double)ctas * out_kb / 1024.0;
+          if (us < best) best = us, c.tn = tn, c.sk = s;
+        }
+    }
   }
   // tuning overrides (the context's ORKB_TC_* values): tile width, accumulators, ring depth, split
   if (!c.swap) {
-    if (tu.tc_tn) c.tn = (!nib && (tu.tc_tn == 256 || tu.tc_tn == 192)) ? tu.tc_tn : 128;
+    if (tu.tc_tn) c.tn = (!nib && (tu.tc_tn == 256 || tu.tc_tn == 192 || tu.tc_tn == 64)) ? tu.tc_tn : 128;
     if (tu.tc_na) c.na = tu.tc_na == 2 ? 2 : 1;
     if (c.na == 2) c.tn = 128;
   }
@@ -1212,6 +1322,7 @@ cudaError_t dispatch(const RunArgs &a, const TcCfg &c, cudaStream_t s, bool pdl)
   if constexpr (!NIB) {
     if (c.tn == 256) return launch_tc<FMT, false, 256, 4>(a, c.sk, s, pdl);
     if (c.tn == 192) return launch_tc<FMT, false, 192, 4>(a, c.sk, s, pdl);
+    if (c.tn == 64) return launch_tc<FMT, false, 64, 8>(a, c.sk, s, pdl);
     if (c.stages == 3) return launch_tc<FMT, false, 128, 3>(a, c.sk, s, pdl);
   }
   return launch_tc<FMT, false, 128, NIB ? 4 : 6>(a, c.sk, s, pdl);

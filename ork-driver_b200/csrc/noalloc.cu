@@ -83,7 +83,7 @@ extern "C" int ork_i8_mm_run_noalloc(ork_npu *c, ork_w *w, int M, const int8_t *
   if (!a_dev && cudaMemcpyAsync((void *)dA, A, abytes, cudaMemcpyDefault, c->stream) != cudaSuccess) return -1;
   const int route = orkb::route_for(c, w, M);
   if (route < 0) return -1;
-  orkb::RunArgs args{w->d, dA, dC, M, w->K, w->N, w->fmt, &c->tune};
+  orkb::RunArgs args{w->d, dA, dC, M, w->K, w->N, w->fmt, &c->tune, c->tune.tc_flags ? c->dF : nullptr};
   int n = 0;
   const cudaError_t e = route == 1 ? orkb::launch_gemm_tc(args, c->stream, c->pdl, &n)
                                    : orkb::launch_gemv(args, c->stream, c->pdl, &n);

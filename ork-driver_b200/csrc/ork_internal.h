@@ -33,11 +33,12 @@ extern const int8_t kNf4Lut[16];
 // once, when it is created (or again on ork_b200_reload_tuning), never per launch; 0 / -1 leave the
 // router's own choice:
 //   tc_tn ORKB_TC_TN (128/192/256), tc_na ORKB_TC_NA (1/2), tc_stages ORKB_TC_STAGES, tc_pair ORKB_TC_PAIR
-//   (1..3), tc_sk ORKB_TC_SK (1..8); gemv_kind ORKB_GEMV_KIND (0 staged / 1 direct), gemv_cpw
+//   (1..3), tc_sk ORKB_TC_SK (1..8), tc_flags ORKB_TC_FLAGS (0: split-K zeroing ordered through a
+//   cluster barrier instead of the tile flags); gemv_kind ORKB_GEMV_KIND (0 staged / 1 direct), gemv_cpw
 //   ORKB_GEMV_CPW (1/2/4), gemv_tr ORKB_GEMV_TR (8/16/32), gemv_nw ORKB_GEMV_NW (4/8/16 warps);
 //   layer_fused ORKB_LAYER_FUSED (0 multi-launch).
 struct Tuning {
-  int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0;
+  int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0, tc_flags = 1;
   int gemv_kind = -1, gemv_cpw = 0, gemv_tr = 0, gemv_nw = 0;
   int layer_fused = -1;
 };
@@ -51,7 +52,11 @@ struct RunArgs {
   int M, K, N;
   int fmt;
   const Tuning *tune = nullptr;  // the context's tuning overrides (nullptr: none)
+  // The context's split-K tile flags for the tensor-core kernel (kTcFlagTiles x 2 words, zero between
+  // launches), or nullptr: split-K then orders its zeroing through a cluster barrier instead.
+  unsigned int *tflag = nullptr;
 };
+constexpr int kTcFlagTiles = 16384;
 
 // Decode path: M <= 8 per launch (the launcher loops over row blocks of 8 for larger M). Two kernels:
 // staged (a CTA copies 8 whole weight rows into shared memory) and direct-load (a warp streams its rows

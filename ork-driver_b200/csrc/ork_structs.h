@@ -28,6 +28,7 @@ struct ork_npu {
   size_t capX = 0;
   void *ltabs = nullptr; // device tables of persistent-layer pointer lists (layer.cu)
   void *dG = nullptr;    // 16 bytes, zero between calls: the argmax's running key and CTA count (decode_glue.cu)
+  unsigned int *dF = nullptr;  // tensor-core split-K tile flags, orkb::kTcFlagTiles x 2 words, zero between launches
   void *hP = nullptr;    // pinned host staging of the ork_async runs (A in, C out), chain.cpp
   size_t capP = 0;
   cudaEvent_t async_ev = nullptr;  // completion of the ork_async job in flight

@@ -332,14 +332,18 @@ def test_tensor_core_and_gemv_routes_agree_int4(ctx, env_clean, nf4, K, N):
         w.free()
 
 
-@pytest.mark.parametrize("na,tn,sk", [(1, 128, 1), (1, 128, 4), (2, 128, 1), (2, 128, 2), (2, 128, 4),
-                                      (1, 256, 1), (1, 256, 2), (1, 192, 1), (1, 192, 4)])
-def test_tensor_core_tile_variants_exact(ctx, env_clean, tune, na, tn, sk):
+@pytest.mark.parametrize("na,tn,sk,flags", [(1, 128, 1, 1), (1, 128, 4, 1), (1, 128, 4, 0), (1, 128, 8, 1),
+                                            (2, 128, 1, 1), (2, 128, 2, 1), (2, 128, 4, 1), (2, 128, 2, 0),
+                                            (1, 256, 1, 1), (1, 256, 2, 1), (1, 192, 1, 1), (1, 192, 4, 1),
+                                            (1, 192, 3, 0), (1, 64, 1, 1), (1, 64, 4, 1), (1, 64, 6, 0)])
+def test_tensor_core_tile_variants_exact(ctx, env_clean, tune, na, tn, sk, flags):
     """Every non-swapped tile shape and split the router may pick (forced through its tuning variables),
-    over M / N / K tails, int8 and NF4 weights."""
+    over M / N / K tails, int8 and NF4 weights; integer split-K with its zeroing ordered by the tile
+    flags (default) and by a cluster barrier (flags off)."""
     tune("ORKB_TC_NA", str(na))
     tune("ORKB_TC_TN", str(tn))
     tune("ORKB_TC_SK", str(sk))
+    tune("ORKB_TC_FLAGS", str(flags))
     L = ork_b200.lib()
     rng = np.random.default_rng(na * 100 + tn + sk)
     K, N = 1056, 640
@@ -415,17 +419,20 @@ def test_tensor_core_nibble_wide_grid_exact(ctx, env_clean, nf4):
         w.free()
 
 
-@pytest.mark.parametrize("pair,tn,sk", [(2, 256, 1), (2, 256, 2), (2, 128, 1), (2, 128, 4), (2, 64, 1),
-                                        (2, 64, 2), (2, 192, 1), (2, 192, 4), (3, 0, 1), (3, 0, 2), (3, 0, 4)])
-def test_tensor_core_pair_tiles_exact(ctx, env_clean, tune, pair, tn, sk):
+@pytest.mark.parametrize("pair,tn,sk,flags", [(2, 256, 1, 1), (2, 256, 2, 1), (2, 256, 4, 1), (2, 256, 2, 0),
+                                              (2, 128, 1, 1), (2, 128, 4, 1), (2, 64, 1, 1), (2, 64, 2, 1),
+                                              (2, 192, 1, 1), (2, 192, 4, 1), (2, 192, 3, 0), (3, 0, 1, 1),
+                                              (3, 0, 2, 1), (3, 0, 4, 1), (3, 0, 4, 0)])
+def test_tensor_core_pair_tiles_exact(ctx, env_clean, tune, pair, tn, sk, flags):
     """CTA-pair (cta_group::2) tiles forced through the tuning variables: pair = 2 puts the activations
     on the 256-row side (M tails leave the second CTA of the last pair entirely out of range at
     M = 300), pair = 3 the weight (N tails, narrow M). int8, NF4 and uniform int4 exact; f16 within
-    its tolerance."""
+    its tolerance. Integer split-K through the tile flags (default) and through the cluster barrier."""
     tune("ORKB_TC_PAIR", str(pair))
     if tn:
         tune("ORKB_TC_TN", str(tn))
     tune("ORKB_TC_SK", str(sk))
+    tune("ORKB_TC_FLAGS", str(flags))
     L = ork_b200.lib()
     rng = np.random.default_rng(pair * 1000 + tn + sk)
     K, N = 1056, 640

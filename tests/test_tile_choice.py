@@ -6,7 +6,10 @@ the narrowest tile covering M for M <= 64, split-K doubling while the grid stays
 for larger M, 128-wide weight tiles widened to 192 / 256 only while the grid would exceed one wave of
 148 CTAs, CTA-pair tiles for nibble weights past one wave, then the largest split of {2, 3, 4, 6}
 that keeps tiles x split <= 132 CTAs and at least 4 k-blocks per split (2 at most for CTA pairs); nibble weights at M <= 16 whose unsplit grid exceeds 296 tiles take the 2-stage ring with a
-2-way split; long int8 rows (K >= 6144) at M <= 32 take a 6-deep ring.
+2-way split; long int8 rows (K >= 6144) at M <= 32 take a 6-deep ring. int8 weights at larger M whose
+grid can fit one wave take the width (64-256) and split (1-6, >= 5 k-blocks each, <= 148 CTAs) that
+minimise the fitted cost 4.17 + 0.0088 * operand KB per CTA + 0.0052 * C KB per CTA + 0.166 * MB of C
+written by all splits (microseconds).
 
 Decode GEMV (M <= 8 per pass): the staged kernel (8 channels per CTA, whole rows in shared memory)
 unless its rows and 8 activation rows exceed 196 KB, or M > 4 with K >= 8192, or nibble weights with
@@ -30,8 +33,8 @@ def choice(fmt, M, K, N):
 
 @pytest.fixture(autouse=True)
 def no_tuning_variables(monkeypatch):
-    for v in ("ORKB_TC_TN", "ORKB_TC_NA", "ORKB_TC_STAGES", "ORKB_TC_PAIR", "ORKB_TC_SK", "ORKB_GEMV_KIND",
-              "ORKB_GEMV_CPW", "ORKB_GEMV_TR"):
+    for v in ("ORKB_TC_TN", "ORKB_TC_NA", "ORKB_TC_STAGES", "ORKB_TC_PAIR", "ORKB_TC_SK", "ORKB_TC_FLAGS",
+              "ORKB_GEMV_KIND", "ORKB_GEMV_CPW", "ORKB_GEMV_TR", "ORKB_GEMV_NW"):
         monkeypatch.delenv(v, raising=False)
 
 
@@ -39,11 +42,11 @@ def no_tuning_variables(monkeypatch):
     # [swap, tile width, K split, ring depth (0 = default), CTA pair]
     (I8, 8, 6144, 2048, [1, 16, 8, 6, 0]),        # decode-sized int8, long rows: 6-deep ring
     (I8, 8, 2048, 6144, [1, 16, 4, 0, 0]),        # 48 tiles: split while <= 320 CTAs
-    (I8, 128, 6144, 2048, [0, 128, 6, 0, 0]),     # 16 tiles, K of 48 blocks: 96 CTAs
-    (I8, 128, 2048, 6144, [0, 128, 2, 0, 0]),     # 48 tiles: split 3 would be 144 CTAs (> 132)
-    (I8, 128, 2048, 2048, [0, 128, 4, 0, 0]),     # 16 tiles, K of 16 blocks: 4 blocks per split
-    (I8, 512, 6144, 2048, [0, 128, 2, 0, 0]),     # 64 tiles, K of 48 blocks
-    (I8, 512, 2048, 6144, [0, 192, 1, 0, 0]),     # 192 tiles of 128 > 148: widened to 192 (128 tiles)
+    (I8, 128, 6144, 2048, [0, 64, 4, 0, 0]),      # cost model: 32 tiles of 64 x split 4 (128 CTAs)
+    (I8, 128, 2048, 6144, [0, 128, 3, 0, 0]),     # 48 tiles x split 3 = 144 CTAs (no cluster cap)
+    (I8, 128, 2048, 2048, [0, 64, 3, 0, 0]),      # 32 tiles of 64 x split 3 (5 k-blocks per split)
+    (I8, 512, 6144, 2048, [0, 192, 3, 0, 0]),     # 44 tiles of 192 x split 3 = 132 CTAs
+    (I8, 512, 2048, 6144, [0, 192, 1, 0, 0]),     # 128 tiles of 192, unsplit
     (I8, 512, 2048, 2048, [0, 128, 2, 0, 0]),     # 64 tiles: split 2 (128 CTAs)
     (F16, 64, 2048, 6144, [1, 64, 4, 0, 0]),      # fp16 decode-sized batch
     (NF4, 8, 8192, 10240, [1, 16, 4, 0, 0]),      # 70B QKV at M = 8: 80 tiles x 4 = 320 CTAs
