@@ -366,8 +366,8 @@ def sharded_70b(args, Ms, dist=None):
         Cfull = {}
         if p2p:
             tab = {}
-            for name, K, N, _ in shapes:
-                tab[name], Cfull[name] = peers.table(M, N, N // world)
+            for name, K, N, _ in shapes:  # with landing buffers: the tagged-word gather
+                tab[name], Cfull[name] = peers.table(M, N, N // world, land=True)
         else:
             Cl = {name: torch.empty((M, N // world), dtype=torch.int32, device="cuda") for name, K, N, _ in shapes}
             Cf = {name: torch.empty((M, N), dtype=torch.int32, device="cuda") for name, K, N, _ in shapes}

@@ -164,6 +164,13 @@ int ork_b200_i4_mm_run_peers_async(ork_npu *ctx, ork_w *w, int M, const int8_t *
 int ork_b200_peers_wait_async(ork_npu *ctx, ork_b200_peers *p);
 int ork_b200_i8_mm_run_gather_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
 int ork_b200_i4_mm_run_gather_async(ork_npu *ctx, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p);
+/* Landing buffers for a faster run + gather of up to `rows` rows: land[r] is rank r's symmetric buffer of
+ * rows * ldc 8-byte words (zero at allocation, 16-byte aligned; every rank attaches the same set). A
+ * run + gather of M <= rows then stores each value with the run's tag into every peer's landing buffer
+ * (an 8-byte word: single-copy atomic) and unpacks the other ranks' tagged words into C once they carry
+ * the tag -- no signal and no system-scope fence (shard widths and ldc multiples of 4; else, and for
+ * larger M, the signalled push). Same reuse rule. 0, or -1 on bad arguments. */
+int ork_b200_peers_land(ork_b200_peers *p, void *const *land, int rows);
 /* Copy `bytes` between any two host / device addresses, ordered after the context's queued work, and wait
  * for it (for callers without a CUDA binding of their own, e.g. to read a symmetric buffer). 0 or -1. */
 int ork_b200_copy(ork_npu *ctx, void *dst, const void *src, size_t bytes);

@@ -175,6 +175,7 @@ Tuning tuning_from_env() {
   t.tc_pair = env_int("ORKB_TC_PAIR", 0);
   t.tc_sk = env_int("ORKB_TC_SK", 0);
   t.tc_flags = env_int("ORKB_TC_FLAGS", 1);
+  t.tc_pre = env_int("ORKB_TC_PRE", 0);
   t.gemv_kind = env_int("ORKB_GEMV_KIND", -1);
   t.gemv_cpw = env_int("ORKB_GEMV_CPW", 0);
   t.gemv_tr = env_int("ORKB_GEMV_TR", 0);

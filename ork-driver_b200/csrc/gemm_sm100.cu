@@ -479,7 +479,7 @@ template <int FMT, bool SWAP, int TN, int STAGES, int NA>
 __global__ void __launch_bounds__(tc_threads<FMT, SWAP>())
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
                const __grid_constant__ CUtensorMap mapC, void *__restrict__ Cout, int M, int N, int K,
-               Nf4Tables tb, unsigned int *__restrict__ tflag) {
+               Nf4Tables tb, unsigned int *__restrict__ tflag, int prew) {
   // NA accumulators of 128 rows stacked along the R side (TM = 128*NA): each K step issues NA MMAs that
   // share the S tile, so S is fetched once per 128*NA rows (less operand traffic per output)
   constexpr bool F16 = FMT == FMT_F16;
@@ -570,7 +570,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
     if (lane == 0) {
       // the weight tiles do not depend on the previous kernel: the first ring's worth is requested
       // before waiting on it (programmatic dependent launch); activations only after the wait
-      const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+      // the first `pre` stages' weight tiles are requested before the wait; after it the activation
+      // tiles go first, then the rest of the first ring (both tiles of a stage)
+      const int ring = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+      const int pre = prew < ring ? prew : ring;
       for (int i = 0; i < pre; i++) {
         mbar_expect_tx(full0 + 8 * i, TX_BYTES);
         load_w(i, kb0 + i);
@@ -581,10 +584,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__
       // swapped grid asks, and for row tiles only the first weight tile's CTAs (each tile once: a
       // prefetch by all 16-48 CTAs sharing it slowed M = 512 runs by 3-4 %)
       if (SWAP ? (blockIdx.x & 7) == 0 : blockIdx.y == 0)
-        for (int i = 0; i < pre; i++) prefetch_a(kb0 + i);
+        for (int i = 0; i < ring; i++) prefetch_a(kb0 + i);
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int i = 0; i < pre; i++) load_a(i, kb0 + i);
-      for (int kb = kb0 + pre; kb < kb1; kb++) {
+      for (int i = pre; i < ring; i++) {
+        mbar_expect_tx(full0 + 8 * i, TX_BYTES);
+        load_a(i, kb0 + i);
+        load_w(i, kb0 + i);
+      }
+      for (int kb = kb0 + ring; kb < kb1; kb++) {
         const int i = kb - kb0, s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) break;
@@ -820,7 +828,7 @@ template <int FMT, bool SWAP, int TN, int STAGES>
 __global__ void __launch_bounds__(192)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_constant__ CUtensorMap mapS,
                     const __grid_constant__ CUtensorMap mapC, void *__restrict__ Cout, int M, int N, int K,
-                    Nf4Tables tb, unsigned int *__restrict__ tflag) {
+                    Nf4Tables tb, unsigned int *__restrict__ tflag, int prew) {
   constexpr bool F16 = FMT == FMT_F16;
   constexpr bool NIB = FMT == FMT_U4 || FMT == FMT_NF4;
   constexpr int HS = TN / 2;                             // S rows held by each CTA
@@ -913,16 +921,22 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap mapR, const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
-      const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+      const int ring = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;  // (as in gemm_tc_kernel)
+      const int pre = prew < ring ? prew : ring;
       for (int i = 0; i < pre; i++) {
         expect(i);
         load_w(i, kb0 + i);
       }
       if (SWAP ? (blockIdx.x & 15) < 2 : blockIdx.y == 0)  // L2 hint before the wait (see gemm_tc_kernel)
-        for (int i = 0; i < pre; i++) prefetch_a(kb0 + i);
+        for (int i = 0; i < ring; i++) prefetch_a(kb0 + i);
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int i = 0; i < pre; i++) load_a(i, kb0 + i);
-      for (int kb = kb0 + pre; kb < kb1; kb++) {
+      for (int i = pre; i < ring; i++) {
+        expect(i);
+        load_a(i, kb0 + i);
+        load_w(i, kb0 + i);
+      }
+      for (int kb = kb0 + ring; kb < kb1; kb++) {
         const int i = kb - kb0, s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) break;
@@ -1126,7 +1140,12 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].val.clusterDim.z = flagz ? 1 : sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb, flagz ? a.tflag : (unsigned int *)nullptr);
+  // weight stages requested before the dependency wait: the whole ring, except the 8-deep ring of the
+  // 64-wide row tiles, where two and then activations first measured faster (6144x2048xM128 8.0 -> 7.5 us;
+  // the other prefill shapes within 1 %, decode-sized grids slower with fewer)
+  const int prew = a.tune && a.tune->tc_pre > 0 ? a.tune->tc_pre : (!SWAP && STAGES >= 8) ? 2 : STAGES;
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb, flagz ? a.tflag : (unsigned int *)nullptr,
+                            prew);
 }
 
 // CTA-pair launch: grid x = 2 CTAs per 256 R rows, y = S tiles of TN, z = split-K; cluster (2, 1, sk).
@@ -1176,7 +1195,8 @@ cudaError_t launch_tc_pair(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   at[1].val.clusterDim.z = flagz ? 1 : sk;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb, flagz ? a.tflag : (unsigned int *)nullptr);
+  return cudaLaunchKernelEx(&cfg, kern, mR, mS, mC, a.C, a.M, a.N, a.K, tb, flagz ? a.tflag : (unsigned int *)nullptr,
+                            a.tune && a.tune->tc_pre > 0 ? a.tune->tc_pre : STAGES);
 }
 
 struct TcCfg {

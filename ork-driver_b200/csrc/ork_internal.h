@@ -34,11 +34,12 @@ extern const int8_t kNf4Lut[16];
 // router's own choice:
 //   tc_tn ORKB_TC_TN (128/192/256), tc_na ORKB_TC_NA (1/2), tc_stages ORKB_TC_STAGES, tc_pair ORKB_TC_PAIR
 //   (1..3), tc_sk ORKB_TC_SK (1..8), tc_flags ORKB_TC_FLAGS (0: split-K zeroing ordered through a
-//   cluster barrier instead of the tile flags); gemv_kind ORKB_GEMV_KIND (0 staged / 1 direct), gemv_cpw
+//   cluster barrier instead of the tile flags), tc_pre ORKB_TC_PRE (weight stages requested before the
+//   dependency wait; default the whole ring); gemv_kind ORKB_GEMV_KIND (0 staged / 1 direct), gemv_cpw
 //   ORKB_GEMV_CPW (1/2/4), gemv_tr ORKB_GEMV_TR (8/16/32), gemv_nw ORKB_GEMV_NW (4/8/16 warps);
 //   layer_fused ORKB_LAYER_FUSED (0 multi-launch).
 struct Tuning {
-  int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0, tc_flags = 1;
+  int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0, tc_flags = 1, tc_pre = 0;
   int gemv_kind = -1, gemv_cpw = 0, gemv_tr = 0, gemv_nw = 0;
   int layer_fused = -1;
 };
@@ -105,6 +106,12 @@ struct PeerTable {                 // device memory, written once when the table
   unsigned int *flag[kMaxPeers];   // every rank's signal counts [kMaxPeers] (index: signalling rank)
   unsigned int *waited;            // this rank's count of completed waits (private)
   unsigned int *done;              // CTAs of the current run finished (private, left at zero)
+  // tagged-word gather (optional): every rank's landing buffer [land_rows][ldc] of 8-byte words (value
+  // in the low half, the run's tag in the high half), this rank's count of tagged runs, and the CTAs of
+  // the current tagged run finished (private, left at zero)
+  uint64_t *land[kMaxPeers];
+  int land_rows;
+  unsigned int *runs, *ldone;
 };
 struct OutStage {
   int mode, mult, shift;

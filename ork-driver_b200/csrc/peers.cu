@@ -131,6 +131,70 @@ __global__ void __launch_bounds__(256) push_kernel(const int32_t *__restrict__ C
   }
 }
 
+// Tagged-word gather of one run (no signal, no system-scope fence). Every value travels as one 8-byte
+// word (value, run tag), which a rank stores into every peer's landing buffer; an aligned 8-byte store is
+// single-copy atomic, so a reader that sees the tag sees the value. This rank's own columns go straight
+// into its C. Then the grid polls (bounded) the landing words of the other ranks' columns until they carry
+// the tag and writes them into C. The tag is this rank's count of tagged runs plus one (read by every
+// CTA after the dependency wait; the run's last CTA advances the count). Grid-strides over 16-byte
+// vectors of the shard (push) and of C (unpack); its size is capped at what is resident at once, so no
+// CTA waits for a peer's data while a CTA that has not started holds back this rank's own push.
+__global__ void __launch_bounds__(256) gather_tag_kernel(const int32_t *__restrict__ Cl, int M, int n,
+                                                          const PeerTable *__restrict__ pt) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the matmul is complete
+  const uint32_t tag = *pt->runs + 1u;
+  const int ldc = pt->ldc, col0 = pt->col0, nv = n / 4, lv = ldc / 4, me = pt->rank;
+  const size_t stride = (size_t)gridDim.x * blockDim.x, first = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int32_t *C = pt->C[me];
+  const uint64_t hi = (uint64_t)tag << 32;
+  for (size_t e = first; e < (size_t)M * nv; e += stride) {
+    const int m = (int)(e / nv), c = (int)(e % nv) * 4;
+    const int4 v = *reinterpret_cast<const int4 *>(Cl + (size_t)m * n + c);
+    const size_t o = (size_t)m * ldc + col0 + c;
+    *reinterpret_cast<int4 *>(C + o) = v;
+    const uint64_t w0 = hi | (uint32_t)v.x, w1 = hi | (uint32_t)v.y, w2 = hi | (uint32_t)v.z, w3 = hi | (uint32_t)v.w;
+    for (int r = 0; r < pt->n; r++) {
+      if (r == me) continue;
+      uint64_t *L = pt->land[r] + o;
+      asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(L), "l"(w0), "l"(w1) : "memory");
+      asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(L + 2), "l"(w2), "l"(w3) : "memory");
+    }
+  }
+  bool ok = true;
+  const uint64_t *L = pt->land[me];
+  for (size_t e = first; e < (size_t)M * lv && ok; e += stride) {
+    const int m = (int)(e / lv), c = (int)(e % lv) * 4;
+    if (c >= col0 && c < col0 + n) continue;  // this rank's own columns
+    const size_t o = (size_t)m * ldc + c;
+    uint64_t w[4];
+    const uint64_t t0 = clock64();
+    while (true) {
+      asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w[0]), "=l"(w[1]) : "l"(L + o) : "memory");
+      asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w[2]), "=l"(w[3]) : "l"(L + o + 2) : "memory");
+      if ((uint32_t)(w[0] >> 32) == tag && (uint32_t)(w[1] >> 32) == tag && (uint32_t)(w[2] >> 32) == tag &&
+          (uint32_t)(w[3] >> 32) == tag)
+        break;
+      if (clock64() - t0 > kPeerSpin) {
+        { atomicOr(&g_peer_error, 1u); err_word_set(); }
+        ok = false;
+        break;
+      }
+    }
+    *reinterpret_cast<int4 *>(C + o) = make_int4((int)(uint32_t)w[0], (int)(uint32_t)w[1], (int)(uint32_t)w[2],
+                                                  (int)(uint32_t)w[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(pt->ldone) : "memory");
+    if (old == gridDim.x - 1u) {  // every CTA has read the tag: advance it for the next run
+      *pt->ldone = 0u;
+      *pt->runs = tag;
+    }
+  }
+}
+
 // One warp: lane r waits until rank r's count of signals here covers one more run than this rank has
 // consumed (each run signals each rank once); bounded (an expired wait sets the error flag and lets the
 // stream go on).
@@ -188,8 +252,16 @@ int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, 
   cfg.numAttrs = 1;
   const int32_t *lc = (const int32_t *)c->dC;
   const PeerTable *dev = p->dev;
-  const cudaError_t e = wait ? cudaLaunchKernelEx(&cfg, push_kernel<true>, lc, M, w->N, dev)
-                             : cudaLaunchKernelEx(&cfg, push_kernel<false>, lc, M, w->N, dev);
+  // the tagged-word gather when the table has landing buffers for M rows and the layout is whole
+  // 16-byte vectors (every rank's columns and the row stride multiples of 4)
+  const bool tagged = wait && M <= t.land_rows && w->N % 4 == 0 && t.ldc % 4 == 0 && t.col0 % 4 == 0;
+  if (tagged) {
+    const size_t cv = (size_t)M * t.ldc / 4;
+    cfg.gridDim = dim3((unsigned int)std::min<size_t>(kPushMax, std::max<size_t>(1, (cv + kPushVecs - 1) / kPushVecs)));
+  }
+  const cudaError_t e = tagged ? cudaLaunchKernelEx(&cfg, gather_tag_kernel, lc, M, w->N, dev)
+                        : wait ? cudaLaunchKernelEx(&cfg, push_kernel<true>, lc, M, w->N, dev)
+                               : cudaLaunchKernelEx(&cfg, push_kernel<false>, lc, M, w->N, dev);
   c->launches += 1;
   if (e != cudaSuccess) {
     log_err(name, e);
@@ -266,13 +338,28 @@ ork_b200_peers *ork_b200_peers_create(ork_npu *c, int nranks, int rank, void *co
   p->waited = (unsigned int *)((uint8_t *)p->dev + ((sizeof(PeerTable) + 255) & ~(size_t)255));
   t.waited = p->waited;
   t.done = p->waited + 1;
-  if (cudaMemset(p->waited, 0, 8) != cudaSuccess ||
+  t.runs = p->waited + 2;
+  t.ldone = p->waited + 3;
+  t.land_rows = 0;
+  if (cudaMemset(p->waited, 0, 16) != cudaSuccess ||
       cudaMemcpy(p->dev, &t, sizeof t, cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaFree(p->dev);
     delete p;
     return nullptr;
   }
   return p;
+}
+
+int ork_b200_peers_land(ork_b200_peers *p, void *const *land, int rows) {
+  if (!p || !land || rows < 1) return -1;
+  PeerTable &t = p->host;
+  for (int r = 0; r < t.n; r++)
+    if (!land[r] || (uintptr_t)land[r] % 16) return -1;
+  DeviceGuard dg(p->ctx->device);
+  for (int r = 0; r < t.n; r++) t.land[r] = (uint64_t *)land[r];
+  t.land_rows = rows;
+  cudaStreamSynchronize(p->ctx->stream);  // no kernel of this table in flight while its copy changes
+  return cudaMemcpy(p->dev, &t, sizeof t, cudaMemcpyHostToDevice) == cudaSuccess ? 0 : -1;
 }
 
 void ork_b200_peers_destroy(ork_b200_peers *p) {

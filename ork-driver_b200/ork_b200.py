@@ -64,6 +64,7 @@ SIGNATURES = [
     ("ork_b200_peers_wait_async", _i, [_vp, _vp]),
     ("ork_b200_i8_mm_run_gather_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_b200_i4_mm_run_gather_async", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ork_b200_peers_land", _i, [_vp, C.POINTER(_vp), _i]),
     ("ork_b200_copy", _i, [_vp, _vp, _vp, _sz]),
     ("ork_b200_i4_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ork_b200_f16_mm_run_async", _i, [_vp, _vp, _i, _vp, _vp]),

@@ -121,7 +121,9 @@ class PeerGroup:
             ptrs.append(q)
         return ptrs
 
-    def table(self, M, N, ncols):
+    def table(self, M, N, ncols, land=False):
+        """land=True also attaches landing buffers (M x N tagged 8-byte words per rank), so run + gather
+        calls of up to M rows take the tagged-word gather (ork_b200_peers_land)."""
         import ctypes as C
 
         if ncols * self.world != N:
@@ -134,6 +136,10 @@ class PeerGroup:
         if not t:
             raise RuntimeError("ork_b200_peers_create failed")
         self.tables.append(t)
+        if land:
+            lps = self._symmetric(M * N * 8)
+            if self.ctx.L.ork_b200_peers_land(t, arr(*lps), M) != 0:
+                raise RuntimeError("ork_b200_peers_land failed")
         return t, cps[self.rank]
 
     def close(self):

@@ -61,6 +61,15 @@ def test_one_rank_table(ctx):
         assert L.ork_b200_i8_mm_run_gather_async(ctx.ctx, w.h, M, tA.data_ptr(), t) == 0
         assert L.ork_b200_sync(ctx.ctx) == 0
         assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A2, B)), M
+    # the tagged-word gather (landing buffers attached for up to Mmax rows)
+    tl, cl = g.table(Mmax, N, N, land=True)
+    for M in (1, 8, 40):
+        A3 = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+        tA = torch.from_numpy(A3).to(dev)
+        torch.cuda.synchronize()
+        assert L.ork_b200_i8_mm_run_gather_async(ctx.ctx, w.h, M, tA.data_ptr(), tl) == 0
+        assert L.ork_b200_sync(ctx.ctx) == 0
+        assert np.array_equal(_read(ctx, cl, (M, N)), of.gemm_i32(A3, B)), ("tagged", M)
     w.free()
     g.close()
 
@@ -140,6 +149,7 @@ def _two_rank_worker(rank, world, port, kind):
     g = shard.PeerGroup(ctx, dist)
     t, cptr = g.table(Mmax, N, ncols)
     t2, cptr2 = g.table(Mmax, N, ncols)
+    tl = [g.table(Mmax, N, ncols, land=True) for _ in range(2)]  # tagged-word gather tables
     try:
         for M in (1, 8, 3, 24):
             A = rng.integers(-128 if kind == "i8" else -8, 128 if kind == "i8" else 8, size=(M, K), dtype=np.int8)
@@ -158,6 +168,15 @@ def _two_rank_worker(rank, world, port, kind):
             assert L.ork_b200_sync(ctx.ctx) == 0
             assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B)), (rank, M, "gather")
             dist.barrier()
+            # and through the tagged-word gather (landing buffers), alternating its two tables
+            A = rng.integers(-128 if kind == "i8" else -8, 128 if kind == "i8" else 8, size=(M, K), dtype=np.int8)
+            tA = torch.from_numpy(A).to(dev)
+            torch.cuda.synchronize()
+            tt, tc = tl[M % 2]
+            assert gather(ctx.ctx, w.h, M, tA.data_ptr(), tt) == 0
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            assert np.array_equal(_read(ctx, tc, (M, N)), of.gemm_i32(A, B)), (rank, M, "tagged")
+            dist.barrier()
         # the run + wait pair captured once and replayed: the counts advance on the device
         M = 4
         A = rng.integers(-8, 8, size=(M, K), dtype=np.int8)
@@ -173,6 +192,22 @@ def _two_rank_worker(rank, world, port, kind):
             torch.cuda.synchronize()
             assert L.ork_b200_sync(ctx.ctx) == 0
             assert np.array_equal(_read(ctx, cptr, (M, N)), of.gemm_i32(A, B))
+            dist.barrier()
+        del graph
+        # a captured chain of tagged gathers alternating two tables, replayed (the tags advance on the device)
+        A = rng.integers(-8, 8, size=(M, K), dtype=np.int8)
+        tA = torch.from_numpy(A).to(dev)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(4):
+                assert gather(ctx.ctx, w.h, M, tA.data_ptr(), tl[i % 2][0]) == 0
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert L.ork_b200_sync(ctx.ctx) == 0
+            for _, tc in tl:
+                assert np.array_equal(_read(ctx, tc, (M, N)), of.gemm_i32(A, B)), "tagged graph"
             dist.barrier()
         del graph
         # a captured chain of run + gather calls alternating between two tables (the reuse rule), replayed
