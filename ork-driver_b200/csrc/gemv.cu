@@ -697,7 +697,13 @@ Cfg choose(int fmt, int M, int K, int N, const Tuning &tu) {
   const size_t rowB = fmt_row_bytes(fmt, K);
   const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
   c.tr = 8;
-  const bool staged_fits = rowB * 8 + (size_t)8 * K * (fmt == FMT_F16 ? 2 : 1) <= 196 * 1024;
+  // 8 weight rows and 8 activation rows in shared memory; rows that fit only with this launch's own
+  // activation rows (up to c.mt) are staged when the direct kernel's grid (N / 32 CTAs of 8 warps) would
+  // not fill the SMs -- the 70B down projection's column shards, NF4 M = 1: 28672x2048 11.6 us staged
+  // against 19.9 direct; at full width (28672x8192) the direct kernel stays ahead, 41.6 against 43.1
+  const size_t esz = fmt == FMT_F16 ? 2 : 1;
+  const bool staged_fits = rowB * 8 + (size_t)8 * K * esz <= 196 * 1024 ||
+                           (rowB * 8 + (size_t)c.mt * K * esz <= 196 * 1024 && N / 32 < 148);
   if (!staged_fits || (c.mt == 8 && K >= 8192)) {
     c.direct = true;
     c.cpw = (!staged_fits || (c.mt == 8 && fmt != FMT_NF4)) ? 4 : 2;
