@@ -256,8 +256,10 @@ int peers_run(ork_npu *c, ork_w *w, int M, const int8_t *dA, ork_b200_peers *p, 
   // 16-byte vectors (every rank's columns and the row stride multiples of 4)
   const bool tagged = wait && M <= t.land_rows && w->N % 4 == 0 && t.ldc % 4 == 0 && t.col0 % 4 == 0;
   if (tagged) {
+    // at most four 256-thread CTAs per SM (the kernel's registers allow six), so the whole grid is
+    // resident at once once the matmul before it has drained; larger runs grid-stride
     const size_t cv = (size_t)M * t.ldc / 4;
-    cfg.gridDim = dim3((unsigned int)std::min<size_t>(kPushMax, std::max<size_t>(1, (cv + kPushVecs - 1) / kPushVecs)));
+    cfg.gridDim = dim3((unsigned int)std::min<size_t>(148 * 4, std::max<size_t>(1, (cv + kPushVecs - 1) / kPushVecs)));
   }
   const cudaError_t e = tagged ? cudaLaunchKernelEx(&cfg, gather_tag_kernel, lc, M, w->N, dev)
                         : wait ? cudaLaunchKernelEx(&cfg, push_kernel<true>, lc, M, w->N, dev)
