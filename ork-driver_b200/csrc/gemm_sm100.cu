@@ -1124,8 +1124,10 @@ cudaError_t launch_tc(const RunArgs &a, int sk, cudaStream_t s, bool pdl) {
   const int gx = (rowsR + TM - 1) / TM, gy = (rowsS + TN - 1) / TN;
   // integer split-K with the context's tile flags: the splits need not share a cluster. Row tiles only:
   // decode-sized (swapped) grids split up to 8 ways into short K ranges, where a cluster barrier was
-  // measured faster (int8 M = 8: 2048x2048 2.98 against 3.6 us, 6144x2048 4.65 against 5.2)
-  const bool flagz = !SWAP && FMT != FMT_F16 && sk > 1 && a.tflag && gx * gy <= kTcFlagTiles;
+  // measured faster (int8 M = 8: 2048x2048 2.98 against 3.6 us, 6144x2048 4.65 against 5.2) -- except
+  // splits of more than 8, which no cluster holds
+  if (sk > 8 && (FMT == FMT_F16 || !a.tflag || gx * gy > kTcFlagTiles)) sk = 8;
+  const bool flagz = (!SWAP || sk > 8) && FMT != FMT_F16 && sk > 1 && a.tflag && gx * gy <= kTcFlagTiles;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gx, gy, sk);
   cfg.blockDim = dim3(tc_threads<FMT, SWAP>());
@@ -1237,6 +1239,16 @@ TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
       c.stages = 2;
       c.sk = 2;
     }
+    // narrow nibble weights with long rows (the 70B linears' column shards) stop at 8 splits for the
+    // cluster; with the tile flags they split further while the grid stays within 256 CTAs. NF4 M = 8:
+    // 8192x1024 6.3 -> 4.9 us (16), 28672x2048 19.9 -> 12.2 (16), 8192x2560 7.5 -> 6.4 (12; 16 on 320
+    // CTAs was slower)
+    if (nib && c.tn == 16 && c.sk == 8 && KB >= 64 && tu.tc_flags)
+      for (int s : {16, 12})
+        if (tiles * s <= 256) {
+          c.sk = s;
+          break;
+        }
   } else {
     const int mt = (M + BM - 1) / BM;
     auto tiles = [&](int tn) { return mt * ((N + tn - 1) / tn); };
@@ -1295,7 +1307,7 @@ TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
     else c.tn = (tu.tc_tn == 64 || tu.tc_tn == 128 || tu.tc_tn == 192) ? tu.tc_tn : 256;
     if (c.sk > 4) c.sk = 4;
   }
-  if (tu.tc_sk >= 1 && tu.tc_sk <= (c.pair ? 4 : 8) && tu.tc_sk <= KB) c.sk = tu.tc_sk;
+  if (tu.tc_sk >= 1 && tu.tc_sk <= (c.pair ? 4 : 16) && tu.tc_sk <= KB) c.sk = tu.tc_sk;
   return c;
 }
 

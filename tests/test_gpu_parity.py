@@ -368,12 +368,13 @@ def test_tensor_core_tile_variants_exact(ctx, env_clean, tune, na, tn, sk, flags
 
 
 @pytest.mark.parametrize("nf4", [False, True])
-@pytest.mark.parametrize("sk", [1, 3])
+@pytest.mark.parametrize("sk", [1, 3, 16])
 @pytest.mark.parametrize("stages", [0, 2])
 def test_tensor_core_nibble_long_k_exact(ctx, env_clean, tune, nf4, sk, stages):
     """Decode-sized M on nibble weights through the tensor-core kernel with a long K per CTA (split
     forced to 1 or 3), so the stage ring (default depth, or the 2-stage ring) wraps many times and every
-    stage is expanded from nibbles; a K tail (K % 128 != 0) ends the last block."""
+    stage is expanded from nibbles; a K tail (K % 128 != 0) ends the last block. Split 16 (more than a
+    cluster holds) orders its zeroing through the tile flags."""
     tune("ORKB_TC_SK", str(sk))
     if stages:
         tune("ORKB_TC_STAGES", str(stages))
@@ -391,6 +392,27 @@ def test_tensor_core_nibble_long_k_exact(ctx, env_clean, tune, nf4, sk, stages):
             A = rand_i8(rng, (M, K))
             rc, Cm = ctx.run(w, A)
             assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, codes)), M
+    finally:
+        L.ork_b200_force_route(ctx.ctx, -1)
+        w.free()
+
+
+@pytest.mark.parametrize("sk", [12, 16])
+def test_tensor_core_swapped_int8_split_past_cluster_exact(ctx, env_clean, tune, sk):
+    """int8 weights at decode-sized M with a split of more than 8 (swapped tiles, tile flags), M and K
+    tails."""
+    tune("ORKB_TC_SK", str(sk))
+    L = ork_b200.lib()
+    rng = np.random.default_rng(900 + sk)
+    K, N = 8224, 384
+    B = rand_i8(rng, (K, N))
+    w = ctx.i8_pack(B)
+    try:
+        assert L.ork_b200_force_route(ctx.ctx, 1) == 0
+        for M in (1, 8, 13, 40):
+            A = rand_i8(rng, (M, K))
+            rc, Cm = ctx.run(w, A)
+            assert rc == 0 and np.array_equal(Cm, of.gemm_i32(A, B)), M
     finally:
         L.ork_b200_force_route(ctx.ctx, -1)
         w.free()
