@@ -444,8 +444,9 @@ def sharded_70b(args, Ms, dist=None):
     desc = {"workload": "Llama-70B-shaped linears, NF4 weights ~N(0,0.02), 80 layers x (QKV 8192x10240, "
                         "O 8192x8192, gate+up 8192x57344, down 28672x8192) + LM head 8192x128256, "
                         f"column-sharded over {world} GPU(s), "
-                        + ("gather fused into each matmul over NVLink peer memory (P2P stores + bounded "
-                           "signal wait)" if p2p else "NCCL all-gather of each int32 C" if world > 1
+                        + ("gather fused into each matmul over NVLink peer memory (each value stored as a "
+                           "tagged 8-byte word into every peer's landing buffer, bounded poll and unpack; "
+                           "no signal)" if p2p else "NCCL all-gather of each int32 C" if world > 1
                            else "one GPU, no gather"),
             "parallelism": f"column shard x{world}",
             "l2": f"inputs larger than L2: {ncopies} distinct copies of the per-rank layer weights "
