@@ -698,15 +698,19 @@ Cfg choose(int fmt, int M, int K, int N, const Tuning &tu) {
   const bool nib = fmt == FMT_U4 || fmt == FMT_NF4;
   c.tr = 8;
   // 8 weight rows and 8 activation rows in shared memory; rows that fit only with this launch's own
-  // activation rows (up to c.mt) are staged when the direct kernel's grid (N / 32 CTAs of 8 warps) would
-  // not fill the SMs -- the 70B down projection's column shards, NF4 M = 1: 28672x2048 11.6 us staged
-  // against 19.9 direct; at full width (28672x8192) the direct kernel stays ahead, 41.6 against 43.1
+  // activation rows (up to c.mt) are staged when even a one-channel-per-warp direct grid (N / 8 CTAs)
+  // would be under two CTAs per SM, and otherwise go to the direct kernel with one channel per warp
+  // while its four-channel grid (N / 32) would not fill the SMs. The 70B down projection's column
+  // shards, NF4 M = 1 (weights cycled past L2): 28672x1024 staged 6.2 us against 15.8 direct,
+  // 28672x2048 12.3 against 17.1, 28672x4096 direct with one channel 19.9 against 24.0 staged and 27.4
+  // with four; at full width (28672x8192) four channels per warp, 30.7 against 34.1 with one
   const size_t esz = fmt == FMT_F16 ? 2 : 1;
-  const bool staged_fits = rowB * 8 + (size_t)8 * K * esz <= 196 * 1024 ||
-                           (rowB * 8 + (size_t)c.mt * K * esz <= 196 * 1024 && N / 32 < 148);
+  const bool fits8 = rowB * 8 + (size_t)8 * K * esz <= 196 * 1024;
+  const bool staged_fits = fits8 || (rowB * 8 + (size_t)c.mt * K * esz <= 196 * 1024 && N / 8 < 296);
   if (!staged_fits || (c.mt == 8 && K >= 8192)) {
     c.direct = true;
     c.cpw = (!staged_fits || (c.mt == 8 && fmt != FMT_NF4)) ? 4 : 2;
+    if (!fits8 && c.mt == 1 && N / 32 < 148) c.cpw = 1;
   } else if (nib && K <= 2048 && N <= 8192) {
     c.direct = true;
     c.cpw = 2;

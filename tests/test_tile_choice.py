@@ -92,7 +92,8 @@ def gemv_choice(fmt, M, K, N):
 @pytest.mark.parametrize("fmt,M,K,N,want", [
     # [direct, channels per warp (direct), channels per CTA (staged), activation rows per pass]
     (NF4, 1, 28672, 8192, [1, 4, 0, 1]),    # 70B down projection: rows too long to stage with 8 A rows
-    (NF4, 1, 28672, 2048, [0, 0, 8, 1]),    # ... its 4-GPU shard: staged with the one A row (direct grid < 148)
+    (NF4, 1, 28672, 4096, [1, 1, 0, 1]),    # ... its 2-GPU shard: direct, one channel per warp (512 CTAs)
+    (NF4, 1, 28672, 2048, [0, 0, 8, 1]),    # ... its 4-GPU shard: staged with the one A row (N / 8 < 296)
     (NF4, 1, 28672, 1024, [0, 0, 8, 1]),    # ... and its 8-GPU shard
     (NF4, 8, 28672, 2048, [1, 4, 0, 8]),    # eight A rows do not fit beside the weight rows
     (NF4, 1, 8192, 57344, [0, 0, 8, 1]),    # 70B gate+up at M = 1: staged
