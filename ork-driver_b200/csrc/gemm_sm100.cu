@@ -1239,11 +1239,12 @@ TcCfg choose_tc(int fmt, int M, int K, int N, const Tuning &tu) {
       c.stages = 2;
       c.sk = 2;
     }
-    // narrow nibble weights with long rows (the 70B linears' column shards) stop at 8 splits for the
-    // cluster; with the tile flags they split further while the grid stays within 256 CTAs. NF4 M = 8:
-    // 8192x1024 6.3 -> 4.9 us (16), 28672x2048 19.9 -> 12.2 (16), 8192x2560 7.5 -> 6.4 (12; 16 on 320
-    // CTAs was slower)
-    if (nib && c.tn == 16 && c.sk == 8 && KB >= 64 && tu.tc_flags)
+    // narrow nibble weights with long rows (the 70B linears' column shards, configs[2]'s 6144x2048) stop
+    // at 8 splits for the cluster; with the tile flags they split further while the grid stays within
+    // 256 CTAs. NF4 M = 8: 8192x1024 6.3 -> 4.9 us (16), 28672x2048 19.9 -> 12.2 (16), 8192x2560 7.5 ->
+    // 6.4 (12; 16 on 320 CTAs was slower), 6144x2048 6.2 -> 4.7; M = 32: 6144x2048 NF4 7.0 -> 5.1, uniform
+    // 6.4 -> 4.8. (int8 weights measured slower past 8 splits.)
+    if (nib && c.tn <= 32 && c.sk == 8 && KB >= 48 && tu.tc_flags)
       for (int s : {16, 12})
         if (tiles * s <= 256) {
           c.sk = s;

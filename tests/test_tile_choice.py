@@ -6,9 +6,9 @@ the narrowest tile covering M for M <= 64, split-K doubling while the grid stays
 for larger M, 128-wide weight tiles widened to 192 / 256 only while the grid would exceed one wave of
 148 CTAs, CTA-pair tiles for nibble weights past one wave, then the largest split of {2, 3, 4, 6}
 that keeps tiles x split <= 132 CTAs and at least 4 k-blocks per split (2 at most for CTA pairs); nibble weights at M <= 16 whose unsplit grid exceeds 296 tiles take the 2-stage ring with a
-2-way split; long int8 rows (K >= 6144) at M <= 32 take a 6-deep ring; narrow nibble weights with
-K >= 8192 that reach 8 splits continue to 16 (or 12) splits through the tile flags while the grid stays
-within 256 CTAs. int8 weights at larger M whose
+2-way split; long int8 rows (K >= 6144) at M <= 32 take a 6-deep ring; narrow nibble weights at
+M <= 32 with K >= 6144 that reach 8 splits continue to 16 (or 12) splits through the tile flags while the
+grid stays within 256 CTAs. int8 weights at larger M whose
 grid can fit one wave take the width (64-256) and split (1-6, >= 5 k-blocks each, <= 148 CTAs) that
 minimise the fitted cost 4.17 + 0.0088 * operand KB per CTA + 0.0052 * C KB per CTA + 0.166 * MB of C
 written by all splits (microseconds).
@@ -56,6 +56,8 @@ def no_tuning_variables(monkeypatch):
     (NF4, 8, 8192, 1024, [1, 16, 16, 0, 0]),      # 8-GPU shard of O: split 16 through the tile flags
     (NF4, 8, 8192, 2560, [1, 16, 12, 0, 0]),      # 4-GPU shard of QKV: 20 tiles, split 12 (240 CTAs)
     (NF4, 8, 28672, 4096, [1, 16, 8, 0, 0]),      # 2-GPU shard of down: 32 tiles, 8 in clusters
+    (U4, 32, 6144, 2048, [1, 32, 16, 0, 0]),      # configs[2] w4a8 M = 32: 16 tiles x 16 splits
+    (I8, 32, 6144, 2048, [1, 32, 8, 6, 0]),       # int8 stays at 8 splits in clusters
     (U4, 32, 8192, 57344, [1, 32, 1, 0, 0]),      # the wide-grid rule is for M <= 16 only
     (NF4, 256, 2048, 12288, [0, 192, 1, 0, 1]),   # nibble weights past one wave: CTA-pair 256 x 192
 ])
