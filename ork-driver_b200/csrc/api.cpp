@@ -176,6 +176,7 @@ Tuning tuning_from_env() {
   t.tc_sk = env_int("ORKB_TC_SK", 0);
   t.tc_flags = env_int("ORKB_TC_FLAGS", 1);
   t.tc_pre = env_int("ORKB_TC_PRE", 0);
+  t.pipe = env_int("ORKB_PIPE", 1);
   t.gemv_kind = env_int("ORKB_GEMV_KIND", -1);
   t.gemv_cpw = env_int("ORKB_GEMV_CPW", 0);
   t.gemv_tr = env_int("ORKB_GEMV_TR", 0);
@@ -253,14 +254,17 @@ int finish_sync(ork_npu *c, cudaStream_t s, const char *name) {
 // have landed, and its results read back (down) once it has finished. PCIe moves data both ways at once,
 // so the upload of block i + 1 and the readback of block i overlap each other and the kernels; the call
 // takes about the larger of the two transfer directions instead of their sum. Blocks hold about 1 MiB of
-// results each (2 to 8 blocks, rows a multiple of 16).
+// results each (2 to 4 blocks, rows a multiple of 16).
 constexpr size_t kPipeMinBytes = (size_t)1 << 20;
 
 int run_pipelined(ork_npu *c, ork_w *w, int M, const void *A, void *C, size_t esz, const char *name) {
   const size_t arow = (size_t)w->K * esz, crow = (size_t)w->N * 4;
   const size_t abytes = (size_t)M * arow, cbytes = (size_t)M * crow;
   int nb = (int)((cbytes + kPipeMinBytes - 1) / kPipeMinBytes);
-  nb = nb < 2 ? 2 : nb > 8 ? 8 : nb;
+  // at most 4 blocks by default (ORKB_PIPE = 2..8 sets it): the configs[1] step measured 0.930 ms with 4,
+  // 0.943 with 8, 0.951-0.984 in one piece -- each block is one more kernel launch
+  const int nbmax = c->tune.pipe >= 2 && c->tune.pipe <= 8 ? c->tune.pipe : 4;
+  nb = nb < 2 ? 2 : nb > nbmax ? nbmax : nb;
   int R = (M + nb - 1) / nb;
   R = (R + 15) & ~15;
   nb = (M + R - 1) / R;
@@ -302,7 +306,8 @@ int run_sync(ork_npu *c, ork_w *w, int M, const void *A, void *C, int want_dtype
   DeviceGuard dg(c->device);
   const bool a_dev = is_device_ptr(A, c->device) && ((uintptr_t)A % 16 == 0);
   const bool c_dev = is_device_ptr(C, c->device) && ((uintptr_t)C % 4 == 0);
-  if (!a_dev && !c_dev && cbytes >= kPipeMinBytes && M >= 32 && c->up && pinned_host_ptr(A) && pinned_host_ptr(C))
+  if (c->tune.pipe && !a_dev && !c_dev && cbytes >= kPipeMinBytes && M >= 32 && c->up && pinned_host_ptr(A) &&
+      pinned_host_ptr(C))
     return run_pipelined(c, w, M, A, C, esz, name);
   const void *dA = A;
   void *dC = C;

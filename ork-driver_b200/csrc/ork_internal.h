@@ -40,6 +40,7 @@ extern const int8_t kNf4Lut[16];
 //   layer_fused ORKB_LAYER_FUSED (0 multi-launch).
 struct Tuning {
   int tc_tn = 0, tc_na = 0, tc_stages = 0, tc_pair = 0, tc_sk = 0, tc_flags = 1, tc_pre = 0;
+  int pipe = 1;  // ORKB_PIPE: 0 = large host-buffer runs in one piece instead of row blocks; 2..8 = most blocks
   int gemv_kind = -1, gemv_cpw = 0, gemv_tr = 0, gemv_nw = 0;
   int layer_fused = -1;
 };
